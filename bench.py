@@ -1,0 +1,410 @@
+"""Benchmark of the attention hot path (decode, Llama-3.1-8B shapes, 8K context).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = the attention block of one decode token through all 32 layers at
+position 8191 of an 8192-entry fp32 KV cache: per layer, the device-side
+append of the token's K/V row and the decode attention (q.K^T, softmax, .V)
+over all 8192 positions.  Per step the KV traffic
+is 32 x 64 MiB = 2 GiB, far larger than the 126 MB L2, so no step reuses
+another's cache lines.
+
+Printed on rank 0 as one JSON line:
+  value      fp32-equivalent KV bytes read per second (GB/s), whole job,
+             inputs resident in HBM, device time (CUDA events, max over ranks)
+  e2e        the same metric through the host-pointer C ABI (l3p_attn_step
+             per layer: pinned host q/k/v in, host output back, per step)
+  roofline   the decode kernel alone: algorithmic bytes per launch / average
+             launch time, against MEASURED_PEAKS.json's HBM copy bandwidth
+  cpu_baseline  the reference's own CPU attention (oracle/_ref, compiled from
+             llama3pure-c-engine.c with its OpenMP flags) on a bounded sample
+Multi-GPU (torchrun): each rank owns n_kv/N KV heads (head sharding, no
+collective on the data path); value = all ranks' bytes / max-rank time.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from llama3pure_b200.synth import CONFIGS, decode_inputs  # noqa: E402
+
+WORKLOAD = "llama31_8b_decode_8k"
+METRIC = "decode-attn KV GB/s (fp32-equivalent), Llama-3.1-8B shapes, ctx 8K, 32 layers, append+decode per layer"
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------
+# clocks
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-f", self.path],
+                stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------
+# reference / CPU baseline
+
+
+class CpuReference:
+    """The reference's own decode attention (Q8_0 cache as shipped, OpenMP
+    over KV heads as at llama3pure-c-engine.c:3327-3328) on `layers` layers of
+    the workload, each timed call = append row pos + attend, per layer."""
+
+    def __init__(self, layers: int = 2):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+
+        self.kind = "reference" if O.ref_available(fast=True) else "port"
+        self.impl = "ref" if self.kind == "reference" else "port"
+        self.sh = sh = CONFIGS[WORKLOAD]
+        self.layers = layers
+        self.o = O.Oracle(sh, O.MODE_Q8, self.impl, fast=True, n_layers=layers)
+        self.rows = []
+        for layer in range(layers):
+            k, v, q = decode_inputs(sh, layer)
+            self.o.load_kv(layer, 0, k[:, : sh.pos], v[:, : sh.pos])
+            self.rows.append((q, np.ascontiguousarray(k[:, sh.pos]), np.ascontiguousarray(v[:, sh.pos])))
+            del k, v
+        self.threads = min(O.threads(self.impl, fast=True), sh.n_kv_heads)
+        self.bytes_per_layer = 2 * (sh.pos + 1) * sh.n_kv_heads * sh.head_dim * 4
+        self.o.decode(0, sh.pos, *self.rows[0])  # warm
+
+    def step(self) -> float:
+        t0 = time.perf_counter()
+        for layer in range(self.layers):
+            self.o.decode(layer, self.sh.pos, *self.rows[layer])
+        return time.perf_counter() - t0
+
+    def describe(self, reps: int, seconds: float) -> str:
+        return (f"{self.layers} of 32 layers x {reps} reps of {WORKLOAD} decode at pos {self.sh.pos} "
+                f"(Q8_0 cache as shipped, append+attend per layer), {seconds:.1f} s of CPU time")
+
+    def close(self):
+        self.o.close()
+
+
+def cpu_baseline(min_seconds: float = 10.0):
+    ref = CpuReference(layers=2)
+    dts = []
+    while sum(dts) < min_seconds or len(dts) < 3:
+        dts.append(ref.step())
+    gbs = ref.bytes_per_layer * ref.layers * len(dts) / sum(dts) / 1e9
+    out = {"value": round(gbs, 3), "unit": "GB/s", "cores": ref.threads, "kind": ref.kind,
+           "sample": ref.describe(len(dts), sum(dts))}
+    ref.close()
+    return out
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    ref = CpuReference(layers=2)
+    for _ in range(args.warmup):
+        ref.step()
+    dts = [ref.step() for _ in range(args.steps)]
+    value = ref.bytes_per_layer * ref.layers * len(dts) / sum(dts) / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(statistics.median(dts) * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "int8 (Q8_0) + f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "layers_per_step": ref.layers, "pos": ref.sh.pos,
+                   "note": "bounded sample: 2 of the 32 layers per step"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": ref.threads, "kind": ref.kind,
+                         "sample": ref.describe(len(dts), sum(dts))},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    ref.close()
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------
+# our arm
+
+
+class DevView:
+    """A raw device range seen by torch through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.shard import plan_shards
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    sh = CONFIGS[WORKLOAD]
+    L, P = sh.n_layers, sh.pos + 1
+    shard = plan_shards(sh.n_kv_heads, sh.seq_len, world, seq_parts=1)[rank]
+    ctx = AttnContext.for_shape(sh, device=local, kv_head_begin=shard.kv_head_begin,
+                                kv_head_count=shard.kv_head_count)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream)
+
+    # resident cache: positions [0, pos) filled on the device, row pos appended per step
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1000 + rank)
+    hk = shard.kv_head_count
+    for layer in range(L):
+        kp, vp = ctx.kv_device_ptr(layer)
+        kt = torch.as_tensor(DevView(kp, (hk, sh.seq_len, sh.head_dim)), device="cuda")
+        vt = torch.as_tensor(DevView(vp, (hk, sh.seq_len, sh.head_dim)), device="cuda")
+        kt[:, : sh.pos].normal_(generator=g)
+        vt[:, : sh.pos].normal_(generator=g)
+    q = torch.randn((L, sh.n_heads, sh.head_dim), device="cuda", generator=g)
+    knew = torch.randn((L, sh.n_kv_heads, sh.head_dim), device="cuda", generator=g)
+    vnew = torch.randn((L, sh.n_kv_heads, sh.head_dim), device="cuda", generator=g)
+    out = torch.zeros_like(q)
+    torch.cuda.synchronize()
+
+    def step():
+        for layer in range(L):
+            ctx.kv_append_dev(layer, sh.pos, knew[layer], vnew[layer], stream)
+            ctx.decode_dev(layer, sh.pos, q[layer], out[layer], stream)
+
+    # capture one step as a CUDA graph (the step is 2*L small launches)
+    n0 = ctx.launch_count()
+    step()
+    torch.cuda.synchronize()
+    launches_per_step = ctx.launch_count() - n0
+    graph = None
+    if not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        cap_stream = torch.cuda.Stream()
+        cap_stream.wait_stream(stream)
+        with torch.cuda.stream(cap_stream):
+            ctx.set_stream(cap_stream)
+            with torch.cuda.graph(graph, stream=cap_stream):
+                for layer in range(L):
+                    ctx.kv_append_dev(layer, sh.pos, knew[layer], vnew[layer], cap_stream)
+                    ctx.decode_dev(layer, sh.pos, q[layer], out[layer], cap_stream)
+        stream.wait_stream(cap_stream)
+        ctx.set_stream(stream)
+
+    def run_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
+
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize()
+    ctx.check()
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        run_step()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms = t0.elapsed_time(t1)
+    ctx.check()
+
+    # decode kernel alone, per launch, on the launching stream (roofline)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(2 * L)]
+    for i in range(2 * L):
+        layer = i % L
+        ev[i][0].record(stream)
+        ctx.decode_dev(layer, sh.pos, q[layer], out[layer], stream)
+        ev[i][1].record(stream)
+    torch.cuda.synchronize()
+    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev[L:])
+    if clocks:
+        clk = clocks.stop()
+    else:
+        clk = None
+
+    if world > 1:
+        t = torch.tensor([ms, kern_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, kern_ms = t.tolist()
+
+    bytes_per_layer_rank = 2 * P * hk * sh.head_dim * 4
+    total_bytes = bytes_per_layer_rank * world * L * args.steps
+    value = total_bytes / (ms / 1e3) / 1e9
+    ms_step = ms / args.steps
+    peak, peak_kind = measured_peaks()
+    achieved = bytes_per_layer_rank / (kern_ms / 1e3) / 1e9
+
+    # end to end through the host-pointer C ABI (rank 0 at N GPUs: every rank runs it)
+    e2e = None
+    if not args.no_e2e:
+        e2e = run_e2e(ctx, sh, world, args, torch)
+        if world > 1:
+            t = torch.tensor([e2e["ms_per_step"]], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e2e["ms_per_step"] = t.item()
+            e2e["value"] = round(bytes_per_layer_rank * world * L / (e2e["ms_per_step"] / 1e3) / 1e9, 3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) fp32 q/K/V, generated on device)",
+            "config": {"workload": WORKLOAD, "n_layers": L, "n_heads": sh.n_heads, "n_kv_heads": sh.n_kv_heads,
+                       "head_dim": sh.head_dim, "pos": sh.pos, "kv_positions": P,
+                       "parallelism": f"kv-head shards x{world}", "launch": "cuda graph" if graph else "stream",
+                       "l2": "inputs larger than L2 (2 GiB KV per step vs 126 MB L2)"},
+            "us_per_layer": round(ms_step * 1e3 / L, 3),
+            "tokens_per_s": round(1e3 / ms_step, 2),
+            "gpu_launches": launches_per_step * args.steps,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "kernel": "decode_f32_kernel<128,4>", "kernel_us": round(kern_ms * 1e3, 3),
+                         "algorithmic_bytes_per_launch": bytes_per_layer_rank, "traffic": args.traffic},
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def run_e2e(ctx, sh, world, args, torch):
+    """l3p_attn_step per layer with pinned host buffers: H2D of q/k/v, append,
+    decode, D2H of the output, every step."""
+    L = sh.n_layers
+    qh = torch.randn((L, sh.n_heads, sh.head_dim)).pin_memory().numpy()
+    kh = torch.randn((L, sh.n_kv_heads, sh.head_dim)).pin_memory().numpy()
+    vh = torch.randn((L, sh.n_kv_heads, sh.head_dim)).pin_memory().numpy()
+    oh = torch.zeros((L, sh.n_heads, sh.head_dim)).pin_memory().numpy()
+    ctx.set_stream(None)
+
+    def step():
+        for layer in range(L):
+            ctx.step(layer, sh.pos, qh[layer], kh[layer], vh[layer], oh[layer])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    r0, r1 = ctx.owned_rows
+    h2d = L * ((r1 - r0) * sh.head_dim + 2 * sh.n_kv_heads * sh.head_dim) * 4
+    d2h = L * (r1 - r0) * sh.head_dim * 4
+    hk = ctx.kv_head_count
+    bytes_step = 2 * (sh.pos + 1) * hk * sh.head_dim * 4 * L * world
+    return {"value": round(bytes_step / dt / 1e9, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 4),
+            "api": "l3p_attn_step (host pointers, pinned)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="ncu dram bytes per decode launch, if captured (reported as roofline.traffic)")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

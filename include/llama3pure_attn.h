@@ -1,0 +1,163 @@
+/*
+ * llama3pure_attn.h -- C ABI of libllama3pure_attn.so, the B200 (sm_100a)
+ * attention step for llama3pure's C and JavaScript engines.
+ *
+ * The reference has no attention function: attention is inlined in
+ * transformer() (llama3pure-c-engine.c:3299-3359), transformer_prefill()
+ * (c:3562-3612) and the four JS forward functions (llama3pure-js-engine.js:
+ * 5099-5188, 5375-5457, 5624-5721, 5951-6041).  This library is the seam cut
+ * at exactly those lines:
+ *   upstream   post-RoPE q, k, v of one token (or a prompt batch) for layer l;
+ *   downstream the attention output xb[n_heads*head_dim] fed to `wo`
+ *              (c:3362, js:5191).
+ *
+ * Conventions
+ *   - Plain C types only; all sizes in elements unless named *_bytes.
+ *   - q is post-RoPE and NOT yet multiplied by the attention scale; the
+ *     library multiplies it by cfg.scale first, as the reference's RoPE loop
+ *     does (c:3264-3265, c:3288-3289).  An engine that already fused the scale
+ *     into its RoPE passes scale = 1.0f.
+ *   - Functions without a suffix take HOST pointers and return when the result
+ *     is in host memory.  *_dev functions take DEVICE pointers and a
+ *     cudaStream_t passed as void* (NULL = the context's stream) and return
+ *     after enqueueing.
+ *   - Every function returns L3P_OK (0) or a negative L3P_E_* code and never
+ *     exits the process (the reference calls exit(1) on allocation failure,
+ *     c:373-379, c:499-500); l3p_attn_last_error() describes the failure.
+ *   - A context is driven by one host thread (the reference calls attention
+ *     from a single thread with OpenMP inside, c:3327-3328; the JS engine is
+ *     single threaded, js:7199).
+ */
+#ifndef LLAMA3PURE_ATTN_H
+#define LLAMA3PURE_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define L3P_OK 0
+#define L3P_E_INVAL (-1)       /* bad argument or configuration */
+#define L3P_E_RANGE (-2)       /* layer / position outside the cache */
+#define L3P_E_CUDA (-3)        /* a CUDA runtime call failed */
+#define L3P_E_NOMEM (-4)       /* device or host allocation failed */
+#define L3P_E_TIMEOUT (-5)     /* a bounded device-side wait gave up */
+#define L3P_E_UNSUPPORTED (-6) /* geometry without a kernel in this build */
+
+#define L3P_KV_F32 0 /* fp32 KV cache (this build's format) */
+
+/* Attention geometry and placement.  Field meanings follow the reference's
+ * Config (c:211-229) and RunState (c:280-338). */
+typedef struct l3p_attn_config {
+    int n_layers;    /* Config.n_layers (c:214) */
+    int n_heads;     /* Config.n_heads: query heads (c:215) */
+    int n_kv_heads;  /* Config.n_kv_heads (c:216); n_heads % n_kv_heads == 0 */
+    int head_dim;    /* Config.head_dim (c:220); 64, 128 or 256 */
+    int seq_len;     /* Config.seq_len: KV capacity in positions (c:218) */
+    float scale;     /* RunState.attn_scale; 0 => 1.0f/sqrtf(head_dim) (c:434) */
+    int is_gemma3;   /* Config.is_gemma3 (c:222) */
+    int swa_window;  /* Config.swa_window; 0 = no sliding window (c:226) */
+    int swa_pattern; /* Config.swa_pattern (c:228); SWA layers: l%p < p-1 */
+    int device;      /* CUDA device ordinal that holds this context's cache */
+    int kv_head_begin; /* first KV head owned by this context (head sharding) */
+    int kv_head_count; /* KV heads owned; 0 => n_kv_heads - kv_head_begin */
+    int seq_begin;     /* first position owned (sequence sharding) */
+    int seq_count;     /* positions owned; 0 => seq_len - seq_begin */
+    int kv_format;     /* L3P_KV_F32 */
+} l3p_attn_config;
+
+typedef struct l3p_attn_ctx l3p_attn_ctx;
+
+/* Allocate the device KV cache, [layer][owned kv head][owned position]
+ * [head_dim] fp32, the same order as the reference's Q8_0 cache
+ * [layer][kv_head][pos][bytes] (c:365-372).  Replaces the KV part of
+ * malloc_run_state (c:346-502). */
+int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out);
+void l3p_attn_destroy(l3p_attn_ctx* ctx);
+const char* l3p_attn_last_error(const l3p_attn_ctx* ctx);
+/* Synchronise the context's stream and report any device-side error flag
+ * (L3P_E_TIMEOUT after a bounded wait gave up), clearing it. */
+int l3p_attn_check(l3p_attn_ctx* ctx);
+/* Stream used by the host-pointer entry points (NULL = a stream the context
+ * created itself). */
+int l3p_attn_set_stream(l3p_attn_ctx* ctx, void* stream);
+
+/* Write token `pos`'s K and V rows (k, v: [n_kv_heads*head_dim], all heads;
+ * the context stores the heads and position it owns).  Replaces the per-head
+ * cache write of c:3299-3308 / js:5099-5119. */
+int l3p_attn_kv_append(l3p_attn_ctx* ctx, int layer, int pos, const float* k, const float* v);
+int l3p_attn_kv_append_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* k, const float* v,
+                           void* stream);
+
+/* Single-token decode attention at `pos` over cached positions
+ * [start_t, pos] (start_t from the SWA rule, c:3316-3321).  q, out:
+ * [n_heads*head_dim]; only the rows of the owned heads are written.  The
+ * context must own the whole sequence (seq_begin == 0, seq_count covering
+ * pos).  Replaces c:3310-3359 / js:5122-5188, js:5647-5721. */
+int l3p_attn_decode(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* out);
+int l3p_attn_decode_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* out,
+                        void* stream);
+
+/* The whole per-layer attention block of the engines in one host call:
+ * append token `pos`'s K/V rows, then decode q at `pos` (c:3299-3359,
+ * js:5099-5188); one host<->device round trip instead of two. */
+int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
+                  const float* v, float* out);
+
+/* Decode for `n_layers` consecutive layers in one launch (q, out:
+ * [n_layers][n_heads*head_dim]).  For latency-bound shapes whose per-layer
+ * work is smaller than one launch; same arithmetic as l3p_attn_decode. */
+int l3p_attn_decode_layers_dev(l3p_attn_ctx* ctx, int layer0, int n_layers, int pos,
+                               const float* q, float* out, void* stream);
+
+/* Sequence-sharded decode: attention over the positions this context owns
+ * within [start_t, pos], emitted as a partial triple per owned q head:
+ *   part_o  [n_heads][head_dim]  normalised partial output,
+ *   part_ml [n_heads][2]         (m, l): m = running max of score*log2(e),
+ *                                l = sum of 2^(score*log2(e) - m);
+ * an empty range yields m = -inf, l = 0, o = 0.  Combine the partials of all
+ * shards with l3p_attn_lse_merge_dev (after an all-gather between GPUs). */
+int l3p_attn_decode_partial_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q,
+                                float* part_o, float* part_ml, void* stream);
+
+/* Log-sum-exp merge of n_parts partial triples (layouts as above, stacked on
+ * a leading [n_parts] axis) into out [rows][head_dim] for rows
+ * [row_begin, row_begin + n_rows).  Has no counterpart in the reference,
+ * whose softmax is monolithic (c:3350). */
+int l3p_attn_lse_merge_dev(l3p_attn_ctx* ctx, int n_parts, int rows_per_part, int row_begin,
+                           int n_rows, const float* parts_o, const float* parts_ml, float* out,
+                           void* stream);
+
+/* Causal prompt prefill of n_tok tokens at positions [start_pos,
+ * start_pos+n_tok): appends their K/V rows, then each token attends to
+ * [start_t(pos), pos] -- the reference's token-by-token loop c:3499-3613 /
+ * js:5318-5458, js:5895-6042.  q, out: [n_tok][n_heads*head_dim];
+ * k, v: [n_tok][n_kv_heads*head_dim]. */
+int l3p_attn_prefill(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,
+                     const float* k, const float* v, float* out);
+int l3p_attn_prefill_dev(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok,
+                         const float* q, const float* k, const float* v, float* out,
+                         void* stream);
+
+/* Bulk cache fill / read-back for positions [pos0, pos0+n_pos) of one layer,
+ * head-major k, v: [n_kv_heads][n_pos][head_dim] (all heads; the context
+ * copies the slice it owns).  Benchmarks and tests use these; the engines do
+ * not (they append token by token). */
+int l3p_attn_load_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, const float* k,
+                     const float* v);
+int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, float* k, float* v);
+
+/* Device addresses of one layer's owned cache: [kv_head_count][seq_count]
+ * [head_dim] fp32 each. */
+int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v);
+
+/* Number of kernels this library has launched since the context was created
+ * (the benchmark reports it per step). */
+long long l3p_attn_launch_count(const l3p_attn_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LLAMA3PURE_ATTN_H */

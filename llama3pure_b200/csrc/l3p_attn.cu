@@ -1,0 +1,623 @@
+// l3p_attn.cu -- the C ABI of libllama3pure_attn.so (include/llama3pure_attn.h):
+// context, device KV cache, launch planning and the host-pointer wrappers.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "decode.cuh"
+#include "llama3pure_attn.h"
+
+using namespace l3p;
+
+#define L3P_API extern "C" __attribute__((visibility("default")))
+
+struct l3p_attn_ctx {
+  l3p_attn_config cfg{};
+  int hd = 0, G = 0, GT = 1, n_hg = 1;
+  int kvh_count = 0, seq_count = 0;
+  float scale = 1.f;
+  int num_sms = 148;
+  float* kc = nullptr;  // [n_layers][kvh_count][seq_count][hd]
+  float* vc = nullptr;
+  long long layer_elems = 0, head_elems = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  // split-K scratch: partial outputs, (m, l) pairs and per-unit tickets
+  float* ws_o = nullptr;
+  float* ws_ml = nullptr;
+  unsigned* counters = nullptr;
+  long long ws_o_floats = 0, ws_ml_floats = 0, n_counters = 0;
+  // device staging for the host-pointer entry points
+  float* st_buf = nullptr;
+  size_t st_floats = 0;
+  // device error word in mapped pinned host memory
+  int* err_host = nullptr;
+  int* err_dev = nullptr;
+  long long launches = 0;
+  std::string last_error;
+};
+
+namespace {
+
+constexpr long long kWsOFloats = 8ll << 20;  // 32 MiB of split partials
+constexpr long long kCounters = 1 << 16;
+constexpr int kDecodeThreads = 256;  // DecodeCfg<*, *>::kThreads
+
+int fail(l3p_attn_ctx* ctx, int code, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->last_error = buf;
+  }
+  return code;
+}
+
+#define L3P_CUDA(ctx, call)                                                                  \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      return fail((ctx), L3P_E_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
+                  __LINE__);                                                                 \
+  } while (0)
+
+// Makes the context's device current for the duration of an entry point and
+// restores the caller's device afterwards.
+struct DeviceScope {
+  int prev = -1;
+  bool changed = false;
+  explicit DeviceScope(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) changed = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceScope() {
+    if (changed) cudaSetDevice(prev);
+  }
+};
+
+cudaStream_t pick_stream(l3p_attn_ctx* ctx, void* s) {
+  return s ? static_cast<cudaStream_t>(s) : ctx->stream;
+}
+
+// --------------------------------------------------------------------------
+// Kernel table: one instantiation per (head_dim, q heads per CTA).
+
+using DecodeFn = void (*)(const DecodeArgs);
+
+template <int HD, int GT>
+DecodeFn decode_fn() {
+  return decode_f32_kernel<HD, GT>;
+}
+
+template <int HD, int GT>
+int decode_smem() {
+  return DecodeCfg<HD, GT>::kSmemBytes;
+}
+
+struct KernelInfo {
+  DecodeFn fn = nullptr;
+  int smem = 0;
+  int rows = 8;
+};
+
+KernelInfo kernel_for(int hd, int gt) {
+  KernelInfo k;
+#define L3P_CASE(H, T)                                        \
+  if (hd == H && gt == T) {                                   \
+    k.fn = decode_fn<H, T>();                                 \
+    k.smem = decode_smem<H, T>();                             \
+    k.rows = DecodeCfg<H, T>::kR;                             \
+    return k;                                                 \
+  }
+  L3P_CASE(64, 1) L3P_CASE(64, 2) L3P_CASE(64, 4) L3P_CASE(64, 8)
+  L3P_CASE(128, 1) L3P_CASE(128, 2) L3P_CASE(128, 4) L3P_CASE(128, 8)
+  L3P_CASE(256, 1) L3P_CASE(256, 2) L3P_CASE(256, 4) L3P_CASE(256, 8)
+#undef L3P_CASE
+  return k;
+}
+
+// Split-K plan: choose splits per unit minimising an estimate of
+//   waves * (chunk streaming time + per-CTA latency) + final merge time
+// with per-SM streaming at ~40 GB/s (HBM share) and the merging CTA reading
+// partials at ~150 GB/s.
+struct Plan {
+  int nsplit = 1, chunk = 1;
+};
+
+Plan plan_splits(const l3p_attn_ctx* ctx, long long P, long long units, int rows_per_tile) {
+  Plan best;
+  best.chunk = (int)std::max<long long>(P, 1);
+  if (P <= 0) return best;
+  const double row_bytes = 2.0 * ctx->hd * 4.0;
+  const double split_bytes = (double)ctx->GT * ctx->hd * 4.0;
+  double best_cost = 1e300;
+  const int max_ns = (int)std::min<long long>(kMaxSplits, (P + rows_per_tile - 1) / rows_per_tile);
+  for (int ns = 1; ns <= max_ns; ++ns) {
+    long long chunk = (P + ns - 1) / ns;
+    chunk = (chunk + rows_per_tile - 1) / rows_per_tile * rows_per_tile;
+    const long long ns_eff = (P + chunk - 1) / chunk;
+    if (ns_eff > 1 && (units * ns_eff * ctx->GT * ctx->hd > ctx->ws_o_floats || units > ctx->n_counters))
+      continue;
+    const long long ctas = units * ns_eff;
+    const long long waves = (ctas + ctx->num_sms - 1) / ctx->num_sms;
+    double cost = waves * (chunk * row_bytes / 40e3 + 1.5);  // microseconds
+    if (ns_eff > 1) cost += ns_eff * split_bytes / 150e3 + 1.0;
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best.nsplit = (int)ns_eff;
+      best.chunk = (int)chunk;
+    }
+  }
+  return best;
+}
+
+int ensure_staging(l3p_attn_ctx* ctx, size_t floats) {
+  if (floats <= ctx->st_floats) return L3P_OK;
+  if (ctx->st_buf) cudaFree(ctx->st_buf);
+  ctx->st_buf = nullptr;
+  ctx->st_floats = 0;
+  size_t want = std::max(floats, (size_t)1 << 16);
+  if (cudaMalloc(&ctx->st_buf, want * sizeof(float)) != cudaSuccess)
+    return fail(ctx, L3P_E_NOMEM, "staging allocation of %zu floats failed", want);
+  ctx->st_floats = want;
+  return L3P_OK;
+}
+
+int check_layer(l3p_attn_ctx* ctx, int layer) {
+  if (layer < 0 || layer >= ctx->cfg.n_layers)
+    return fail(ctx, L3P_E_RANGE, "layer %d outside [0, %d)", layer, ctx->cfg.n_layers);
+  return L3P_OK;
+}
+
+int read_err(l3p_attn_ctx* ctx) {
+  const int e = *reinterpret_cast<volatile int*>(ctx->err_host);
+  if (e) {
+    *reinterpret_cast<volatile int*>(ctx->err_host) = 0;
+    if (e & kErrTimeout) return fail(ctx, L3P_E_TIMEOUT, "a bounded device wait gave up");
+    return fail(ctx, L3P_E_CUDA, "device error flag %d", e);
+  }
+  return L3P_OK;
+}
+
+// Decode core shared by the single-layer, multi-layer, prefill and partial
+// entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
+int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
+                  const float* q, float* out, float* part_o, float* part_ml, cudaStream_t s) {
+  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT);
+  if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
+  // longest attended range over the slices (upper bound; the kernel clips per slice)
+  const int pos_max = pos0 + (nz - 1) * pos_step;
+  const long long lo = ctx->cfg.seq_begin;
+  const long long hi = std::min<long long>(pos_max + 1, (long long)ctx->cfg.seq_begin + ctx->seq_count);
+  const long long P = std::max<long long>(hi - lo, 0);
+  const long long units = (long long)nz * ctx->kvh_count * ctx->n_hg;
+  const Plan plan = plan_splits(ctx, P, units, ki.rows);
+
+  DecodeArgs a{};
+  a.kc = ctx->kc;
+  a.vc = ctx->vc;
+  a.layer_stride = ctx->layer_elems;
+  a.head_stride = ctx->head_elems;
+  a.q = q;
+  a.q_zstride = (long long)ctx->cfg.n_heads * ctx->hd;
+  a.out = out;
+  a.part_o = part_o;
+  a.part_ml = part_ml;
+  a.ml_zstride = 2ll * ctx->cfg.n_heads;
+  a.ws_o = ctx->ws_o;
+  a.ws_ml = ctx->ws_ml;
+  a.counters = ctx->counters;
+  a.err = ctx->err_dev;
+  a.scale = ctx->scale;
+  a.layer0 = layer0;
+  a.layer_step = layer_step;
+  a.pos0 = pos0;
+  a.pos_step = pos_step;
+  a.seq_begin = ctx->cfg.seq_begin;
+  a.cap = ctx->seq_count;
+  a.kv_head_begin = ctx->cfg.kv_head_begin;
+  a.G = ctx->G;
+  a.n_hg = ctx->n_hg;
+  a.nsplit = plan.nsplit;
+  a.chunk = plan.chunk;
+  a.is_gemma3 = ctx->cfg.is_gemma3;
+  a.swa_window = ctx->cfg.swa_window;
+  a.swa_pattern = ctx->cfg.swa_pattern;
+  a.partial = part_o != nullptr;
+
+  for (int z0 = 0; z0 < nz; z0 += 65535) {
+    const int zc = std::min(nz - z0, 65535);
+    DecodeArgs b = a;
+    b.layer0 = a.layer0 + z0 * layer_step;
+    b.pos0 = a.pos0 + z0 * pos_step;
+    b.q = a.q + (long long)z0 * a.q_zstride;
+    if (b.out) b.out = a.out + (long long)z0 * a.q_zstride;
+    if (b.part_o) b.part_o = a.part_o + (long long)z0 * a.q_zstride;
+    if (b.part_ml) b.part_ml = a.part_ml + (long long)z0 * a.ml_zstride;
+    dim3 grid(plan.nsplit, ctx->kvh_count * ctx->n_hg, zc);
+    ki.fn<<<grid, kDecodeThreads, ki.smem, s>>>(b);
+    ++ctx->launches;
+    L3P_CUDA(ctx, cudaGetLastError());
+  }
+  return L3P_OK;
+}
+
+int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v,
+                  cudaStream_t s) {
+  // clip the tokens to the owned position range
+  const int own_lo = ctx->cfg.seq_begin, own_hi = ctx->cfg.seq_begin + ctx->seq_count;
+  const int t_lo = std::max(pos0, own_lo), t_hi = std::min(pos0 + n_tok, own_hi);
+  if (t_hi <= t_lo) return L3P_OK;
+  const long long src_stride = (long long)ctx->cfg.n_kv_heads * ctx->hd;
+  const long long off = (long long)layer * ctx->layer_elems;
+  const float* ks = k + (long long)(t_lo - pos0) * src_stride;
+  const float* vs = v + (long long)(t_lo - pos0) * src_stride;
+  for (int t0 = t_lo; t0 < t_hi; t0 += 65535) {
+    const int nt = std::min(t_hi - t0, 65535);
+    dim3 grid(nt, ctx->kvh_count);
+    kv_append_kernel<<<grid, ctx->hd / 4, 0, s>>>(ctx->kc + off, ctx->vc + off, ctx->head_elems, ctx->hd,
+                                                   ks + (long long)(t0 - t_lo) * src_stride,
+                                                   vs + (long long)(t0 - t_lo) * src_stride, src_stride,
+                                                   ctx->cfg.kv_head_begin, t0 - own_lo);
+    ++ctx->launches;
+    L3P_CUDA(ctx, cudaGetLastError());
+  }
+  return L3P_OK;
+}
+
+int check_pos_full(l3p_attn_ctx* ctx, int pos) {
+  if (pos < 0 || pos >= ctx->cfg.seq_len)
+    return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
+  if (ctx->cfg.seq_begin != 0 || ctx->seq_count <= pos)
+    return fail(ctx, L3P_E_INVAL,
+                "full decode needs the whole sequence [0, %d] on this context (owned [%d, %d)); "
+                "use l3p_attn_decode_partial_dev",
+                pos, ctx->cfg.seq_begin, ctx->cfg.seq_begin + ctx->seq_count);
+  return L3P_OK;
+}
+
+}  // namespace
+
+// ==========================================================================
+// Lifecycle
+
+L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
+  if (!out) return L3P_E_INVAL;
+  *out = nullptr;
+  if (!cfg) return L3P_E_INVAL;
+  const l3p_attn_config& c = *cfg;
+  if (c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.seq_len <= 0 ||
+      c.n_heads % c.n_kv_heads != 0 || c.kv_format != L3P_KV_F32)
+    return L3P_E_INVAL;
+  if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return L3P_E_UNSUPPORTED;
+  const int kvh_count = c.kv_head_count > 0 ? c.kv_head_count : c.n_kv_heads - c.kv_head_begin;
+  const int seq_count = c.seq_count > 0 ? c.seq_count : c.seq_len - c.seq_begin;
+  if (c.kv_head_begin < 0 || kvh_count <= 0 || c.kv_head_begin + kvh_count > c.n_kv_heads ||
+      c.seq_begin < 0 || seq_count <= 0 || c.seq_begin + seq_count > c.seq_len)
+    return L3P_E_INVAL;
+
+  l3p_attn_ctx* ctx = new (std::nothrow) l3p_attn_ctx();
+  if (!ctx) return L3P_E_NOMEM;
+  ctx->cfg = c;
+  ctx->cfg.kv_head_count = kvh_count;
+  ctx->cfg.seq_count = seq_count;
+  ctx->hd = c.head_dim;
+  ctx->G = c.n_heads / c.n_kv_heads;
+  ctx->GT = (ctx->G % 8 == 0) ? 8 : (ctx->G % 4 == 0) ? 4 : (ctx->G % 2 == 0) ? 2 : 1;
+  ctx->n_hg = ctx->G / ctx->GT;
+  ctx->kvh_count = kvh_count;
+  ctx->seq_count = seq_count;
+  // attn_scale = 1.0f / sqrtf((float)head_size), c:434
+  ctx->scale = c.scale != 0.f ? c.scale : 1.0f / sqrtf((float)c.head_dim);
+  ctx->head_elems = (long long)seq_count * c.head_dim;
+  ctx->layer_elems = ctx->head_elems * kvh_count;
+
+  DeviceScope dev(c.device);
+  auto bail = [&](int code, const char* what) {
+    fail(ctx, code, "%s", what);
+    l3p_attn_destroy(ctx);
+    return code;
+  };
+  if (cudaSetDevice(c.device) != cudaSuccess) return bail(L3P_E_CUDA, "cudaSetDevice failed");
+  cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, c.device);
+  const size_t cache_bytes = (size_t)ctx->layer_elems * c.n_layers * sizeof(float);
+  if (cudaMalloc(&ctx->kc, cache_bytes) != cudaSuccess || cudaMalloc(&ctx->vc, cache_bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return bail(L3P_E_NOMEM, "KV cache allocation failed");
+  }
+  // zero the cache: positions never written read as 0 rather than garbage
+  if (cudaMemset(ctx->kc, 0, cache_bytes) != cudaSuccess || cudaMemset(ctx->vc, 0, cache_bytes) != cudaSuccess)
+    return bail(L3P_E_CUDA, "cache memset failed");
+  ctx->ws_o_floats = kWsOFloats;
+  ctx->ws_ml_floats = kWsOFloats / 64 * 2;  // GT*HD >= 64, two floats per (split, q head)
+  ctx->n_counters = kCounters;
+  if (cudaMalloc(&ctx->ws_o, ctx->ws_o_floats * sizeof(float)) != cudaSuccess ||
+      cudaMalloc(&ctx->ws_ml, ctx->ws_ml_floats * sizeof(float)) != cudaSuccess ||
+      cudaMalloc(&ctx->counters, ctx->n_counters * sizeof(unsigned)) != cudaSuccess) {
+    cudaGetLastError();
+    return bail(L3P_E_NOMEM, "scratch allocation failed");
+  }
+  if (cudaMemset(ctx->counters, 0, ctx->n_counters * sizeof(unsigned)) != cudaSuccess)
+    return bail(L3P_E_CUDA, "counter memset failed");
+  if (cudaHostAlloc(&ctx->err_host, sizeof(int), cudaHostAllocMapped) != cudaSuccess ||
+      cudaHostGetDevicePointer(&ctx->err_dev, ctx->err_host, 0) != cudaSuccess) {
+    cudaGetLastError();
+    return bail(L3P_E_CUDA, "error word allocation failed");
+  }
+  *ctx->err_host = 0;
+  if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
+    return bail(L3P_E_CUDA, "stream creation failed");
+  ctx->own_stream = true;
+  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT);
+  if (!ki.fn) return bail(L3P_E_UNSUPPORTED, "no decode kernel for this geometry");
+  if (cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem) != cudaSuccess)
+    return bail(L3P_E_CUDA, "cudaFuncSetAttribute failed");
+  *out = ctx;
+  return L3P_OK;
+}
+
+L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
+  if (!ctx) return;
+  DeviceScope dev(ctx->cfg.device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  cudaFree(ctx->kc);
+  cudaFree(ctx->vc);
+  cudaFree(ctx->ws_o);
+  cudaFree(ctx->ws_ml);
+  cudaFree(ctx->counters);
+  cudaFree(ctx->st_buf);
+  if (ctx->err_host) cudaFreeHost(ctx->err_host);
+  if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+L3P_API const char* l3p_attn_last_error(const l3p_attn_ctx* ctx) {
+  return ctx ? ctx->last_error.c_str() : "null context";
+}
+
+L3P_API int l3p_attn_check(l3p_attn_ctx* ctx) {
+  if (!ctx) return L3P_E_INVAL;
+  DeviceScope dev(ctx->cfg.device);
+  L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  L3P_CUDA(ctx, cudaDeviceSynchronize());
+  return read_err(ctx);
+}
+
+L3P_API int l3p_attn_set_stream(l3p_attn_ctx* ctx, void* stream) {
+  if (!ctx) return L3P_E_INVAL;
+  DeviceScope dev(ctx->cfg.device);
+  if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+  ctx->own_stream = false;
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  if (!stream) {
+    L3P_CUDA(ctx, cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+    ctx->own_stream = true;
+  }
+  return L3P_OK;
+}
+
+L3P_API long long l3p_attn_launch_count(const l3p_attn_ctx* ctx) { return ctx ? ctx->launches : -1; }
+
+// ==========================================================================
+// Device-pointer entry points
+
+L3P_API int l3p_attn_kv_append_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* k, const float* v,
+                                   void* stream) {
+  if (!ctx || !k || !v) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
+  DeviceScope dev(ctx->cfg.device);
+  return launch_append(ctx, layer, pos, 1, k, v, pick_stream(ctx, stream));
+}
+
+L3P_API int l3p_attn_decode_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* out, void* stream) {
+  if (!ctx || !q || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (int rc = check_pos_full(ctx, pos)) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream));
+}
+
+L3P_API int l3p_attn_decode_layers_dev(l3p_attn_ctx* ctx, int layer0, int n_layers, int pos, const float* q,
+                                       float* out, void* stream) {
+  if (!ctx || !q || !out || n_layers <= 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer0)) return rc;
+  if (int rc = check_layer(ctx, layer0 + n_layers - 1)) return rc;
+  if (int rc = check_pos_full(ctx, pos)) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  return launch_decode(ctx, layer0, 1, pos, 0, n_layers, q, out, nullptr, nullptr, pick_stream(ctx, stream));
+}
+
+L3P_API int l3p_attn_decode_partial_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* part_o,
+                                        float* part_ml, void* stream) {
+  if (!ctx || !q || !part_o || !part_ml) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
+  DeviceScope dev(ctx->cfg.device);
+  return launch_decode(ctx, layer, 0, pos, 0, 1, q, nullptr, part_o, part_ml, pick_stream(ctx, stream));
+}
+
+L3P_API int l3p_attn_lse_merge_dev(l3p_attn_ctx* ctx, int n_parts, int rows_per_part, int row_begin, int n_rows,
+                                   const float* parts_o, const float* parts_ml, float* out, void* stream) {
+  if (!ctx || !parts_o || !parts_ml || !out || n_parts <= 0 || n_rows < 0 || row_begin < 0 ||
+      row_begin + n_rows > rows_per_part)
+    return ctx ? fail(ctx, L3P_E_INVAL, "bad merge arguments") : L3P_E_INVAL;
+  if (n_rows == 0) return L3P_OK;
+  DeviceScope dev(ctx->cfg.device);
+  lse_merge_kernel<<<n_rows, 128, 0, pick_stream(ctx, stream)>>>(n_parts, rows_per_part, row_begin, ctx->hd,
+                                                                 parts_o, parts_ml, out);
+  ++ctx->launches;
+  L3P_CUDA(ctx, cudaGetLastError());
+  return L3P_OK;
+}
+
+L3P_API int l3p_attn_prefill_dev(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,
+                                 const float* k, const float* v, float* out, void* stream) {
+  if (!ctx || !q || !k || !v || !out || n_tok < 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (n_tok == 0) return L3P_OK;
+  if (start_pos < 0 || start_pos + n_tok > ctx->cfg.seq_len)
+    return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", start_pos, start_pos + n_tok, ctx->cfg.seq_len);
+  if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  if (int rc = launch_append(ctx, layer, start_pos, n_tok, k, v, s)) return rc;
+  return launch_decode(ctx, layer, 0, start_pos, 1, n_tok, q, out, nullptr, nullptr, s);
+}
+
+L3P_API int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v) {
+  if (!ctx) return L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (k) *k = ctx->kc + (long long)layer * ctx->layer_elems;
+  if (v) *v = ctx->vc + (long long)layer * ctx->layer_elems;
+  return L3P_OK;
+}
+
+// ==========================================================================
+// Host-pointer entry points: stage through device memory, synchronise.
+
+namespace {
+
+int finish_host_call(l3p_attn_ctx* ctx) {
+  L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  return read_err(ctx);
+}
+
+// rows of the q/out arrays this context owns: [row_lo, row_hi) in head_dim units
+void owned_rows(const l3p_attn_ctx* ctx, int* row_lo, int* row_hi) {
+  *row_lo = ctx->cfg.kv_head_begin * ctx->G;
+  *row_hi = (ctx->cfg.kv_head_begin + ctx->kvh_count) * ctx->G;
+}
+
+}  // namespace
+
+L3P_API int l3p_attn_kv_append(l3p_attn_ctx* ctx, int layer, int pos, const float* k, const float* v) {
+  if (!ctx || !k || !v) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
+  DeviceScope dev(ctx->cfg.device);
+  const size_t kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
+  if (int rc = ensure_staging(ctx, 2 * kvd)) return rc;
+  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, k, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
+  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf + kvd, v, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (int rc = launch_append(ctx, layer, pos, 1, ctx->st_buf, ctx->st_buf + kvd, ctx->stream)) return rc;
+  return finish_host_call(ctx);
+}
+
+L3P_API int l3p_attn_decode(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* out) {
+  if (!ctx || !q || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (int rc = check_pos_full(ctx, pos)) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd;
+  if (int rc = ensure_staging(ctx, 2 * qd)) return rc;
+  float* dq = ctx->st_buf;
+  float* dout = ctx->st_buf + qd;
+  int r0, r1;
+  owned_rows(ctx, &r0, &r1);
+  L3P_CUDA(ctx, cudaMemcpyAsync(dq + (size_t)r0 * ctx->hd, q + (size_t)r0 * ctx->hd,
+                                (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, dq, dout, nullptr, nullptr, ctx->stream)) return rc;
+  L3P_CUDA(ctx, cudaMemcpyAsync(out + (size_t)r0 * ctx->hd, dout + (size_t)r0 * ctx->hd,
+                                (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  return finish_host_call(ctx);
+}
+
+L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
+                          const float* v, float* out) {
+  if (!ctx || !q || !k || !v || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (int rc = check_pos_full(ctx, pos)) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
+  if (int rc = ensure_staging(ctx, 2 * qd + 2 * kvd)) return rc;
+  float* dq = ctx->st_buf;
+  float* dout = dq + qd;
+  float* dk = dout + qd;
+  float* dv = dk + kvd;
+  int r0, r1;
+  owned_rows(ctx, &r0, &r1);
+  L3P_CUDA(ctx, cudaMemcpyAsync(dk, k, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
+  L3P_CUDA(ctx, cudaMemcpyAsync(dv, v, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
+  L3P_CUDA(ctx, cudaMemcpyAsync(dq + (size_t)r0 * ctx->hd, q + (size_t)r0 * ctx->hd,
+                                (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (int rc = launch_append(ctx, layer, pos, 1, dk, dv, ctx->stream)) return rc;
+  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, dq, dout, nullptr, nullptr, ctx->stream)) return rc;
+  L3P_CUDA(ctx, cudaMemcpyAsync(out + (size_t)r0 * ctx->hd, dout + (size_t)r0 * ctx->hd,
+                                (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  return finish_host_call(ctx);
+}
+
+L3P_API int l3p_attn_prefill(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,
+                             const float* k, const float* v, float* out) {
+  if (!ctx || !q || !k || !v || !out || n_tok < 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (n_tok == 0) return L3P_OK;
+  if (start_pos < 0 || start_pos + n_tok > ctx->cfg.seq_len)
+    return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", start_pos, start_pos + n_tok, ctx->cfg.seq_len);
+  if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
+  const size_t nq = qd * n_tok, nkv = kvd * n_tok;
+  if (int rc = ensure_staging(ctx, 2 * nq + 2 * nkv)) return rc;
+  float* dq = ctx->st_buf;
+  float* dout = dq + nq;
+  float* dk = dout + nq;
+  float* dv = dk + nkv;
+  L3P_CUDA(ctx, cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
+  L3P_CUDA(ctx, cudaMemcpyAsync(dk, k, nkv * 4, cudaMemcpyHostToDevice, ctx->stream));
+  L3P_CUDA(ctx, cudaMemcpyAsync(dv, v, nkv * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (int rc = launch_append(ctx, layer, start_pos, n_tok, dk, dv, ctx->stream)) return rc;
+  if (int rc = launch_decode(ctx, layer, 0, start_pos, 1, n_tok, dq, dout, nullptr, nullptr, ctx->stream)) return rc;
+  int r0, r1;
+  owned_rows(ctx, &r0, &r1);
+  // owned rows of every token: a strided copy
+  L3P_CUDA(ctx, cudaMemcpy2DAsync(out + (size_t)r0 * ctx->hd, qd * 4, dout + (size_t)r0 * ctx->hd, qd * 4,
+                                  (size_t)(r1 - r0) * ctx->hd * 4, n_tok, cudaMemcpyDeviceToHost, ctx->stream));
+  return finish_host_call(ctx);
+}
+
+L3P_API int l3p_attn_load_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, const float* k, const float* v) {
+  if (!ctx || !k || !v || n_pos < 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (pos0 < 0 || pos0 + n_pos > ctx->cfg.seq_len)
+    return fail(ctx, L3P_E_RANGE, "positions [%d, %d) outside [0, %d)", pos0, pos0 + n_pos, ctx->cfg.seq_len);
+  const int lo = std::max(pos0, ctx->cfg.seq_begin), hi = std::min(pos0 + n_pos, ctx->cfg.seq_begin + ctx->seq_count);
+  if (hi <= lo) return L3P_OK;
+  DeviceScope dev(ctx->cfg.device);
+  const size_t row = (size_t)ctx->hd;
+  for (int h = 0; h < ctx->kvh_count; ++h) {
+    const size_t src = ((size_t)(ctx->cfg.kv_head_begin + h) * n_pos + (lo - pos0)) * row;
+    const size_t dst = (size_t)layer * ctx->layer_elems + (size_t)h * ctx->head_elems +
+                       (size_t)(lo - ctx->cfg.seq_begin) * row;
+    L3P_CUDA(ctx, cudaMemcpyAsync(ctx->kc + dst, k + src, (size_t)(hi - lo) * row * 4, cudaMemcpyHostToDevice, ctx->stream));
+    L3P_CUDA(ctx, cudaMemcpyAsync(ctx->vc + dst, v + src, (size_t)(hi - lo) * row * 4, cudaMemcpyHostToDevice, ctx->stream));
+  }
+  return finish_host_call(ctx);
+}
+
+L3P_API int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, float* k, float* v) {
+  if (!ctx || !k || !v || n_pos < 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (pos0 < 0 || pos0 + n_pos > ctx->cfg.seq_len)
+    return fail(ctx, L3P_E_RANGE, "positions [%d, %d) outside [0, %d)", pos0, pos0 + n_pos, ctx->cfg.seq_len);
+  const int lo = std::max(pos0, ctx->cfg.seq_begin), hi = std::min(pos0 + n_pos, ctx->cfg.seq_begin + ctx->seq_count);
+  if (hi <= lo) return L3P_OK;
+  DeviceScope dev(ctx->cfg.device);
+  const size_t row = (size_t)ctx->hd;
+  for (int h = 0; h < ctx->kvh_count; ++h) {
+    const size_t dst = ((size_t)(ctx->cfg.kv_head_begin + h) * n_pos + (lo - pos0)) * row;
+    const size_t src = (size_t)layer * ctx->layer_elems + (size_t)h * ctx->head_elems +
+                       (size_t)(lo - ctx->cfg.seq_begin) * row;
+    L3P_CUDA(ctx, cudaMemcpyAsync(k + dst, ctx->kc + src, (size_t)(hi - lo) * row * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    L3P_CUDA(ctx, cudaMemcpyAsync(v + dst, ctx->vc + src, (size_t)(hi - lo) * row * 4, cudaMemcpyDeviceToHost, ctx->stream));
+  }
+  return finish_host_call(ctx);
+}

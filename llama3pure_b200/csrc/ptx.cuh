@@ -1,0 +1,84 @@
+// ptx.cuh -- inline-PTX helpers for sm_100a: mbarriers with bounded waits and
+// 1-D bulk asynchronous copies (global -> shared, completed on an mbarrier).
+//
+// No multicast form of any copy is used anywhere in this library.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace l3p {
+
+// Error bits a kernel may set in the context's error word.
+enum : int { kErrTimeout = 1, kErrBadArg = 2 };
+
+// A bounded wait gives up after this many failed try_wait probes (each probe
+// may itself block for a hardware-defined interval), sets kErrTimeout and
+// lets the kernel finish without the data.
+constexpr uint32_t kMaxWaitProbes = 1u << 24;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+// Make mbarrier initialisation visible to the async proxy (bulk copies).
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for phase `parity` of `bar` to complete, giving up after
+// kMaxWaitProbes probes.  Returns false on timeout and records it in *err
+// (a plain store: the error word may live in mapped host memory).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+  for (uint32_t i = 0; i < kMaxWaitProbes; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  if (err) *reinterpret_cast<volatile int*>(err) = kErrTimeout;
+  return false;
+}
+
+// L2 policy for data read exactly once (the KV stream of a decode step).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
+// 1-D bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned)
+// from global to this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                         uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ float4 lds128(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+
+}  // namespace l3p

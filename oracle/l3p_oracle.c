@@ -1,0 +1,378 @@
+/*
+ * l3p_oracle.c -- plain-C restatement of llama3pure's attention step.
+ *
+ * TEST INFRASTRUCTURE ONLY (see l3p_oracle.h).  The shipped library never
+ * links or calls this file; it is the checker for the CUDA kernels and the
+ * "port" CPU baseline when the reference harness is not built.
+ *
+ * Every function restates one piece of llama3pure-c-engine.c (cited as
+ * c:<line>) in this repository's own code.  Summation order, rounding points
+ * and the skip rule follow the reference so that, built without fast-math and
+ * without FMA contraction, the results are bit-identical to the reference's
+ * own functions (tests/test_oracle.py checks this against oracle/_ref/ and
+ * against the committed golden vectors in tests/golden/).
+ *
+ * Parity is pinned: golden vectors were produced by the reference's own code
+ * compiled from llama3pure-c-engine.c (oracle/ref_harness.c,
+ * tests/golden/make_golden.py).
+ */
+#include "l3p_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define QK 32          /* values per Q8_0 block (c:120 QK8_0) */
+#define QBLOCK 34      /* bytes per Q8_0 block: fp16 scale + 32 int8 (c:123) */
+#define SKIP_EPS 1e-8f /* near-zero weight skip threshold (c:1602) */
+
+/* ------------------------------------------------------------------------ */
+/* fp16 <-> fp32, as the Q8_0 KV codec stores its block scale.               */
+
+/* fp16 bits -> fp32.  Same values as the reference's 65536-entry table built
+ * by init_fp16_table (c:545-578): exact for normals and subnormals, inf/nan
+ * keep their payload shifted into the fp32 mantissa. */
+float l3po_fp16_to_fp32(uint16_t h) {
+    uint32_t sign = (uint32_t)(h >> 15) << 31;
+    uint32_t e = (h >> 10) & 0x1f;
+    uint32_t m = h & 0x3ff;
+    uint32_t bits;
+    if (e == 0x1f) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else if (e != 0) {
+        bits = sign | ((e + 112u) << 23) | (m << 13);
+    } else if (m == 0) {
+        bits = sign;
+    } else {
+        /* subnormal half: value = m * 2^-24, renormalise */
+        int shift = 0;
+        while ((m & 0x400) == 0) {
+            m <<= 1;
+            ++shift;
+        }
+        bits = sign | ((uint32_t)(113 - shift) << 23) | ((m & 0x3ff) << 13);
+    }
+    float f;
+    memcpy(&f, &bits, sizeof f);
+    return f;
+}
+
+/* fp32 -> fp16 by TRUNCATION of the mantissa (no round-to-nearest), with
+ * values below half's subnormal range flushed to signed zero and anything at
+ * or above 2^16 (including nan) mapped to signed inf -- fp32_to_fp16,
+ * c:585-599. */
+uint16_t l3po_fp32_to_fp16(float f) {
+    uint32_t b;
+    memcpy(&b, &f, sizeof b);
+    uint16_t sign = (uint16_t)((b >> 16) & 0x8000u);
+    int e = (int)((b >> 23) & 0xff) - 112; /* rebias 127 -> 15 */
+    uint32_t sig = (b & 0x7fffffu) | 0x800000u; /* 24-bit significand */
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e > 0) return (uint16_t)(sign | (uint16_t)(e << 10) | (uint16_t)((b >> 13) & 0x3ffu));
+    if (e < -10) return sign;
+    /* subnormal result: drop 13 mantissa bits plus (1 - e) more */
+    return (uint16_t)(sign | (uint16_t)(sig >> (14 - e)));
+}
+
+/* ------------------------------------------------------------------------ */
+/* Q8_0 KV codec                                                             */
+
+/* One Q8_0 encode of `count` floats (multiple of 32): per block, the scale
+ * d = amax/127 stored as truncated fp16, and q = round-half-away(x*127/amax)
+ * clamped to int8 -- quantize_to_q8_0_cache, c:1535-1570. */
+void l3po_q8_quantize(const float* src, uint8_t* dst, int count) {
+    for (int b = 0; b < count / QK; ++b) {
+        const float* x = src + b * QK;
+        uint8_t* blk = dst + b * QBLOCK;
+        float amax = 0.0f;
+        for (int j = 0; j < QK; ++j) {
+            float a = fabsf(x[j]);
+            if (a > amax) amax = a;
+        }
+        float d = amax / 127.0f;
+        float inv = (d > 0.0f) ? 127.0f / amax : 0.0f;
+        uint16_t dh = l3po_fp32_to_fp16(d);
+        blk[0] = (uint8_t)(dh & 0xff);
+        blk[1] = (uint8_t)(dh >> 8);
+        for (int j = 0; j < QK; ++j) {
+            int qv = (int)roundf(x[j] * inv);
+            qv = qv > 127 ? 127 : (qv < -128 ? -128 : qv);
+            blk[2 + j] = (uint8_t)(int8_t)qv;
+        }
+    }
+}
+
+static inline float block_scale(const uint8_t* blk) {
+    return l3po_fp16_to_fp32((uint16_t)(blk[0] | (blk[1] << 8)));
+}
+
+/* Q8_0 x Q8_0 dot: sum over blocks of (d_a*d_b)*int32(sum of int8 products),
+ * accumulated in fp32 in block order -- dot_q8_0_q8_0_cache, c:1574-1597. */
+float l3po_q8_dot(const uint8_t* a, const uint8_t* b, int count) {
+    float acc = 0.0f;
+    for (int blkno = 0; blkno < count / QK; ++blkno) {
+        const uint8_t* ba = a + blkno * QBLOCK;
+        const uint8_t* bb = b + blkno * QBLOCK;
+        int32_t isum = 0;
+        for (int j = 0; j < QK; ++j) isum += (int32_t)(int8_t)ba[2 + j] * (int32_t)(int8_t)bb[2 + j];
+        float dd = block_scale(ba) * block_scale(bb);
+        acc += dd * (float)isum;
+    }
+    return acc;
+}
+
+/* out += w * dequant(V row), skipped entirely when |w| < 1e-8; the product is
+ * formed as int8 * (d*w) -- accum_q8_0_cache, c:1600-1622. */
+void l3po_q8_accum(float* out, const uint8_t* v, float w, int count) {
+    if (w > -SKIP_EPS && w < SKIP_EPS) return;
+    for (int blkno = 0; blkno < count / QK; ++blkno) {
+        const uint8_t* blk = v + blkno * QBLOCK;
+        float sw = block_scale(blk) * w;
+        float* o = out + blkno * QK;
+        for (int j = 0; j < QK; ++j) o[j] += (float)(int8_t)blk[2 + j] * sw;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* softmax and the fp32 forms                                                */
+
+/* In-place softmax: running max (first element seeds it, strict >), expf of
+ * the shifted values summed in order, then scaled by the reciprocal of the
+ * sum -- softmax, c:3167-3186. */
+void l3po_softmax(float* x, int n) {
+    float mx = x[0];
+    for (int i = 1; i < n; ++i)
+        if (x[i] > mx) mx = x[i];
+    float total = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        x[i] = expf(x[i] - mx);
+        total += x[i];
+    }
+    float r = 1.0f / total;
+    for (int i = 0; i < n; ++i) x[i] *= r;
+}
+
+/* Sequential fp32 dot -- vec_dot_f32, c:1487-1494. */
+static inline float dot_f32(const float* x, const float* w, int n) {
+    float acc = 0.0f;
+    for (int i = 0; i < n; ++i) acc += x[i] * w[i];
+    return acc;
+}
+
+/* fp32 form of accum_q8_0_cache (c:1600-1622): same skip rule, out += w*v. */
+static inline void accum_f32(float* out, const float* v, float w, int n) {
+    if (w > -SKIP_EPS && w < SKIP_EPS) return;
+    for (int i = 0; i < n; ++i) out[i] += w * v[i];
+}
+
+/* ------------------------------------------------------------------------ */
+/* Attention step                                                            */
+
+typedef struct {
+    l3p_oracle_cfg c;
+    int mode;
+    float scale;
+    int kv_mul;
+    int hd;
+    int row_q8; /* bytes of one Q8_0 head row */
+    float** kf; /* per layer [Hkv][cap][hd] (f32 mode), lazily allocated */
+    float** vf;
+    uint8_t** kq; /* per layer [Hkv][cap][row_q8] (q8 mode) */
+    uint8_t** vq;
+    float* att;   /* [Hq][cap] scores / weights (c:290, c:363) */
+    float* qs;    /* scaled query [Hq*hd] */
+    uint8_t* qq;  /* Q8_0 query [Hq][row_q8] (c:321-322) */
+} octx;
+
+/* Sliding-window start: only Gemma-3 SWA layers (l % pattern < pattern-1)
+ * with a positive window start at pos-window+1 (clamped at 0) -- c:3246 and
+ * c:3316-3321 (decode), c:3496 and c:3574-3580 (prefill). */
+int l3po_start_t(const l3p_oracle_cfg* c, int layer, int pos) {
+    int swa_layer = c->swa_pattern > 0 && (layer % c->swa_pattern) < c->swa_pattern - 1;
+    if (c->is_gemma3 && swa_layer && c->swa_window > 0) {
+        int s = pos - c->swa_window + 1;
+        return s < 0 ? 0 : s;
+    }
+    return 0;
+}
+
+void* l3po_create(const l3p_oracle_cfg* cfg, int mode) {
+    if (!cfg || cfg->n_layers <= 0 || cfg->n_heads <= 0 || cfg->n_kv_heads <= 0 ||
+        cfg->head_dim <= 0 || cfg->head_dim % QK != 0 || cfg->seq_len <= 0 ||
+        cfg->n_heads % cfg->n_kv_heads != 0)
+        return NULL;
+    octx* o = (octx*)calloc(1, sizeof(octx));
+    if (!o) return NULL;
+    o->c = *cfg;
+    o->mode = mode;
+    o->hd = cfg->head_dim;
+    /* attn_scale = 1/sqrtf(head_size), c:434 */
+    o->scale = cfg->scale != 0.0f ? cfg->scale : 1.0f / sqrtf((float)cfg->head_dim);
+    o->kv_mul = cfg->n_heads / cfg->n_kv_heads; /* c:428 */
+    o->row_q8 = cfg->head_dim / QK * QBLOCK;    /* c:365 head_q8_bytes */
+    o->kf = (float**)calloc((size_t)cfg->n_layers, sizeof(float*));
+    o->vf = (float**)calloc((size_t)cfg->n_layers, sizeof(float*));
+    o->kq = (uint8_t**)calloc((size_t)cfg->n_layers, sizeof(uint8_t*));
+    o->vq = (uint8_t**)calloc((size_t)cfg->n_layers, sizeof(uint8_t*));
+    o->att = (float*)calloc((size_t)cfg->n_heads * cfg->seq_len, sizeof(float));
+    o->qs = (float*)calloc((size_t)cfg->n_heads * cfg->head_dim, sizeof(float));
+    o->qq = (uint8_t*)calloc((size_t)cfg->n_heads * o->row_q8, 1);
+    if (!o->kf || !o->vf || !o->kq || !o->vq || !o->att || !o->qs || !o->qq) {
+        l3po_destroy(o);
+        return NULL;
+    }
+    return o;
+}
+
+void l3po_destroy(void* ctx) {
+    octx* o = (octx*)ctx;
+    if (!o) return;
+    for (int l = 0; l < o->c.n_layers; ++l) {
+        if (o->kf) free(o->kf[l]);
+        if (o->vf) free(o->vf[l]);
+        if (o->kq) free(o->kq[l]);
+        if (o->vq) free(o->vq[l]);
+    }
+    free(o->kf);
+    free(o->vf);
+    free(o->kq);
+    free(o->vq);
+    free(o->att);
+    free(o->qs);
+    free(o->qq);
+    free(o);
+}
+
+/* Make sure the cache of `layer` exists (the reference preallocates all
+ * layers at c:365-379; this oracle allocates on first use so that a test can
+ * hold one layer of a long-context configuration). */
+static int ensure_layer(octx* o, int layer) {
+    size_t rows = (size_t)o->c.n_kv_heads * o->c.seq_len;
+    if (o->mode == L3P_MODE_F32) {
+        if (!o->kf[layer]) o->kf[layer] = (float*)calloc(rows * o->hd, sizeof(float));
+        if (!o->vf[layer]) o->vf[layer] = (float*)calloc(rows * o->hd, sizeof(float));
+        return o->kf[layer] && o->vf[layer];
+    }
+    if (!o->kq[layer]) o->kq[layer] = (uint8_t*)calloc(rows * o->row_q8, 1);
+    if (!o->vq[layer]) o->vq[layer] = (uint8_t*)calloc(rows * o->row_q8, 1);
+    return o->kq[layer] && o->vq[layer];
+}
+
+/* Write one head row of K and V at `pos` -- the per-head cache write of
+ * c:3299-3308 (decode) / c:3562-3567 (prefill); Q8_0-encoded in q8 mode. */
+static void put_row(octx* o, int layer, int kvh, int pos, const float* krow, const float* vrow) {
+    size_t r = (size_t)kvh * o->c.seq_len + (size_t)pos;
+    if (o->mode == L3P_MODE_F32) {
+        memcpy(o->kf[layer] + r * o->hd, krow, (size_t)o->hd * sizeof(float));
+        memcpy(o->vf[layer] + r * o->hd, vrow, (size_t)o->hd * sizeof(float));
+    } else {
+        l3po_q8_quantize(krow, o->kq[layer] + r * o->row_q8, o->hd);
+        l3po_q8_quantize(vrow, o->vq[layer] + r * o->row_q8, o->hd);
+    }
+}
+
+int l3po_load_kv(void* ctx, int layer, int pos0, int n_pos, const float* k, const float* v) {
+    octx* o = (octx*)ctx;
+    if (!o || layer < 0 || layer >= o->c.n_layers || pos0 < 0 || n_pos < 0 ||
+        pos0 + n_pos > o->c.seq_len)
+        return -2;
+    if (!ensure_layer(o, layer)) return -4;
+    for (int h = 0; h < o->c.n_kv_heads; ++h)
+        for (int t = 0; t < n_pos; ++t) {
+            size_t src = ((size_t)h * n_pos + t) * o->hd;
+            put_row(o, layer, h, pos0 + t, k + src, v + src);
+        }
+    return 0;
+}
+
+/* Attention of one token at `pos` over cached positions [start_t, pos],
+ * writing out[Hq*hd].  Body of c:3310-3359 (decode) and c:3569-3612
+ * (prefill, which runs the KV-head loop without OpenMP). */
+static long long attend(octx* o, int layer, int pos, const float* q, float* out, int parallel) {
+    const int hd = o->hd, g = o->kv_mul, cap = o->c.seq_len;
+    const int qdim = o->c.n_heads * hd;
+    /* q arrives post-RoPE; the reference multiplies by attn_scale inside its
+     * RoPE loop (c:3264-3265, c:3288-3289), so scale each element once. */
+    for (int i = 0; i < qdim; ++i) o->qs[i] = q[i] * o->scale;
+    if (o->mode == L3P_MODE_Q8) l3po_q8_quantize(o->qs, o->qq, qdim); /* c:3312 */
+    memset(out, 0, (size_t)qdim * sizeof(float));                      /* c:3314 */
+    const int start = l3po_start_t(&o->c, layer, pos);
+    const int n = pos - start + 1;
+    long long skipped = 0;
+    int kvh;
+#pragma omp parallel for reduction(+ : skipped) if (parallel)
+    for (kvh = 0; kvh < o->c.n_kv_heads; ++kvh) {
+        const size_t base = (size_t)kvh * cap;
+        /* scores, position-first over the GQA group (c:3333-3344) */
+        for (int t = start; t <= pos; ++t) {
+            for (int j = 0; j < g; ++j) {
+                int h = kvh * g + j;
+                float s;
+                if (o->mode == L3P_MODE_F32)
+                    s = dot_f32(o->qs + (size_t)h * hd, o->kf[layer] + (base + t) * hd, hd);
+                else
+                    s = l3po_q8_dot(o->qq + (size_t)h * o->row_q8,
+                                    o->kq[layer] + (base + t) * o->row_q8, hd);
+                o->att[(size_t)h * cap + (t - start)] = s;
+            }
+        }
+        /* per-head softmax then weighted V sum in position order (c:3347-3358) */
+        for (int j = 0; j < g; ++j) {
+            int h = kvh * g + j;
+            float* w = o->att + (size_t)h * cap;
+            l3po_softmax(w, n);
+            float* oh = out + (size_t)h * hd;
+            for (int t = start; t <= pos; ++t) {
+                float wt = w[t - start];
+                if (wt > -SKIP_EPS && wt < SKIP_EPS) ++skipped;
+                if (o->mode == L3P_MODE_F32)
+                    accum_f32(oh, o->vf[layer] + (base + t) * hd, wt, hd);
+                else
+                    l3po_q8_accum(oh, o->vq[layer] + (base + t) * o->row_q8, wt, hd);
+            }
+        }
+    }
+    return skipped;
+}
+
+int l3po_decode(void* ctx, int layer, int pos, const float* q, const float* k_row,
+                const float* v_row, float* out, long long* skipped) {
+    octx* o = (octx*)ctx;
+    if (!o || !q || !out || layer < 0 || layer >= o->c.n_layers || pos < 0 || pos >= o->c.seq_len)
+        return -2;
+    if (!ensure_layer(o, layer)) return -4;
+    if (k_row && v_row)
+        for (int h = 0; h < o->c.n_kv_heads; ++h)
+            put_row(o, layer, h, pos, k_row + (size_t)h * o->hd, v_row + (size_t)h * o->hd);
+    long long s = attend(o, layer, pos, q, out, 1);
+    if (skipped) *skipped = s;
+    return 0;
+}
+
+/* Token-by-token causal prefill: token b (pos = start_pos+b) first appends
+ * its own K/V row, then attends to [start_t, pos] -- c:3499-3613.  The
+ * attention loop there carries no OpenMP pragma (c:3583), so neither does
+ * this one. */
+int l3po_prefill(void* ctx, int layer, int start_pos, int n_tok, const float* q,
+                 const float* k, const float* v, float* out, long long* skipped) {
+    octx* o = (octx*)ctx;
+    if (!o || !q || !out || layer < 0 || layer >= o->c.n_layers || start_pos < 0 || n_tok < 0 ||
+        start_pos + n_tok > o->c.seq_len)
+        return -2;
+    if (!ensure_layer(o, layer)) return -4;
+    const size_t qdim = (size_t)o->c.n_heads * o->hd, kvdim = (size_t)o->c.n_kv_heads * o->hd;
+    long long total = 0;
+    for (int b = 0; b < n_tok; ++b) {
+        int pos = start_pos + b;
+        if (k && v)
+            for (int h = 0; h < o->c.n_kv_heads; ++h)
+                put_row(o, layer, h, pos, k + b * kvdim + (size_t)h * o->hd,
+                        v + b * kvdim + (size_t)h * o->hd);
+        total += attend(o, layer, pos, q + b * qdim, out + b * qdim, 0);
+    }
+    if (skipped) *skipped = total;
+    return 0;
+}

@@ -1,0 +1,90 @@
+/*
+ * l3p_oracle.h -- CPU parity oracle for llama3pure's attention hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  Nothing in the shipped library links, loads or
+ * calls this code; only tests/, __graft_entry__.smoke() and bench.py's CPU
+ * baseline leg use it, and only as the checker / the timed CPU reference.
+ *
+ * Two implementations share this interface:
+ *   - l3po_*   : a plain-C restatement of the reference's attention step
+ *                (oracle/l3p_oracle.c), written for this repository;
+ *   - l3pref_* : a harness (oracle/ref_harness.c) that compiles the
+ *                reference's own llama3pure-c-engine.c in place and drives
+ *                the reference's own static primitives
+ *                (quantize_to_q8_0_cache, dot_q8_0_q8_0_cache,
+ *                accum_q8_0_cache, softmax, vec_dot_f32, malloc_run_state).
+ *                It is built into oracle/_ref/ (git-ignored) and pins the
+ *                restatement bit-for-bit.
+ *
+ * Modes:
+ *   L3P_MODE_F32 : the reference loop with an fp32 KV cache (the 1e-4 parity
+ *                  contract for the fp32 device kernels);
+ *   L3P_MODE_Q8  : the reference exactly as shipped (Q8_0 KV cache and Q8_0
+ *                  query, int8*int8 block dots).
+ *
+ * Layouts (all fp32, row-major):
+ *   q      [n_heads][head_dim]          post-RoPE, NOT yet scaled
+ *   k, v   head-major bulk loads        [n_kv_heads][n_pos][head_dim]
+ *   k_row  one token's K or V           [n_kv_heads][head_dim]
+ *   out    [n_heads][head_dim]
+ */
+#ifndef L3P_ORACLE_H
+#define L3P_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define L3P_MODE_F32 0
+#define L3P_MODE_Q8 1
+
+typedef struct {
+    int n_layers;
+    int n_heads;
+    int n_kv_heads;
+    int head_dim;
+    int seq_len;     /* KV capacity in positions */
+    float scale;     /* 0 => 1/sqrtf(head_dim) */
+    int is_gemma3;
+    int swa_window;  /* 0 => no sliding window */
+    int swa_pattern; /* 0 => no SWA layers */
+} l3p_oracle_cfg;
+
+/* ---- restatement (oracle/l3p_oracle.c) ---- */
+void* l3po_create(const l3p_oracle_cfg* cfg, int mode);
+void l3po_destroy(void* ctx);
+int l3po_load_kv(void* ctx, int layer, int pos0, int n_pos, const float* k, const float* v);
+int l3po_decode(void* ctx, int layer, int pos, const float* q, const float* k_row,
+                const float* v_row, float* out, long long* skipped);
+int l3po_prefill(void* ctx, int layer, int start_pos, int n_tok, const float* q,
+                 const float* k, const float* v, float* out, long long* skipped);
+int l3po_start_t(const l3p_oracle_cfg* cfg, int layer, int pos);
+float l3po_fp16_to_fp32(uint16_t h);
+uint16_t l3po_fp32_to_fp16(float f);
+void l3po_q8_quantize(const float* src, uint8_t* dst, int count);
+float l3po_q8_dot(const uint8_t* a, const uint8_t* b, int count);
+void l3po_q8_accum(float* out, const uint8_t* v, float w, int count);
+void l3po_softmax(float* x, int n);
+
+/* ---- reference harness (oracle/ref_harness.c -> oracle/_ref/) ---- */
+void* l3pref_create(const l3p_oracle_cfg* cfg, int mode);
+void l3pref_destroy(void* ctx);
+int l3pref_load_kv(void* ctx, int layer, int pos0, int n_pos, const float* k, const float* v);
+int l3pref_decode(void* ctx, int layer, int pos, const float* q, const float* k_row,
+                  const float* v_row, float* out, long long* skipped);
+int l3pref_prefill(void* ctx, int layer, int start_pos, int n_tok, const float* q,
+                   const float* k, const float* v, float* out, long long* skipped);
+float l3pref_fp16_to_fp32(uint16_t h);
+uint16_t l3pref_fp32_to_fp16(float f);
+void l3pref_q8_quantize(const float* src, uint8_t* dst, int count);
+float l3pref_q8_dot(const uint8_t* a, const uint8_t* b, int count);
+void l3pref_q8_accum(float* out, const uint8_t* v, float w, int count);
+void l3pref_softmax(float* x, int n);
+int l3pref_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

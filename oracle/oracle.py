@@ -1,0 +1,178 @@
+"""ctypes access to the CPU parity oracle (TEST INFRASTRUCTURE ONLY).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module, and only as the checker or the timed CPU reference.  The shipped
+library (llama3pure_b200) never imports it.
+
+Two backends with one interface:
+  impl="port" -> oracle/liboracle.so        (restatement, l3p_oracle.c)
+  impl="ref"  -> oracle/_ref/libl3p_ref.so  (the reference's own functions,
+                 compiled in place from llama3pure-c-engine.c)
+`fast=True` selects the -Ofast OpenMP builds used for timing.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+MODE_F32 = 0
+MODE_Q8 = 1
+
+_LIBS: dict = {}
+
+
+class OracleCfg(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_int),
+        ("n_heads", C.c_int),
+        ("n_kv_heads", C.c_int),
+        ("head_dim", C.c_int),
+        ("seq_len", C.c_int),
+        ("scale", C.c_float),
+        ("is_gemma3", C.c_int),
+        ("swa_window", C.c_int),
+        ("swa_pattern", C.c_int),
+    ]
+
+
+def lib_path(impl: str, fast: bool = False) -> str:
+    if impl == "port":
+        return os.path.join(HERE, "liboracle_fast.so" if fast else "liboracle.so")
+    if impl == "ref":
+        return os.path.join(HERE, "_ref", "libl3p_ref_fast.so" if fast else "libl3p_ref.so")
+    raise ValueError(impl)
+
+
+def ref_available(fast: bool = False) -> bool:
+    return os.path.exists(lib_path("ref", fast))
+
+
+def build_port() -> None:
+    """Compile the restatement (gcc is present wherever this repo runs)."""
+    subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
+
+
+def _load(impl: str, fast: bool):
+    key = (impl, fast)
+    if key in _LIBS:
+        return _LIBS[key]
+    path = lib_path(impl, fast)
+    if not os.path.exists(path):
+        if impl != "port":
+            raise FileNotFoundError(f"{path} not built (needs the reference source; run `make -C oracle ref`)")
+        build_port()
+    lib = C.CDLL(path)
+    pre = "l3po_" if impl == "port" else "l3pref_"
+    fp = C.POINTER(C.c_float)
+    sig = {
+        "create": (C.c_void_p, [C.POINTER(OracleCfg), C.c_int]),
+        "destroy": (None, [C.c_void_p]),
+        "load_kv": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, fp, fp]),
+        "decode": (C.c_int, [C.c_void_p, C.c_int, C.c_int, fp, fp, fp, fp, C.POINTER(C.c_longlong)]),
+        "prefill": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_int, fp, fp, fp, fp, C.POINTER(C.c_longlong)]),
+        "fp16_to_fp32": (C.c_float, [C.c_uint16]),
+        "fp32_to_fp16": (C.c_uint16, [C.c_float]),
+        "q8_quantize": (None, [fp, C.c_void_p, C.c_int]),
+        "q8_dot": (C.c_float, [C.c_void_p, C.c_void_p, C.c_int]),
+        "q8_accum": (None, [fp, C.c_void_p, C.c_float, C.c_int]),
+        "softmax": (None, [fp, C.c_int]),
+    }
+    fns = {}
+    for name, (res, args) in sig.items():
+        f = getattr(lib, pre + name)
+        f.restype = res
+        f.argtypes = args
+        fns[name] = f
+    if impl == "ref":
+        lib.l3pref_threads.restype = C.c_int
+        fns["threads"] = lib.l3pref_threads
+    _LIBS[key] = (lib, fns)
+    return _LIBS[key]
+
+
+def _fptr(a):
+    if a is None:
+        return None
+    assert a.dtype == np.float32 and a.flags.c_contiguous
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+class Oracle:
+    """One attention context of the oracle: its own KV cache for n_layers."""
+
+    def __init__(self, shape, mode: int = MODE_F32, impl: str = "port", fast: bool = False,
+                 n_layers: int | None = None, seq_len: int | None = None):
+        self.shape = shape
+        self.mode = mode
+        self.impl = impl
+        _, self.f = _load(impl, fast)
+        cfg = OracleCfg(
+            n_layers if n_layers is not None else shape.n_layers,
+            shape.n_heads,
+            shape.n_kv_heads,
+            shape.head_dim,
+            seq_len if seq_len is not None else shape.seq_len,
+            0.0,
+            shape.is_gemma3,
+            shape.swa_window,
+            shape.swa_pattern,
+        )
+        self.cfg = cfg
+        self.ctx = self.f["create"](C.byref(cfg), mode)
+        if not self.ctx:
+            raise RuntimeError("oracle create failed")
+
+    def close(self):
+        if self.ctx:
+            self.f["destroy"](self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load_kv(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        rc = self.f["load_kv"](self.ctx, layer, pos0, k.shape[1], _fptr(k), _fptr(v))
+        if rc:
+            raise RuntimeError(f"oracle load_kv rc={rc}")
+
+    def decode(self, layer: int, pos: int, q: np.ndarray, k_row=None, v_row=None):
+        q = np.ascontiguousarray(q, np.float32)
+        out = np.empty(self.shape.n_heads * self.shape.head_dim, np.float32)
+        sk = C.c_longlong(0)
+        kr = None if k_row is None else np.ascontiguousarray(k_row, np.float32)
+        vr = None if v_row is None else np.ascontiguousarray(v_row, np.float32)
+        rc = self.f["decode"](self.ctx, layer, pos, _fptr(q), _fptr(kr), _fptr(vr), _fptr(out), C.byref(sk))
+        if rc:
+            raise RuntimeError(f"oracle decode rc={rc}")
+        return out.reshape(self.shape.n_heads, self.shape.head_dim), int(sk.value)
+
+    def prefill(self, layer: int, start_pos: int, q: np.ndarray, k: np.ndarray, v: np.ndarray):
+        q = np.ascontiguousarray(q, np.float32)
+        k = np.ascontiguousarray(k, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        n = q.shape[0]
+        out = np.empty((n, self.shape.n_heads, self.shape.head_dim), np.float32)
+        sk = C.c_longlong(0)
+        rc = self.f["prefill"](self.ctx, layer, start_pos, n, _fptr(q), _fptr(k), _fptr(v), _fptr(out), C.byref(sk))
+        if rc:
+            raise RuntimeError(f"oracle prefill rc={rc}")
+        return out, int(sk.value)
+
+
+def primitives(impl: str = "port"):
+    """The codec/softmax primitives of one backend, for exhaustive pinning."""
+    return _load(impl, False)[1]
+
+
+def threads(impl: str = "ref", fast: bool = True) -> int:
+    fns = _load(impl, fast)[1]
+    return int(fns["threads"]()) if "threads" in fns else 1

@@ -1,0 +1,144 @@
+"""Generate tests/golden/attn_golden.npz from the REFERENCE's own code.
+
+Run in a container that has the reference source (it needs oracle/_ref/,
+built by `make -C oracle ref` from llama3pure-c-engine.c in place):
+
+    python tests/golden/make_golden.py
+
+Each case records its geometry, the SHA-256 of its seeded inputs (so generator
+drift is caught) and the reference's attention output in both oracle modes:
+"f32" (the reference loop with an fp32 KV cache, the 1e-4 contract) and "q8"
+(the reference as shipped, Q8_0 cache).  Large outputs are stored as a row
+subsample plus float64 row sums.
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import oracle as O  # noqa: E402
+from llama3pure_b200.synth import (  # noqa: E402
+    CONFIGS,
+    GEMMA_SWA,
+    AttnShape,
+    decode_inputs,
+    prefill_inputs,
+    sha256_arrays,
+)
+
+PREFILL_ROWS = (0, 1, 2, 31, 32, 33, 1023, 2047)
+
+
+def decode_cases():
+    c = CONFIGS
+    small = AttnShape("mha_hd32", 1, 4, 4, 32, 128, pos=100, seed=11)
+    return [
+        ("l1b_layer0", c["llama32_1b_decode"], 0, False),
+        ("l1b_layer5", c["llama32_1b_decode"], 5, False),
+        ("l8b_8k_layer0_append", c["llama31_8b_decode_8k"], 0, True),
+        ("l8b_128k_layer0", c["llama31_8b_decode_128k"], 0, False),
+        ("gemma_layer0", c["gemma_2b_decode"], 0, False),
+        ("gemma_swa_layer0", GEMMA_SWA, 0, False),
+        ("gemma_swa_layer5", GEMMA_SWA, 5, False),
+        ("pos0", c["llama32_1b_decode"].with_(pos=0), 0, False),
+        ("gemma_window1", GEMMA_SWA.with_(swa_window=1), 0, False),
+        ("mha_hd32", small, 0, False),
+        ("gqa2_hd256_odd", AttnShape("gqa2", 1, 4, 2, 256, 700, pos=612, seed=12), 0, True),
+    ]
+
+
+def prefill_cases():
+    return [
+        ("prefill_gqa_s48", AttnShape("pf_gqa", 1, 8, 2, 128, 48, pos=47, seed=4, prefill=True), 0),
+        ("prefill_mqa_swa_s80", AttnShape("pf_swa", 1, 8, 1, 256, 80, pos=79, seed=5, prefill=True,
+                                          is_gemma3=1, swa_window=16, swa_pattern=6), 0),
+        ("prefill_8b_2k_layer0", CONFIGS["llama31_8b_prefill_2k"], 0),
+    ]
+
+
+def run_decode(shape: AttnShape, layer: int, append: bool, mode: int):
+    k, v, q = decode_inputs(shape, layer)
+    o = O.Oracle(shape, mode, "ref", n_layers=layer + 1)
+    if append:
+        o.load_kv(layer, 0, k[:, : shape.pos], v[:, : shape.pos])
+        out, sk = o.decode(layer, shape.pos, q, k[:, shape.pos].copy(), v[:, shape.pos].copy())
+    else:
+        o.load_kv(layer, 0, k, v)
+        out, sk = o.decode(layer, shape.pos, q)
+    o.close()
+    return out, sk, sha256_arrays(k, v, q)
+
+
+def run_prefill(shape: AttnShape, layer: int, mode: int):
+    k, v, q = prefill_inputs(shape, layer)
+    o = O.Oracle(shape, mode, "ref", n_layers=layer + 1)
+    out, sk = o.prefill(layer, 0, q, k, v)
+    o.close()
+    return out, sk, sha256_arrays(k, v, q)
+
+
+def main():
+    if not O.ref_available():
+        sys.exit("oracle/_ref/libl3p_ref.so missing: run `make -C oracle ref` where the reference source exists")
+    data = {}
+    names = []
+    for name, shape, layer, append in decode_cases():
+        for mode, tag in ((O.MODE_F32, "f32"), (O.MODE_Q8, "q8")):
+            out, sk, sha = run_decode(shape, layer, append, mode)
+            data[f"{name}/{tag}"] = out
+            data[f"{name}/{tag}_skipped"] = np.int64(sk)
+        data[f"{name}/sha256"] = np.array(sha)
+        data[f"{name}/geom"] = np.array([shape.n_heads, shape.n_kv_heads, shape.head_dim, shape.seq_len,
+                                         shape.pos, shape.seed, layer, int(append), shape.is_gemma3,
+                                         shape.swa_window, shape.swa_pattern], np.int64)
+        data[f"{name}/k_scale"] = np.float64(shape.k_scale)
+        names.append(name)
+        print("decode", name, "done", flush=True)
+    for name, shape, layer in prefill_cases():
+        for mode, tag in ((O.MODE_F32, "f32"), (O.MODE_Q8, "q8")):
+            out, sk, sha = run_prefill(shape, layer, mode)
+            s = out.shape[0]
+            rows = np.array([r for r in PREFILL_ROWS if r < s] if s > 32 else list(range(s)), np.int64)
+            data[f"{name}/{tag}_rows"] = rows
+            data[f"{name}/{tag}"] = out[rows]
+            data[f"{name}/{tag}_rowsum"] = out.astype(np.float64).sum(axis=(1, 2))
+            data[f"{name}/{tag}_skipped"] = np.int64(sk)
+        data[f"{name}/sha256"] = np.array(sha)
+        data[f"{name}/geom"] = np.array([shape.n_heads, shape.n_kv_heads, shape.head_dim, shape.seq_len,
+                                         shape.pos, shape.seed, layer, 0, shape.is_gemma3,
+                                         shape.swa_window, shape.swa_pattern], np.int64)
+        data[f"{name}/k_scale"] = np.float64(shape.k_scale)
+        names.append(name)
+        print("prefill", name, "done", flush=True)
+
+    # codec known-answer vectors from the reference's own primitives
+    prim = O.primitives("ref")
+    table = np.array([prim["fp16_to_fp32"](h) for h in range(65536)], np.float32)
+    data["kat/fp16_to_fp32_sha256"] = np.array(sha256_arrays(table))
+    data["kat/fp16_to_fp32_sample"] = table[::257]
+    rng = np.random.default_rng(7)
+    xs = (rng.standard_normal(4096).astype(np.float32)
+          * (np.float32(10.0) ** rng.integers(-9, 6, 4096).astype(np.float32))).astype(np.float32)
+    data["kat/fp32_in"] = xs
+    data["kat/fp32_to_fp16"] = np.array([prim["fp32_to_fp16"](float(x)) for x in xs], np.uint16)
+    blk_in = rng.standard_normal(256).astype(np.float32) * np.float32(3.0)
+    blk_in[32:64] = 0.0  # an all-zero block (d = 0 path, c:1550)
+    qbuf = np.zeros(256 // 32 * 34, np.uint8)
+    prim["q8_quantize"](O._fptr(blk_in), qbuf.ctypes.data, 256)
+    data["kat/q8_in"] = blk_in
+    data["kat/q8_blocks"] = qbuf
+    data["cases"] = np.array(names)
+    out_path = os.path.join(HERE, "attn_golden.npz")
+    np.savez_compressed(out_path, **data)
+    print("wrote", out_path, os.path.getsize(out_path), "bytes")
+
+
+if __name__ == "__main__":
+    main()
