@@ -5,7 +5,8 @@
 One step = the attention block of one decode token through all 32 layers at
 position 8191 of an 8192-entry fp32 KV cache: per layer, the device-side
 append of the token's K/V row and the decode attention (q.K^T, softmax, .V)
-over all 8192 positions.  Per step the KV traffic
+over all 8192 positions, one fused kernel launch
+per layer (l3p_attn_step_dev).  Per step the KV traffic
 is 32 x 64 MiB = 2 GiB, far larger than the 126 MB L2, so no step reuses
 another's cache lines.
 
@@ -137,7 +138,7 @@ class CpuReference:
         return time.perf_counter() - t0
 
     def describe(self, reps: int, seconds: float) -> str:
-        return (f"{self.layers} of 32 layers x {reps} reps of {WORKLOAD} decode at pos {self.sh.pos} "
+        return (f"{self.layers} of 32 layers x {reps} steps of {WORKLOAD} decode at pos {self.sh.pos} "
                 f"(Q8_0 cache as shipped, append+attend per layer), {seconds:.1f} s of CPU time")
 
     def close(self):
@@ -145,7 +146,7 @@ class CpuReference:
 
 
 def cpu_baseline(min_seconds: float = 10.0):
-    ref = CpuReference(layers=2)
+    ref = CpuReference(layers=CONFIGS[WORKLOAD].n_layers)
     dts = []
     while sum(dts) < min_seconds or len(dts) < 3:
         dts.append(ref.step())
@@ -160,7 +161,7 @@ def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    ref = CpuReference(layers=2)
+    ref = CpuReference(layers=CONFIGS[WORKLOAD].n_layers)
     for _ in range(args.warmup):
         ref.step()
     dts = [ref.step() for _ in range(args.steps)]
@@ -171,7 +172,7 @@ def run_reference_arm(args):
         "ms_per_step": round(statistics.median(dts) * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "int8 (Q8_0) + f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "layers_per_step": ref.layers, "pos": ref.sh.pos,
-                   "note": "bounded sample: 2 of the 32 layers per step"},
+                   "note": "every step is the full 32-layer workload"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": ref.threads, "kind": ref.kind,
                          "sample": ref.describe(len(dts), sum(dts))},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -234,9 +235,9 @@ def run_ours(args):
     torch.cuda.synchronize()
 
     def step():
+        # per layer ONE launch: the new K/V row is appended and attended in the decode kernel
         for layer in range(L):
-            ctx.kv_append_dev(layer, sh.pos, knew[layer], vnew[layer], stream)
-            ctx.decode_dev(layer, sh.pos, q[layer], out[layer], stream)
+            ctx.step_dev(layer, sh.pos, q[layer], knew[layer], vnew[layer], out[layer], stream)
 
     # capture one step as a CUDA graph (the step is 2*L small launches)
     n0 = ctx.launch_count()
@@ -252,8 +253,7 @@ def run_ours(args):
             ctx.set_stream(cap_stream)
             with torch.cuda.graph(graph, stream=cap_stream):
                 for layer in range(L):
-                    ctx.kv_append_dev(layer, sh.pos, knew[layer], vnew[layer], cap_stream)
-                    ctx.decode_dev(layer, sh.pos, q[layer], out[layer], cap_stream)
+                    ctx.step_dev(layer, sh.pos, q[layer], knew[layer], vnew[layer], out[layer], cap_stream)
         stream.wait_stream(cap_stream)
         ctx.set_stream(stream)
 
@@ -336,6 +336,7 @@ def run_ours(args):
             "config": {"workload": WORKLOAD, "n_layers": L, "n_heads": sh.n_heads, "n_kv_heads": sh.n_kv_heads,
                        "head_dim": sh.head_dim, "pos": sh.pos, "kv_positions": P,
                        "parallelism": f"kv-head shards x{world}", "launch": "cuda graph" if graph else "stream",
+                       "split_k": dict(zip(("ctas_per_kv_head", "cluster"), ctx.decode_plan(sh.pos))),
                        "l2": "inputs larger than L2 (2 GiB KV per step vs 126 MB L2)"},
             "us_per_layer": round(ms_step * 1e3 / L, 3),
             "tokens_per_s": round(1e3 / ms_step, 2),
@@ -354,6 +355,48 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def run_kernel_only(args):
+    """Decode kernel alone on `--layers` layers of the workload (a small case
+    for ncu captures: layers x 64 MiB of KV, still larger than L2)."""
+    import torch
+
+    from llama3pure_b200.attn import AttnContext
+
+    sh = CONFIGS[WORKLOAD]
+    L = args.layers
+    ctx = AttnContext.for_shape(sh, n_layers=L)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(7)
+    for layer in range(L):
+        for p in ctx.kv_device_ptr(layer):
+            torch.as_tensor(DevView(p, (sh.n_kv_heads, sh.seq_len, sh.head_dim)), device="cuda").normal_(generator=g)
+    q = torch.randn((L, sh.n_heads, sh.head_dim), device="cuda", generator=g)
+    out = torch.zeros_like(q)
+    for _ in range(args.warmup):
+        for layer in range(L):
+            ctx.decode_dev(layer, sh.pos, q[layer], out[layer], stream)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        for layer in range(L):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ctx.decode_dev(layer, sh.pos, q[layer], out[layer], stream)
+            b.record(stream)
+            times.append((a, b))
+    torch.cuda.synchronize()
+    ctx.check()
+    us = statistics.median(a.elapsed_time(b) * 1e3 for a, b in times)
+    nbytes = 2 * (sh.pos + 1) * sh.n_kv_heads * sh.head_dim * 4
+    print(json.dumps({"mode": "kernel-only", "layers": L, "launches": len(times), "median_us": round(us, 3),
+                      "gbs": round(nbytes / us / 1e3, 1)}), flush=True)
+    ctx.close()
     return 0
 
 
@@ -396,6 +439,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
+    ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per decode launch, if captured (reported as roofline.traffic)")
     args = ap.parse_args()
@@ -403,6 +448,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return run_reference_arm(args)
+    if args.kernel_only:
+        return run_kernel_only(args)
     return run_ours(args)
 
 

@@ -18,9 +18,9 @@
  *     does (c:3264-3265, c:3288-3289).  An engine that already fused the scale
  *     into its RoPE passes scale = 1.0f.
  *   - Functions without a suffix take HOST pointers and return when the result
- *     is in host memory.  *_dev functions take DEVICE pointers and a
- *     cudaStream_t passed as void* (NULL = the context's stream) and return
- *     after enqueueing.
+ *     is in host memory.  *_dev functions take DEVICE pointers (16-byte
+ *     aligned) and a cudaStream_t passed as void* (NULL = the context's
+ *     stream) and return after enqueueing.
  *   - Every function returns L3P_OK (0) or a negative L3P_E_* code and never
  *     exits the process (the reference calls exit(1) on allocation failure,
  *     c:373-379, c:499-500); l3p_attn_last_error() describes the failure.
@@ -105,6 +105,11 @@ int l3p_attn_decode_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, f
  * js:5099-5188); one host<->device round trip instead of two. */
 int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
                   const float* v, float* out);
+/* Device form of l3p_attn_step: ONE kernel launch that takes the new K/V row
+ * straight from k, v ([n_kv_heads*head_dim]), uses it for position pos and
+ * stores it into the cache. */
+int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
+                      const float* v, float* out, void* stream);
 
 /* Decode for `n_layers` consecutive layers in one launch (q, out:
  * [n_layers][n_heads*head_dim]).  For latency-bound shapes whose per-layer
@@ -154,8 +159,14 @@ int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, float* k
 int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v);
 
 /* Number of kernels this library has launched since the context was created
- * (the benchmark reports it per step). */
+ * (the benchmark reports it per step).  No counterpart in the reference. */
 long long l3p_attn_launch_count(const l3p_attn_ctx* ctx);
+
+/* The split-K decomposition a decode launch at `pos` over `n_slices` layers
+ * (or prefill tokens) would use: CTAs per KV-head group (*nsplit) and CTAs
+ * per thread-block cluster (*cluster).  Introspection for tests and
+ * benchmarks; no counterpart in the reference. */
+int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* nsplit, int* cluster);
 
 #ifdef __cplusplus
 }

@@ -39,6 +39,7 @@ EXPORTS = (
     "l3p_attn_decode",
     "l3p_attn_decode_dev",
     "l3p_attn_step",
+    "l3p_attn_step_dev",
     "l3p_attn_decode_layers_dev",
     "l3p_attn_decode_partial_dev",
     "l3p_attn_lse_merge_dev",
@@ -48,6 +49,7 @@ EXPORTS = (
     "l3p_attn_read_kv",
     "l3p_attn_kv_device_ptr",
     "l3p_attn_launch_count",
+    "l3p_attn_decode_plan",
 )
 
 
@@ -106,6 +108,7 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_decode": (i, [vp, i, i, fp, fp]),
         "l3p_attn_decode_dev": (i, [vp, i, i, fp, fp, vp]),
         "l3p_attn_step": (i, [vp, i, i, fp, fp, fp, fp]),
+        "l3p_attn_step_dev": (i, [vp, i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_decode_layers_dev": (i, [vp, i, i, i, fp, fp, vp]),
         "l3p_attn_decode_partial_dev": (i, [vp, i, i, fp, fp, fp, vp]),
         "l3p_attn_lse_merge_dev": (i, [vp, i, i, i, i, fp, fp, fp, vp]),
@@ -115,6 +118,7 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_read_kv": (i, [vp, i, i, i, fp, fp]),
         "l3p_attn_kv_device_ptr": (i, [vp, i, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
         "l3p_attn_launch_count": (C.c_longlong, [vp]),
+        "l3p_attn_decode_plan": (i, [vp, i, i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)
@@ -223,6 +227,12 @@ class AttnContext:
     def launch_count(self) -> int:
         return int(self.lib.l3p_attn_launch_count(self.h))
 
+    def decode_plan(self, pos: int, n_slices: int = 1) -> tuple[int, int]:
+        """(CTAs per KV-head group, CTAs per cluster) of a decode launch at pos."""
+        ns, cs = C.c_int(), C.c_int()
+        self._ok(self.lib.l3p_attn_decode_plan(self.h, pos, n_slices, C.byref(ns), C.byref(cs)), "decode_plan")
+        return ns.value, cs.value
+
     # -- host-pointer entry points ---------------------------------------------
     def load_kv(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
         self._ok(self.lib.l3p_attn_load_kv(self.h, layer, pos0, k.shape[1], _host(k), _host(v)), "load_kv")
@@ -270,6 +280,10 @@ class AttnContext:
 
     def decode_dev(self, layer, pos, q, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_decode_dev(self.h, layer, pos, _dev(q), _dev(out), _stream(stream)), "decode_dev")
+
+    def step_dev(self, layer, pos, q, k_row, v_row, out, stream=None) -> None:
+        self._ok(self.lib.l3p_attn_step_dev(self.h, layer, pos, _dev(q), _dev(k_row), _dev(v_row), _dev(out),
+                                            _stream(stream)), "step_dev")
 
     def decode_layers_dev(self, layer0, n_layers, pos, q, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_decode_layers_dev(self.h, layer0, n_layers, pos, _dev(q), _dev(out),

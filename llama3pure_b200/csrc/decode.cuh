@@ -4,26 +4,36 @@
 // (llama3pure-c-engine.c:3310-3359): scores q.K^T for every cached position
 // of the window, softmax, and the softmax-weighted sum of V rows, for all
 // q heads of a GQA group (c:3333-3357).  The same kernel serves the
-// token-by-token causal prefill (c:3582-3612) with one grid slice per token.
+// token-by-token causal prefill (c:3582-3612) with one grid slice per token,
+// and can take the new token's K/V row straight from its producer (fused
+// append, c:3299-3308).
 //
 // Work decomposition
 //   grid.x  split of the attended position range (split-K)
 //   grid.y  (owned KV head, group of GT q heads of that KV head)
 //   grid.z  layer (multi-layer decode) or token (prefill)
-// One CTA of 8 warps streams a contiguous chunk of K and V rows of one KV head
-// exactly once and serves all GT q heads of the group with it (the reference
-// re-reads every V row once per q head, c:3352-3357).  Each warp owns a ring
-// of kStages shared-memory stages; lane 0 fills a stage with two 1-D bulk
-// async copies (R rows of K, R rows of V, cp.async.bulk + mbarrier), so every
-// warp keeps kStages-1 tiles in flight while it computes on one.
+// One CTA of 8 warps reads every K and V row of its share of the range once
+// and serves all GT q heads of the group with it (the reference re-reads
+// every V row once per q head, c:3352-3357).  The range is cut into tiles of
+// R rows dealt round-robin over the CTAs of the unit and their warps, so at
+// any moment all SMs read neighbouring tiles.  Each warp streams its tiles
+// through a private ring of kStages shared-memory stages with 16-byte
+// cp.async copies (kStages-1 tiles in flight while it computes on one);
+// copies past the range zero-fill instead of reading.
 //
 // Per tile a warp forms R*GT partial dot products per lane, reduces them with
 // a transposing butterfly (31 shuffles for 32 values, leaving lane j the full
 // score of value j), and runs the online softmax in base 2: running max m and
-// running sum l per q head, accumulator rescaled by 2^(m_old - m_new).  Warps
-// of a CTA are merged in shared memory; splits of a position range are merged
-// by the last CTA to finish (atomic ticket on a per-unit counter in scratch
-// memory), so one launch produces the final normalised output.
+// running sum l per q head, accumulator rescaled by 2^(m_old - m_new).
+//
+// Merging, so that one launch produces the final normalised output:
+//   1. the warps of a CTA, in shared memory;
+//   2. the CTAs of a thread-block cluster (up to 16, one cluster per unit
+//      when it fits in a wave), through distributed shared memory, each rank
+//      merging a slice of the output elements;
+//   3. only when a unit spans several clusters (or runs without clusters),
+//      the last part to finish merges the parts' partials from global scratch
+//      (atomic ticket on a per-unit counter).
 //
 // Differences from the reference's arithmetic, all inside the 1e-4 contract:
 //   * summation order (lane-parallel dot products, blocked softmax sums);
@@ -33,12 +43,18 @@
 //     weight when it reads V, so every row contributes; the difference is at
 //     most (number of such rows) * 1e-8 * max|v| per output element.
 #pragma once
+#include <cooperative_groups.h>
+
 #include "ptx.cuh"
 
 namespace l3p {
 
+namespace cg = cooperative_groups;
+
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kMaxSplits = 160;  // splits of one position range per launch
+constexpr int kMaxSplits = 160;  // CTAs sharing one position range per launch
+constexpr int kMaxCluster = 16;  // CTAs of one thread-block cluster (non-portable size)
+constexpr int kMergeBatch = 16;  // partials fetched together by the global merge
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -46,13 +62,29 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 16-byte global->shared copy; src_bytes = 0 writes zeros and reads nothing.
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_addr(smem_dst)), "l"(gmem_src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 struct DecodeArgs {
   const float* kc;         // K cache, all layers: [n_layers][kvh_count][cap][HD]
-  const float* vc;         // V cache, same layout
+  float* vc;               // V cache, same layout
+  float* kc_w;             // writable alias of kc (fused append)
   long long layer_stride;  // kvh_count * cap * HD
   long long head_stride;   // cap * HD
   const float* q;          // row of absolute q head h in slice z: q + z*q_zstride + h*HD
   long long q_zstride;
+  const float* k_new;      // optional: token row of slice z at k_new + z*new_zstride (all KV heads)
+  const float* v_new;
+  long long new_zstride;
   float* out;              // final output, indexed like q (partial == 0)
   float* part_o;           // normalised partial output, indexed like q (partial == 1)
   float* part_ml;          // (m, l) per q head: part_ml + z*ml_zstride + 2*h
@@ -67,32 +99,66 @@ struct DecodeArgs {
   int seq_begin, cap;      // cache row r holds position seq_begin + r
   int kv_head_begin;       // absolute index of the first owned KV head
   int G, n_hg;             // q heads per KV head (kv_mul), groups of GT per KV head
-  int nsplit, chunk;       // splits per unit and positions per split
+  int nsplit;              // CTAs per unit
+  int cluster;             // CTAs per thread-block cluster (1 = no cluster); divides nsplit
   int is_gemma3, swa_window, swa_pattern;
   int partial;
 };
+
+#ifndef L3P_DECODE_WARPS
+#define L3P_DECODE_WARPS 8  // warps per CTA
+#endif
+#ifndef L3P_DECODE_RING_KB
+#define L3P_DECODE_RING_KB 192  // shared-memory ring per CTA
+#endif
+#ifndef L3P_DECODE_ROWS
+#define L3P_DECODE_ROWS 8  // rows per tile for groups of <= 4 q heads and head_dim <= 128
+#endif
 
 template <int HD, int GT>
 struct DecodeCfg {
   static_assert(HD == 64 || HD == 128 || HD == 256, "head_dim");
   static_assert(GT == 1 || GT == 2 || GT == 4 || GT == 8, "group");
-  static constexpr int kWarps = 8;
+  static constexpr int kWarps = L3P_DECODE_WARPS;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kR = (GT >= 8 || HD >= 256) ? 4 : 8;  // rows per tile
+  static constexpr int kR = (GT >= 8 || HD >= 256) ? 4 : L3P_DECODE_ROWS;  // rows per tile
   static constexpr int kNV = kR * GT;           // partial sums per lane per tile
   static constexpr int kLogNV = (kNV == 32) ? 5 : (kNV == 16) ? 4 : (kNV == 8) ? 3 : 2;
   static constexpr int kSH = 5 - kLogNV;        // lane j holds value (j >> kSH)
   static constexpr int kEPL = HD / 32;          // elements of a row per lane
   static constexpr int kTileFloats = kR * HD;
+  static constexpr int kCopies = kTileFloats / 128;     // 16-byte copies per lane per tile
   static constexpr int kStageFloats = 2 * kTileFloats;  // K tile + V tile
   static constexpr int kStageBytes = kStageFloats * 4;
-  static constexpr int kStagesRaw = (24 * 1024) / kStageBytes;
-  static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > 6 ? 6 : kStagesRaw);
+  static constexpr int kStagesRaw = (L3P_DECODE_RING_KB * 1024 / kWarps) / kStageBytes;
+  static constexpr int kStages = kStagesRaw < 1 ? 1 : (kStagesRaw > 8 ? 8 : kStagesRaw);
   static constexpr int kRingBytes = kWarps * kStages * kStageBytes;
-  static constexpr int kSmemBytes = kRingBytes + kWarps * kStages * 8;
+  static constexpr int kSmemBytes = kRingBytes;
+  static_assert(kNV <= 32, "values per tile");
   static_assert(kWarps * GT * HD * 4 <= kRingBytes, "merge buffer fits in the ring");
-  static_assert(kSmemBytes <= 200 * 1024, "ring fits one CTA per SM");
+  static_assert(kMaxSplits * GT * 3 * 4 <= kRingBytes, "split merge buffer fits in the ring");
+  static_assert(kSmemBytes <= 200 * 1024, "ring fits the SM");
+  static constexpr int kCtasPerSm = (kSmemBytes + 8 * 1024) * 2 <= 227 * 1024 ? 2 : 1;
+  // Narrow score phase: 8 lanes share a K row (4 rows per warp pass), so the
+  // cross-lane reduction is 3 levels over 8 values instead of 5 over 32.
+  // Used when a tile holds exactly 8 (row pass, q head) values per lane and
+  // the lane's slice of q fits in registers (head_dim <= 128).
+  static constexpr bool kNarrow = HD <= 128 && (kR / 4) * GT == 8 && GT * (HD / 8) <= 64;
+  static constexpr int kSegC = HD / 32;  // 16-byte chunks of a row per lane (narrow phase)
 };
+
+// Shared-memory position of 16-byte chunk `ch` of a K/V row.  The narrow
+// score phase reads chunks sg*kSegC + c with 8 lanes per row; XOR-ing the chunk
+// with bits of its segment spreads those reads (and the 32-lane V reads) over
+// all eight 16-byte bank groups.
+template <int HD, bool ON>
+__device__ __forceinline__ int swz(int ch) {
+  if constexpr (ON) {
+    return ch ^ ((ch >> 3) & (HD / 32 - 1));
+  } else {
+    return ch;
+  }
+}
 
 // Elements of a row owned by a lane: HD=64 -> {2*lane, 2*lane+1};
 // HD>=128 -> {c*128 + 4*lane + i}, so every warp-wide 16-byte access is
@@ -155,17 +221,19 @@ __device__ __forceinline__ int swa_start(const DecodeArgs& a, int layer, int pos
 }
 
 template <int HD, int GT>
-__global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, 1)
+__global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>::kCtasPerSm)
     decode_f32_kernel(const DecodeArgs a) {
   using C = DecodeCfg<HD, GT>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float* ring = reinterpret_cast<float*>(smem_raw);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw + C::kRingBytes);
-  __shared__ float s_m[C::kWarps][GT];
-  __shared__ float s_l[C::kWarps][GT];
-  __shared__ float s_w[kMaxSplits][GT];  // per-split merge weights
-  __shared__ float s_L[GT];
+  __shared__ float s_m[C::kWarps][GT];   // per-warp running max
+  __shared__ float s_l[C::kWarps][GT];   // per-warp running sum
+  __shared__ float s_ww[C::kWarps][GT];  // warp merge weights
+  __shared__ float s_cm[GT], s_cl[GT];   // CTA partial (max, sum), read by the cluster
+  __shared__ float s_rw[kMaxCluster][GT];  // cluster merge weights
+  __shared__ float s_M[GT], s_L[GT];
   __shared__ int s_last;
+  __shared__ __align__(16) float s_p[C::kNarrow ? C::kWarps : 1][C::kR * GT + 8];  // weights + rescales
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -173,53 +241,99 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, 1)
   const int kvh_local = blockIdx.y / a.n_hg;
   const int hg = blockIdx.y - kvh_local * a.n_hg;
   const int z = blockIdx.z;
-  const int units_per_z = gridDim.y;
-  const int unit = z * units_per_z + blockIdx.y;
+  const int unit = z * gridDim.y + blockIdx.y;
   const int layer = a.layer0 + z * a.layer_step;
   const int pos = a.pos0 + z * a.pos_step;
+  const int kvh = a.kv_head_begin + kvh_local;
 
   const int lo = max(swa_start(a, layer, pos), a.seq_begin);
   const int hi = min(pos + 1, a.seq_begin + a.cap);
-  const int c0 = lo + split * a.chunk;
-  const int n_rows = max(0, min(hi, c0 + a.chunk) - c0);
+  const int n_rows = max(0, hi - lo);
   const int n_tiles = (n_rows + C::kR - 1) / C::kR;
-  const int h0 = (a.kv_head_begin + kvh_local) * a.G + hg * GT;
+  const int h0 = kvh * a.G + hg * GT;
 
   const long long row_off = (long long)layer * a.layer_stride + (long long)kvh_local * a.head_stride +
-                            (long long)(c0 - a.seq_begin) * HD;
+                            (long long)(lo - a.seq_begin) * HD;
   const float* kbase = a.kc + row_off;
   const float* vbase = a.vc + row_off;
+  // the new token's row, when fused: read from the producer instead of the cache
+  const bool fused = a.k_new != nullptr && pos >= lo && pos < hi;
+  const float* knew = fused ? a.k_new + (long long)z * a.new_zstride + (long long)kvh * HD : nullptr;
+  const float* vnew = fused ? a.v_new + (long long)z * a.new_zstride + (long long)kvh * HD : nullptr;
+  const int new_row = pos - lo;  // index of the new token's row in the range
 
-  if (threadIdx.x < C::kWarps * C::kStages) mbar_init(&bars[threadIdx.x], 1);
-  fence_mbar_init();
-  __syncthreads();
+  // tiles of this warp: t = split + nsplit * (warp + kWarps * i)
+  const int first = split + a.nsplit * warp;
+  const int step = a.nsplit * C::kWarps;
+  const int my_tiles = n_tiles > first ? (n_tiles - first + step - 1) / step : 0;
+  float* wring = ring + warp * C::kStages * C::kStageFloats;
 
-  // query rows of the group, scaled as the reference's fused RoPE does
-  float qr[GT][C::kEPL];
+  auto issue = [&](int i) {
+    const int t = first + i * step;
+    const int r0 = t * C::kR;
+    float* kd = wring + (i % C::kStages) * C::kStageFloats;
+    float* vd = kd + C::kTileFloats;
+#pragma unroll
+    for (int c = 0; c < C::kCopies; ++c) {
+      const int off = c * 128 + lane * 4;  // float offset inside the tile
+      const int row = r0 + off / HD;
+      const bool ok = row < n_rows;
+      const float* ks = kbase + (long long)r0 * HD + off;
+      const float* vs = vbase + (long long)r0 * HD + off;
+      if (fused && row == new_row) {
+        ks = knew + (off % HD);
+        vs = vnew + (off % HD);
+      }
+      const int ch = (off % HD) / 4;
+      const int dst = off - 4 * ch + 4 * swz<HD, C::kNarrow>(ch);
+      cp_async16(kd + dst, ok ? ks : kbase, ok ? 16u : 0u);
+      cp_async16(vd + dst, ok ? vs : vbase, ok ? 16u : 0u);
+    }
+  };
+
+  // start the stream before anything else
+#pragma unroll
+  for (int i = 0; i < C::kStages - 1; ++i) {
+    if (i < my_tiles) issue(i);
+    cp_async_commit();
+  }
+
+  // the fused append: one CTA per KV head writes the new row into the cache
+  if (fused && split == 0 && hg == 0) {
+    float* kw = a.kc_w + row_off + (long long)new_row * HD;
+    float* vw = a.vc + row_off + (long long)new_row * HD;
+    for (int e = threadIdx.x; e < HD; e += C::kThreads) {
+      kw[e] = knew[e];
+      vw[e] = vnew[e];
+    }
+  }
+
+  // query rows of the group, scaled as the reference's fused RoPE does.
+  // Wide layout: lane holds elements lane_elem(lane, e) of every row.
+  // Narrow layout: lane (rq, sg) holds elements [sg*HD/8, (sg+1)*HD/8).
+  constexpr int kQ = C::kNarrow ? HD / 8 : C::kEPL;
+  float qr[GT][kQ];
   const float* qz = a.q + (long long)z * a.q_zstride;
 #pragma unroll
   for (int g = 0; g < GT; ++g) {
-    load_row<HD>(qz + (long long)(h0 + g) * HD, qr[g], lane);
+    const float* qrow = qz + (long long)(h0 + g) * HD;
+    if constexpr (C::kNarrow) {
 #pragma unroll
-    for (int e = 0; e < C::kEPL; ++e) qr[g][e] *= a.scale;
-  }
-
-  float* wring = ring + warp * C::kStages * C::kStageFloats;
-  uint64_t* wbar = bars + warp * C::kStages;
-  const int my_tiles = n_tiles > warp ? (n_tiles - warp + C::kWarps - 1) / C::kWarps : 0;
-  uint64_t policy = 0;
-  if (lane == 0) {
-    policy = l2_evict_first_policy();
-    const int pre = my_tiles < C::kStages ? my_tiles : C::kStages;
-    for (int i = 0; i < pre; ++i) {
-      const int tile = warp + i * C::kWarps;
-      const int rows = min(C::kR, n_rows - tile * C::kR);
-      const uint32_t bytes = (uint32_t)rows * HD * 4u;
-      float* st = wring + i * C::kStageFloats;
-      mbar_arrive_expect_tx(&wbar[i], 2u * bytes);
-      bulk_g2s(st, kbase + (long long)tile * C::kR * HD, bytes, &wbar[i], policy);
-      bulk_g2s(st + C::kTileFloats, vbase + (long long)tile * C::kR * HD, bytes, &wbar[i], policy);
+      for (int c = 0; c < C::kSegC; ++c) {
+        const float4 t = *reinterpret_cast<const float4*>(qrow + (lane & 7) * (HD / 8) + 4 * c);
+        qr[g][4 * c + 0] = t.x;
+        qr[g][4 * c + 1] = t.y;
+        qr[g][4 * c + 2] = t.z;
+        qr[g][4 * c + 3] = t.w;
+      }
+    } else {
+      float t[C::kEPL];
+      load_row<HD>(qrow, t, lane);
+#pragma unroll
+      for (int e = 0; e < C::kEPL; ++e) qr[g][e] = t[e];
     }
+#pragma unroll
+    for (int e = 0; e < kQ; ++e) qr[g][e] *= a.scale;
   }
 
   float my_m = -INFINITY, my_l = 0.f;
@@ -229,181 +343,354 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, 1)
 #pragma unroll
     for (int e = 0; e < C::kEPL; ++e) acc[g][e] = 0.f;
 
-  int consumed = 0;
-  bool timed_out = false;
   for (int i = 0; i < my_tiles; ++i) {
-    const int st = i % C::kStages;
-    const bool ready = mbar_wait_bounded(&wbar[st], (uint32_t)((i / C::kStages) & 1), a.err);
-    if (!__all_sync(0xffffffffu, ready)) {
-      timed_out = true;
-      break;
-    }
-    const float* ks = wring + st * C::kStageFloats;
-    const float* vs = ks + C::kTileFloats;
-    const int tile = warp + i * C::kWarps;
-    const int nvalid = min(C::kR, n_rows - tile * C::kR);
-
-    float part[C::kNV];
-#pragma unroll
-    for (int r = 0; r < C::kR; ++r) {
-      float kx[C::kEPL];
-      load_row<HD>(ks + r * HD, kx, lane);
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        float d = 0.f;
-#pragma unroll
-        for (int e = 0; e < C::kEPL; ++e) d = fmaf(qr[g][e], kx[e], d);
-        part[r * GT + g] = d;
-      }
-    }
-    transpose_reduce<C::kNV>(part, lane);
-    const int j = lane >> C::kSH;
-    const float s = (j / GT < nvalid) ? part[0] * kLog2e : -INFINITY;
-    float tmax = s;
-#pragma unroll
-    for (int off = GT << C::kSH; off < 32; off <<= 1)
-      tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-    const float m_new = fmaxf(my_m, tmax);  // finite: row 0 of a tile is valid
-    const float p = fast_exp2(s - m_new);
-    const float alpha = fast_exp2(my_m - m_new);
-    float tsum = p;
-#pragma unroll
-    for (int off = GT << C::kSH; off < 32; off <<= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
-    my_l = my_l * alpha + tsum;
-    my_m = m_new;
-#pragma unroll
-    for (int g = 0; g < GT; ++g) {
-      const float ag = __shfl_sync(0xffffffffu, alpha, g << C::kSH);
-#pragma unroll
-      for (int e = 0; e < C::kEPL; ++e) acc[g][e] *= ag;
-    }
-#pragma unroll
-    for (int r = 0; r < C::kR; ++r) {
-      float vx[C::kEPL];
-      load_row<HD>(vs + r * HD, vx, lane);
-      if (r >= nvalid) {
-        // rows past the chunk's end were not copied; their stage memory is stale
-#pragma unroll
-        for (int e = 0; e < C::kEPL; ++e) vx[e] = 0.f;
-      }
-#pragma unroll
-      for (int g = 0; g < GT; ++g) {
-        const float pr = __shfl_sync(0xffffffffu, p, (r * GT + g) << C::kSH);
-#pragma unroll
-        for (int e = 0; e < C::kEPL; ++e) acc[g][e] = fmaf(pr, vx[e], acc[g][e]);
-      }
-    }
+    if (i + C::kStages - 1 < my_tiles) issue(i + C::kStages - 1);
+    cp_async_commit();
+    cp_async_wait<C::kStages - 1>();
     __syncwarp();
-    consumed = i + 1;
-    if (lane == 0 && i + C::kStages < my_tiles) {
-      const int ni = i + C::kStages;
-      const int ntile = warp + ni * C::kWarps;
-      const int rows = min(C::kR, n_rows - ntile * C::kR);
-      const uint32_t bytes = (uint32_t)rows * HD * 4u;
-      float* stp = wring + st * C::kStageFloats;
-      mbar_arrive_expect_tx(&wbar[st], 2u * bytes);
-      bulk_g2s(stp, kbase + (long long)ntile * C::kR * HD, bytes, &wbar[st], policy);
-      bulk_g2s(stp + C::kTileFloats, vbase + (long long)ntile * C::kR * HD, bytes, &wbar[st], policy);
+    const float* ks = wring + (i % C::kStages) * C::kStageFloats;
+    const float* vs = ks + C::kTileFloats;
+    const int nvalid = min(C::kR, n_rows - (first + i * step) * C::kR);
+
+    if constexpr (C::kNarrow) {
+      // ---- score phase, 8 lanes per K row ----
+      const int rq = lane >> 3, sg = lane & 7;
+      float part[8];
+#pragma unroll
+      for (int pp = 0; pp < C::kR / 4; ++pp) {
+        const float* krow = ks + (rq + 4 * pp) * HD;
+#pragma unroll
+        for (int g = 0; g < GT; ++g) part[pp * GT + g] = 0.f;
+#pragma unroll
+        for (int c = 0; c < C::kSegC; ++c) {
+          const float4 kx = lds128(krow + 4 * swz<HD, true>(sg * C::kSegC + c));
+#pragma unroll
+          for (int g = 0; g < GT; ++g) {
+            float d = part[pp * GT + g];
+            d = fmaf(qr[g][4 * c + 0], kx.x, d);
+            d = fmaf(qr[g][4 * c + 1], kx.y, d);
+            d = fmaf(qr[g][4 * c + 2], kx.z, d);
+            d = fmaf(qr[g][4 * c + 3], kx.w, d);
+            part[pp * GT + g] = d;
+          }
+        }
+      }
+      // transposing reduction over the 8 lanes of a row group: lane sg ends
+      // with value sg = (row pass, q head)
+#pragma unroll
+      for (int n = 8, off = 4; n > 1; n >>= 1, off >>= 1) {
+        const bool upper = (lane & off) != 0;
+#pragma unroll
+        for (int k = 0; k < n / 2; ++k) {
+          const float send = upper ? part[k] : part[k + n / 2];
+          const float keep = upper ? part[k + n / 2] : part[k];
+          part[k] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      }
+      const int g_mine = sg & (GT - 1);
+      const int row_mine = rq + 4 * (sg / GT);
+      const float s = row_mine < nvalid ? part[0] * kLog2e : -INFINITY;
+      // rows of one q head differ in rq (lane bits 3, 4) and in the row pass
+      float tmax = s;
+#pragma unroll
+      for (int off = GT; off < 32; off <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+      const float m_new = fmaxf(my_m, tmax);  // finite: row 0 of a tile is valid
+      const float p = fast_exp2(s - m_new);
+      const float alpha = fast_exp2(my_m - m_new);
+      float tsum = p;
+#pragma unroll
+      for (int off = GT; off < 32; off <<= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
+      my_l = my_l * alpha + tsum;
+      my_m = m_new;
+      // every lane needs every (row, head) weight: publish through shared memory
+      float* sp = s_p[warp];
+      sp[row_mine * GT + g_mine] = p;
+      if (row_mine == 0) sp[C::kR * GT + g_mine] = alpha;
+      __syncwarp();
+      float ag[GT];
+#pragma unroll
+      for (int g = 0; g < GT; g += 4) {
+        const float4 t = lds128(sp + C::kR * GT + g);
+        ag[g] = t.x;
+        if (g + 1 < GT) ag[g + 1] = t.y;
+        if (g + 2 < GT) ag[g + 2] = t.z;
+        if (g + 3 < GT) ag[g + 3] = t.w;
+      }
+#pragma unroll
+      for (int g = 0; g < GT; ++g)
+#pragma unroll
+        for (int e = 0; e < C::kEPL; ++e) acc[g][e] *= ag[g];
+      // ---- value phase, 32 lanes per V row ----
+#pragma unroll
+      for (int r = 0; r < C::kR; ++r) {
+        float vx[C::kEPL];
+        if constexpr (HD == 128) {
+          const float4 t = lds128(vs + r * HD + 4 * swz<HD, true>(lane));
+          vx[0] = t.x;
+          vx[1] = t.y;
+          vx[2] = t.z;
+          vx[3] = t.w;
+        } else {
+          const float2 t =
+              *reinterpret_cast<const float2*>(vs + r * HD + 4 * swz<HD, true>(lane >> 1) + 2 * (lane & 1));
+          vx[0] = t.x;
+          vx[1] = t.y;
+        }
+        float pr[GT];
+#pragma unroll
+        for (int g = 0; g < GT; g += 4) {
+          const float4 t = lds128(sp + r * GT + g);
+          pr[g] = t.x;
+          if (g + 1 < GT) pr[g + 1] = t.y;
+          if (g + 2 < GT) pr[g + 2] = t.z;
+          if (g + 3 < GT) pr[g + 3] = t.w;
+        }
+#pragma unroll
+        for (int g = 0; g < GT; ++g)
+#pragma unroll
+          for (int e = 0; e < C::kEPL; ++e) acc[g][e] = fmaf(pr[g], vx[e], acc[g][e]);
+      }
+    } else {
+      float part[C::kNV];
+  #pragma unroll
+      for (int r = 0; r < C::kR; ++r) {
+        float kx[C::kEPL];
+        load_row<HD>(ks + r * HD, kx, lane);
+  #pragma unroll
+        for (int g = 0; g < GT; ++g) {
+          float d = 0.f;
+  #pragma unroll
+          for (int e = 0; e < C::kEPL; ++e) d = fmaf(qr[g][e], kx[e], d);
+          part[r * GT + g] = d;
+        }
+      }
+      transpose_reduce<C::kNV>(part, lane);
+      const int j = lane >> C::kSH;
+      const float s = (j / GT < nvalid) ? part[0] * kLog2e : -INFINITY;
+      float tmax = s;
+  #pragma unroll
+      for (int off = GT << C::kSH; off < 32; off <<= 1)
+        tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
+      const float m_new = fmaxf(my_m, tmax);  // finite: row 0 of a tile is valid
+      const float p = fast_exp2(s - m_new);
+      const float alpha = fast_exp2(my_m - m_new);
+      float tsum = p;
+  #pragma unroll
+      for (int off = GT << C::kSH; off < 32; off <<= 1) tsum += __shfl_xor_sync(0xffffffffu, tsum, off);
+      my_l = my_l * alpha + tsum;
+      my_m = m_new;
+  #pragma unroll
+      for (int g = 0; g < GT; ++g) {
+        const float ag = __shfl_sync(0xffffffffu, alpha, g << C::kSH);
+  #pragma unroll
+        for (int e = 0; e < C::kEPL; ++e) acc[g][e] *= ag;
+      }
+  #pragma unroll
+      for (int r = 0; r < C::kR; ++r) {
+        float vx[C::kEPL];  // rows past the range were zero-filled
+        load_row<HD>(vs + r * HD, vx, lane);
+  #pragma unroll
+        for (int g = 0; g < GT; ++g) {
+          const float pr = __shfl_sync(0xffffffffu, p, (r * GT + g) << C::kSH);
+  #pragma unroll
+          for (int e = 0; e < C::kEPL; ++e) acc[g][e] = fmaf(pr, vx[e], acc[g][e]);
+        }
+      }
     }
+    __syncwarp();  // every lane is done with this stage before it is refilled
   }
-  if (timed_out && lane == 0) {
-    // drain the copies still in flight (bounded) before the ring is reused
-    const int issued = min(my_tiles, consumed + C::kStages);
-    for (int i = consumed; i < issued; ++i)
-      mbar_wait_bounded(&wbar[i % C::kStages], (uint32_t)((i / C::kStages) & 1), a.err);
-  }
+  cp_async_wait<0>();
   __syncthreads();
 
-  // ---- merge the warps of this CTA (the ring becomes the merge buffer) ----
-  float* wacc = ring;  // [kWarps][GT][HD]
+  // ---- CTA partial: merge the warps (the ring becomes the merge buffer) ----
+  float* wacc = ring;                          // [kWarps][GT][HD]
+  float* cta_o = ring + C::kWarps * GT * HD;   // [GT][HD], unnormalised, relative to s_cm
 #pragma unroll
   for (int g = 0; g < GT; ++g)
 #pragma unroll
     for (int e = 0; e < C::kEPL; ++e) wacc[(warp * GT + g) * HD + lane_elem<HD>(lane, e)] = acc[g][e];
-  if ((lane & ((1 << C::kSH) - 1)) == 0 && (lane >> C::kSH) < GT) {
+  // the lane holding head g's running (max, sum): g (narrow) or g << kSH (wide)
+  if constexpr (C::kNarrow) {
+    if (lane < GT) {
+      s_m[warp][lane] = my_m;
+      s_l[warp][lane] = my_l;
+    }
+  } else if ((lane & ((1 << C::kSH) - 1)) == 0 && (lane >> C::kSH) < GT) {
     s_m[warp][lane >> C::kSH] = my_m;
     s_l[warp][lane >> C::kSH] = my_l;
   }
   __syncthreads();
-
-  const bool single = a.nsplit == 1;
-  for (int idx = threadIdx.x; idx < GT * HD; idx += C::kThreads) {
-    const int g = idx / HD, e = idx - g * HD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < C::kWarps; ++w) M = fmaxf(M, s_m[w][g]);
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < C::kWarps; ++w) {
-        const float f = fast_exp2(s_m[w][g] - M);
-        L = fmaf(s_l[w][g], f, L);
-        O = fmaf(wacc[(w * GT + g) * HD + e], f, O);
-      }
-    }
-    const int h = h0 + g;
-    if (single) {
-      if (!a.partial) {
-        a.out[(long long)z * a.q_zstride + (long long)h * HD + e] = O / L;
-      } else {
-        a.part_o[(long long)z * a.q_zstride + (long long)h * HD + e] = L > 0.f ? O / L : 0.f;
-        if (e == 0) {
-          a.part_ml[(long long)z * a.ml_zstride + 2 * h] = M;
-          a.part_ml[(long long)z * a.ml_zstride + 2 * h + 1] = L;
-        }
-      }
-    } else {
-      const long long slot = (long long)unit * a.nsplit + split;
-      a.ws_o[(slot * GT + g) * HD + e] = O;
-      if (e == 0) {
-        a.ws_ml[(slot * GT + g) * 2] = M;
-        a.ws_ml[(slot * GT + g) * 2 + 1] = L;
-      }
-    }
-  }
-  if (single) return;
-
-  // ---- the last CTA of this unit merges all splits ----
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(&a.counters[unit], 1u) == (unsigned)(a.nsplit - 1));
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-
-  const long long slot0 = (long long)unit * a.nsplit;
   if (threadIdx.x < GT) {
     const int g = threadIdx.x;
     float M = -INFINITY;
-    for (int sp = 0; sp < a.nsplit; ++sp) M = fmaxf(M, __ldcg(&a.ws_ml[((slot0 + sp) * GT + g) * 2]));
+#pragma unroll
+    for (int w = 0; w < C::kWarps; ++w) M = fmaxf(M, s_m[w][g]);
     float L = 0.f;
-    for (int sp = 0; sp < a.nsplit; ++sp) {
-      const float m = __ldcg(&a.ws_ml[((slot0 + sp) * GT + g) * 2]);
-      const float l = __ldcg(&a.ws_ml[((slot0 + sp) * GT + g) * 2 + 1]);
-      const float f = (M == -INFINITY) ? 0.f : fast_exp2(m - M);
-      s_w[sp][g] = f;
-      L = fmaf(l, f, L);
+#pragma unroll
+    for (int w = 0; w < C::kWarps; ++w) {
+      const float f = (M == -INFINITY) ? 0.f : fast_exp2(s_m[w][g] - M);
+      s_ww[w][g] = f;
+      L = fmaf(s_l[w][g], f, L);
     }
-    s_L[g] = L;
-    if (a.partial) {
-      const int h = h0 + g;
-      a.part_ml[(long long)z * a.ml_zstride + 2 * h] = M;
-      a.part_ml[(long long)z * a.ml_zstride + 2 * h + 1] = L;
-    }
+    s_cm[g] = M;
+    s_cl[g] = L;
   }
   __syncthreads();
   for (int idx = threadIdx.x; idx < GT * HD; idx += C::kThreads) {
-    const int g = idx / HD, e = idx - g * HD;
+    const int g = idx / HD;
     float O = 0.f;
-    for (int sp = 0; sp < a.nsplit; ++sp) O = fmaf(__ldcg(&a.ws_o[((slot0 + sp) * GT + g) * HD + e]), s_w[sp][g], O);
-    const float L = s_L[g];
-    const long long o = (long long)z * a.q_zstride + (long long)(h0 + g) * HD + e;
-    if (!a.partial)
-      a.out[o] = O / L;
-    else
-      a.part_o[o] = L > 0.f ? O / L : 0.f;
+#pragma unroll
+    for (int w = 0; w < C::kWarps; ++w) O = fmaf(wacc[w * GT * HD + idx], s_ww[w][g], O);
+    cta_o[idx] = O;
   }
-  if (threadIdx.x == 0) a.counters[unit] = 0u;  // ticket ready for the next launch
+  __syncthreads();
+
+  float* const out_base = (a.partial ? a.part_o : a.out) + (long long)z * a.q_zstride + (long long)h0 * HD;
+  float* const ml_base = a.partial ? a.part_ml + (long long)z * a.ml_zstride + 2 * h0 : nullptr;
+
+  if (a.nsplit == 1) {  // this CTA covers the whole range
+    for (int idx = threadIdx.x; idx < GT * HD; idx += C::kThreads) {
+      const float L = s_cl[idx / HD];
+      out_base[idx] = (a.partial && !(L > 0.f)) ? 0.f : cta_o[idx] / L;
+    }
+    if (ml_base && threadIdx.x < GT) {
+      ml_base[2 * threadIdx.x] = s_cm[threadIdx.x];
+      ml_base[2 * threadIdx.x + 1] = s_cl[threadIdx.x];
+    }
+    return;
+  }
+
+  int n_parts = a.nsplit;  // partials the global stage merges
+  int part = split;
+  int rank = 0, cs = 1;
+  if (a.cluster > 1) {
+    // ---- cluster stage: the CTAs of a cluster merge through distributed shared memory ----
+    cg::cluster_group cluster = cg::this_cluster();
+    cs = (int)cluster.num_blocks();
+    rank = (int)cluster.block_rank();
+    n_parts = a.nsplit / cs;
+    part = split / cs;
+    cluster.sync();  // every CTA partial of the cluster is in shared memory
+    if (threadIdx.x < GT) {
+      const int g = threadIdx.x;
+      float M = -INFINITY;
+      for (int r = 0; r < cs; ++r) M = fmaxf(M, *cluster.map_shared_rank(&s_cm[g], r));
+      float L = 0.f;
+      for (int r = 0; r < cs; ++r) {
+        const float m = *cluster.map_shared_rank(&s_cm[g], r);
+        const float f = (M == -INFINITY) ? 0.f : fast_exp2(m - M);
+        s_rw[r][g] = f;
+        L = fmaf(*cluster.map_shared_rank(&s_cl[g], r), f, L);
+      }
+      s_M[g] = M;
+      s_L[g] = L;
+    }
+    __syncthreads();
+    // this rank owns elements [rank*slice, (rank+1)*slice) of the group's output
+    const int slice = GT * HD / cs;
+    const bool last_stage = n_parts == 1;
+    const long long gslot = ((long long)unit * n_parts + part) * GT * HD;
+    for (int t = threadIdx.x; t < slice; t += C::kThreads) {
+      const int idx = rank * slice + t;
+      const int g = idx / HD;
+      float O = 0.f;
+      for (int r = 0; r < cs; ++r) O = fmaf(*cluster.map_shared_rank(&cta_o[idx], r), s_rw[r][g], O);
+      if (last_stage) {
+        const float L = s_L[g];
+        out_base[idx] = (a.partial && !(L > 0.f)) ? 0.f : O / L;
+      } else {
+        a.ws_o[gslot + idx] = O;
+      }
+    }
+    if (threadIdx.x < GT) {
+      if (last_stage) {
+        if (ml_base && rank == 0) {
+          ml_base[2 * threadIdx.x] = s_M[threadIdx.x];
+          ml_base[2 * threadIdx.x + 1] = s_L[threadIdx.x];
+        }
+      } else if (rank == 0) {
+        a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2] = s_M[threadIdx.x];
+        a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2 + 1] = s_L[threadIdx.x];
+      }
+    }
+    if (last_stage) {
+      cluster.sync();  // no CTA leaves while another still reads its shared memory
+      return;
+    }
+    __threadfence();
+    cluster.sync();  // the cluster's partial is written and visible
+    if (rank == 0 && threadIdx.x == 0) {
+      const int last = atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts - 1);
+      for (int r = 0; r < cs; ++r) *cluster.map_shared_rank(&s_last, r) = last;
+    }
+    cluster.sync();
+  } else {
+    // ---- no cluster: every CTA is a part of the global stage ----
+    const long long gslot = ((long long)unit * n_parts + part) * GT * HD;
+    for (int idx = threadIdx.x; idx < GT * HD; idx += C::kThreads) a.ws_o[gslot + idx] = cta_o[idx];
+    if (threadIdx.x < GT) {
+      a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2] = s_cm[threadIdx.x];
+      a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2 + 1] = s_cl[threadIdx.x];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts - 1);
+    __syncthreads();
+  }
+  if (!s_last) return;
+  __threadfence();
+
+  // ---- global stage: the last part to finish merges all n_parts partials ----
+  // (with a cluster, each rank of the last cluster merges its slice).  Every
+  // thread fetches the (m, l) pairs of its q head and its float4 of each
+  // partial in one batch, so the stage costs a single L2 round trip.
+  const long long slot0 = (long long)unit * n_parts;
+  const int slice4 = GT * HD / 4 / cs;
+  const float2* ml2 = reinterpret_cast<const float2*>(a.ws_ml) + slot0 * GT;  // [n_parts][GT]
+  const float4* o4 = reinterpret_cast<const float4*>(a.ws_o + slot0 * GT * HD);
+  for (int t = threadIdx.x; t < slice4; t += C::kThreads) {
+    const int idx4 = rank * slice4 + t;
+    const int g = (idx4 * 4) / HD;
+    float M = -INFINITY, L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp0 = 0; sp0 < n_parts; sp0 += kMergeBatch) {
+      float2 ml[kMergeBatch];
+      float4 v[kMergeBatch];
+#pragma unroll
+      for (int j = 0; j < kMergeBatch; ++j) {
+        const int sp = sp0 + j;
+        ml[j] = sp < n_parts ? __ldcg(ml2 + (long long)sp * GT + g) : make_float2(-INFINITY, 0.f);
+        v[j] = sp < n_parts ? __ldcg(o4 + (long long)sp * (GT * HD / 4) + idx4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float Mb = M;
+#pragma unroll
+      for (int j = 0; j < kMergeBatch; ++j) Mb = fmaxf(Mb, ml[j].x);
+      if (Mb == -INFINITY) continue;
+      const float r = fast_exp2(M - Mb);  // rescale what was accumulated so far
+      L *= r;
+      O.x *= r;
+      O.y *= r;
+      O.z *= r;
+      O.w *= r;
+#pragma unroll
+      for (int j = 0; j < kMergeBatch; ++j) {
+        const float w = fast_exp2(ml[j].x - Mb);  // 0 for empty partials (m = -inf)
+        L = fmaf(ml[j].y, w, L);
+        O.x = fmaf(v[j].x, w, O.x);
+        O.y = fmaf(v[j].y, w, O.y);
+        O.z = fmaf(v[j].z, w, O.z);
+        O.w = fmaf(v[j].w, w, O.w);
+      }
+      M = Mb;
+    }
+    const float inv = (a.partial && !(L > 0.f)) ? 0.f : 1.f / L;
+    *reinterpret_cast<float4*>(out_base + idx4 * 4) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+    if (ml_base && (idx4 * 4) % HD == 0) {
+      ml_base[2 * g] = M;
+      ml_base[2 * g + 1] = L;
+    }
+  }
+  if (rank == 0 && threadIdx.x == 0) a.counters[unit] = 0u;  // ticket ready for the next launch
 }
 
 // Token K/V rows -> head-major cache rows.  k, v: [n_tok][src_stride] with

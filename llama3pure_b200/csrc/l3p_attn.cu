@@ -6,7 +6,9 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <initializer_list>
 #include <new>
 #include <string>
 
@@ -40,6 +42,11 @@ struct l3p_attn_ctx {
   int* err_host = nullptr;
   int* err_dev = nullptr;
   long long launches = 0;
+  // clusters of 2^i CTAs of this context's decode kernel that fit on the GPU at once
+  int max_clusters[5] = {0, 0, 0, 0, 0};
+  // L3P_DECODE_PLAN="nsplit:cluster" pins the decomposition (tests use it to
+  // exercise every merge path); 0 = automatic
+  int force_nsplit = 0, force_cluster = 0;
   std::string last_error;
 };
 
@@ -47,7 +54,7 @@ namespace {
 
 constexpr long long kWsOFloats = 8ll << 20;  // 32 MiB of split partials
 constexpr long long kCounters = 1 << 16;
-constexpr int kDecodeThreads = 256;  // DecodeCfg<*, *>::kThreads
+constexpr int kDecodeThreads = L3P_DECODE_WARPS * 32;  // DecodeCfg<*, *>::kThreads
 
 int fail(l3p_attn_ctx* ctx, int code, const char* fmt, ...) {
   if (ctx) {
@@ -105,6 +112,7 @@ struct KernelInfo {
   DecodeFn fn = nullptr;
   int smem = 0;
   int rows = 8;
+  int ctas_per_sm = 1;
 };
 
 KernelInfo kernel_for(int hd, int gt) {
@@ -114,6 +122,7 @@ KernelInfo kernel_for(int hd, int gt) {
     k.fn = decode_fn<H, T>();                                 \
     k.smem = decode_smem<H, T>();                             \
     k.rows = DecodeCfg<H, T>::kR;                             \
+    k.ctas_per_sm = DecodeCfg<H, T>::kCtasPerSm;              \
     return k;                                                 \
   }
   L3P_CASE(64, 1) L3P_CASE(64, 2) L3P_CASE(64, 4) L3P_CASE(64, 8)
@@ -123,39 +132,82 @@ KernelInfo kernel_for(int hd, int gt) {
   return k;
 }
 
-// Split-K plan: choose splits per unit minimising an estimate of
-//   waves * (chunk streaming time + per-CTA latency) + final merge time
-// with per-SM streaming at ~40 GB/s (HBM share) and the merging CTA reading
-// partials at ~150 GB/s.
+// Split-K plan: how many CTAs share one unit's position range (nsplit) and
+// how they are grouped into thread-block clusters (cluster | nsplit).  Tiles
+// are dealt round-robin, so every CTA of a unit gets the same share.  The
+// estimate minimised is
+//   streaming: max(all bytes / ~5.3 TB/s, waves * share bytes / ~42 GB/s)
+//   + per-wave latency
+//   + cluster launch and merge (~2.5 us: cluster scheduling costs more than
+//     the merge through distributed shared memory saves at one cluster per unit)
+//   + global merge when a unit spans several clusters or has no cluster
+//     (fence, ticket and an L2 round trip, ~1.5 us, plus the partials' bytes)
+// The bandwidth figures are what one launch sustains on B200 (a 64 MiB
+// stream reaches ~5.3 TB/s with 128 to 148 CTAs, i.e. up to ~42 GB/s per SM).
 struct Plan {
-  int nsplit = 1, chunk = 1;
+  int nsplit = 1;
+  int cluster = 1;
 };
 
-Plan plan_splits(const l3p_attn_ctx* ctx, long long P, long long units, int rows_per_tile) {
+Plan plan_splits(const l3p_attn_ctx* ctx, long long P, long long units, int rows_per_tile, int ctas_per_sm) {
   Plan best;
-  best.chunk = (int)std::max<long long>(P, 1);
   if (P <= 0) return best;
+  if (ctx->force_nsplit > 0) {
+    const long long n_tiles = (P + rows_per_tile - 1) / rows_per_tile;
+    const int cs = ctx->force_cluster > 0 ? ctx->force_cluster : 1;
+    int ci = 0;
+    while ((1 << ci) < cs) ++ci;
+    const int ns = ctx->force_nsplit;
+    const long long gparts = cs > 1 ? ns / cs : ns;
+    const bool ok = (1 << ci) == cs && ci < 5 && ns % cs == 0 && ns <= n_tiles && ns <= kMaxSplits &&
+                    (cs == 1 || ctx->max_clusters[ci] > 0) && ctx->GT * ctx->hd / 4 >= cs &&
+                    (gparts <= 1 || (units * gparts * ctx->GT * ctx->hd <= ctx->ws_o_floats && units <= ctx->n_counters));
+    if (ok) {
+      best.nsplit = ns;
+      best.cluster = cs;
+      return best;
+    }
+  }
   const double row_bytes = 2.0 * ctx->hd * 4.0;
-  const double split_bytes = (double)ctx->GT * ctx->hd * 4.0;
+  const double part_bytes = (double)ctx->GT * ctx->hd * 4.0;
+  const long long n_tiles = (P + rows_per_tile - 1) / rows_per_tile;
+  const long long slots = (long long)ctx->num_sms * ctas_per_sm;
+  const double total_us = (double)units * P * row_bytes / 5300e3;
   double best_cost = 1e300;
-  const int max_ns = (int)std::min<long long>(kMaxSplits, (P + rows_per_tile - 1) / rows_per_tile);
-  for (int ns = 1; ns <= max_ns; ++ns) {
-    long long chunk = (P + ns - 1) / ns;
-    chunk = (chunk + rows_per_tile - 1) / rows_per_tile * rows_per_tile;
-    const long long ns_eff = (P + chunk - 1) / chunk;
-    if (ns_eff > 1 && (units * ns_eff * ctx->GT * ctx->hd > ctx->ws_o_floats || units > ctx->n_counters))
-      continue;
-    const long long ctas = units * ns_eff;
-    const long long waves = (ctas + ctx->num_sms - 1) / ctx->num_sms;
-    double cost = waves * (chunk * row_bytes / 40e3 + 1.5);  // microseconds
-    if (ns_eff > 1) cost += ns_eff * split_bytes / 150e3 + 1.0;
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best.nsplit = (int)ns_eff;
-      best.chunk = (int)chunk;
+  for (int ci = 0; ci < 5; ++ci) {
+    const int cs = 1 << ci;
+    if (cs > 1 && (ctx->max_clusters[ci] <= 0 || cs > n_tiles || ctx->GT * ctx->hd / 4 < cs)) continue;
+    for (int nc = 1; nc * cs <= kMaxSplits && nc * cs <= n_tiles; ++nc) {
+      const int ns = nc * cs;
+      const int gparts = cs > 1 ? nc : ns;  // partials of the global stage
+      const bool global = gparts > 1;
+      if (global && (units * gparts * ctx->GT * ctx->hd > ctx->ws_o_floats || units > ctx->n_counters)) break;
+      long long waves;
+      if (cs > 1)
+        waves = (units * nc + ctx->max_clusters[ci] - 1) / ctx->max_clusters[ci];
+      else
+        waves = (units * ns + slots - 1) / slots;
+      const double share = (double)((n_tiles + ns - 1) / ns) * rows_per_tile * row_bytes;
+      double cost = std::max(total_us, waves * share / 42e3) + waves * 1.0;
+      if (cs > 1) cost += 2.5;  // cluster launches measured ~2-3 us slower at 128 CTAs
+      if (global) cost += 1.5 + gparts * part_bytes / 400e3;
+      if (cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best.nsplit = ns;
+        best.cluster = cs;
+      }
     }
   }
   return best;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Device buffers are read and written 16 bytes at a time.
+int check_aligned(l3p_attn_ctx* ctx, std::initializer_list<const void*> ptrs) {
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return fail(ctx, L3P_E_INVAL, "device pointer %p is not 16-byte aligned", p);
+  return L3P_OK;
 }
 
 int ensure_staging(l3p_attn_ctx* ctx, size_t floats) {
@@ -189,7 +241,8 @@ int read_err(l3p_attn_ctx* ctx) {
 // Decode core shared by the single-layer, multi-layer, prefill and partial
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
-                  const float* q, float* out, float* part_o, float* part_ml, cudaStream_t s) {
+                  const float* q, float* out, float* part_o, float* part_ml, cudaStream_t s,
+                  const float* k_new = nullptr, const float* v_new = nullptr) {
   const KernelInfo ki = kernel_for(ctx->hd, ctx->GT);
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
   // longest attended range over the slices (upper bound; the kernel clips per slice)
@@ -198,11 +251,15 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   const long long hi = std::min<long long>(pos_max + 1, (long long)ctx->cfg.seq_begin + ctx->seq_count);
   const long long P = std::max<long long>(hi - lo, 0);
   const long long units = (long long)nz * ctx->kvh_count * ctx->n_hg;
-  const Plan plan = plan_splits(ctx, P, units, ki.rows);
+  const Plan plan = plan_splits(ctx, P, units, ki.rows, ki.ctas_per_sm);
 
   DecodeArgs a{};
   a.kc = ctx->kc;
   a.vc = ctx->vc;
+  a.kc_w = ctx->kc;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.new_zstride = (long long)ctx->cfg.n_kv_heads * ctx->hd;
   a.layer_stride = ctx->layer_elems;
   a.head_stride = ctx->head_elems;
   a.q = q;
@@ -226,7 +283,7 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   a.G = ctx->G;
   a.n_hg = ctx->n_hg;
   a.nsplit = plan.nsplit;
-  a.chunk = plan.chunk;
+  a.cluster = plan.cluster;
   a.is_gemma3 = ctx->cfg.is_gemma3;
   a.swa_window = ctx->cfg.swa_window;
   a.swa_pattern = ctx->cfg.swa_pattern;
@@ -241,10 +298,22 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
     if (b.out) b.out = a.out + (long long)z0 * a.q_zstride;
     if (b.part_o) b.part_o = a.part_o + (long long)z0 * a.q_zstride;
     if (b.part_ml) b.part_ml = a.part_ml + (long long)z0 * a.ml_zstride;
-    dim3 grid(plan.nsplit, ctx->kvh_count * ctx->n_hg, zc);
-    ki.fn<<<grid, kDecodeThreads, ki.smem, s>>>(b);
+    if (b.k_new) b.k_new = a.k_new + (long long)z0 * a.new_zstride;
+    if (b.v_new) b.v_new = a.v_new + (long long)z0 * a.new_zstride;
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(plan.nsplit, ctx->kvh_count * ctx->n_hg, zc);
+    lc.blockDim = dim3(kDecodeThreads, 1, 1);
+    lc.dynamicSmemBytes = ki.smem;
+    lc.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = plan.cluster;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = plan.cluster > 1 ? 1 : 0;
+    L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, ki.fn, b));
     ++ctx->launches;
-    L3P_CUDA(ctx, cudaGetLastError());
   }
   return L3P_OK;
 }
@@ -314,6 +383,9 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   ctx->n_hg = ctx->G / ctx->GT;
   ctx->kvh_count = kvh_count;
   ctx->seq_count = seq_count;
+  if (const char* plan = getenv("L3P_DECODE_PLAN")) {
+    if (sscanf(plan, "%d:%d", &ctx->force_nsplit, &ctx->force_cluster) < 1) ctx->force_nsplit = 0;
+  }
   // attn_scale = 1.0f / sqrtf((float)head_size), c:434
   ctx->scale = c.scale != 0.f ? c.scale : 1.0f / sqrtf((float)c.head_dim);
   ctx->head_elems = (long long)seq_count * c.head_dim;
@@ -359,6 +431,29 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   if (!ki.fn) return bail(L3P_E_UNSUPPORTED, "no decode kernel for this geometry");
   if (cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem) != cudaSuccess)
     return bail(L3P_E_CUDA, "cudaFuncSetAttribute failed");
+  // clusters of up to 16 CTAs (16 is a non-portable size); record how many of
+  // each size fit on this GPU at once (0 = that size is not available)
+  if (cudaFuncSetAttribute(ki.fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    cudaGetLastError();
+  for (int ci = 1; ci < 5; ++ci) {
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(1 << ci, 1, 1);
+    lc.blockDim = dim3(kDecodeThreads, 1, 1);
+    lc.dynamicSmemBytes = ki.smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1 << ci;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, ki.fn, &lc) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    ctx->max_clusters[ci] = n;
+  }
   *out = ctx;
   return L3P_OK;
 }
@@ -405,6 +500,18 @@ L3P_API int l3p_attn_set_stream(l3p_attn_ctx* ctx, void* stream) {
 
 L3P_API long long l3p_attn_launch_count(const l3p_attn_ctx* ctx) { return ctx ? ctx->launches : -1; }
 
+L3P_API int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* nsplit, int* cluster) {
+  if (!ctx || n_slices <= 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
+  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT);
+  if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
+  const long long hi = std::min<long long>((long long)pos + 1, (long long)ctx->cfg.seq_begin + ctx->seq_count);
+  const long long P = std::max<long long>(hi - ctx->cfg.seq_begin, 0);
+  const Plan plan = plan_splits(ctx, P, (long long)n_slices * ctx->kvh_count * ctx->n_hg, ki.rows, ki.ctas_per_sm);
+  if (nsplit) *nsplit = plan.nsplit;
+  if (cluster) *cluster = plan.cluster;
+  return L3P_OK;
+}
+
 // ==========================================================================
 // Device-pointer entry points
 
@@ -413,6 +520,7 @@ L3P_API int l3p_attn_kv_append_dev(l3p_attn_ctx* ctx, int layer, int pos, const 
   if (!ctx || !k || !v) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
   if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
+  if (int rc = check_aligned(ctx, {k, v})) return rc;
   DeviceScope dev(ctx->cfg.device);
   return launch_append(ctx, layer, pos, 1, k, v, pick_stream(ctx, stream));
 }
@@ -421,8 +529,19 @@ L3P_API int l3p_attn_decode_dev(l3p_attn_ctx* ctx, int layer, int pos, const flo
   if (!ctx || !q || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
   if (int rc = check_pos_full(ctx, pos)) return rc;
+  if (int rc = check_aligned(ctx, {q, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
   return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream));
+}
+
+L3P_API int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k, const float* v,
+                              float* out, void* stream) {
+  if (!ctx || !q || !k || !v || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (int rc = check_pos_full(ctx, pos)) return rc;
+  if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), k, v);
 }
 
 L3P_API int l3p_attn_decode_layers_dev(l3p_attn_ctx* ctx, int layer0, int n_layers, int pos, const float* q,
@@ -431,6 +550,7 @@ L3P_API int l3p_attn_decode_layers_dev(l3p_attn_ctx* ctx, int layer0, int n_laye
   if (int rc = check_layer(ctx, layer0)) return rc;
   if (int rc = check_layer(ctx, layer0 + n_layers - 1)) return rc;
   if (int rc = check_pos_full(ctx, pos)) return rc;
+  if (int rc = check_aligned(ctx, {q, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
   return launch_decode(ctx, layer0, 1, pos, 0, n_layers, q, out, nullptr, nullptr, pick_stream(ctx, stream));
 }
@@ -440,6 +560,7 @@ L3P_API int l3p_attn_decode_partial_dev(l3p_attn_ctx* ctx, int layer, int pos, c
   if (!ctx || !q || !part_o || !part_ml) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
   if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
+  if (int rc = check_aligned(ctx, {q, part_o})) return rc;
   DeviceScope dev(ctx->cfg.device);
   return launch_decode(ctx, layer, 0, pos, 0, 1, q, nullptr, part_o, part_ml, pick_stream(ctx, stream));
 }
@@ -466,6 +587,7 @@ L3P_API int l3p_attn_prefill_dev(l3p_attn_ctx* ctx, int layer, int start_pos, in
   if (start_pos < 0 || start_pos + n_tok > ctx->cfg.seq_len)
     return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", start_pos, start_pos + n_tok, ctx->cfg.seq_len);
   if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
+  if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
   cudaStream_t s = pick_stream(ctx, stream);
   if (int rc = launch_append(ctx, layer, start_pos, n_tok, k, v, s)) return rc;
@@ -548,8 +670,7 @@ L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q,
   L3P_CUDA(ctx, cudaMemcpyAsync(dv, v, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
   L3P_CUDA(ctx, cudaMemcpyAsync(dq + (size_t)r0 * ctx->hd, q + (size_t)r0 * ctx->hd,
                                 (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyHostToDevice, ctx->stream));
-  if (int rc = launch_append(ctx, layer, pos, 1, dk, dv, ctx->stream)) return rc;
-  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, dq, dout, nullptr, nullptr, ctx->stream)) return rc;
+  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, dq, dout, nullptr, nullptr, ctx->stream, dk, dv)) return rc;
   L3P_CUDA(ctx, cudaMemcpyAsync(out + (size_t)r0 * ctx->hd, dout + (size_t)r0 * ctx->hd,
                                 (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyDeviceToHost, ctx->stream));
   return finish_host_call(ctx);

@@ -157,3 +157,27 @@ def test_errors_are_reported_not_fatal():
             ctx.decode(2, 3, q)
         assert e.value.code == -2
         ctx.decode(1, 3, q)  # the context stays usable
+
+
+@pytest.mark.parametrize("plan", ["1:1", "5:1", "16:1", "16:16", "32:16", "24:8", "8:2", "64:4"])
+@pytest.mark.parametrize("name", ["llama31_8b_decode_8k", "gemma_2b_decode"])
+def test_every_merge_path(monkeypatch, plan, name):
+    """Pin the split-K decomposition (single CTA, global last-arriver merge,
+    cluster merge, cluster + global merge) and check each against the oracle."""
+    monkeypatch.setenv("L3P_DECODE_PLAN", plan)
+    sh = CONFIGS[name].with_(pos=2047, seq_len=2048)
+    k, v, q = decode_inputs(sh, 0)
+    with AttnContext.for_shape(sh, n_layers=1) as ctx:
+        assert ctx.decode_plan(sh.pos) == tuple(int(x) for x in plan.split(":")), "plan not applied"
+        got = _gpu_step(ctx, sh, 0, k, v, q)
+    want, _ = _oracle(sh, 0, k, v, q)
+    _check(got, want, f"{name} plan {plan}")
+
+
+def test_default_plans_are_reported():
+    for name in ("llama31_8b_decode_8k", "gemma_2b_decode", "llama32_1b_decode"):
+        sh = CONFIGS[name]
+        with AttnContext.for_shape(sh, n_layers=1) as ctx:
+            ns, cs = ctx.decode_plan(sh.pos)
+            print(f"{name}: nsplit={ns} cluster={cs}")
+            assert ns >= 1 and cs >= 1 and ns % cs == 0
