@@ -168,6 +168,39 @@ long long l3p_attn_launch_count(const l3p_attn_ctx* ctx);
  * benchmarks; no counterpart in the reference. */
 int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* nsplit, int* cluster);
 
+/* Decode attention that allocates nothing.  No counterpart in the reference.
+ *
+ * For callers that own every byte of device memory themselves -- typically
+ * an engine that plans one arena when the model loads and hands out pointers
+ * from it -- and so cannot let a library call cudaMalloc while generating: a
+ * runtime allocation can synchronise the device, can fail mid-generation once
+ * the arena holds the memory, and escapes the caller's accounting.  The
+ * caller creates no context and passes everything:
+ *   cfg      geometry as for l3p_attn_create (kv_head_begin/kv_head_count
+ *            select the KV heads k_cache/v_cache hold; the whole sequence:
+ *            seq_begin 0, seq_count 0 or seq_len; device ignored -- the
+ *            current device is used);
+ *   layer    used only for the sliding-window rule (c:3316-3321);
+ *   k_cache, v_cache  one layer's cache, [kv_head_count][seq_len][head_dim]
+ *            fp32 on the current device, rows [start_t, pos] filled;
+ *   q, out   [n_heads*head_dim] on the device (owned heads' rows written);
+ *   stream   cudaStream_t as void*, NULL = legacy default stream.
+ * All device pointers 16-byte aligned.  It calls no cudaMalloc, cudaFree or
+ * allocating library routine: the split-K partials and tickets live in a
+ * fixed 2 MiB + 4 KiB array in the library's device image, which every GPU
+ * that loads the library holds until the process exits.  Geometries whose
+ * partials would not fit are rejected with L3P_E_RANGE (at most 1024 (KV
+ * head, q-head group) units; a plan is chosen within 2 MiB of partials).
+ * The first call on each device looks up the array's device address and sets
+ * the kernel's shared-memory attribute; make that first call before any stream
+ * capture.  Every call uses the same array: calls whose kernels may overlap on
+ * the GPU (other streams, other host threads) race and must be serialised by
+ * the caller.  l3p_attn_noalloc_last_error() describes the last failure of the
+ * calling thread. */
+int l3p_attn_decode_noalloc(const l3p_attn_config* cfg, int layer, int pos, const float* k_cache,
+                            const float* v_cache, const float* q, float* out, void* stream);
+const char* l3p_attn_noalloc_last_error(void);
+
 #ifdef __cplusplus
 }
 #endif

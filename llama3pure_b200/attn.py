@@ -50,6 +50,8 @@ EXPORTS = (
     "l3p_attn_kv_device_ptr",
     "l3p_attn_launch_count",
     "l3p_attn_decode_plan",
+    "l3p_attn_decode_noalloc",
+    "l3p_attn_noalloc_last_error",
 )
 
 
@@ -119,6 +121,8 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_kv_device_ptr": (i, [vp, i, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
         "l3p_attn_launch_count": (C.c_longlong, [vp]),
         "l3p_attn_decode_plan": (i, [vp, i, i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+        "l3p_attn_decode_noalloc": (i, [C.POINTER(AttnConfig), i, i, fp, fp, fp, fp, vp]),
+        "l3p_attn_noalloc_last_error": (C.c_char_p, []),
     }
     for name, (res, args) in sig.items():
         f = getattr(lib, name)
@@ -300,3 +304,15 @@ class AttnContext:
     def prefill_dev(self, layer, start_pos, n_tok, q, k, v, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_prefill_dev(self.h, layer, start_pos, n_tok, _dev(q), _dev(k), _dev(v), _dev(out),
                                                _stream(stream)), "prefill_dev")
+
+
+def decode_noalloc(cfg: AttnConfig, layer: int, pos: int, k_cache, v_cache, q, out, stream=None, lib=None) -> None:
+    """l3p_attn_decode_noalloc: decode over a caller-owned layer cache without
+    any device allocation (the split partials use the library's fixed scratch
+    array; overlapping calls race)."""
+    lib = lib or load_library()
+    rc = lib.l3p_attn_decode_noalloc(C.byref(cfg), layer, pos, _dev(k_cache), _dev(v_cache), _dev(q), _dev(out),
+                                     _stream(stream))
+    if rc != L3P_OK:
+        msg = lib.l3p_attn_noalloc_last_error()
+        raise AttnError(rc, f"decode_noalloc: {msg.decode() if msg else ''}")

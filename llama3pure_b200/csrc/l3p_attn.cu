@@ -9,6 +9,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <initializer_list>
+#include <mutex>
 #include <new>
 #include <string>
 
@@ -149,7 +150,15 @@ struct Plan {
   int cluster = 1;
 };
 
-Plan plan_splits(const l3p_attn_ctx* ctx, long long P, long long units, int rows_per_tile, int ctas_per_sm) {
+// What a split-K plan may use: the GPU, the kernel geometry and the scratch.
+struct PlanLimits {
+  int hd = 0, GT = 1, num_sms = 148;
+  int max_clusters[5] = {0, 0, 0, 0, 0};
+  long long ws_o_floats = 0, n_counters = 0;
+  int force_nsplit = 0, force_cluster = 0;
+};
+
+Plan plan_splits(const PlanLimits* ctx, long long P, long long units, int rows_per_tile, int ctas_per_sm) {
   Plan best;
   if (P <= 0) return best;
   if (ctx->force_nsplit > 0) {
@@ -199,6 +208,19 @@ Plan plan_splits(const l3p_attn_ctx* ctx, long long P, long long units, int rows
     }
   }
   return best;
+}
+
+PlanLimits limits_of(const l3p_attn_ctx* ctx) {
+  PlanLimits l;
+  l.hd = ctx->hd;
+  l.GT = ctx->GT;
+  l.num_sms = ctx->num_sms;
+  for (int i = 0; i < 5; ++i) l.max_clusters[i] = ctx->max_clusters[i];
+  l.ws_o_floats = ctx->ws_o_floats;
+  l.n_counters = ctx->n_counters;
+  l.force_nsplit = ctx->force_nsplit;
+  l.force_cluster = ctx->force_cluster;
+  return l;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -251,7 +273,8 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   const long long hi = std::min<long long>(pos_max + 1, (long long)ctx->cfg.seq_begin + ctx->seq_count);
   const long long P = std::max<long long>(hi - lo, 0);
   const long long units = (long long)nz * ctx->kvh_count * ctx->n_hg;
-  const Plan plan = plan_splits(ctx, P, units, ki.rows, ki.ctas_per_sm);
+  const PlanLimits lim = limits_of(ctx);
+  const Plan plan = plan_splits(&lim, P, units, ki.rows, ki.ctas_per_sm);
 
   DecodeArgs a{};
   a.kc = ctx->kc;
@@ -506,7 +529,8 @@ L3P_API int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* 
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
   const long long hi = std::min<long long>((long long)pos + 1, (long long)ctx->cfg.seq_begin + ctx->seq_count);
   const long long P = std::max<long long>(hi - ctx->cfg.seq_begin, 0);
-  const Plan plan = plan_splits(ctx, P, (long long)n_slices * ctx->kvh_count * ctx->n_hg, ki.rows, ki.ctas_per_sm);
+  const PlanLimits lim = limits_of(ctx);
+  const Plan plan = plan_splits(&lim, P, (long long)n_slices * ctx->kvh_count * ctx->n_hg, ki.rows, ki.ctas_per_sm);
   if (nsplit) *nsplit = plan.nsplit;
   if (cluster) *cluster = plan.cluster;
   return L3P_OK;
@@ -741,4 +765,169 @@ L3P_API int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, 
     L3P_CUDA(ctx, cudaMemcpyAsync(v + dst, ctx->vc + src, (size_t)(hi - lo) * row * 4, cudaMemcpyDeviceToHost, ctx->stream));
   }
   return finish_host_call(ctx);
+}
+
+// ==========================================================================
+// Decode without any allocation (l3p_attn_decode_noalloc).
+//
+// For callers that own every byte of device memory themselves -- an engine
+// that plans one arena when the model loads and hands out pointers from it --
+// and therefore cannot let a library call cudaMalloc on the token path: a
+// runtime allocation can synchronise the device, can fail mid-generation
+// once the arena has taken the memory, and escapes the caller's accounting.
+// The caller passes the KV cache, q and out; the split-K partials and the
+// per-unit tickets live in the fixed array below, which every GPU that loads
+// this library holds until the process exits.
+
+namespace {
+
+constexpr long long kNoAllocFloats = 512 * 1024;     // 2 MiB: partial outputs + (m, l) pairs
+constexpr long long kNoAllocCounters = 1024;          // tickets, one per (KV head, q-head group)
+constexpr int kMaxDevices = 64;
+
+__device__ __align__(256) float g_noalloc_scratch[kNoAllocFloats + kNoAllocCounters];
+
+struct NoAllocDevice {
+  bool ready = false;
+  float* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  int num_sms = 0;
+};
+NoAllocDevice g_noalloc_dev[kMaxDevices];
+unsigned g_noalloc_attr_done[kMaxDevices];  // bit i: smem attribute set for kernel table entry i
+std::mutex g_noalloc_mu;
+thread_local char g_noalloc_err[256];
+
+int noalloc_fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_noalloc_err, sizeof g_noalloc_err, fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int kernel_index(int hd, int gt) {
+  const int h = hd == 64 ? 0 : hd == 128 ? 1 : hd == 256 ? 2 : -1;
+  const int g = gt == 1 ? 0 : gt == 2 ? 1 : gt == 4 ? 2 : gt == 8 ? 3 : -1;
+  return (h < 0 || g < 0) ? -1 : h * 4 + g;
+}
+
+}  // namespace
+
+L3P_API const char* l3p_attn_noalloc_last_error(void) { return g_noalloc_err; }
+
+L3P_API int l3p_attn_decode_noalloc(const l3p_attn_config* cfg, int layer, int pos, const float* k_cache,
+                                    const float* v_cache, const float* q, float* out, void* stream) {
+  g_noalloc_err[0] = '\0';
+  if (!cfg || !k_cache || !v_cache || !q || !out) return noalloc_fail(L3P_E_INVAL, "null argument");
+  const l3p_attn_config& c = *cfg;
+  if (c.n_heads <= 0 || c.n_kv_heads <= 0 || c.seq_len <= 0 || c.n_heads % c.n_kv_heads != 0 ||
+      c.kv_format != L3P_KV_F32)
+    return noalloc_fail(L3P_E_INVAL, "bad configuration");
+  const int kvh_count = c.kv_head_count > 0 ? c.kv_head_count : c.n_kv_heads - c.kv_head_begin;
+  if (c.kv_head_begin < 0 || kvh_count <= 0 || c.kv_head_begin + kvh_count > c.n_kv_heads)
+    return noalloc_fail(L3P_E_INVAL, "bad KV-head range");
+  if (c.seq_begin != 0 || (c.seq_count != 0 && c.seq_count != c.seq_len))
+    return noalloc_fail(L3P_E_INVAL, "the no-allocation decode needs the whole sequence (seq_begin 0)");
+  if (pos < 0 || pos >= c.seq_len) return noalloc_fail(L3P_E_RANGE, "pos %d outside [0, %d)", pos, c.seq_len);
+  for (const void* p : {(const void*)k_cache, (const void*)v_cache, (const void*)q, (const void*)out})
+    if (!aligned16(p)) return noalloc_fail(L3P_E_INVAL, "device pointer %p is not 16-byte aligned", p);
+  const int hd = c.head_dim;
+  const int G = c.n_heads / c.n_kv_heads;
+  const int GT = (G % 8 == 0) ? 8 : (G % 4 == 0) ? 4 : (G % 2 == 0) ? 2 : 1;
+  const KernelInfo ki = kernel_for(hd, GT);
+  const int kidx = kernel_index(hd, GT);
+  if (!ki.fn || kidx < 0) return noalloc_fail(L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", hd);
+
+  // once per device, with that device current: the device address of the
+  // scratch array and the kernel's shared-memory attribute
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return noalloc_fail(L3P_E_CUDA, "no current CUDA device");
+  NoAllocDevice& d = g_noalloc_dev[dev];
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!d.ready) {
+      void* ptr = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess) return noalloc_fail(L3P_E_CUDA, "cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+      e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return noalloc_fail(L3P_E_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+      d.scratch = static_cast<float*>(ptr);
+      d.ready = true;
+    }
+    if (!(g_noalloc_attr_done[dev] & (1u << kidx))) {
+      const cudaError_t e = cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem);
+      if (e != cudaSuccess) return noalloc_fail(L3P_E_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      g_noalloc_attr_done[dev] |= 1u << kidx;
+    }
+  }
+
+  // split-K plan within the fixed scratch (no clusters: the partials of every
+  // split go through the scratch array)
+  const int swa = (c.is_gemma3 && c.swa_window > 0 && c.swa_pattern > 0 && (layer % c.swa_pattern) < c.swa_pattern - 1)
+                      ? std::max(0, pos - c.swa_window + 1)
+                      : 0;
+  const long long P = (long long)pos + 1 - swa;
+  const int n_hg = G / GT;
+  const long long units = (long long)kvh_count * n_hg;
+  if (units > kNoAllocCounters)
+    return noalloc_fail(L3P_E_RANGE, "%lld (KV head, q-head group) units exceed the no-allocation limit of %lld",
+                        units, kNoAllocCounters);
+  PlanLimits lim;
+  lim.hd = hd;
+  lim.GT = GT;
+  lim.num_sms = d.num_sms;
+  lim.ws_o_floats = kNoAllocFloats * hd / (hd + 2);  // room for the (m, l) pairs after the outputs
+  lim.n_counters = kNoAllocCounters;
+  const Plan plan = plan_splits(&lim, P, units, ki.rows, ki.ctas_per_sm);
+  const long long o_floats = plan.nsplit > 1 ? units * plan.nsplit * GT * hd : 0;
+  const long long ml_floats = plan.nsplit > 1 ? units * plan.nsplit * GT * 2 : 0;
+  if (o_floats + ml_floats > kNoAllocFloats)
+    return noalloc_fail(L3P_E_RANGE, "split partials need %lld floats, above the no-allocation limit of %lld",
+                        o_floats + ml_floats, kNoAllocFloats);
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* ws_o = d.scratch;
+  float* ws_ml = d.scratch + o_floats;
+  unsigned* counters = reinterpret_cast<unsigned*>(d.scratch + kNoAllocFloats);
+  if (plan.nsplit > 1) {
+    // tickets must start at zero; an earlier call may have stopped early
+    const cudaError_t e = cudaMemsetAsync(counters, 0, units * sizeof(unsigned), s);
+    if (e != cudaSuccess) return noalloc_fail(L3P_E_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  }
+
+  DecodeArgs a{};
+  a.kc = k_cache;
+  a.vc = const_cast<float*>(v_cache);
+  a.kc_w = const_cast<float*>(k_cache);
+  a.layer_stride = 0;
+  a.head_stride = (long long)c.seq_len * hd;
+  a.q = q;
+  a.q_zstride = (long long)c.n_heads * hd;
+  a.out = out;
+  a.ml_zstride = 2ll * c.n_heads;
+  a.ws_o = ws_o;
+  a.ws_ml = ws_ml;
+  a.counters = counters;
+  a.scale = c.scale != 0.f ? c.scale : 1.0f / sqrtf((float)hd);
+  a.layer0 = layer;
+  a.pos0 = pos;
+  a.seq_begin = 0;
+  a.cap = c.seq_len;
+  a.kv_head_begin = c.kv_head_begin;
+  a.G = G;
+  a.n_hg = n_hg;
+  a.nsplit = plan.nsplit;
+  a.cluster = 1;
+  a.is_gemma3 = c.is_gemma3;
+  a.swa_window = c.swa_window;
+  a.swa_pattern = c.swa_pattern;
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(plan.nsplit, kvh_count * n_hg, 1);
+  lc.blockDim = dim3(kDecodeThreads, 1, 1);
+  lc.dynamicSmemBytes = ki.smem;
+  lc.stream = s;
+  const cudaError_t e = cudaLaunchKernelEx(&lc, ki.fn, a);
+  if (e != cudaSuccess) return noalloc_fail(L3P_E_CUDA, "launch: %s", cudaGetErrorString(e));
+  return L3P_OK;
 }
