@@ -239,7 +239,12 @@ def run_ours(args):
         for layer in range(L):
             ctx.step_dev(layer, sh.pos, q[layer], knew[layer], vnew[layer], out[layer], stream)
 
-    # capture one step as a CUDA graph (the step is 2*L small launches)
+    # consecutive step launches belong to different layers, so a launch may
+    # start streaming its cache while the previous layer's kernel finishes
+    # (programmatic dependent launch; see l3p_attn_set_overlap)
+    if not args.no_overlap:
+        ctx.set_overlap(True)
+    # capture one step as a CUDA graph (the step is L launches)
     n0 = ctx.launch_count()
     step()
     torch.cuda.synchronize()
@@ -287,15 +292,30 @@ def run_ours(args):
     ms = t0.elapsed_time(t1)
     ctx.check()
 
-    # decode kernel alone, per launch, on the launching stream (roofline)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(2 * L)]
-    for i in range(2 * L):
-        layer = i % L
-        ev[i][0].record(stream)
-        ctx.decode_dev(layer, sh.pos, q[layer], out[layer], stream)
-        ev[i][1].record(stream)
+    # decode kernel alone (roofline): a CUDA graph of 2*L decode launches with
+    # no overlap between them, timed with CUDA events on the launching stream
+    ctx.set_overlap(False)
+    kgraph = torch.cuda.CUDAGraph()
+    kstream = torch.cuda.Stream()
+    kstream.wait_stream(stream)
+    with torch.cuda.stream(kstream):
+        ctx.set_stream(kstream)
+        with torch.cuda.graph(kgraph, stream=kstream):
+            for i in range(2 * L):
+                ctx.decode_dev(i % L, sh.pos, q[i % L], out[i % L], kstream)
+    stream.wait_stream(kstream)
+    ctx.set_stream(stream)
+    kgraph.replay()
     torch.cuda.synchronize()
-    kern_ms = statistics.mean(a.elapsed_time(b) for a, b in ev[L:])
+    k0 = torch.cuda.Event(enable_timing=True)
+    k1 = torch.cuda.Event(enable_timing=True)
+    k0.record(stream)
+    for _ in range(3):
+        kgraph.replay()
+    k1.record(stream)
+    torch.cuda.synchronize()
+    kern_ms = k0.elapsed_time(k1) / (3 * 2 * L)
+    del kgraph
     if clocks:
         clk = clocks.stop()
     else:
@@ -335,7 +355,8 @@ def run_ours(args):
             "data": "synthetic (seeded N(0,1) fp32 q/K/V, generated on device)",
             "config": {"workload": WORKLOAD, "n_layers": L, "n_heads": sh.n_heads, "n_kv_heads": sh.n_kv_heads,
                        "head_dim": sh.head_dim, "pos": sh.pos, "kv_positions": P,
-                       "parallelism": f"kv-head shards x{world}", "launch": "cuda graph" if graph else "stream",
+                       "parallelism": f"kv-head shards x{world}",
+                       "launch": ("cuda graph" if graph else "stream") + ("" if args.no_overlap else " + programmatic dependent launch"),
                        "split_k": dict(zip(("ctas_per_kv_head", "cluster"), ctx.decode_plan(sh.pos))),
                        "l2": "inputs larger than L2 (2 GiB KV per step vs 126 MB L2)"},
             "us_per_layer": round(ms_step * 1e3 / L, 3),
@@ -344,6 +365,7 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "kernel": "decode_f32_kernel<128,4>", "kernel_us": round(kern_ms * 1e3, 3),
+                         "kernel_timing": "graph of 64 decode launches without overlap, CUDA events",
                          "algorithmic_bytes_per_launch": bytes_per_layer_rank, "traffic": args.traffic},
             "e2e": e2e,
             "cpu_baseline": cpu,
@@ -437,6 +459,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true", help="no programmatic dependent launch between layers")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")

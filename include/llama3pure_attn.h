@@ -158,6 +158,18 @@ int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, float* k
  * [head_dim] fp32 each. */
 int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v);
 
+/* Overlap mode (off by default).  When enabled, the decode launches of the
+ * *_dev decode entry points (decode, step, decode_layers, decode_partial) use
+ * programmatic dependent launch: a launch may start while the preceding kernel
+ * on its stream is still running and stream the cached rows [start_t, pos)
+ * meanwhile; it reads q and the new K/V row only after that kernel has
+ * completed.  Enable it only when the kernel that precedes a decode launch
+ * does not write this context's KV cache (true when it is the engine's QKV
+ * projection or another layer's attention; false right after
+ * l3p_attn_kv_append_dev or a prefill of the same layer).  No counterpart in
+ * the reference. */
+int l3p_attn_set_overlap(l3p_attn_ctx* ctx, int enable);
+
 /* Number of kernels this library has launched since the context was created
  * (the benchmark reports it per step).  No counterpart in the reference. */
 long long l3p_attn_launch_count(const l3p_attn_ctx* ctx);

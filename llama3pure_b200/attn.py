@@ -49,6 +49,7 @@ EXPORTS = (
     "l3p_attn_read_kv",
     "l3p_attn_kv_device_ptr",
     "l3p_attn_launch_count",
+    "l3p_attn_set_overlap",
     "l3p_attn_decode_plan",
     "l3p_attn_decode_noalloc",
     "l3p_attn_noalloc_last_error",
@@ -120,6 +121,7 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_read_kv": (i, [vp, i, i, i, fp, fp]),
         "l3p_attn_kv_device_ptr": (i, [vp, i, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
         "l3p_attn_launch_count": (C.c_longlong, [vp]),
+        "l3p_attn_set_overlap": (i, [vp, i]),
         "l3p_attn_decode_plan": (i, [vp, i, i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "l3p_attn_decode_noalloc": (i, [C.POINTER(AttnConfig), i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_noalloc_last_error": (C.c_char_p, []),
@@ -227,6 +229,10 @@ class AttnContext:
 
     def set_stream(self, stream) -> None:
         self._ok(self.lib.l3p_attn_set_stream(self.h, _stream(stream)), "set_stream")
+
+    def set_overlap(self, enable: bool) -> None:
+        """Programmatic dependent launch for decode (see l3p_attn_set_overlap)."""
+        self._ok(self.lib.l3p_attn_set_overlap(self.h, int(bool(enable))), "set_overlap")
 
     def launch_count(self) -> int:
         return int(self.lib.l3p_attn_launch_count(self.h))

@@ -69,6 +69,11 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src,
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Programmatic dependent launch: let the next kernel of the stream start
+// launching, and wait for the previous kernel's results (no-ops when the
+// launch carries no programmatic dependency).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
@@ -291,12 +296,25 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
     }
   };
 
-  // start the stream before anything else
+  // Start the stream before anything else.  Cached rows [start_t, pos) were
+  // written by earlier launches; q and the new row come from the kernel that
+  // precedes this one, so with programmatic dependent launch they are read
+  // only after pdl_wait() (a tile holding the new row waits first).
+  pdl_launch_dependents();
+  bool waited = false;
 #pragma unroll
   for (int i = 0; i < C::kStages - 1; ++i) {
-    if (i < my_tiles) issue(i);
+    if (i < my_tiles) {
+      const int r0 = (first + i * step) * C::kR;
+      if (fused && !waited && new_row >= r0 && new_row < r0 + C::kR) {
+        pdl_wait();
+        waited = true;
+      }
+      issue(i);
+    }
     cp_async_commit();
   }
+  pdl_wait();
 
   // the fused append: one CTA per KV head writes the new row into the cache
   if (fused && split == 0 && hg == 0) {

@@ -39,6 +39,11 @@ struct l3p_attn_ctx {
   // device staging for the host-pointer entry points
   float* st_buf = nullptr;
   size_t st_floats = 0;
+  // pinned, device-mapped host staging for the single-token host calls: the
+  // inputs cross in one copy and the kernel writes the output straight into it
+  float* hst = nullptr;
+  float* hst_dev = nullptr;
+  size_t hst_floats = 0;
   // device error word in mapped pinned host memory
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -48,6 +53,11 @@ struct l3p_attn_ctx {
   // L3P_DECODE_PLAN="nsplit:cluster" pins the decomposition (tests use it to
   // exercise every merge path); 0 = automatic
   int force_nsplit = 0, force_cluster = 0;
+  // overlap mode: decode launches carry programmatic stream serialisation
+  bool overlap = false;
+  // split scratch is used in kScratchSlots rotating slices so that launches
+  // overlapping on the GPU never share partials or tickets
+  unsigned long long launch_seq = 0;
   std::string last_error;
 };
 
@@ -55,6 +65,7 @@ namespace {
 
 constexpr long long kWsOFloats = 8ll << 20;  // 32 MiB of split partials
 constexpr long long kCounters = 1 << 16;
+constexpr int kScratchSlots = 4;
 constexpr int kDecodeThreads = L3P_DECODE_WARPS * 32;  // DecodeCfg<*, *>::kThreads
 
 int fail(l3p_attn_ctx* ctx, int code, const char* fmt, ...) {
@@ -216,8 +227,8 @@ PlanLimits limits_of(const l3p_attn_ctx* ctx) {
   l.GT = ctx->GT;
   l.num_sms = ctx->num_sms;
   for (int i = 0; i < 5; ++i) l.max_clusters[i] = ctx->max_clusters[i];
-  l.ws_o_floats = ctx->ws_o_floats;
-  l.n_counters = ctx->n_counters;
+  l.ws_o_floats = ctx->ws_o_floats / kScratchSlots;
+  l.n_counters = ctx->n_counters / kScratchSlots;
   l.force_nsplit = ctx->force_nsplit;
   l.force_cluster = ctx->force_cluster;
   return l;
@@ -244,6 +255,23 @@ int ensure_staging(l3p_attn_ctx* ctx, size_t floats) {
   return L3P_OK;
 }
 
+int ensure_host_staging(l3p_attn_ctx* ctx, size_t floats) {
+  if (floats <= ctx->hst_floats) return L3P_OK;
+  if (ctx->hst) cudaFreeHost(ctx->hst);
+  ctx->hst = ctx->hst_dev = nullptr;
+  ctx->hst_floats = 0;
+  const size_t want = std::max(floats, (size_t)1 << 14);
+  if (cudaHostAlloc(&ctx->hst, want * sizeof(float), cudaHostAllocMapped) != cudaSuccess ||
+      cudaHostGetDevicePointer(&ctx->hst_dev, ctx->hst, 0) != cudaSuccess) {
+    cudaGetLastError();
+    if (ctx->hst) cudaFreeHost(ctx->hst);
+    ctx->hst = ctx->hst_dev = nullptr;
+    return fail(ctx, L3P_E_NOMEM, "pinned staging allocation of %zu floats failed", want);
+  }
+  ctx->hst_floats = want;
+  return L3P_OK;
+}
+
 int check_layer(l3p_attn_ctx* ctx, int layer) {
   if (layer < 0 || layer >= ctx->cfg.n_layers)
     return fail(ctx, L3P_E_RANGE, "layer %d outside [0, %d)", layer, ctx->cfg.n_layers);
@@ -264,7 +292,7 @@ int read_err(l3p_attn_ctx* ctx) {
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
                   const float* q, float* out, float* part_o, float* part_ml, cudaStream_t s,
-                  const float* k_new = nullptr, const float* v_new = nullptr) {
+                  const float* k_new = nullptr, const float* v_new = nullptr, bool allow_overlap = false) {
   const KernelInfo ki = kernel_for(ctx->hd, ctx->GT);
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
   // longest attended range over the slices (upper bound; the kernel clips per slice)
@@ -275,6 +303,7 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   const long long units = (long long)nz * ctx->kvh_count * ctx->n_hg;
   const PlanLimits lim = limits_of(ctx);
   const Plan plan = plan_splits(&lim, P, units, ki.rows, ki.ctas_per_sm);
+  const int slot = (int)(ctx->launch_seq++ % kScratchSlots);
 
   DecodeArgs a{};
   a.kc = ctx->kc;
@@ -291,9 +320,9 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   a.part_o = part_o;
   a.part_ml = part_ml;
   a.ml_zstride = 2ll * ctx->cfg.n_heads;
-  a.ws_o = ctx->ws_o;
-  a.ws_ml = ctx->ws_ml;
-  a.counters = ctx->counters;
+  a.ws_o = ctx->ws_o + slot * (ctx->ws_o_floats / kScratchSlots);
+  a.ws_ml = ctx->ws_ml + slot * (ctx->ws_ml_floats / kScratchSlots);
+  a.counters = ctx->counters + slot * (ctx->n_counters / kScratchSlots);
   a.err = ctx->err_dev;
   a.scale = ctx->scale;
   a.layer0 = layer0;
@@ -328,13 +357,22 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
     lc.blockDim = dim3(kDecodeThreads, 1, 1);
     lc.dynamicSmemBytes = ki.smem;
     lc.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = plan.cluster;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    unsigned n_attr = 0;
+    if (plan.cluster > 1) {
+      attr[n_attr].id = cudaLaunchAttributeClusterDimension;
+      attr[n_attr].val.clusterDim.x = plan.cluster;
+      attr[n_attr].val.clusterDim.y = 1;
+      attr[n_attr].val.clusterDim.z = 1;
+      ++n_attr;
+    }
+    if (allow_overlap && ctx->overlap) {
+      attr[n_attr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[n_attr].val.programmaticStreamSerializationAllowed = 1;
+      ++n_attr;
+    }
     lc.attrs = attr;
-    lc.numAttrs = plan.cluster > 1 ? 1 : 0;
+    lc.numAttrs = n_attr;
     L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, ki.fn, b));
     ++ctx->launches;
   }
@@ -491,6 +529,7 @@ L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
   cudaFree(ctx->ws_ml);
   cudaFree(ctx->counters);
   cudaFree(ctx->st_buf);
+  if (ctx->hst) cudaFreeHost(ctx->hst);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
@@ -522,6 +561,12 @@ L3P_API int l3p_attn_set_stream(l3p_attn_ctx* ctx, void* stream) {
 }
 
 L3P_API long long l3p_attn_launch_count(const l3p_attn_ctx* ctx) { return ctx ? ctx->launches : -1; }
+
+L3P_API int l3p_attn_set_overlap(l3p_attn_ctx* ctx, int enable) {
+  if (!ctx) return L3P_E_INVAL;
+  ctx->overlap = enable != 0;
+  return L3P_OK;
+}
 
 L3P_API int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* nsplit, int* cluster) {
   if (!ctx || n_slices <= 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
@@ -555,7 +600,8 @@ L3P_API int l3p_attn_decode_dev(l3p_attn_ctx* ctx, int layer, int pos, const flo
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
-  return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream));
+  return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), nullptr,
+                       nullptr, true);
 }
 
 L3P_API int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k, const float* v,
@@ -565,7 +611,7 @@ L3P_API int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
-  return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), k, v);
+  return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), k, v, true);
 }
 
 L3P_API int l3p_attn_decode_layers_dev(l3p_attn_ctx* ctx, int layer0, int n_layers, int pos, const float* q,
@@ -576,7 +622,8 @@ L3P_API int l3p_attn_decode_layers_dev(l3p_attn_ctx* ctx, int layer0, int n_laye
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
-  return launch_decode(ctx, layer0, 1, pos, 0, n_layers, q, out, nullptr, nullptr, pick_stream(ctx, stream));
+  return launch_decode(ctx, layer0, 1, pos, 0, n_layers, q, out, nullptr, nullptr, pick_stream(ctx, stream),
+                       nullptr, nullptr, true);
 }
 
 L3P_API int l3p_attn_decode_partial_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* part_o,
@@ -586,7 +633,8 @@ L3P_API int l3p_attn_decode_partial_dev(l3p_attn_ctx* ctx, int layer, int pos, c
   if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
   if (int rc = check_aligned(ctx, {q, part_o})) return rc;
   DeviceScope dev(ctx->cfg.device);
-  return launch_decode(ctx, layer, 0, pos, 0, 1, q, nullptr, part_o, part_ml, pick_stream(ctx, stream));
+  return launch_decode(ctx, layer, 0, pos, 0, 1, q, nullptr, part_o, part_ml, pick_stream(ctx, stream), nullptr,
+                       nullptr, true);
 }
 
 L3P_API int l3p_attn_lse_merge_dev(l3p_attn_ctx* ctx, int n_parts, int rows_per_part, int row_begin, int n_rows,
@@ -651,8 +699,10 @@ L3P_API int l3p_attn_kv_append(l3p_attn_ctx* ctx, int layer, int pos, const floa
   DeviceScope dev(ctx->cfg.device);
   const size_t kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
   if (int rc = ensure_staging(ctx, 2 * kvd)) return rc;
-  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, k, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
-  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf + kvd, v, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (int rc = ensure_host_staging(ctx, 2 * kvd)) return rc;
+  memcpy(ctx->hst, k, kvd * 4);
+  memcpy(ctx->hst + kvd, v, kvd * 4);
+  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, ctx->hst, 2 * kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
   if (int rc = launch_append(ctx, layer, pos, 1, ctx->st_buf, ctx->st_buf + kvd, ctx->stream)) return rc;
   return finish_host_call(ctx);
 }
@@ -663,17 +713,19 @@ L3P_API int l3p_attn_decode(l3p_attn_ctx* ctx, int layer, int pos, const float* 
   if (int rc = check_pos_full(ctx, pos)) return rc;
   DeviceScope dev(ctx->cfg.device);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd;
-  if (int rc = ensure_staging(ctx, 2 * qd)) return rc;
-  float* dq = ctx->st_buf;
-  float* dout = ctx->st_buf + qd;
+  if (int rc = ensure_staging(ctx, qd)) return rc;
+  if (int rc = ensure_host_staging(ctx, 2 * qd)) return rc;
   int r0, r1;
   owned_rows(ctx, &r0, &r1);
-  L3P_CUDA(ctx, cudaMemcpyAsync(dq + (size_t)r0 * ctx->hd, q + (size_t)r0 * ctx->hd,
-                                (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyHostToDevice, ctx->stream));
-  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, dq, dout, nullptr, nullptr, ctx->stream)) return rc;
-  L3P_CUDA(ctx, cudaMemcpyAsync(out + (size_t)r0 * ctx->hd, dout + (size_t)r0 * ctx->hd,
-                                (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  return finish_host_call(ctx);
+  const size_t row0 = (size_t)r0 * ctx->hd, nrow = (size_t)(r1 - r0) * ctx->hd;
+  memcpy(ctx->hst + row0, q + row0, nrow * 4);
+  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf + row0, ctx->hst + row0, nrow * 4, cudaMemcpyHostToDevice, ctx->stream));
+  // the kernel writes the output into mapped pinned memory
+  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + qd, nullptr, nullptr, ctx->stream))
+    return rc;
+  if (int rc = finish_host_call(ctx)) return rc;
+  memcpy(out + row0, ctx->hst + qd + row0, nrow * 4);
+  return L3P_OK;
 }
 
 L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
@@ -683,21 +735,24 @@ L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q,
   if (int rc = check_pos_full(ctx, pos)) return rc;
   DeviceScope dev(ctx->cfg.device);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
-  if (int rc = ensure_staging(ctx, 2 * qd + 2 * kvd)) return rc;
-  float* dq = ctx->st_buf;
-  float* dout = dq + qd;
-  float* dk = dout + qd;
-  float* dv = dk + kvd;
+  const size_t in = qd + 2 * kvd;  // staged inputs: q | k | v
+  if (int rc = ensure_staging(ctx, in)) return rc;
+  if (int rc = ensure_host_staging(ctx, in + qd)) return rc;
   int r0, r1;
   owned_rows(ctx, &r0, &r1);
-  L3P_CUDA(ctx, cudaMemcpyAsync(dk, k, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
-  L3P_CUDA(ctx, cudaMemcpyAsync(dv, v, kvd * 4, cudaMemcpyHostToDevice, ctx->stream));
-  L3P_CUDA(ctx, cudaMemcpyAsync(dq + (size_t)r0 * ctx->hd, q + (size_t)r0 * ctx->hd,
-                                (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyHostToDevice, ctx->stream));
-  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, dq, dout, nullptr, nullptr, ctx->stream, dk, dv)) return rc;
-  L3P_CUDA(ctx, cudaMemcpyAsync(out + (size_t)r0 * ctx->hd, dout + (size_t)r0 * ctx->hd,
-                                (size_t)(r1 - r0) * ctx->hd * 4, cudaMemcpyDeviceToHost, ctx->stream));
-  return finish_host_call(ctx);
+  const size_t row0 = (size_t)r0 * ctx->hd, nrow = (size_t)(r1 - r0) * ctx->hd;
+  memcpy(ctx->hst + row0, q + row0, nrow * 4);
+  memcpy(ctx->hst + qd, k, kvd * 4);
+  memcpy(ctx->hst + qd + kvd, v, kvd * 4);
+  // one host->device copy of all inputs; the kernel writes the output into
+  // mapped pinned memory, so no device->host copy follows
+  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, ctx->hst, in * 4, cudaMemcpyHostToDevice, ctx->stream));
+  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr, ctx->stream,
+                             ctx->st_buf + qd, ctx->st_buf + qd + kvd))
+    return rc;
+  if (int rc = finish_host_call(ctx)) return rc;
+  memcpy(out + row0, ctx->hst + in + row0, nrow * 4);
+  return L3P_OK;
 }
 
 L3P_API int l3p_attn_prefill(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,

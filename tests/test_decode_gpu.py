@@ -181,3 +181,48 @@ def test_default_plans_are_reported():
             ns, cs = ctx.decode_plan(sh.pos)
             print(f"{name}: nsplit={ns} cluster={cs}")
             assert ns >= 1 and cs >= 1 and ns % cs == 0
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_overlap_mode_consecutive_layers(use_graph):
+    """Programmatic dependent launch between the layers of one decode step
+    (each launch's predecessor is another layer's attention): same results."""
+    import torch
+
+    sh = CONFIGS["llama31_8b_decode_8k"].with_(pos=3000, seq_len=4096)
+    n_layers = 6
+    stream = torch.cuda.Stream()
+    with AttnContext.for_shape(sh, n_layers=n_layers) as ctx:
+        qs, ks, vs, wants = [], [], [], []
+        for layer in range(n_layers):
+            k, v, q = decode_inputs(sh, layer)
+            ctx.load_kv(layer, 0, np.ascontiguousarray(k[:, : sh.pos]), np.ascontiguousarray(v[:, : sh.pos]))
+            qs.append(q)
+            ks.append(np.ascontiguousarray(k[:, sh.pos]))
+            vs.append(np.ascontiguousarray(v[:, sh.pos]))
+            wants.append(_oracle(sh, layer, k, v, q)[0])
+        dq = torch.from_numpy(np.stack(qs)).cuda()
+        dk = torch.from_numpy(np.stack(ks)).cuda()
+        dv = torch.from_numpy(np.stack(vs)).cuda()
+        out = torch.zeros_like(dq)
+        ctx.set_overlap(True)
+        torch.cuda.synchronize()
+
+        def run():
+            for layer in range(n_layers):
+                ctx.step_dev(layer, sh.pos, dq[layer], dk[layer], dv[layer], out[layer], stream)
+
+        if use_graph:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                run()
+            for _ in range(3):
+                g.replay()
+        else:
+            for _ in range(3):
+                run()
+        torch.cuda.synchronize()
+        ctx.check()
+    got = out.cpu().numpy()
+    for layer in range(n_layers):
+        _check(got[layer], wants[layer], f"overlap layer {layer}")
