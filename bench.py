@@ -346,6 +346,13 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
+    prefill = None
+    if rank == 0 and not args.no_prefill:
+        prefill = run_prefill(args, torch)
+        tf32 = measure_tf32_peak(torch)
+        prefill["tf32_dense_tflops_measured"] = round(tf32, 1)
+        prefill["roofline_3xtf32_tflops"] = round(tf32 / 3, 1)
+        prefill["frac_of_3xtf32"] = round(prefill["tflops"] / (tf32 / 3), 4)
 
     if rank == 0:
         line = {
@@ -369,6 +376,7 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": bytes_per_layer_rank, "traffic": args.traffic},
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "prefill": prefill,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -422,6 +430,64 @@ def run_kernel_only(args):
     return 0
 
 
+def measure_tf32_peak(torch):
+    """Dense TF32 tensor throughput of this GPU, measured live: an fp32
+    torch.matmul with TF32 enabled, 8192^3, best of 5 (2*N^3 flops).  The
+    3xTF32 prefill roofline is a third of it."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    n = 8192
+    a = torch.randn((n, n), device="cuda")
+    b = torch.randn((n, n), device="cuda")
+    c = a @ b
+    best = 1e9
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        c = a @ b
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c
+    return 2 * n ** 3 / (best / 1e3) / 1e12
+
+
+def run_prefill(args, torch):
+    """Causal prefill of BASELINE configs[4] (Llama-3.1-8B shapes, 2048
+    tokens, one layer per launch) through l3p_attn_prefill_dev."""
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.synth import prefill_flops
+
+    sh = CONFIGS["llama31_8b_prefill_2k"]
+    S = sh.pos + 1
+    L = 4  # layers cycled (16 MiB of K/V each)
+    ctx = AttnContext.for_shape(sh, n_layers=L)
+    stream = torch.cuda.current_stream()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(11)
+    q = torch.randn((L, S, sh.n_heads, sh.head_dim), device="cuda", generator=g)
+    k = torch.randn((L, S, sh.n_kv_heads, sh.head_dim), device="cuda", generator=g)
+    v = torch.randn((L, S, sh.n_kv_heads, sh.head_dim), device="cuda", generator=g)
+    out = torch.zeros_like(q)
+    for i in range(args.warmup):
+        ctx.prefill_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], stream)
+    torch.cuda.synchronize()
+    reps = max(args.steps // 2, 4)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(reps):
+        ctx.prefill_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ctx.check()
+    ms = e0.elapsed_time(e1) / reps
+    tflops = prefill_flops(sh) / (ms / 1e3) / 1e12
+    ctx.close()
+    return {"workload": "llama31_8b_prefill_2k", "ms_per_layer": round(ms, 4), "tflops": round(tflops, 2),
+            "flops_per_layer": prefill_flops(sh), "kernel": "prefill_tc_kernel (tcgen05 3xTF32) + prefill_prep_kernel"}
+
+
 def run_e2e(ctx, sh, world, args, torch):
     """l3p_attn_step per layer with pinned host buffers: H2D of q/k/v, append,
     decode, D2H of the output, every step."""
@@ -462,6 +528,7 @@ def main():
     ap.add_argument("--no-overlap", action="store_true", help="no programmatic dependent launch between layers")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--traffic", type=float, default=None,

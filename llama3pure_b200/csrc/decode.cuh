@@ -51,16 +51,9 @@ namespace l3p {
 
 namespace cg = cooperative_groups;
 
-constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxSplits = 160;  // CTAs sharing one position range per launch
 constexpr int kMaxCluster = 16;  // CTAs of one thread-block cluster (non-portable size)
 constexpr int kMergeBatch = 16;  // partials fetched together by the global merge
-
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 // 16-byte global->shared copy; src_bytes = 0 writes zeros and reads nothing.
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src, uint32_t src_bytes) {

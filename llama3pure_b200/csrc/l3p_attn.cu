@@ -14,6 +14,7 @@
 #include <string>
 
 #include "decode.cuh"
+#include "prefill_tc.cuh"
 #include "llama3pure_attn.h"
 
 using namespace l3p;
@@ -44,6 +45,10 @@ struct l3p_attn_ctx {
   float* hst = nullptr;
   float* hst_dev = nullptr;
   size_t hst_floats = 0;
+  // prefill: pre-split K/V tile images for the tensor-core kernel
+  float* pf_img = nullptr;
+  size_t pf_img_floats = 0;
+  bool prefill_tc = false;  // head_dim 128 uses the tcgen05 kernel (L3P_PREFILL_PATH=ffma forces the other)
   // device error word in mapped pinned host memory
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -402,6 +407,58 @@ int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float
   return L3P_OK;
 }
 
+// Tensor-core prefill: split the cached K/V rows [0, start_pos+n_tok) into
+// tf32 hi/lo tile images, then run the tcgen05 flash-attention kernel.
+int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
+                      cudaStream_t s) {
+  const int n_keys = start_pos + n_tok;
+  const int n_ktiles = (n_keys + kPfBN - 1) / kPfBN;
+  const size_t need = (size_t)ctx->kvh_count * n_ktiles * kPfImgFloats;  // per K and per V
+  if (2 * need > ctx->pf_img_floats) {
+    if (ctx->pf_img) {
+      L3P_CUDA(ctx, cudaStreamSynchronize(s));
+      cudaFree(ctx->pf_img);
+    }
+    ctx->pf_img = nullptr;
+    ctx->pf_img_floats = 0;
+    if (cudaMalloc(&ctx->pf_img, 2 * need * sizeof(float)) != cudaSuccess) {
+      cudaGetLastError();
+      return fail(ctx, L3P_E_NOMEM, "prefill image allocation of %zu floats failed", 2 * need);
+    }
+    ctx->pf_img_floats = 2 * need;
+  }
+  float* kimg = ctx->pf_img;
+  float* vimg = ctx->pf_img + need;
+  const long long off = (long long)layer * ctx->layer_elems;
+  prefill_prep_kernel<<<dim3(n_ktiles, ctx->kvh_count), 256, 0, s>>>(ctx->kc + off, ctx->vc + off, ctx->head_elems,
+                                                                    n_keys, n_ktiles, kimg, vimg);
+  ++ctx->launches;
+  L3P_CUDA(ctx, cudaGetLastError());
+  PrefillArgs a{};
+  a.q = q;
+  a.out = out;
+  a.kimg = kimg;
+  a.vimg = vimg;
+  a.n_heads = ctx->cfg.n_heads;
+  a.G = ctx->G;
+  a.kv_head_begin = ctx->cfg.kv_head_begin;
+  a.n_qh = ctx->kvh_count * ctx->G;
+  a.q_pos0 = start_pos;
+  a.n_tok = n_tok;
+  a.n_qtiles = (n_tok + kPfBM - 1) / kPfBM;
+  a.n_ktiles = n_ktiles;
+  a.scale = ctx->scale;
+  a.layer = layer;
+  a.is_gemma3 = ctx->cfg.is_gemma3;
+  a.swa_window = ctx->cfg.swa_window;
+  a.swa_pattern = ctx->cfg.swa_pattern;
+  a.err = ctx->err_dev;
+  prefill_tc_kernel<<<a.n_qtiles * a.n_qh, 256, kPfSmemBytes, s>>>(a);
+  ++ctx->launches;
+  L3P_CUDA(ctx, cudaGetLastError());
+  return L3P_OK;
+}
+
 int check_pos_full(l3p_attn_ctx* ctx, int pos) {
   if (pos < 0 || pos >= ctx->cfg.seq_len)
     return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
@@ -492,6 +549,13 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   if (!ki.fn) return bail(L3P_E_UNSUPPORTED, "no decode kernel for this geometry");
   if (cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem) != cudaSuccess)
     return bail(L3P_E_CUDA, "cudaFuncSetAttribute failed");
+  // head_dim 128 prefill runs on the tensor cores unless L3P_PREFILL_PATH=ffma
+  ctx->prefill_tc = c.head_dim == kPfHD;
+  if (const char* path = getenv("L3P_PREFILL_PATH"))
+    if (strcmp(path, "ffma") == 0) ctx->prefill_tc = false;
+  if (ctx->prefill_tc &&
+      cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes) != cudaSuccess)
+    return bail(L3P_E_CUDA, "cudaFuncSetAttribute (prefill) failed");
   // clusters of up to 16 CTAs (16 is a non-portable size); record how many of
   // each size fit on this GPU at once (0 = that size is not available)
   if (cudaFuncSetAttribute(ki.fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
@@ -529,6 +593,7 @@ L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
   cudaFree(ctx->ws_ml);
   cudaFree(ctx->counters);
   cudaFree(ctx->st_buf);
+  cudaFree(ctx->pf_img);
   if (ctx->hst) cudaFreeHost(ctx->hst);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -663,6 +728,7 @@ L3P_API int l3p_attn_prefill_dev(l3p_attn_ctx* ctx, int layer, int start_pos, in
   DeviceScope dev(ctx->cfg.device);
   cudaStream_t s = pick_stream(ctx, stream);
   if (int rc = launch_append(ctx, layer, start_pos, n_tok, k, v, s)) return rc;
+  if (ctx->prefill_tc) return launch_prefill_tc(ctx, layer, start_pos, n_tok, q, out, s);
   return launch_decode(ctx, layer, 0, start_pos, 1, n_tok, q, out, nullptr, nullptr, s);
 }
 
@@ -775,7 +841,11 @@ L3P_API int l3p_attn_prefill(l3p_attn_ctx* ctx, int layer, int start_pos, int n_
   L3P_CUDA(ctx, cudaMemcpyAsync(dk, k, nkv * 4, cudaMemcpyHostToDevice, ctx->stream));
   L3P_CUDA(ctx, cudaMemcpyAsync(dv, v, nkv * 4, cudaMemcpyHostToDevice, ctx->stream));
   if (int rc = launch_append(ctx, layer, start_pos, n_tok, dk, dv, ctx->stream)) return rc;
-  if (int rc = launch_decode(ctx, layer, 0, start_pos, 1, n_tok, dq, dout, nullptr, nullptr, ctx->stream)) return rc;
+  if (ctx->prefill_tc) {
+    if (int rc = launch_prefill_tc(ctx, layer, start_pos, n_tok, dq, dout, ctx->stream)) return rc;
+  } else if (int rc = launch_decode(ctx, layer, 0, start_pos, 1, n_tok, dq, dout, nullptr, nullptr, ctx->stream)) {
+    return rc;
+  }
   int r0, r1;
   owned_rows(ctx, &r0, &r1);
   // owned rows of every token: a strided copy

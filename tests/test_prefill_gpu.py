@@ -30,12 +30,28 @@ def _check(got, want, what):
     AttnShape("pf_mqa_swa", 1, 8, 1, 256, 80, pos=79, seed=5, is_gemma3=1, swa_window=16, swa_pattern=6),
     AttnShape("pf_hd64", 1, 32, 8, 64, 200, pos=199, seed=6),
     AttnShape("pf_one_token", 1, 8, 2, 128, 8, pos=0, seed=7),
+    AttnShape("pf_swa_hd128", 1, 8, 2, 128, 300, pos=299, seed=10, is_gemma3=1, swa_window=50, swa_pattern=6),
+    AttnShape("pf_ragged_hd128", 1, 12, 3, 128, 333, pos=332, seed=12),
 ])
 def test_prefill_small_matches_oracle(shape):
     k, v, q = prefill_inputs(shape, 0)
     with AttnContext.for_shape(shape, n_layers=1) as ctx:
         got = ctx.prefill(0, 0, q, k, v)
     _check(got, _oracle(shape, q, k, v), shape.name)
+
+
+@pytest.mark.parametrize("path", ["tc", "ffma"])
+def test_prefill_paths_agree_with_oracle(monkeypatch, path):
+    """head_dim 128 prefill runs on the tcgen05 tensor cores (3xTF32); the
+    FFMA path (decode kernel, one slice per token) is kept for other head
+    sizes.  Both must meet the same tolerance."""
+    if path == "ffma":
+        monkeypatch.setenv("L3P_PREFILL_PATH", "ffma")
+    sh = AttnShape("pf_path", 1, 32, 8, 128, 640, pos=639, seed=13)
+    k, v, q = prefill_inputs(sh, 0)
+    with AttnContext.for_shape(sh, n_layers=1) as ctx:
+        got = ctx.prefill(0, 0, q, k, v)
+    _check(got, _oracle(sh, q, k, v), f"prefill path {path}")
 
 
 def test_prefill_continues_an_existing_cache():
