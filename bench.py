@@ -531,6 +531,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
     ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--prefill-only", action="store_true", help="prefill measurement alone (ncu case)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per decode launch, if captured (reported as roofline.traffic)")
     args = ap.parse_args()
@@ -540,6 +541,14 @@ def main():
         return run_reference_arm(args)
     if args.kernel_only:
         return run_kernel_only(args)
+    if args.prefill_only:
+        import torch
+
+        torch.cuda.set_device(0)
+        line = run_prefill(args, torch)
+        line["tf32_dense_tflops_measured"] = round(measure_tf32_peak(torch), 1)
+        print(json.dumps({"mode": "prefill-only", **line}), flush=True)
+        return 0
     return run_ours(args)
 
 
