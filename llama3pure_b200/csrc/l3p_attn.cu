@@ -408,37 +408,34 @@ int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float
 }
 
 // Tensor-core prefill: split the cached K/V rows [0, start_pos+n_tok) into
-// tf32 hi/lo tile images, then run the tcgen05 flash-attention kernel.
+// tf32 hi/lo chunk images, then run the tcgen05 flash-attention kernel.
 int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
                       cudaStream_t s) {
   const int n_keys = start_pos + n_tok;
   const int n_ktiles = (n_keys + kPfBN - 1) / kPfBN;
-  const size_t need = (size_t)ctx->kvh_count * n_ktiles * kPfImgFloats;  // per K and per V
-  if (2 * need > ctx->pf_img_floats) {
+  const size_t need = (size_t)ctx->kvh_count * n_ktiles * kPfTileFloats;
+  if (need > ctx->pf_img_floats) {
     if (ctx->pf_img) {
       L3P_CUDA(ctx, cudaStreamSynchronize(s));
       cudaFree(ctx->pf_img);
     }
     ctx->pf_img = nullptr;
     ctx->pf_img_floats = 0;
-    if (cudaMalloc(&ctx->pf_img, 2 * need * sizeof(float)) != cudaSuccess) {
+    if (cudaMalloc(&ctx->pf_img, need * sizeof(float)) != cudaSuccess) {
       cudaGetLastError();
-      return fail(ctx, L3P_E_NOMEM, "prefill image allocation of %zu floats failed", 2 * need);
+      return fail(ctx, L3P_E_NOMEM, "prefill image allocation of %zu floats failed", need);
     }
-    ctx->pf_img_floats = 2 * need;
+    ctx->pf_img_floats = need;
   }
-  float* kimg = ctx->pf_img;
-  float* vimg = ctx->pf_img + need;
   const long long off = (long long)layer * ctx->layer_elems;
   prefill_prep_kernel<<<dim3(n_ktiles, ctx->kvh_count), 256, 0, s>>>(ctx->kc + off, ctx->vc + off, ctx->head_elems,
-                                                                    n_keys, n_ktiles, kimg, vimg);
+                                                                    n_keys, n_ktiles, ctx->pf_img);
   ++ctx->launches;
   L3P_CUDA(ctx, cudaGetLastError());
   PrefillArgs a{};
   a.q = q;
   a.out = out;
-  a.kimg = kimg;
-  a.vimg = vimg;
+  a.img = ctx->pf_img;
   a.n_heads = ctx->cfg.n_heads;
   a.G = ctx->G;
   a.kv_head_begin = ctx->cfg.kv_head_begin;
