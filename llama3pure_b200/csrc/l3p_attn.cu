@@ -49,6 +49,7 @@ struct l3p_attn_ctx {
   float* pf_img = nullptr;
   size_t pf_img_floats = 0;
   bool prefill_tc = false;  // head_dim 128 uses the tcgen05 kernel (L3P_PREFILL_PATH=ffma forces the other)
+  int prefill_cg = 1;       // CTAs per tcgen05 prefill unit: 2 (CTA pairs) when the GQA group is even
   // device error word in mapped pinned host memory
   int* err_host = nullptr;
   int* err_dev = nullptr;
@@ -428,8 +429,9 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
     ctx->pf_img_floats = need;
   }
   const long long off = (long long)layer * ctx->layer_elems;
-  prefill_prep_kernel<<<dim3(n_ktiles, ctx->kvh_count), 256, 0, s>>>(ctx->kc + off, ctx->vc + off, ctx->head_elems,
-                                                                    n_keys, n_ktiles, ctx->pf_img);
+  const int cg = ctx->prefill_cg;
+  (cg == 2 ? prefill_prep_kernel<2> : prefill_prep_kernel<1>)<<<dim3(n_ktiles, ctx->kvh_count), 256, 0, s>>>(
+      ctx->kc + off, ctx->vc + off, ctx->head_elems, n_keys, n_ktiles, ctx->pf_img);
   ++ctx->launches;
   L3P_CUDA(ctx, cudaGetLastError());
   PrefillArgs a{};
@@ -450,7 +452,23 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
   a.swa_window = ctx->cfg.swa_window;
   a.swa_pattern = ctx->cfg.swa_pattern;
   a.err = ctx->err_dev;
-  prefill_tc_kernel<<<a.n_qtiles * a.n_qh, 256, kPfSmemBytes, s>>>(a);
+  if (cg == 2) {
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = dim3(a.n_qtiles * a.n_qh, 1, 1);
+    lc.blockDim = dim3(256, 1, 1);
+    lc.dynamicSmemBytes = PfCfg<2>::kSmemBytes;
+    lc.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, prefill_tc_kernel<2>, a));
+  } else {
+    prefill_tc_kernel<1><<<a.n_qtiles * a.n_qh, 256, PfCfg<1>::kSmemBytes, s>>>(a);
+  }
   ++ctx->launches;
   L3P_CUDA(ctx, cudaGetLastError());
   return L3P_OK;
@@ -550,8 +568,18 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   ctx->prefill_tc = c.head_dim == kPfHD;
   if (const char* path = getenv("L3P_PREFILL_PATH"))
     if (strcmp(path, "ffma") == 0) ctx->prefill_tc = false;
+  // single CTAs by default (measured faster: the pair form pays a second
+  // commit per barrier and a relay per chunk); L3P_PREFILL_CG=2 selects CTA
+  // pairs (cta_group::2), which take two q heads of one KV head and so need an
+  // even GQA group
+  ctx->prefill_cg = 1;
+  if (const char* cg = getenv("L3P_PREFILL_CG"))
+    if (strcmp(cg, "2") == 0 && ctx->G % 2 == 0) ctx->prefill_cg = 2;
   if (ctx->prefill_tc &&
-      cudaFuncSetAttribute(prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPfSmemBytes) != cudaSuccess)
+      (cudaFuncSetAttribute(prefill_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfCfg<1>::kSmemBytes) !=
+           cudaSuccess ||
+       cudaFuncSetAttribute(prefill_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfCfg<2>::kSmemBytes) !=
+           cudaSuccess))
     return bail(L3P_E_CUDA, "cudaFuncSetAttribute (prefill) failed");
   // clusters of up to 16 CTAs (16 is a non-portable size); record how many of
   // each size fit on this GPU at once (0 = that size is not available)

@@ -12,33 +12,52 @@
 // hi*hi + hi*lo + lo*hi, accumulated in fp32 in tensor memory.  The dropped
 // lo*lo term and the tf32 rounding of lo are ~2^-21 relative.
 //
-// One CTA = one q head x 128 query rows; keys in tiles of 128.  Every MMA is
-// M=128 N=128 K=8: one tcgen05.mma costs the issuing thread ~44 cycles and the
-// tensor core 64 cycles at N=128, so narrower MMAs would leave the tensor core
-// waiting on the issuer.
-//   warp 0       producer: 1-D bulk copies of pre-split K/V chunk images
-//                (prefill_prep_kernel) into a 5-stage ring of 32 KB stages,
-//                in the order the MMA issuer consumes them
-//   warp 1       MMA issuer (one thread), per key tile j:
-//                S_j = Q.K_j^T: 4 K chunks x 4 k-steps x 3 MMAs, Q hi from
-//                tensor memory (TS form), Q lo from shared memory (SS form);
-//                O += P_j.V_j: 4 V chunks (32 keys) x 4 k-steps x 3 MMAs, P
-//                from tensor memory.  S_{j+1} is issued before P_j.V_j, so the
-//                tensor core computes the next scores while the softmax
-//                warps turn S_j into P_j.
+// One CTA = one q head x 128 query rows; keys in tiles of 128.  Every MMA has
+// N=128, K=8: one tcgen05.mma costs the issuing thread ~44 cycles and the
+// tensor core 64 cycles per 128 rows at N=128, so narrower MMAs would leave
+// the tensor core waiting on the issuer.
+//
+// CG = 2 (GQA groups of even size): the CTAs of a 2-CTA cluster take two q
+// heads of the same KV head and the same query rows, and every MMA is
+// cta_group::2 with M = 256 issued by the even CTA.  Each CTA stages only half
+// of every K/V chunk (the B operand is split by columns across the pair), so a
+// CTA streams half the bytes per flop: at M = 128 the stream needs ~42
+// bytes/cycle/SM from L2, more than a ring of 1-D bulk copies (~4.5K cycles
+// latency under this load) delivers.  CG = 1 is the single-CTA form.
+//
+// Roles (256 threads per CTA):
+//   warps 0,2,3  producers (one thread each, chunks in turn): 1-D bulk
+//                copies of this CTA's half of the pre-split K/V chunk images
+//                (prefill_prep_kernel) into a ring of kStages stages, in the
+//                order the MMA issuer consumes them
+//   warp 1       even CTA: MMA issuer (one thread), per key tile j:
+//                  S_j = Q.K_j^T: 4 K chunks x 4 k-steps x 3 MMAs, Q hi from
+//                  tensor memory (TS form), Q lo from shared memory (SS form);
+//                  O += P_j.V_j: 4 V chunks (32 keys) x 4 k-steps x 3 MMAs,
+//                  P from tensor memory.  S_{j+1} is issued before P_j.V_j,
+//                  so the tensor core computes the next scores while the
+//                  softmax warps turn S_j into P_j.
+//                odd CTA: relays each landed chunk to the even CTA's issuer
 //   warps 4..7   one query row per thread: Q hi into tensor memory and Q lo
 //                into shared memory, online softmax on S, P in 32-key quarters
-//                into a two-slot tensor-memory ring, lazy rescale of O (only
-//                when the running max grows by more than 2^8), epilogue.
-// Tensor memory (512 columns): Q hi [0,128) O [128,256) S [256,384)
+//                into a two-slot tensor-memory ring (a quarter waits only for
+//                its slot's previous quarter to be multiplied in), lazy
+//                rescale of O (only when the running max grows by more than
+//                2^8; only then does a warp wait for every P.V MMA issued so
+//                far), epilogue through shared memory with whole-row global
+//                stores.
+// Barriers the issuers wait on (kv_peer, s_free, p_full, q_ready) live in the
+// even CTA and count arrivals from both CTAs; barriers the issuers complete
+// (kv_empty, s_full, p_free, pv_done) get one commit per CTA of the pair.
+// Tensor memory (512 columns per CTA): Q hi [0,128) O [128,256) S [256,384)
 // P slot 0 [384,448) P slot 1 [448,512) (each slot: 32 hi then 32 lo columns).
 // Shared memory: Q lo image (64 KB) then the stage ring.
-//   K chunk c (dims 32c..32c+31 of 128 keys): K-major, 128-byte swizzle,
-//            hi 16 KB then lo 16 KB.
-//   V chunk v (keys 32v..32v+31, all 128 dims): MN-major, 128-byte swizzle
-//            with 32-byte units (the only MN-major layout the tensor cores
-//            accept for 32-bit elements), four 32-dim atoms of eight 4-key
-//            groups, hi 16 KB then lo 16 KB.
+//   K chunk c (dims 32c..32c+31), this CTA's 128/CG keys: K-major, 128-byte
+//            swizzle, hi then lo.
+//   V chunk v (keys 32v..32v+31), this CTA's 128/CG dims: MN-major, 128-byte
+//            swizzle with 32-byte units (the only MN-major layout the tensor
+//            cores accept for 32-bit elements), 32-dim atoms of eight 4-key
+//            groups, hi then lo.
 #pragma once
 #include "ptx.cuh"
 #include "tc.cuh"
@@ -48,14 +67,21 @@ namespace l3p {
 constexpr int kPfBM = 128;  // query rows per CTA
 constexpr int kPfBN = 128;  // keys per tile
 constexpr int kPfHD = 128;  // head_dim of this kernel
-constexpr int kPfChunkBytes = 32768;  // one K or V chunk image, hi + lo
-constexpr int kPfChunkFloats = kPfChunkBytes / 4;
-constexpr int kPfTileFloats = 8 * kPfChunkFloats;  // K chunks 0..3 then V chunks 0..3 of one key tile
-constexpr int kPfStages = 5;
+constexpr int kPfChunkBytes = 32768;  // one K or V chunk image, hi + lo, both CTAs' halves
+constexpr int kPfTileFloats = 8 * kPfChunkBytes / 4;  // one key tile: 8 chunks
 constexpr int kPfQloBytes = kPfBM * kPfHD * 4;
-constexpr int kPfSmemBytes = kPfQloBytes + kPfStages * kPfChunkBytes + 1024;  // + alignment slack
 constexpr float kPfRescale = 8.f;  // lazy rescale threshold (log2 units)
-static_assert(kPfSmemBytes <= 232448, "prefill shared memory exceeds the per-CTA limit");
+constexpr int kProducers = 2;      // producer threads (warps 0, 2)
+
+template <int CG>
+struct PfCfg {
+  static constexpr int kStageBytes = kPfChunkBytes / CG;  // this CTA's share of a chunk image
+  static constexpr int kStageFloats = kStageBytes / 4;
+  static constexpr int kStages = 5 * CG;
+  static constexpr int kRows = 128 / CG;  // B rows per CTA: keys of a K chunk, dims of a V chunk
+  static constexpr int kSmemBytes = kPfQloBytes + kStages * kStageBytes + 1024;  // + alignment slack
+  static_assert(kSmemBytes <= 232448, "prefill shared memory exceeds the per-CTA limit");
+};
 
 struct PrefillArgs {
   const float* q;    // [n_tok][n_heads][128], query token t at position q_pos0 + t
@@ -90,20 +116,26 @@ __device__ __forceinline__ uint64_t sdesc_mn_sw128_32b(uint32_t addr) {
 // offset >> 4 without carrying into the next field.
 __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) { return d + (byte_off >> 4); }
 
+template <int CG>
 __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a) {
+  using C = PfCfg<CG>;
+  constexpr int S = C::kStages;
   extern __shared__ unsigned char pf_smem_raw[];
   __shared__ uint32_t s_tmem;
-  __shared__ __align__(8) uint64_t bar_kv_full[kPfStages], bar_kv_empty[kPfStages];
+  __shared__ __align__(8) uint64_t bar_kv_full[S], bar_kv_empty[S], bar_kv_peer[S];
   __shared__ __align__(8) uint64_t bar_s_full, bar_s_free, bar_p_full[2], bar_p_free[2];
-  __shared__ __align__(8) uint64_t bar_pv_done, bar_q_ready, bar_mma_idle;
+  __shared__ __align__(8) uint64_t bar_pv_done, bar_q_ready, bar_mma_idle[2];
   unsigned char* sbase = (unsigned char*)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* qlo = sbase;
   unsigned char* ring = sbase + kPfQloBytes;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // heaviest query tiles first
-  const int qt = a.n_qtiles - 1 - (int)blockIdx.x / a.n_qh;
-  const int hq = (int)blockIdx.x % a.n_qh;
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
+  // heaviest query tiles first; CG = 2: a cluster takes q heads 2p and 2p + 1
+  const int unit = (int)blockIdx.x / CG;
+  const int units_per_qt = a.n_qh / CG;
+  const int qt = a.n_qtiles - 1 - unit / units_per_qt;
+  const int hq = (unit % units_per_qt) * CG + (int)rank;
   const int h = a.kv_head_begin * a.G + hq;  // absolute q head
   const int kvh_local = hq / a.G;
   const int qbase = a.q_pos0 + qt * kPfBM;
@@ -113,37 +145,76 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
   const int j1 = k_hi / kPfBN;
   const int nt = j1 - j0 + 1;
 
+  // The softmax warps fetch their Q rows before the setup barrier, every load
+  // of a row in flight at once, so the latency overlaps the allocation.
+  float4 qv[kPfHD / 4];
+  if (warp >= 4) {
+    const int qpos = qbase + (warp - 4) * 32 + lane;
+    const float* qrow = a.q + ((long long)(qpos - a.q_pos0) * a.n_heads + h) * kPfHD;
+#pragma unroll
+    for (int i = 0; i < kPfHD / 4; ++i)
+      qv[i] = qpos < q_end ? __ldg(reinterpret_cast<const float4*>(qrow) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   if (warp == 0) {
-    tc::tmem_alloc(&s_tmem, 512);
-    tc::tmem_relinquish();
+    tc::tmem_alloc_g<CG>(&s_tmem, 512);
+    tc::tmem_relinquish_g<CG>();
   }
   if (tid == 32) {
-    for (int s = 0; s < kPfStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&bar_kv_full[s], 1);
       mbar_init(&bar_kv_empty[s], 1);
+      mbar_init(&bar_kv_peer[s], 1);
     }
     mbar_init(&bar_s_full, 1);
-    mbar_init(&bar_s_free, 4);
+    mbar_init(&bar_s_free, 4 * CG);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&bar_p_full[b], 4);
+      mbar_init(&bar_p_full[b], 4 * CG);
       mbar_init(&bar_p_free[b], 1);
     }
     mbar_init(&bar_pv_done, 1);
-    mbar_init(&bar_q_ready, 4);
-    mbar_init(&bar_mma_idle, 1);
+    mbar_init(&bar_q_ready, 4 * CG);
+    mbar_init(&bar_mma_idle[0], 1);
+    mbar_init(&bar_mma_idle[1], 1);
     fence_mbar_init();
   }
   tc::fence_before_sync();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync_all();  // the peer's barriers are initialised before any remote arrive
+  else
+    __syncthreads();
   tc::fence_after_sync();
   const uint32_t tm = s_tmem;
   const uint32_t T_QHI = tm + 0, T_O = tm + 128, T_S = tm + 256, T_P = tm + 384;
 
-  if (warp == 0) {
-    // ---------------- producer ----------------
+  // bounded waits: cluster-scope acquire when the pair shares the barriers
+  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if constexpr (CG == 2)
+      return mbar_wait_bounded_cluster(bar, parity, a.err);
+    else
+      return mbar_wait_bounded(bar, parity, a.err);
+  };
+  // arrive on a barrier of the issuing (even) CTA
+  auto arrive_issuer = [&](uint64_t* bar) {
+    if constexpr (CG == 2)
+      mbar_arrive_cluster(mapa_shared(smem_addr(bar), 0));
+    else
+      mbar_arrive(bar);
+  };
+  // complete a barrier in every CTA of the pair once the MMAs issued so far are done
+  auto commit_all = [&](uint64_t* bar) {
+    tc::commit_g<CG>(smem_addr(bar));
+    if constexpr (CG == 2) tc::commit_g<CG>(mapa_shared(smem_addr(bar), 1));
+  };
+
+  if (warp == 0 || warp == 2) {
+    // ---------------- producers ----------------
+    // Two threads in different warps issue chunks in turn: the bulk copies of
+    // one thread complete one after another, so one thread alone cannot keep
+    // the ring full.
     if (lane == 0) {
-      const float* img = a.img + ((long long)kvh_local * a.n_ktiles + j0) * kPfTileFloats;
-      int c = 0;  // chunks issued
+      const int me = warp >> 1;  // chunks c with c % kProducers == me
+      const float* img = a.img + ((long long)kvh_local * a.n_ktiles + j0) * kPfTileFloats + rank * 8 * C::kStageFloats;
+      int c = 0;  // chunks enumerated
       bool ok = true;
       // consumption order: K of tile 0; then per step n, K of tile n and V of tile n-1
       for (int n = 0; ok && n <= nt; ++n) {
@@ -151,100 +222,114 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
           const int t = n - part;
           if (t < 0 || t >= nt) continue;
           for (int ch = 0; ch < 4; ++ch, ++c) {
-            const int s = c % kPfStages, u = c / kPfStages;
-            if (u >= 1 && !mbar_wait_bounded(&bar_kv_empty[s], (uint32_t)((u - 1) & 1), a.err)) {
+            if (c % kProducers != me) continue;
+            const int s = c % S, u = c / S;
+            if (u >= 1 && !wait(&bar_kv_empty[s], (uint32_t)((u - 1) & 1))) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&bar_kv_full[s], (uint32_t)kPfChunkBytes);
+            mbar_arrive_expect_tx(&bar_kv_full[s], (uint32_t)C::kStageBytes);
             asm volatile(
                 "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                    smem_addr(ring + s * kPfChunkBytes)),
-                "l"(img + (long long)t * kPfTileFloats + (part * 4 + ch) * kPfChunkFloats),
-                "r"((uint32_t)kPfChunkBytes), "r"(smem_addr(&bar_kv_full[s]))
+                    smem_addr(ring + s * C::kStageBytes)),
+                "l"(img + (long long)t * kPfTileFloats + (part * 4 + ch) * C::kStageFloats),
+                "r"((uint32_t)C::kStageBytes), "r"(smem_addr(&bar_kv_full[s]))
                 : "memory");
           }
         }
       }
-      // no copy may still be landing when the CTA tears down
-      for (int i = c > kPfStages ? c - kPfStages : 0; i < c; ++i)
-        mbar_wait_bounded(&bar_kv_full[i % kPfStages], (uint32_t)((i / kPfStages) & 1), a.err);
+      // no copy of this thread may still be landing when the CTA tears down
+      for (int i = c > S ? c - S : 0; i < c; ++i)
+        if (i % kProducers == me) wait(&bar_kv_full[i % S], (uint32_t)((i / S) & 1));
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+  } else if (warp == 1 && rank == 1) {
+    // ---------------- relay (odd CTA): chunk landed here -> issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t id_s = tc::idesc_tf32(kPfBM, kPfBN, false);
-      constexpr uint32_t id_o = tc::idesc_tf32(kPfBM, kPfHD, true);
-      const uint64_t qlo_d = tc::sdesc_sw128(smem_addr(qlo), 16, 1024);
-      const uint64_t k_d = tc::sdesc_sw128(smem_addr(ring), 16, 1024);
-      const uint64_t v_d = sdesc_mn_sw128_32b(smem_addr(ring));
-      int c = 0;  // chunks consumed
-      bool ok = mbar_wait_bounded(&bar_q_ready, 0, a.err);
-      tc::fence_after_sync();
-      auto next_chunk = [&](uint32_t& off) -> bool {
-        const int s = c % kPfStages, u = c / kPfStages;
-        off = (uint32_t)(s * kPfChunkBytes);
-        if (!mbar_wait_bounded(&bar_kv_full[s], (uint32_t)(u & 1), a.err)) return false;
+      for (int c = 0; c < 8 * nt; ++c) {
+        if (!wait(&bar_kv_full[c % S], (uint32_t)((c / S) & 1))) break;
+        mbar_arrive_cluster(mapa_shared(smem_addr(&bar_kv_peer[c % S]), 0));
+      }
+    }
+  } else if ((warp == 1 || warp == 3) && rank == 0) {
+    // ---------------- MMA issuers ----------------
+    // warp 1 issues S = Q.K^T, warp 3 issues O += P.V.  One thread pays ~44
+    // cycles per tcgen05.mma and more per commit or barrier wait, while the
+    // tensor core takes 64 cycles per N=128 MMA: a single issuer leaves it
+    // idle, two issuers in different warps keep it busy.
+    if (lane == 0) {
+      // chunk c = 4 * block + i of the ring sequence K0 K1 V0 K2 V1 ... V(nt-1)
+      auto k_block = [&](int t) { return t == 0 ? 0 : 2 * t - 1; };
+      auto v_block = [&](int t) { return t + 1 < nt ? 2 * t + 2 : 2 * t + 1; };
+      auto chunk_ready = [&](int c, uint32_t& off) -> bool {
+        const int s = c % S, u = c / S;
+        off = (uint32_t)(s * C::kStageBytes);
+        if (!wait(&bar_kv_full[s], (uint32_t)(u & 1))) return false;
+        if (CG == 2 && !wait(&bar_kv_peer[s], (uint32_t)(u & 1))) return false;
         tc::fence_after_sync();
         return true;
       };
-      auto issue_s = [&]() -> bool {
-#pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t off;
-          if (!next_chunk(off)) return false;
-          const uint64_t kh = desc_add(k_d, off), kl = desc_add(k_d, off + kPfChunkBytes / 2);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t a_col = T_QHI + ch * 32 + kk * 8;
-            const uint64_t bh = desc_add(kh, kk * 32), bl = desc_add(kl, kk * 32);
-            tc::mma_tf32_ts(T_S, a_col, bh, id_s, ch > 0 || kk > 0);
-            tc::mma_tf32_ts(T_S, a_col, bl, id_s, true);
-            tc::mma_tf32_ss(T_S, desc_add(qlo_d, ch * 16384 + kk * 32), bh, id_s, true);
+      if (warp == 1) {
+        constexpr uint32_t id_s = tc::idesc_tf32(kPfBM * CG, kPfBN, false);
+        const uint64_t qlo_d = tc::sdesc_sw128(smem_addr(qlo), 16, 1024);
+        const uint64_t k_d = tc::sdesc_sw128(smem_addr(ring), 16, 1024);
+        bool ok = wait(&bar_q_ready, 0);
+        tc::fence_after_sync();
+        for (int t = 0; ok && t < nt; ++t) {
+          if (t >= 1) {
+            // S_t overwrites S: the softmax warps must have read S_{t-1}
+            if (!wait(&bar_s_free, (uint32_t)((t - 1) & 1))) break;
+            tc::fence_after_sync();
           }
-          tc::commit(&bar_kv_empty[c % kPfStages]);
-          ++c;
-        }
-        tc::commit(&bar_s_full);
-        return true;
-      };
-      auto issue_pv = [&](int jj) -> bool {
 #pragma unroll 1
-        for (int qq = 0; qq < 4; ++qq) {
-          uint32_t off;
-          if (!next_chunk(off)) return false;
-          const int slot = qq & 1;
-          if (!mbar_wait_bounded(&bar_p_full[slot], (uint32_t)((qq >> 1) & 1), a.err)) return false;
-          tc::fence_after_sync();
-          const uint64_t vh = desc_add(v_d, off), vl = desc_add(v_d, off + kPfChunkBytes / 2);
-          const uint32_t p_hi = T_P + slot * 64, p_lo = p_hi + 32;
+          for (int ch = 0; ok && ch < 4; ++ch) {
+            const int c = 4 * k_block(t) + ch;
+            uint32_t off;
+            if (!(ok = chunk_ready(c, off))) break;
+            const uint64_t kh = desc_add(k_d, off), kl = desc_add(k_d, off + C::kStageBytes / 2);
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            const uint64_t bh = desc_add(vh, ks * 1024), bl = desc_add(vl, ks * 1024);
-            tc::mma_tf32_ts(T_O, p_hi + ks * 8, bh, id_o, jj > 0 || qq > 0 || ks > 0);
-            tc::mma_tf32_ts(T_O, p_hi + ks * 8, bl, id_o, true);
-            tc::mma_tf32_ts(T_O, p_lo + ks * 8, bh, id_o, true);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t a_col = T_QHI + ch * 32 + kk * 8;
+              const uint64_t bh = desc_add(kh, kk * 32), bl = desc_add(kl, kk * 32);
+              tc::mma_tf32_ts_g<CG>(T_S, a_col, bh, id_s, ch > 0 || kk > 0);
+              tc::mma_tf32_ts_g<CG>(T_S, a_col, bl, id_s, true);
+              tc::mma_tf32_ss_g<CG>(T_S, desc_add(qlo_d, ch * 16384 + kk * 32), bh, id_s, true);
+            }
+            commit_all(&bar_kv_empty[c % S]);
           }
-          tc::commit(&bar_kv_empty[c % kPfStages]);
-          tc::commit(&bar_p_free[slot]);
-          ++c;
+          if (ok) commit_all(&bar_s_full);
         }
-        tc::commit(&bar_pv_done);
-        return true;
-      };
-      if (ok) ok = issue_s();
-      for (int jj = 0; ok && jj < nt; ++jj) {
-        if (jj + 1 < nt) {
-          // S_{jj+1} overwrites S: the softmax warps must have read S_jj
-          if (!mbar_wait_bounded(&bar_s_free, (uint32_t)(jj & 1), a.err)) break;
-          tc::fence_after_sync();
-          if (!issue_s()) break;
+        // every MMA of this issuer completes before tensor memory is released
+        tc::commit_g<CG>(smem_addr(&bar_mma_idle[0]));
+        wait(&bar_mma_idle[0], 0);
+      } else {
+        constexpr uint32_t id_o = tc::idesc_tf32(kPfBM * CG, kPfHD, true);
+        const uint64_t v_d = sdesc_mn_sw128_32b(smem_addr(ring));
+        bool ok = true;
+        for (int t = 0; ok && t < nt; ++t) {
+#pragma unroll 1
+          for (int qq = 0; ok && qq < 4; ++qq) {
+            const int c = 4 * v_block(t) + qq, slot = qq & 1;
+            uint32_t off;
+            if (!(ok = chunk_ready(c, off))) break;
+            if (!(ok = wait(&bar_p_full[slot], (uint32_t)((qq >> 1) & 1)))) break;
+            tc::fence_after_sync();
+            const uint64_t vh = desc_add(v_d, off), vl = desc_add(v_d, off + C::kStageBytes / 2);
+            const uint32_t p_hi = T_P + slot * 64, p_lo = p_hi + 32;
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              const uint64_t bh = desc_add(vh, ks * 1024), bl = desc_add(vl, ks * 1024);
+              tc::mma_tf32_ts_g<CG>(T_O, p_hi + ks * 8, bh, id_o, t > 0 || qq > 0 || ks > 0);
+              tc::mma_tf32_ts_g<CG>(T_O, p_hi + ks * 8, bl, id_o, true);
+              tc::mma_tf32_ts_g<CG>(T_O, p_lo + ks * 8, bh, id_o, true);
+            }
+            commit_all(&bar_kv_empty[c % S]);
+            commit_all(&bar_p_free[slot]);
+          }
+          if (ok) commit_all(&bar_pv_done);
         }
-        if (!issue_pv(jj)) break;
+        tc::commit_g<CG>(smem_addr(&bar_mma_idle[1]));
+        wait(&bar_mma_idle[1], 0);
       }
-      // every MMA of this CTA completes before tensor memory is released
-      tc::commit(&bar_mma_idle);
-      mbar_wait_bounded(&bar_mma_idle, 0, a.err);
     }
   } else if (warp >= 4) {
     // ---------------- softmax warpgroup: thread = query row ----------------
@@ -253,13 +338,12 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
     const bool valid = qpos < q_end;
     const int kmin = valid ? pf_start_t(a, qpos) : 0;
     const uint32_t lb = (uint32_t)((warp - 4) * 32) << 16;
-    const float* qrow = a.q + ((long long)(qpos - a.q_pos0) * a.n_heads + h) * kPfHD;
-#pragma unroll 1
+#pragma unroll
     for (int c = 0; c < 4; ++c) {
       float hi[32], lo[32];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float4 t = valid ? *reinterpret_cast<const float4*>(qrow + c * 32 + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 t = qv[c * 8 + i];
         const float x[4] = {t.x * a.scale, t.y * a.scale, t.z * a.scale, t.w * a.scale};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -279,12 +363,12 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // shared stores -> tensor-core reads
     tc::fence_before_sync();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&bar_q_ready);
+    if (lane == 0) arrive_issuer(&bar_q_ready);
 
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int jj = 0; jj < nt; ++jj) {
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar_s_full, (uint32_t)(jj & 1), a.err));
+      ok = __all_sync(0xffffffffu, wait(&bar_s_full, (uint32_t)(jj & 1)));
       if (!ok) break;
       tc::fence_after_sync();
       float sv[kPfBN];
@@ -298,7 +382,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
       tc::wait_ld();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_s_free);
+      if (lane == 0) arrive_issuer(&bar_s_free);
       const int key0 = (j0 + jj) * kPfBN;
       float mt = -INFINITY;
       if (__all_sync(0xffffffffu, valid && key0 >= kmin && key0 + kPfBN - 1 <= qpos)) {
@@ -316,12 +400,6 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
           mt = fmaxf(mt, sv[c]);
         }
       }
-      if (jj >= 1) {
-        // P_{jj-1}.V_{jj-1} complete: O is stable and both P slots are free
-        ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar_pv_done, (uint32_t)((jj - 1) & 1), a.err));
-        if (!ok) break;
-        tc::fence_after_sync();
-      }
       const float m_new = fmaxf(m, mt);
       const bool grow = m_new > m + kPfRescale;  // true on the first finite score (m = -inf)
       float alpha = 1.f;
@@ -331,7 +409,12 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
         m = m_new;
       }
       if (jj >= 1 && __any_sync(0xffffffffu, grow)) {
-        // rescale O (warp-wide tensor-memory access; rows that keep their max use 1)
+        // rescale O (warp-wide tensor-memory access; rows that keep their max
+        // use 1).  Every P.V MMA issued so far must be complete; the next one
+        // waits for this warp's P.  Warps that keep their max skip the wait.
+        ok = __all_sync(0xffffffffu, wait(&bar_pv_done, (uint32_t)((jj - 1) & 1)));
+        if (!ok) break;
+        tc::fence_after_sync();
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           float ov[32];
@@ -346,9 +429,12 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
 #pragma unroll
       for (int qq = 0; qq < 4; ++qq) {
         const int slot = qq & 1;
-        if (qq >= 2) {
-          // the slot's previous quarter (qq - 2) has been multiplied into O
-          ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar_p_free[slot], 0u, a.err));
+        if (jj >= 1 || qq >= 2) {
+          // the slot's previous quarter (this tile's qq - 2, or the previous
+          // tile's qq + 2) has been multiplied into O: p_free[slot] completes
+          // once per quarter in the slot, the previous one is number
+          // 2 * jj + qq / 2 - 1
+          ok = __all_sync(0xffffffffu, wait(&bar_p_free[slot], (uint32_t)((qq >> 1) ^ 1)));
           if (!ok) break;
           tc::fence_after_sync();
         }
@@ -367,49 +453,67 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
         tc::wait_st();
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bar_p_full[slot]);
+        if (lane == 0) arrive_issuer(&bar_p_full[slot]);
       }
       if (!ok) break;
     }
     // ---------------- epilogue ----------------
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(&bar_pv_done, (uint32_t)((nt - 1) & 1), a.err));
+    if (ok) ok = __all_sync(0xffffffffu, wait(&bar_pv_done, (uint32_t)((nt - 1) & 1)));
     if (ok) {
       tc::fence_after_sync();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      float* orow = a.out + ((long long)(qpos - a.q_pos0) * a.n_heads + h) * kPfHD;
+      // O rows go through shared memory (the Q lo image is dead once the last
+      // S is done) so that global stores are whole 512-byte rows.  16-byte
+      // piece i of row r sits at piece i ^ (r % 8): conflict-free for the
+      // row-per-thread writes and the row-per-warp reads.
+      unsigned char* srow = qlo + row * (kPfHD * 4);
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         float ov[32];
         tc::ld32(T_O + lb + c * 32, ov);
         tc::wait_ld();
-        if (valid) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            *reinterpret_cast<float4*>(orow + c * 32 + 4 * i) =
-                make_float4(ov[4 * i] * inv, ov[4 * i + 1] * inv, ov[4 * i + 2] * inv, ov[4 * i + 3] * inv);
-        }
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<float4*>(srow + (((c * 8 + i) ^ (row & 7)) << 4)) =
+              make_float4(ov[4 * i] * inv, ov[4 * i + 1] * inv, ov[4 * i + 2] * inv, ov[4 * i + 3] * inv);
+      }
+      __syncwarp();
+#pragma unroll 4
+      for (int r = 0; r < 32; ++r) {
+        const int rr = (warp - 4) * 32 + r;
+        const int pos = qbase + rr;
+        if (pos < q_end)
+          *reinterpret_cast<float4*>(a.out + ((long long)(pos - a.q_pos0) * a.n_heads + h) * kPfHD + 4 * lane) =
+              *reinterpret_cast<const float4*>(qlo + rr * (kPfHD * 4) + ((lane ^ (rr & 7)) << 4));
       }
     }
   }
   tc::fence_before_sync();
-  __syncthreads();
+  if constexpr (CG == 2)
+    cluster_sync_all();  // no CTA leaves while its peer may still signal it or read its memory
+  else
+    __syncthreads();
   if (warp == 0) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tm, 512);
+    tc::tmem_dealloc_g<CG>(tm, 512);
   }
 }
 
-// K/V chunk images for prefill_tc_kernel: per (owned KV head, 128-key tile),
-// K chunks 0..3 then V chunks 0..3, each hi then lo, from the head-major
-// cache.  Keys at or beyond n_keys read as 0.  grid (n_ktiles, kvh_count),
-// 256 threads.
+// K/V chunk images for prefill_tc_kernel<CG>: per (owned KV head, 128-key
+// tile), per CTA half r of the pair: K chunks 0..3 then V chunks 0..3, each
+// hi then lo, from the head-major cache.  K chunk c of half r holds keys
+// [r*128/CG, (r+1)*128/CG) of dims 32c..32c+31; V chunk v of half r holds
+// keys 32v..32v+31 of dims [r*128/CG, (r+1)*128/CG).  Keys at or beyond
+// n_keys read as 0.  grid (n_ktiles, kvh_count), 256 threads.
+template <int CG>
 __global__ void prefill_prep_kernel(const float* __restrict__ kc, const float* __restrict__ vc, long long head_stride,
                                     int n_keys, int n_ktiles, float* __restrict__ img) {
+  using C = PfCfg<CG>;
   const int j = blockIdx.x, hl = blockIdx.y;
   unsigned char* base = reinterpret_cast<unsigned char*>(img + ((long long)hl * n_ktiles + j) * kPfTileFloats);
-  constexpr int kHalf = kPfChunkBytes / 2;  // bytes of one hi (or lo) image
+  constexpr int kHalf = C::kStageBytes / 2;  // bytes of one hi (or lo) image
   for (int idx = threadIdx.x; idx < kPfBN * kPfHD / 4; idx += blockDim.x) {
-    const int key = idx / (kPfHD / 4), c16 = idx % (kPfHD / 4);  // 16-byte chunk of the row
+    const int key = idx / (kPfHD / 4), c16 = idx % (kPfHD / 4);  // 16-byte piece of the row
     const int pos = j * kPfBN + key;
     float4 kx = make_float4(0.f, 0.f, 0.f, 0.f), vx = kx;
     if (pos < n_keys) {
@@ -420,14 +524,17 @@ __global__ void prefill_prep_kernel(const float* __restrict__ kc, const float* _
     const float4 klo = make_float4(kx.x - khi.x, kx.y - khi.y, kx.z - khi.z, kx.w - khi.w);
     const float4 vhi = make_float4(tc::tf32_hi(vx.x), tc::tf32_hi(vx.y), tc::tf32_hi(vx.z), tc::tf32_hi(vx.w));
     const float4 vlo = make_float4(vx.x - vhi.x, vx.y - vhi.y, vx.z - vhi.z, vx.w - vhi.w);
-    const int atom = c16 >> 3, part = c16 & 7;  // 32-dim block, 16-byte piece within its 128 bytes
-    // K chunk `atom`: K-major, 128-byte swizzle (16-byte piece ^ key % 8), 128 keys x 128 bytes
-    const int kb = atom * kPfChunkBytes + key * 128 + ((part ^ (key & 7)) << 4);
+    const int part = c16 & 7;  // 16-byte piece within its 128-byte (32-dim) block
+    // K chunk c16/8, half key/kRows: K-major, 128-byte swizzle (piece ^ key % 8)
+    const int kr = key / C::kRows, kl = key % C::kRows;
+    const int kb = (kr * 8 + (c16 >> 3)) * C::kStageBytes + kl * 128 + ((part ^ (kl & 7)) << 4);
     *reinterpret_cast<float4*>(base + kb) = khi;
     *reinterpret_cast<float4*>(base + kb + kHalf) = klo;
-    // V chunk key/32: MN-major, 32-byte units ^ (key % 4), 32-dim atoms of eight 4-key groups
+    // V chunk key/32, half dim/kRows: MN-major, 32-byte units ^ (key % 4),
+    // 32-dim atoms of eight 4-key groups
+    const int dim = 4 * c16, vr = dim / C::kRows, atom = (dim % C::kRows) >> 5;
     const int kv = key & 31, byte = part * 16;
-    const int vb = (4 + (key >> 5)) * kPfChunkBytes + atom * 4096 + (kv >> 2) * 512 + (kv & 3) * 128 +
+    const int vb = (vr * 8 + 4 + (key >> 5)) * C::kStageBytes + atom * 4096 + (kv >> 2) * 512 + (kv & 3) * 128 +
                    ((((byte >> 5) ^ (kv & 3)) << 5) | (byte & 31));
     *reinterpret_cast<float4*>(base + vb) = vhi;
     *reinterpret_cast<float4*>(base + vb + kHalf) = vlo;

@@ -81,6 +81,73 @@ __device__ __forceinline__ void commit(uint64_t* bar) {
                : "memory");
 }
 
+// ---- CTA-group variants: CG = 1 (this CTA) or 2 (the CTA pair of a cluster;
+// M = 256, rows 0..127 in the even CTA's tensor memory, 128..255 in the odd
+// one's, B split by columns: the even CTA's shared memory holds columns
+// [0, N/2), the odd CTA's [N/2, N)).  Allocation, relinquish and dealloc are
+// executed by the same warp in both CTAs of a pair; MMAs and commits by one
+// thread of the even CTA.
+template <int CG>
+__device__ __forceinline__ void tmem_alloc_g(uint32_t* smem_result, uint32_t ncols) {
+  if constexpr (CG == 2)
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(smem_result)),
+                 "r"(ncols)
+                 : "memory");
+  else
+    tmem_alloc(smem_result, ncols);
+}
+template <int CG>
+__device__ __forceinline__ void tmem_relinquish_g() {
+  if constexpr (CG == 2)
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  else
+    tmem_relinquish();
+}
+template <int CG>
+__device__ __forceinline__ void tmem_dealloc_g(uint32_t taddr, uint32_t ncols) {
+  if constexpr (CG == 2)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+  else
+    tmem_dealloc(taddr, ncols);
+}
+template <int CG>
+__device__ __forceinline__ void mma_tf32_ts_g(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              bool accumulate) {
+  if constexpr (CG == 2)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+  else
+    mma_tf32_ts(d_tmem, a_tmem, b_desc, idesc, accumulate);
+}
+template <int CG>
+__device__ __forceinline__ void mma_tf32_ss_g(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                              bool accumulate) {
+  if constexpr (CG == 2)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"((uint32_t)accumulate)
+        : "memory");
+  else
+    mma_tf32_ss(d_tmem, a_desc, b_desc, idesc, accumulate);
+}
+// Arrive once on the mbarrier at cluster address `bar` (this CTA's or the
+// peer's) when every MMA this thread issued so far has completed.
+template <int CG>
+__device__ __forceinline__ void commit_g(uint32_t bar_cluster_addr) {
+  if constexpr (CG == 2)
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
+                 : "memory");
+  else
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
+                 : "memory");
+}
+
 __device__ __forceinline__ void fence_before_sync() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_after_sync() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 

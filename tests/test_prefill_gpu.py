@@ -32,6 +32,7 @@ def _check(got, want, what):
     AttnShape("pf_one_token", 1, 8, 2, 128, 8, pos=0, seed=7),
     AttnShape("pf_swa_hd128", 1, 8, 2, 128, 300, pos=299, seed=10, is_gemma3=1, swa_window=50, swa_pattern=6),
     AttnShape("pf_ragged_hd128", 1, 12, 3, 128, 333, pos=332, seed=12),
+    AttnShape("pf_odd_group_hd128", 1, 6, 2, 128, 290, pos=289, seed=14),
 ])
 def test_prefill_small_matches_oracle(shape):
     k, v, q = prefill_inputs(shape, 0)
@@ -40,13 +41,16 @@ def test_prefill_small_matches_oracle(shape):
     _check(got, _oracle(shape, q, k, v), shape.name)
 
 
-@pytest.mark.parametrize("path", ["tc", "ffma"])
+@pytest.mark.parametrize("path", ["tc_pair", "tc_single", "ffma"])
 def test_prefill_paths_agree_with_oracle(monkeypatch, path):
-    """head_dim 128 prefill runs on the tcgen05 tensor cores (3xTF32); the
-    FFMA path (decode kernel, one slice per token) is kept for other head
-    sizes.  Both must meet the same tolerance."""
+    """head_dim 128 prefill runs on the tcgen05 tensor cores (3xTF32): CTA
+    pairs (cta_group::2) for even GQA groups, single CTAs otherwise; the FFMA
+    path (decode kernel, one slice per token) is kept for other head sizes.
+    All must meet the same tolerance."""
     if path == "ffma":
         monkeypatch.setenv("L3P_PREFILL_PATH", "ffma")
+    if path == "tc_pair":
+        monkeypatch.setenv("L3P_PREFILL_CG", "2")
     sh = AttnShape("pf_path", 1, 32, 8, 128, 640, pos=639, seed=13)
     k, v, q = prefill_inputs(sh, 0)
     with AttnContext.for_shape(sh, n_layers=1) as ctx:
