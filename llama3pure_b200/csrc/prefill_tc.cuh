@@ -145,15 +145,19 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
   const int j1 = k_hi / kPfBN;
   const int nt = j1 - j0 + 1;
 
-  // The softmax warps fetch their Q rows before the setup barrier, every load
-  // of a row in flight at once, so the latency overlaps the allocation.
-  float4 qv[kPfHD / 4];
+  // The softmax warps fetch their Q rows before the setup barrier so the
+  // latency overlaps the allocation: each warp its 32 rows, one whole 512-byte
+  // row per load (lane = 16-byte piece), all in flight at once.  Rows past
+  // the batch read the last row and are zeroed later, so no load result is
+  // needed before the barrier.
+  float4 qv[32];
   if (warp >= 4) {
-    const int qpos = qbase + (warp - 4) * 32 + lane;
-    const float* qrow = a.q + ((long long)(qpos - a.q_pos0) * a.n_heads + h) * kPfHD;
 #pragma unroll
-    for (int i = 0; i < kPfHD / 4; ++i)
-      qv[i] = qpos < q_end ? __ldg(reinterpret_cast<const float4*>(qrow) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < 32; ++r) {
+      const int qpos = min(qbase + (warp - 4) * 32 + r, q_end - 1);
+      qv[r] = __ldg(reinterpret_cast<const float4*>(a.q + ((long long)(qpos - a.q_pos0) * a.n_heads + h) * kPfHD) +
+                    lane);
+    }
   }
   if (warp == 0) {
     tc::tmem_alloc_g<CG>(&s_tmem, 512);
@@ -338,6 +342,20 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
     const bool valid = qpos < q_end;
     const int kmin = valid ? pf_start_t(a, qpos) : 0;
     const uint32_t lb = (uint32_t)((warp - 4) * 32) << 16;
+    // Rows to threads through the Q lo region: 16-byte piece i of row r at
+    // piece i ^ (r % 8) of the row's 512 bytes (conflict-free both ways).
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      const int rr = (warp - 4) * 32 + r;
+      *reinterpret_cast<float4*>(qlo + rr * (kPfHD * 4) + ((lane ^ (rr & 7)) << 4)) =
+          qbase + rr < q_end ? qv[r] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      qv[i] = *reinterpret_cast<const float4*>(qlo + row * (kPfHD * 4) + ((i ^ (row & 7)) << 4));
+    // every softmax warp has its row before the Q lo image overwrites the region
+    asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       float hi[32], lo[32];
