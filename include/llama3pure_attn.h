@@ -46,7 +46,12 @@ extern "C" {
 #define L3P_E_TIMEOUT (-5)     /* a bounded device-side wait gave up */
 #define L3P_E_UNSUPPORTED (-6) /* geometry without a kernel in this build */
 
-#define L3P_KV_F32 0 /* fp32 KV cache (this build's format) */
+#define L3P_KV_F32 0  /* fp32 KV cache: the 1e-4 contract against the reference's fp32 loop */
+#define L3P_KV_Q8_0 1 /* the reference's own cache format (c:120-123, c:365-372): per 32-value
+                         block an fp16 scale (truncating conversion, c:585-599) and 32 int8;
+                         K/V rows and q quantised as quantize_to_q8_0_cache (c:1535-1570),
+                         scores and V sums as dot_q8_0_q8_0_cache / accum_q8_0_cache
+                         (c:1574-1622) */
 
 /* Attention geometry and placement.  Field meanings follow the reference's
  * Config (c:211-229) and RunState (c:280-338). */
@@ -65,7 +70,7 @@ typedef struct l3p_attn_config {
     int kv_head_count; /* KV heads owned; 0 => n_kv_heads - kv_head_begin */
     int seq_begin;     /* first position owned (sequence sharding) */
     int seq_count;     /* positions owned; 0 => seq_len - seq_begin */
-    int kv_format;     /* L3P_KV_F32 */
+    int kv_format;     /* L3P_KV_F32 or L3P_KV_Q8_0 */
 } l3p_attn_config;
 
 typedef struct l3p_attn_ctx l3p_attn_ctx;
@@ -153,9 +158,22 @@ int l3p_attn_prefill_dev(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok,
 int l3p_attn_load_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, const float* k,
                      const float* v);
 int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, float* k, float* v);
+/* With an L3P_KV_Q8_0 cache, load_kv quantises the rows as kv_append does and
+ * read_kv returns the dequantised values d * int8. */
+
+/* An L3P_KV_Q8_0 cache in the reference's own bytes: per KV head and position,
+ * head_dim/32 blocks of 34 bytes (fp16 scale little-endian, then 32 int8) --
+ * the rows of the reference's key_cache / value_cache (c:365-372).  k_blocks,
+ * v_blocks: [n_kv_heads][n_pos][head_dim/32*34] (all heads; the context
+ * copies the slice it owns).  An engine that already holds a Q8_0 cache
+ * hands it over with load_kv_q8; read_kv_q8 reads the cache back bit for bit. */
+int l3p_attn_load_kv_q8(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, const uint8_t* k_blocks,
+                        const uint8_t* v_blocks);
+int l3p_attn_read_kv_q8(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, uint8_t* k_blocks,
+                        uint8_t* v_blocks);
 
 /* Device addresses of one layer's owned cache: [kv_head_count][seq_count]
- * [head_dim] fp32 each. */
+ * [head_dim] fp32 each (fp32 caches only; L3P_E_UNSUPPORTED for Q8_0). */
 int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v);
 
 /* Overlap mode (off by default).  When enabled, the decode launches of the

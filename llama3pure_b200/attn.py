@@ -47,6 +47,8 @@ EXPORTS = (
     "l3p_attn_prefill_dev",
     "l3p_attn_load_kv",
     "l3p_attn_read_kv",
+    "l3p_attn_load_kv_q8",
+    "l3p_attn_read_kv_q8",
     "l3p_attn_kv_device_ptr",
     "l3p_attn_launch_count",
     "l3p_attn_set_overlap",
@@ -119,6 +121,8 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_prefill_dev": (i, [vp, i, i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_load_kv": (i, [vp, i, i, i, fp, fp]),
         "l3p_attn_read_kv": (i, [vp, i, i, i, fp, fp]),
+        "l3p_attn_load_kv_q8": (i, [vp, i, i, i, fp, fp]),
+        "l3p_attn_read_kv_q8": (i, [vp, i, i, i, fp, fp]),
         "l3p_attn_kv_device_ptr": (i, [vp, i, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
         "l3p_attn_launch_count": (C.c_longlong, [vp]),
         "l3p_attn_set_overlap": (i, [vp, i]),
@@ -174,11 +178,12 @@ class AttnContext:
     def __init__(self, n_layers: int, n_heads: int, n_kv_heads: int, head_dim: int, seq_len: int,
                  scale: float = 0.0, is_gemma3: int = 0, swa_window: int = 0, swa_pattern: int = 0,
                  device: int = 0, kv_head_begin: int = 0, kv_head_count: int = 0, seq_begin: int = 0,
-                 seq_count: int = 0, lib=None):
+                 seq_count: int = 0, kv_format: int = 0, lib=None):
         self.lib = lib or load_library()
         self.cfg = AttnConfig(n_layers, n_heads, n_kv_heads, head_dim, seq_len, scale, is_gemma3,
                               swa_window, swa_pattern, device, kv_head_begin, kv_head_count, seq_begin,
-                              seq_count, 0)
+                              seq_count, kv_format)
+        self.kv_format = kv_format
         self.n_heads, self.n_kv_heads, self.head_dim = n_heads, n_kv_heads, head_dim
         self.kv_head_begin = kv_head_begin
         self.kv_head_count = kv_head_count or (n_kv_heads - kv_head_begin)
@@ -251,6 +256,22 @@ class AttnContext:
         k = np.zeros((self.n_kv_heads, n_pos, self.head_dim), np.float32)
         v = np.zeros_like(k)
         self._ok(self.lib.l3p_attn_read_kv(self.h, layer, pos0, n_pos, _host(k), _host(v)), "read_kv")
+        return k, v
+
+    def load_kv_q8(self, layer: int, pos0: int, k_blocks: np.ndarray, v_blocks: np.ndarray) -> None:
+        """Q8_0 cache from the reference's 34-byte blocks, uint8
+        [n_kv_heads][n_pos][head_dim/32*34]."""
+        for a in (k_blocks, v_blocks):
+            if a.dtype != np.uint8 or not a.flags.c_contiguous:
+                raise TypeError("block arrays must be C-contiguous uint8")
+        self._ok(self.lib.l3p_attn_load_kv_q8(self.h, layer, pos0, k_blocks.shape[1], k_blocks.ctypes.data,
+                                              v_blocks.ctypes.data), "load_kv_q8")
+
+    def read_kv_q8(self, layer: int, pos0: int, n_pos: int):
+        """The Q8_0 cache as the reference's 34-byte blocks."""
+        k = np.zeros((self.n_kv_heads, n_pos, self.head_dim // 32 * 34), np.uint8)
+        v = np.zeros_like(k)
+        self._ok(self.lib.l3p_attn_read_kv_q8(self.h, layer, pos0, n_pos, k.ctypes.data, v.ctypes.data), "read_kv_q8")
         return k, v
 
     def kv_append(self, layer: int, pos: int, k_row: np.ndarray, v_row: np.ndarray) -> None:

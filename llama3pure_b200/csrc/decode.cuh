@@ -75,6 +75,10 @@ __device__ __forceinline__ void cp_async_wait() {
 struct DecodeArgs {
   const float* kc;         // K cache, all layers: [n_layers][kvh_count][cap][HD]
   float* vc;               // V cache, same layout
+  const int8_t* k8;        // Q8_0 cache (decode_q8_kernel): int8 values, same layout as kc
+  const int8_t* v8;
+  const uint16_t* ksc;     // fp16 block scales: [n_layers][kvh_count][cap][HD/32]
+  const uint16_t* vsc;
   float* kc_w;             // writable alias of kc (fused append)
   long long layer_stride;  // kvh_count * cap * HD
   long long head_stride;   // cap * HD
@@ -218,19 +222,229 @@ __device__ __forceinline__ int swa_start(const DecodeArgs& a, int layer, int pos
   return 0;
 }
 
+// Shared state of the merge stages (per CTA).
+template <int GT, int W>
+struct DecodeMergeSmem {
+  float m[W][GT];   // per-warp running max
+  float l[W][GT];   // per-warp running sum
+  float ww[W][GT];  // warp merge weights
+  float cm[GT], cl[GT];   // CTA partial (max, sum), read by the cluster
+  float rw[kMaxCluster][GT];  // cluster merge weights
+  float M[GT], L[GT];
+  int last;
+};
+
+// Everything after the position loop of a decode kernel: merge the W warps of
+// the CTA (their running (m, l) already in ms.m / ms.l, their accumulators in
+// acc with lane_elem<HD> layout), then the CTAs of a cluster, then -- when a
+// unit spans several clusters -- the parts of the unit through global scratch,
+// and write the normalised output (or the partial triple).  The ring is free
+// on entry and becomes the merge buffer.  Shared by the fp32 and Q8_0 kernels.
+template <int HD, int GT, int W, int T>
+__device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSmem<GT, W>& ms, float* ring,
+                                              const float (&acc)[GT][HD / 32], int warp, int lane, int split,
+                                              int unit, int z, int h0) {
+  float (&s_m)[W][GT] = ms.m;
+  float (&s_l)[W][GT] = ms.l;
+  float (&s_ww)[W][GT] = ms.ww;
+  float (&s_cm)[GT] = ms.cm;
+  float (&s_cl)[GT] = ms.cl;
+  float (&s_rw)[kMaxCluster][GT] = ms.rw;
+  float (&s_M)[GT] = ms.M;
+  float (&s_L)[GT] = ms.L;
+  int& s_last = ms.last;
+  (void)s_m;
+  (void)s_l;
+  // ---- CTA partial: merge the warps (the ring becomes the merge buffer) ----
+  float* wacc = ring;                          // [kWarps][GT][HD]
+  float* cta_o = ring + W * GT * HD;   // [GT][HD], unnormalised, relative to s_cm
+#pragma unroll
+  for (int g = 0; g < GT; ++g)
+#pragma unroll
+    for (int e = 0; e < HD / 32; ++e) wacc[(warp * GT + g) * HD + lane_elem<HD>(lane, e)] = acc[g][e];
+  __syncthreads();
+  if (threadIdx.x < GT) {
+    const int g = threadIdx.x;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < W; ++w) M = fmaxf(M, s_m[w][g]);
+    float L = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+      const float f = (M == -INFINITY) ? 0.f : fast_exp2(s_m[w][g] - M);
+      s_ww[w][g] = f;
+      L = fmaf(s_l[w][g], f, L);
+    }
+    s_cm[g] = M;
+    s_cl[g] = L;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < GT * HD; idx += T) {
+    const int g = idx / HD;
+    float O = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) O = fmaf(wacc[w * GT * HD + idx], s_ww[w][g], O);
+    cta_o[idx] = O;
+  }
+  __syncthreads();
+
+  float* const out_base = (a.partial ? a.part_o : a.out) + (long long)z * a.q_zstride + (long long)h0 * HD;
+  float* const ml_base = a.partial ? a.part_ml + (long long)z * a.ml_zstride + 2 * h0 : nullptr;
+
+  if (a.nsplit == 1) {  // this CTA covers the whole range
+    for (int idx = threadIdx.x; idx < GT * HD; idx += T) {
+      const float L = s_cl[idx / HD];
+      out_base[idx] = (a.partial && !(L > 0.f)) ? 0.f : cta_o[idx] / L;
+    }
+    if (ml_base && threadIdx.x < GT) {
+      ml_base[2 * threadIdx.x] = s_cm[threadIdx.x];
+      ml_base[2 * threadIdx.x + 1] = s_cl[threadIdx.x];
+    }
+    return;
+  }
+
+  int n_parts = a.nsplit;  // partials the global stage merges
+  int part = split;
+  int rank = 0, cs = 1;
+  if (a.cluster > 1) {
+    // ---- cluster stage: the CTAs of a cluster merge through distributed shared memory ----
+    cg::cluster_group cluster = cg::this_cluster();
+    cs = (int)cluster.num_blocks();
+    rank = (int)cluster.block_rank();
+    n_parts = a.nsplit / cs;
+    part = split / cs;
+    cluster.sync();  // every CTA partial of the cluster is in shared memory
+    if (threadIdx.x < GT) {
+      const int g = threadIdx.x;
+      float M = -INFINITY;
+      for (int r = 0; r < cs; ++r) M = fmaxf(M, *cluster.map_shared_rank(&s_cm[g], r));
+      float L = 0.f;
+      for (int r = 0; r < cs; ++r) {
+        const float m = *cluster.map_shared_rank(&s_cm[g], r);
+        const float f = (M == -INFINITY) ? 0.f : fast_exp2(m - M);
+        s_rw[r][g] = f;
+        L = fmaf(*cluster.map_shared_rank(&s_cl[g], r), f, L);
+      }
+      s_M[g] = M;
+      s_L[g] = L;
+    }
+    __syncthreads();
+    // this rank owns elements [rank*slice, (rank+1)*slice) of the group's output
+    const int slice = GT * HD / cs;
+    const bool last_stage = n_parts == 1;
+    const long long gslot = ((long long)unit * n_parts + part) * GT * HD;
+    for (int t = threadIdx.x; t < slice; t += T) {
+      const int idx = rank * slice + t;
+      const int g = idx / HD;
+      float O = 0.f;
+      for (int r = 0; r < cs; ++r) O = fmaf(*cluster.map_shared_rank(&cta_o[idx], r), s_rw[r][g], O);
+      if (last_stage) {
+        const float L = s_L[g];
+        out_base[idx] = (a.partial && !(L > 0.f)) ? 0.f : O / L;
+      } else {
+        a.ws_o[gslot + idx] = O;
+      }
+    }
+    if (threadIdx.x < GT) {
+      if (last_stage) {
+        if (ml_base && rank == 0) {
+          ml_base[2 * threadIdx.x] = s_M[threadIdx.x];
+          ml_base[2 * threadIdx.x + 1] = s_L[threadIdx.x];
+        }
+      } else if (rank == 0) {
+        a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2] = s_M[threadIdx.x];
+        a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2 + 1] = s_L[threadIdx.x];
+      }
+    }
+    if (last_stage) {
+      cluster.sync();  // no CTA leaves while another still reads its shared memory
+      return;
+    }
+    __threadfence();
+    cluster.sync();  // the cluster's partial is written and visible
+    if (rank == 0 && threadIdx.x == 0) {
+      const int last = atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts - 1);
+      for (int r = 0; r < cs; ++r) *cluster.map_shared_rank(&s_last, r) = last;
+    }
+    cluster.sync();
+  } else {
+    // ---- no cluster: every CTA is a part of the global stage ----
+    const long long gslot = ((long long)unit * n_parts + part) * GT * HD;
+    for (int idx = threadIdx.x; idx < GT * HD; idx += T) a.ws_o[gslot + idx] = cta_o[idx];
+    if (threadIdx.x < GT) {
+      a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2] = s_cm[threadIdx.x];
+      a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2 + 1] = s_cl[threadIdx.x];
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts - 1);
+    __syncthreads();
+  }
+  if (!s_last) return;
+  __threadfence();
+
+  // ---- global stage: the last part to finish merges all n_parts partials ----
+  // (with a cluster, each rank of the last cluster merges its slice).  Every
+  // thread fetches the (m, l) pairs of its q head and its float4 of each
+  // partial in one batch, so the stage costs a single L2 round trip.
+  const long long slot0 = (long long)unit * n_parts;
+  const int slice4 = GT * HD / 4 / cs;
+  const float2* ml2 = reinterpret_cast<const float2*>(a.ws_ml) + slot0 * GT;  // [n_parts][GT]
+  const float4* o4 = reinterpret_cast<const float4*>(a.ws_o + slot0 * GT * HD);
+  for (int t = threadIdx.x; t < slice4; t += T) {
+    const int idx4 = rank * slice4 + t;
+    const int g = (idx4 * 4) / HD;
+    float M = -INFINITY, L = 0.f;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp0 = 0; sp0 < n_parts; sp0 += kMergeBatch) {
+      float2 ml[kMergeBatch];
+      float4 v[kMergeBatch];
+#pragma unroll
+      for (int j = 0; j < kMergeBatch; ++j) {
+        const int sp = sp0 + j;
+        ml[j] = sp < n_parts ? __ldcg(ml2 + (long long)sp * GT + g) : make_float2(-INFINITY, 0.f);
+        v[j] = sp < n_parts ? __ldcg(o4 + (long long)sp * (GT * HD / 4) + idx4) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float Mb = M;
+#pragma unroll
+      for (int j = 0; j < kMergeBatch; ++j) Mb = fmaxf(Mb, ml[j].x);
+      if (Mb == -INFINITY) continue;
+      const float r = fast_exp2(M - Mb);  // rescale what was accumulated so far
+      L *= r;
+      O.x *= r;
+      O.y *= r;
+      O.z *= r;
+      O.w *= r;
+#pragma unroll
+      for (int j = 0; j < kMergeBatch; ++j) {
+        const float w = fast_exp2(ml[j].x - Mb);  // 0 for empty partials (m = -inf)
+        L = fmaf(ml[j].y, w, L);
+        O.x = fmaf(v[j].x, w, O.x);
+        O.y = fmaf(v[j].y, w, O.y);
+        O.z = fmaf(v[j].z, w, O.z);
+        O.w = fmaf(v[j].w, w, O.w);
+      }
+      M = Mb;
+    }
+    const float inv = (a.partial && !(L > 0.f)) ? 0.f : 1.f / L;
+    *reinterpret_cast<float4*>(out_base + idx4 * 4) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+    if (ml_base && (idx4 * 4) % HD == 0) {
+      ml_base[2 * g] = M;
+      ml_base[2 * g + 1] = L;
+    }
+  }
+  if (rank == 0 && threadIdx.x == 0) a.counters[unit] = 0u;  // ticket ready for the next launch
+}
+
 template <int HD, int GT>
 __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>::kCtasPerSm)
     decode_f32_kernel(const DecodeArgs a) {
   using C = DecodeCfg<HD, GT>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float* ring = reinterpret_cast<float*>(smem_raw);
-  __shared__ float s_m[C::kWarps][GT];   // per-warp running max
-  __shared__ float s_l[C::kWarps][GT];   // per-warp running sum
-  __shared__ float s_ww[C::kWarps][GT];  // warp merge weights
-  __shared__ float s_cm[GT], s_cl[GT];   // CTA partial (max, sum), read by the cluster
-  __shared__ float s_rw[kMaxCluster][GT];  // cluster merge weights
-  __shared__ float s_M[GT], s_L[GT];
-  __shared__ int s_last;
+  __shared__ DecodeMergeSmem<GT, C::kWarps> ms;
+  float (&s_m)[C::kWarps][GT] = ms.m;
+  float (&s_l)[C::kWarps][GT] = ms.l;
   __shared__ __align__(16) float s_p[C::kNarrow ? C::kWarps : 1][C::kR * GT + 8];  // weights + rescales
 
   const int lane = threadIdx.x & 31;
@@ -512,14 +726,6 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
   }
   cp_async_wait<0>();
   __syncthreads();
-
-  // ---- CTA partial: merge the warps (the ring becomes the merge buffer) ----
-  float* wacc = ring;                          // [kWarps][GT][HD]
-  float* cta_o = ring + C::kWarps * GT * HD;   // [GT][HD], unnormalised, relative to s_cm
-#pragma unroll
-  for (int g = 0; g < GT; ++g)
-#pragma unroll
-    for (int e = 0; e < C::kEPL; ++e) wacc[(warp * GT + g) * HD + lane_elem<HD>(lane, e)] = acc[g][e];
   // the lane holding head g's running (max, sum): g (narrow) or g << kSH (wide)
   if constexpr (C::kNarrow) {
     if (lane < GT) {
@@ -530,178 +736,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
     s_m[warp][lane >> C::kSH] = my_m;
     s_l[warp][lane >> C::kSH] = my_l;
   }
-  __syncthreads();
-  if (threadIdx.x < GT) {
-    const int g = threadIdx.x;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < C::kWarps; ++w) M = fmaxf(M, s_m[w][g]);
-    float L = 0.f;
-#pragma unroll
-    for (int w = 0; w < C::kWarps; ++w) {
-      const float f = (M == -INFINITY) ? 0.f : fast_exp2(s_m[w][g] - M);
-      s_ww[w][g] = f;
-      L = fmaf(s_l[w][g], f, L);
-    }
-    s_cm[g] = M;
-    s_cl[g] = L;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < GT * HD; idx += C::kThreads) {
-    const int g = idx / HD;
-    float O = 0.f;
-#pragma unroll
-    for (int w = 0; w < C::kWarps; ++w) O = fmaf(wacc[w * GT * HD + idx], s_ww[w][g], O);
-    cta_o[idx] = O;
-  }
-  __syncthreads();
-
-  float* const out_base = (a.partial ? a.part_o : a.out) + (long long)z * a.q_zstride + (long long)h0 * HD;
-  float* const ml_base = a.partial ? a.part_ml + (long long)z * a.ml_zstride + 2 * h0 : nullptr;
-
-  if (a.nsplit == 1) {  // this CTA covers the whole range
-    for (int idx = threadIdx.x; idx < GT * HD; idx += C::kThreads) {
-      const float L = s_cl[idx / HD];
-      out_base[idx] = (a.partial && !(L > 0.f)) ? 0.f : cta_o[idx] / L;
-    }
-    if (ml_base && threadIdx.x < GT) {
-      ml_base[2 * threadIdx.x] = s_cm[threadIdx.x];
-      ml_base[2 * threadIdx.x + 1] = s_cl[threadIdx.x];
-    }
-    return;
-  }
-
-  int n_parts = a.nsplit;  // partials the global stage merges
-  int part = split;
-  int rank = 0, cs = 1;
-  if (a.cluster > 1) {
-    // ---- cluster stage: the CTAs of a cluster merge through distributed shared memory ----
-    cg::cluster_group cluster = cg::this_cluster();
-    cs = (int)cluster.num_blocks();
-    rank = (int)cluster.block_rank();
-    n_parts = a.nsplit / cs;
-    part = split / cs;
-    cluster.sync();  // every CTA partial of the cluster is in shared memory
-    if (threadIdx.x < GT) {
-      const int g = threadIdx.x;
-      float M = -INFINITY;
-      for (int r = 0; r < cs; ++r) M = fmaxf(M, *cluster.map_shared_rank(&s_cm[g], r));
-      float L = 0.f;
-      for (int r = 0; r < cs; ++r) {
-        const float m = *cluster.map_shared_rank(&s_cm[g], r);
-        const float f = (M == -INFINITY) ? 0.f : fast_exp2(m - M);
-        s_rw[r][g] = f;
-        L = fmaf(*cluster.map_shared_rank(&s_cl[g], r), f, L);
-      }
-      s_M[g] = M;
-      s_L[g] = L;
-    }
-    __syncthreads();
-    // this rank owns elements [rank*slice, (rank+1)*slice) of the group's output
-    const int slice = GT * HD / cs;
-    const bool last_stage = n_parts == 1;
-    const long long gslot = ((long long)unit * n_parts + part) * GT * HD;
-    for (int t = threadIdx.x; t < slice; t += C::kThreads) {
-      const int idx = rank * slice + t;
-      const int g = idx / HD;
-      float O = 0.f;
-      for (int r = 0; r < cs; ++r) O = fmaf(*cluster.map_shared_rank(&cta_o[idx], r), s_rw[r][g], O);
-      if (last_stage) {
-        const float L = s_L[g];
-        out_base[idx] = (a.partial && !(L > 0.f)) ? 0.f : O / L;
-      } else {
-        a.ws_o[gslot + idx] = O;
-      }
-    }
-    if (threadIdx.x < GT) {
-      if (last_stage) {
-        if (ml_base && rank == 0) {
-          ml_base[2 * threadIdx.x] = s_M[threadIdx.x];
-          ml_base[2 * threadIdx.x + 1] = s_L[threadIdx.x];
-        }
-      } else if (rank == 0) {
-        a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2] = s_M[threadIdx.x];
-        a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2 + 1] = s_L[threadIdx.x];
-      }
-    }
-    if (last_stage) {
-      cluster.sync();  // no CTA leaves while another still reads its shared memory
-      return;
-    }
-    __threadfence();
-    cluster.sync();  // the cluster's partial is written and visible
-    if (rank == 0 && threadIdx.x == 0) {
-      const int last = atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts - 1);
-      for (int r = 0; r < cs; ++r) *cluster.map_shared_rank(&s_last, r) = last;
-    }
-    cluster.sync();
-  } else {
-    // ---- no cluster: every CTA is a part of the global stage ----
-    const long long gslot = ((long long)unit * n_parts + part) * GT * HD;
-    for (int idx = threadIdx.x; idx < GT * HD; idx += C::kThreads) a.ws_o[gslot + idx] = cta_o[idx];
-    if (threadIdx.x < GT) {
-      a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2] = s_cm[threadIdx.x];
-      a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2 + 1] = s_cl[threadIdx.x];
-    }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts - 1);
-    __syncthreads();
-  }
-  if (!s_last) return;
-  __threadfence();
-
-  // ---- global stage: the last part to finish merges all n_parts partials ----
-  // (with a cluster, each rank of the last cluster merges its slice).  Every
-  // thread fetches the (m, l) pairs of its q head and its float4 of each
-  // partial in one batch, so the stage costs a single L2 round trip.
-  const long long slot0 = (long long)unit * n_parts;
-  const int slice4 = GT * HD / 4 / cs;
-  const float2* ml2 = reinterpret_cast<const float2*>(a.ws_ml) + slot0 * GT;  // [n_parts][GT]
-  const float4* o4 = reinterpret_cast<const float4*>(a.ws_o + slot0 * GT * HD);
-  for (int t = threadIdx.x; t < slice4; t += C::kThreads) {
-    const int idx4 = rank * slice4 + t;
-    const int g = (idx4 * 4) / HD;
-    float M = -INFINITY, L = 0.f;
-    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp0 = 0; sp0 < n_parts; sp0 += kMergeBatch) {
-      float2 ml[kMergeBatch];
-      float4 v[kMergeBatch];
-#pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j) {
-        const int sp = sp0 + j;
-        ml[j] = sp < n_parts ? __ldcg(ml2 + (long long)sp * GT + g) : make_float2(-INFINITY, 0.f);
-        v[j] = sp < n_parts ? __ldcg(o4 + (long long)sp * (GT * HD / 4) + idx4) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      float Mb = M;
-#pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j) Mb = fmaxf(Mb, ml[j].x);
-      if (Mb == -INFINITY) continue;
-      const float r = fast_exp2(M - Mb);  // rescale what was accumulated so far
-      L *= r;
-      O.x *= r;
-      O.y *= r;
-      O.z *= r;
-      O.w *= r;
-#pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j) {
-        const float w = fast_exp2(ml[j].x - Mb);  // 0 for empty partials (m = -inf)
-        L = fmaf(ml[j].y, w, L);
-        O.x = fmaf(v[j].x, w, O.x);
-        O.y = fmaf(v[j].y, w, O.y);
-        O.z = fmaf(v[j].z, w, O.z);
-        O.w = fmaf(v[j].w, w, O.w);
-      }
-      M = Mb;
-    }
-    const float inv = (a.partial && !(L > 0.f)) ? 0.f : 1.f / L;
-    *reinterpret_cast<float4*>(out_base + idx4 * 4) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-    if (ml_base && (idx4 * 4) % HD == 0) {
-      ml_base[2 * g] = M;
-      ml_base[2 * g + 1] = L;
-    }
-  }
-  if (rank == 0 && threadIdx.x == 0) a.counters[unit] = 0u;  // ticket ready for the next launch
+  decode_finish<HD, GT, C::kWarps, C::kThreads>(a, ms, ring, acc, warp, lane, split, unit, z, h0);
 }
 
 // Token K/V rows -> head-major cache rows.  k, v: [n_tok][src_stride] with

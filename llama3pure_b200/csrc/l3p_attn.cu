@@ -14,6 +14,7 @@
 #include <string>
 
 #include "decode.cuh"
+#include "decode_q8.cuh"
 #include "prefill_tc.cuh"
 #include "llama3pure_attn.h"
 
@@ -27,8 +28,13 @@ struct l3p_attn_ctx {
   int kvh_count = 0, seq_count = 0;
   float scale = 1.f;
   int num_sms = 148;
-  float* kc = nullptr;  // [n_layers][kvh_count][seq_count][hd]
+  float* kc = nullptr;  // fp32 cache: [n_layers][kvh_count][seq_count][hd]
   float* vc = nullptr;
+  bool q8 = false;      // Q8_0 cache (kv_format L3P_KV_Q8_0) instead of kc/vc:
+  int8_t* k8 = nullptr;  //   int8 values, same layout as kc
+  int8_t* v8 = nullptr;
+  uint16_t* ksc = nullptr;  //   fp16 block scales [n_layers][kvh_count][seq_count][hd/32]
+  uint16_t* vsc = nullptr;
   long long layer_elems = 0, head_elems = 0;
   cudaStream_t stream = nullptr;
   bool own_stream = false;
@@ -133,8 +139,23 @@ struct KernelInfo {
   int ctas_per_sm = 1;
 };
 
-KernelInfo kernel_for(int hd, int gt) {
+KernelInfo kernel_for(int hd, int gt, bool q8 = false) {
   KernelInfo k;
+  if (q8) {
+#define L3P_CASE8(H, T)                                   \
+  if (hd == H && gt == T) {                               \
+    k.fn = decode_q8_kernel<H, T>;                        \
+    k.smem = DecodeQ8Cfg<H, T>::kSmemBytes;               \
+    k.rows = DecodeQ8Cfg<H, T>::kR;                       \
+    k.ctas_per_sm = DecodeQ8Cfg<H, T>::kCtasPerSm;        \
+    return k;                                             \
+  }
+    L3P_CASE8(64, 1) L3P_CASE8(64, 2) L3P_CASE8(64, 4) L3P_CASE8(64, 8)
+    L3P_CASE8(128, 1) L3P_CASE8(128, 2) L3P_CASE8(128, 4) L3P_CASE8(128, 8)
+    L3P_CASE8(256, 1) L3P_CASE8(256, 2) L3P_CASE8(256, 4) L3P_CASE8(256, 8)
+#undef L3P_CASE8
+    return k;
+  }
 #define L3P_CASE(H, T)                                        \
   if (hd == H && gt == T) {                                   \
     k.fn = decode_fn<H, T>();                                 \
@@ -170,6 +191,7 @@ struct Plan {
 // What a split-K plan may use: the GPU, the kernel geometry and the scratch.
 struct PlanLimits {
   int hd = 0, GT = 1, num_sms = 148;
+  double row_bytes = 0;  // K + V bytes of one cached position
   int max_clusters[5] = {0, 0, 0, 0, 0};
   long long ws_o_floats = 0, n_counters = 0;
   int force_nsplit = 0, force_cluster = 0;
@@ -194,7 +216,7 @@ Plan plan_splits(const PlanLimits* ctx, long long P, long long units, int rows_p
       return best;
     }
   }
-  const double row_bytes = 2.0 * ctx->hd * 4.0;
+  const double row_bytes = ctx->row_bytes > 0 ? ctx->row_bytes : 2.0 * ctx->hd * 4.0;
   const double part_bytes = (double)ctx->GT * ctx->hd * 4.0;
   const long long n_tiles = (P + rows_per_tile - 1) / rows_per_tile;
   const long long slots = (long long)ctx->num_sms * ctas_per_sm;
@@ -231,6 +253,8 @@ PlanLimits limits_of(const l3p_attn_ctx* ctx) {
   PlanLimits l;
   l.hd = ctx->hd;
   l.GT = ctx->GT;
+  // fp32: 4 bytes per value; Q8_0: 1 byte per value + a 2-byte scale per 32
+  l.row_bytes = ctx->q8 ? 2.0 * (ctx->hd + ctx->hd / 16) : 2.0 * ctx->hd * 4.0;
   l.num_sms = ctx->num_sms;
   for (int i = 0; i < 5; ++i) l.max_clusters[i] = ctx->max_clusters[i];
   l.ws_o_floats = ctx->ws_o_floats / kScratchSlots;
@@ -299,8 +323,9 @@ int read_err(l3p_attn_ctx* ctx) {
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
                   const float* q, float* out, float* part_o, float* part_ml, cudaStream_t s,
                   const float* k_new = nullptr, const float* v_new = nullptr, bool allow_overlap = false) {
-  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT);
+  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT, ctx->q8);
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
+  if (ctx->q8 && k_new) return fail(ctx, L3P_E_INVAL, "fused append needs an fp32 cache");
   // longest attended range over the slices (upper bound; the kernel clips per slice)
   const int pos_max = pos0 + (nz - 1) * pos_step;
   const long long lo = ctx->cfg.seq_begin;
@@ -315,6 +340,10 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   a.kc = ctx->kc;
   a.vc = ctx->vc;
   a.kc_w = ctx->kc;
+  a.k8 = ctx->k8;
+  a.v8 = ctx->v8;
+  a.ksc = ctx->ksc;
+  a.vsc = ctx->vsc;
   a.k_new = k_new;
   a.v_new = v_new;
   a.new_zstride = (long long)ctx->cfg.n_kv_heads * ctx->hd;
@@ -385,6 +414,27 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   return L3P_OK;
 }
 
+// Q8_0 rows: one warp per (token, KV head) row.  k8/ksc point at the first row
+// of the destination head block; grid.y heads of head_elems values each.
+int launch_append_q8(l3p_attn_ctx* ctx, int8_t* k8, int8_t* v8, uint16_t* ksc, uint16_t* vsc, dim3 grid,
+                     const float* k, const float* v, long long src_stride, int kv_head_begin, int row0,
+                     cudaStream_t s) {
+  switch (ctx->hd) {
+    case 64:
+      kv_append_q8_kernel<64><<<grid, 32, 0, s>>>(k8, v8, ksc, vsc, ctx->head_elems, k, v, src_stride, kv_head_begin, row0);
+      break;
+    case 128:
+      kv_append_q8_kernel<128><<<grid, 32, 0, s>>>(k8, v8, ksc, vsc, ctx->head_elems, k, v, src_stride, kv_head_begin, row0);
+      break;
+    default:
+      kv_append_q8_kernel<256><<<grid, 32, 0, s>>>(k8, v8, ksc, vsc, ctx->head_elems, k, v, src_stride, kv_head_begin, row0);
+      break;
+  }
+  ++ctx->launches;
+  L3P_CUDA(ctx, cudaGetLastError());
+  return L3P_OK;
+}
+
 int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v,
                   cudaStream_t s) {
   // clip the tokens to the owned position range
@@ -398,6 +448,14 @@ int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float
   for (int t0 = t_lo; t0 < t_hi; t0 += 65535) {
     const int nt = std::min(t_hi - t0, 65535);
     dim3 grid(nt, ctx->kvh_count);
+    if (ctx->q8) {
+      // quantise the rows into the Q8_0 cache (quantize_to_q8_0_cache, c:1535-1570)
+      if (int rc = launch_append_q8(ctx, ctx->k8 + off, ctx->v8 + off, ctx->ksc + off / 32, ctx->vsc + off / 32, grid,
+                                    ks + (long long)(t0 - t_lo) * src_stride, vs + (long long)(t0 - t_lo) * src_stride,
+                                    src_stride, ctx->cfg.kv_head_begin, t0 - own_lo, s))
+        return rc;
+      continue;
+    }
     kv_append_kernel<<<grid, ctx->hd / 4, 0, s>>>(ctx->kc + off, ctx->vc + off, ctx->head_elems, ctx->hd,
                                                    ks + (long long)(t0 - t_lo) * src_stride,
                                                    vs + (long long)(t0 - t_lo) * src_stride, src_stride,
@@ -431,7 +489,9 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
   const long long off = (long long)layer * ctx->layer_elems;
   const int cg = ctx->prefill_cg;
   (cg == 2 ? prefill_prep_kernel<2> : prefill_prep_kernel<1>)<<<dim3(n_ktiles, ctx->kvh_count), 256, 0, s>>>(
-      ctx->kc + off, ctx->vc + off, ctx->head_elems, n_keys, n_ktiles, ctx->pf_img);
+      ctx->q8 ? nullptr : ctx->kc + off, ctx->q8 ? nullptr : ctx->vc + off, ctx->head_elems, n_keys, n_ktiles,
+      ctx->pf_img, ctx->q8 ? ctx->k8 + off : nullptr, ctx->q8 ? ctx->v8 + off : nullptr,
+      ctx->q8 ? ctx->ksc + off / 32 : nullptr, ctx->q8 ? ctx->vsc + off / 32 : nullptr);
   ++ctx->launches;
   L3P_CUDA(ctx, cudaGetLastError());
   PrefillArgs a{};
@@ -451,6 +511,7 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
   a.is_gemma3 = ctx->cfg.is_gemma3;
   a.swa_window = ctx->cfg.swa_window;
   a.swa_pattern = ctx->cfg.swa_pattern;
+  a.q8 = ctx->q8 ? 1 : 0;
   a.err = ctx->err_dev;
   if (cg == 2) {
     cudaLaunchConfig_t lc{};
@@ -496,7 +557,7 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   if (!cfg) return L3P_E_INVAL;
   const l3p_attn_config& c = *cfg;
   if (c.n_layers <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.seq_len <= 0 ||
-      c.n_heads % c.n_kv_heads != 0 || c.kv_format != L3P_KV_F32)
+      c.n_heads % c.n_kv_heads != 0 || (c.kv_format != L3P_KV_F32 && c.kv_format != L3P_KV_Q8_0))
     return L3P_E_INVAL;
   if (c.head_dim != 64 && c.head_dim != 128 && c.head_dim != 256) return L3P_E_UNSUPPORTED;
   const int kvh_count = c.kv_head_count > 0 ? c.kv_head_count : c.n_kv_heads - c.kv_head_begin;
@@ -532,14 +593,28 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   };
   if (cudaSetDevice(c.device) != cudaSuccess) return bail(L3P_E_CUDA, "cudaSetDevice failed");
   cudaDeviceGetAttribute(&ctx->num_sms, cudaDevAttrMultiProcessorCount, c.device);
-  const size_t cache_bytes = (size_t)ctx->layer_elems * c.n_layers * sizeof(float);
-  if (cudaMalloc(&ctx->kc, cache_bytes) != cudaSuccess || cudaMalloc(&ctx->vc, cache_bytes) != cudaSuccess) {
-    cudaGetLastError();
-    return bail(L3P_E_NOMEM, "KV cache allocation failed");
+  ctx->q8 = c.kv_format == L3P_KV_Q8_0;
+  if (ctx->q8) {
+    const size_t vals = (size_t)ctx->layer_elems * c.n_layers, scales = vals / 32;
+    if (cudaMalloc(&ctx->k8, vals) != cudaSuccess || cudaMalloc(&ctx->v8, vals) != cudaSuccess ||
+        cudaMalloc(&ctx->ksc, scales * 2) != cudaSuccess || cudaMalloc(&ctx->vsc, scales * 2) != cudaSuccess) {
+      cudaGetLastError();
+      return bail(L3P_E_NOMEM, "KV cache allocation failed");
+    }
+    // zero the cache: positions never written read as 0 (scale 0) rather than garbage
+    if (cudaMemset(ctx->k8, 0, vals) != cudaSuccess || cudaMemset(ctx->v8, 0, vals) != cudaSuccess ||
+        cudaMemset(ctx->ksc, 0, scales * 2) != cudaSuccess || cudaMemset(ctx->vsc, 0, scales * 2) != cudaSuccess)
+      return bail(L3P_E_CUDA, "cache memset failed");
+  } else {
+    const size_t cache_bytes = (size_t)ctx->layer_elems * c.n_layers * sizeof(float);
+    if (cudaMalloc(&ctx->kc, cache_bytes) != cudaSuccess || cudaMalloc(&ctx->vc, cache_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return bail(L3P_E_NOMEM, "KV cache allocation failed");
+    }
+    // zero the cache: positions never written read as 0 rather than garbage
+    if (cudaMemset(ctx->kc, 0, cache_bytes) != cudaSuccess || cudaMemset(ctx->vc, 0, cache_bytes) != cudaSuccess)
+      return bail(L3P_E_CUDA, "cache memset failed");
   }
-  // zero the cache: positions never written read as 0 rather than garbage
-  if (cudaMemset(ctx->kc, 0, cache_bytes) != cudaSuccess || cudaMemset(ctx->vc, 0, cache_bytes) != cudaSuccess)
-    return bail(L3P_E_CUDA, "cache memset failed");
   ctx->ws_o_floats = kWsOFloats;
   ctx->ws_ml_floats = kWsOFloats / 64 * 2;  // GT*HD >= 64, two floats per (split, q head)
   ctx->n_counters = kCounters;
@@ -560,7 +635,7 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(L3P_E_CUDA, "stream creation failed");
   ctx->own_stream = true;
-  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT);
+  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT, ctx->q8);
   if (!ki.fn) return bail(L3P_E_UNSUPPORTED, "no decode kernel for this geometry");
   if (cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem) != cudaSuccess)
     return bail(L3P_E_CUDA, "cudaFuncSetAttribute failed");
@@ -614,6 +689,10 @@ L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   cudaFree(ctx->kc);
   cudaFree(ctx->vc);
+  cudaFree(ctx->k8);
+  cudaFree(ctx->v8);
+  cudaFree(ctx->ksc);
+  cudaFree(ctx->vsc);
   cudaFree(ctx->ws_o);
   cudaFree(ctx->ws_ml);
   cudaFree(ctx->counters);
@@ -660,7 +739,7 @@ L3P_API int l3p_attn_set_overlap(l3p_attn_ctx* ctx, int enable) {
 
 L3P_API int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* nsplit, int* cluster) {
   if (!ctx || n_slices <= 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
-  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT);
+  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT, ctx->q8);
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
   const long long hi = std::min<long long>((long long)pos + 1, (long long)ctx->cfg.seq_begin + ctx->seq_count);
   const long long P = std::max<long long>(hi - ctx->cfg.seq_begin, 0);
@@ -701,6 +780,12 @@ L3P_API int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
+  if (ctx->q8) {
+    // the new row must be quantised before it is attended to (c:3299-3312): two launches
+    if (int rc = launch_append(ctx, layer, pos, 1, k, v, pick_stream(ctx, stream))) return rc;
+    return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), nullptr,
+                         nullptr, true);
+  }
   return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), k, v, true);
 }
 
@@ -760,6 +845,7 @@ L3P_API int l3p_attn_prefill_dev(l3p_attn_ctx* ctx, int layer, int start_pos, in
 L3P_API int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v) {
   if (!ctx) return L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
+  if (ctx->q8) return fail(ctx, L3P_E_UNSUPPORTED, "the cache is Q8_0: no fp32 rows to point at");
   if (k) *k = ctx->kc + (long long)layer * ctx->layer_elems;
   if (v) *v = ctx->vc + (long long)layer * ctx->layer_elems;
   return L3P_OK;
@@ -838,9 +924,14 @@ L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q,
   // one host->device copy of all inputs; the kernel writes the output into
   // mapped pinned memory, so no device->host copy follows
   L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, ctx->hst, in * 4, cudaMemcpyHostToDevice, ctx->stream));
-  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr, ctx->stream,
-                             ctx->st_buf + qd, ctx->st_buf + qd + kvd))
+  if (ctx->q8) {
+    if (int rc = launch_append(ctx, layer, pos, 1, ctx->st_buf + qd, ctx->st_buf + qd + kvd, ctx->stream)) return rc;
+    if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr, ctx->stream))
+      return rc;
+  } else if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr,
+                                    ctx->stream, ctx->st_buf + qd, ctx->st_buf + qd + kvd)) {
     return rc;
+  }
   if (int rc = finish_host_call(ctx)) return rc;
   memcpy(out + row0, ctx->hst + in + row0, nrow * 4);
   return L3P_OK;
@@ -888,6 +979,25 @@ L3P_API int l3p_attn_load_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, 
   if (hi <= lo) return L3P_OK;
   DeviceScope dev(ctx->cfg.device);
   const size_t row = (size_t)ctx->hd;
+  if (ctx->q8) {
+    // stage each head's rows and quantise them on the device, as kv_append does
+    const size_t n = (size_t)(hi - lo) * row;
+    if (int rc = ensure_staging(ctx, 2 * n)) return rc;
+    for (int h = 0; h < ctx->kvh_count; ++h) {
+      const size_t src = ((size_t)(ctx->cfg.kv_head_begin + h) * n_pos + (lo - pos0)) * row;
+      L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, k + src, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+      L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf + n, v + src, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+      const long long off = (long long)layer * ctx->layer_elems + (long long)h * ctx->head_elems;
+      for (int t0 = 0; t0 < hi - lo; t0 += 65535) {
+        const int nt = std::min(hi - lo - t0, 65535);
+        if (int rc = launch_append_q8(ctx, ctx->k8 + off, ctx->v8 + off, ctx->ksc + off / 32, ctx->vsc + off / 32,
+                                      dim3(nt, 1), ctx->st_buf + (size_t)t0 * row, ctx->st_buf + n + (size_t)t0 * row,
+                                      (long long)row, 0, lo - ctx->cfg.seq_begin + t0, ctx->stream))
+          return rc;
+      }
+    }
+    return finish_host_call(ctx);
+  }
   for (int h = 0; h < ctx->kvh_count; ++h) {
     const size_t src = ((size_t)(ctx->cfg.kv_head_begin + h) * n_pos + (lo - pos0)) * row;
     const size_t dst = (size_t)layer * ctx->layer_elems + (size_t)h * ctx->head_elems +
@@ -907,6 +1017,25 @@ L3P_API int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, 
   if (hi <= lo) return L3P_OK;
   DeviceScope dev(ctx->cfg.device);
   const size_t row = (size_t)ctx->hd;
+  if (ctx->q8) {
+    // dequantised values d * int8 (exact in fp32)
+    const size_t n = (size_t)(hi - lo) * row;
+    if (int rc = ensure_staging(ctx, 2 * n)) return rc;
+    for (int h = 0; h < ctx->kvh_count; ++h) {
+      const size_t dst = ((size_t)(ctx->cfg.kv_head_begin + h) * n_pos + (lo - pos0)) * row;
+      const long long off = (long long)layer * ctx->layer_elems + (long long)h * ctx->head_elems +
+                            (long long)(lo - ctx->cfg.seq_begin) * row;
+      const int nb = (int)std::min<size_t>((n / 32 + 255) / 256, 4096);
+      q8_dequant_kernel<<<nb, 256, 0, ctx->stream>>>(ctx->k8 + off, ctx->ksc + off / 32, (long long)n / 32, ctx->st_buf);
+      q8_dequant_kernel<<<nb, 256, 0, ctx->stream>>>(ctx->v8 + off, ctx->vsc + off / 32, (long long)n / 32,
+                                                     ctx->st_buf + n);
+      ctx->launches += 2;
+      L3P_CUDA(ctx, cudaGetLastError());
+      L3P_CUDA(ctx, cudaMemcpyAsync(k + dst, ctx->st_buf, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+      L3P_CUDA(ctx, cudaMemcpyAsync(v + dst, ctx->st_buf + n, n * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    }
+    return finish_host_call(ctx);
+  }
   for (int h = 0; h < ctx->kvh_count; ++h) {
     const size_t dst = ((size_t)(ctx->cfg.kv_head_begin + h) * n_pos + (lo - pos0)) * row;
     const size_t src = (size_t)layer * ctx->layer_elems + (size_t)h * ctx->head_elems +
@@ -915,6 +1044,66 @@ L3P_API int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, 
     L3P_CUDA(ctx, cudaMemcpyAsync(v + dst, ctx->vc + src, (size_t)(hi - lo) * row * 4, cudaMemcpyDeviceToHost, ctx->stream));
   }
   return finish_host_call(ctx);
+}
+
+// The Q8_0 cache in the reference's own block format: per owned KV head and
+// owned position in [pos0, pos0+n_pos), head_dim/32 blocks of 34 bytes (fp16
+// scale, little-endian, then 32 int8) -- the bytes of the reference's
+// key_cache/value_cache rows (c:365-372).  blocks: [n_kv_heads][n_pos][head_dim/32*34].
+namespace {
+int q8_block_io(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, uint8_t* kb, uint8_t* vb, const uint8_t* kin,
+                const uint8_t* vin) {
+  if (!ctx || n_pos < 0 || (!kb && !kin)) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
+  if (!ctx->q8) return fail(ctx, L3P_E_INVAL, "the cache is not Q8_0");
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (pos0 < 0 || pos0 + n_pos > ctx->cfg.seq_len)
+    return fail(ctx, L3P_E_RANGE, "positions [%d, %d) outside [0, %d)", pos0, pos0 + n_pos, ctx->cfg.seq_len);
+  const int lo = std::max(pos0, ctx->cfg.seq_begin), hi = std::min(pos0 + n_pos, ctx->cfg.seq_begin + ctx->seq_count);
+  if (hi <= lo) return L3P_OK;
+  DeviceScope dev(ctx->cfg.device);
+  const size_t rowb = (size_t)ctx->hd / 32 * 34;
+  const long long nblk = (long long)(hi - lo) * (ctx->hd / 32);
+  const size_t bytes = (size_t)nblk * 34;
+  if (int rc = ensure_staging(ctx, (2 * bytes + 3) / 4)) return rc;
+  uint8_t* st_k = reinterpret_cast<uint8_t*>(ctx->st_buf);
+  uint8_t* st_v = st_k + bytes;
+  const int nb = (int)std::min<long long>((nblk + 255) / 256, 4096);
+  for (int h = 0; h < ctx->kvh_count; ++h) {
+    const size_t hoff = ((size_t)(ctx->cfg.kv_head_begin + h) * n_pos + (lo - pos0)) * rowb;
+    const long long off = (long long)layer * ctx->layer_elems + (long long)h * ctx->head_elems +
+                          (long long)(lo - ctx->cfg.seq_begin) * ctx->hd;
+    if (kin) {
+      L3P_CUDA(ctx, cudaMemcpyAsync(st_k, kin + hoff, bytes, cudaMemcpyHostToDevice, ctx->stream));
+      L3P_CUDA(ctx, cudaMemcpyAsync(st_v, vin + hoff, bytes, cudaMemcpyHostToDevice, ctx->stream));
+      q8_unblock_kernel<<<nb, 256, 0, ctx->stream>>>(st_k, nblk, ctx->k8 + off, ctx->ksc + off / 32);
+      q8_unblock_kernel<<<nb, 256, 0, ctx->stream>>>(st_v, nblk, ctx->v8 + off, ctx->vsc + off / 32);
+    } else {
+      q8_blocks_kernel<<<nb, 256, 0, ctx->stream>>>(ctx->k8 + off, ctx->ksc + off / 32, nblk, st_k);
+      q8_blocks_kernel<<<nb, 256, 0, ctx->stream>>>(ctx->v8 + off, ctx->vsc + off / 32, nblk, st_v);
+    }
+    ctx->launches += 2;
+    L3P_CUDA(ctx, cudaGetLastError());
+    if (!kin) {
+      L3P_CUDA(ctx, cudaMemcpyAsync(kb + hoff, st_k, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+      L3P_CUDA(ctx, cudaMemcpyAsync(vb + hoff, st_v, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    }
+    // the staging buffer is reused by the next head
+    L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
+  }
+  return finish_host_call(ctx);
+}
+}  // namespace
+
+L3P_API int l3p_attn_read_kv_q8(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, uint8_t* k_blocks,
+                                uint8_t* v_blocks) {
+  if (!k_blocks || !v_blocks) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  return q8_block_io(ctx, layer, pos0, n_pos, k_blocks, v_blocks, nullptr, nullptr);
+}
+
+L3P_API int l3p_attn_load_kv_q8(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, const uint8_t* k_blocks,
+                                const uint8_t* v_blocks) {
+  if (!k_blocks || !v_blocks) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  return q8_block_io(ctx, layer, pos0, n_pos, nullptr, nullptr, k_blocks, v_blocks);
 }
 
 // ==========================================================================

@@ -59,6 +59,7 @@
 //            cores accept for 32-bit elements), 32-dim atoms of eight 4-key
 //            groups, hi then lo.
 #pragma once
+#include "decode_q8.cuh"
 #include "ptx.cuh"
 #include "tc.cuh"
 
@@ -91,6 +92,7 @@ struct PrefillArgs {
   int q_pos0, n_tok, n_qtiles, n_ktiles;
   float scale;
   int layer, is_gemma3, swa_window, swa_pattern;
+  int q8;  // Q8_0 cache: q is quantised to Q8_0 per 32-value block and back (c:3569-3570)
   int* err;
 };
 
@@ -362,12 +364,34 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float4 t = qv[c * 8 + i];
-        const float x[4] = {t.x * a.scale, t.y * a.scale, t.z * a.scale, t.w * a.scale};
+        lo[4 * i] = t.x * a.scale;
+        lo[4 * i + 1] = t.y * a.scale;
+        lo[4 * i + 2] = t.z * a.scale;
+        lo[4 * i + 3] = t.w * a.scale;
+      }
+      if (a.q8) {
+        // dims 32c..32c+31 are one Q8_0 block: d = amax/127 as truncated fp16,
+        // q = round-half-away(x*127/amax); the attention sees q * d, exactly
+        // what the reference's int8 dot products compute with
+        // (quantize_to_q8_0_cache c:1535-1570, dot_q8_0_q8_0_cache c:1574-1597)
+        float amax = 0.f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          hi[4 * i + e] = tc::tf32_hi(x[e]);
-          lo[4 * i + e] = x[e] - hi[4 * i + e];
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(lo[i]));
+        const float d = amax / 127.0f;
+        const float inv = d > 0.0f ? 127.0f / amax : 0.0f;
+        const float dq = fp16_to_f32(fp32_to_fp16_trunc(d));
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          int qi = (int)roundf(lo[i] * inv);
+          qi = qi > 127 ? 127 : (qi < -128 ? -128 : qi);
+          lo[i] = (float)qi * dq;
         }
+      }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float x = lo[i];
+        hi[i] = tc::tf32_hi(x);
+        lo[i] = x - hi[i];
       }
       tc::st32(T_QHI + lb + c * 32, hi);
       // Q lo: K-major 128-byte-swizzled image, 16 KB per 32 dims
@@ -519,13 +543,16 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
 
 // K/V chunk images for prefill_tc_kernel<CG>: per (owned KV head, 128-key
 // tile), per CTA half r of the pair: K chunks 0..3 then V chunks 0..3, each
-// hi then lo, from the head-major cache.  K chunk c of half r holds keys
+// hi then lo, from the head-major cache (fp32 kc/vc, or the Q8_0 arrays
+// k8/ksc, v8/vsc when k8 is set).  K chunk c of half r holds keys
 // [r*128/CG, (r+1)*128/CG) of dims 32c..32c+31; V chunk v of half r holds
 // keys 32v..32v+31 of dims [r*128/CG, (r+1)*128/CG).  Keys at or beyond
 // n_keys read as 0.  grid (n_ktiles, kvh_count), 256 threads.
 template <int CG>
 __global__ void prefill_prep_kernel(const float* __restrict__ kc, const float* __restrict__ vc, long long head_stride,
-                                    int n_keys, int n_ktiles, float* __restrict__ img) {
+                                    int n_keys, int n_ktiles, float* __restrict__ img, const int8_t* __restrict__ k8,
+                                    const int8_t* __restrict__ v8, const uint16_t* __restrict__ ksc,
+                                    const uint16_t* __restrict__ vsc) {
   using C = PfCfg<CG>;
   const int j = blockIdx.x, hl = blockIdx.y;
   unsigned char* base = reinterpret_cast<unsigned char*>(img + ((long long)hl * n_ktiles + j) * kPfTileFloats);
@@ -535,8 +562,18 @@ __global__ void prefill_prep_kernel(const float* __restrict__ kc, const float* _
     const int pos = j * kPfBN + key;
     float4 kx = make_float4(0.f, 0.f, 0.f, 0.f), vx = kx;
     if (pos < n_keys) {
-      kx = *reinterpret_cast<const float4*>(kc + hl * head_stride + (long long)pos * kPfHD + 4 * c16);
-      vx = *reinterpret_cast<const float4*>(vc + hl * head_stride + (long long)pos * kPfHD + 4 * c16);
+      const long long e = hl * head_stride + (long long)pos * kPfHD + 4 * c16;
+      if (k8) {
+        // Q8_0 cache: the values the reference's dot products use, d * int8 (exact)
+        const char4 kq = *reinterpret_cast<const char4*>(k8 + e);
+        const char4 vq = *reinterpret_cast<const char4*>(v8 + e);
+        const float dk = fp16_to_f32(ksc[e / 32]), dv = fp16_to_f32(vsc[e / 32]);
+        kx = make_float4((float)kq.x * dk, (float)kq.y * dk, (float)kq.z * dk, (float)kq.w * dk);
+        vx = make_float4((float)vq.x * dv, (float)vq.y * dv, (float)vq.z * dv, (float)vq.w * dv);
+      } else {
+        kx = *reinterpret_cast<const float4*>(kc + e);
+        vx = *reinterpret_cast<const float4*>(vc + e);
+      }
     }
     const float4 khi = make_float4(tc::tf32_hi(kx.x), tc::tf32_hi(kx.y), tc::tf32_hi(kx.z), tc::tf32_hi(kx.w));
     const float4 klo = make_float4(kx.x - khi.x, kx.y - khi.y, kx.z - khi.z, kx.w - khi.w);

@@ -60,7 +60,7 @@ def _cfg(**kw):
         (dict(kv_head_begin=1, kv_head_count=2), -1),  # shard past the last KV head
         (dict(seq_begin=60, seq_count=8), -1),    # shard past the capacity
         (dict(n_layers=0), -1),
-        (dict(kv_format=1), -1),                  # Q8_0 cache not in this build
+        (dict(kv_format=2), -1),                  # no such cache format
     ],
 )
 def test_create_rejects_bad_config_without_device(lib, kw, code):
