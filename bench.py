@@ -346,6 +346,9 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline()
+    q8 = None
+    if rank == 0 and world == 1 and not args.no_q8:
+        q8 = run_q8(args, torch)
     prefill = None
     if rank == 0 and not args.no_prefill:
         prefill = run_prefill(args, torch)
@@ -377,6 +380,7 @@ def run_ours(args):
             "e2e": e2e,
             "cpu_baseline": cpu,
             "prefill": prefill,
+            "q8_decode": q8,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -488,6 +492,81 @@ def run_prefill(args, torch):
             "flops_per_layer": prefill_flops(sh), "kernel": "prefill_tc_kernel (tcgen05 3xTF32) + prefill_prep_kernel"}
 
 
+def run_q8(args, torch, layers: int = 16):
+    """Decode over the reference's own cache format (kv_format L3P_KV_Q8_0,
+    272 bytes per position and KV head instead of 1024) on the workload's
+    geometry: `layers` layers of random Q8_0 blocks (285 MB at 16 layers, more
+    than L2), the decode kernel alone timed over a CUDA graph of 2*layers
+    launches, and the engine's per-layer step (append + decode)."""
+    from llama3pure_b200.attn import AttnContext
+
+    sh = CONFIGS[WORKLOAD]
+    L = layers
+    ctx = AttnContext.for_shape(sh, n_layers=L, kv_format=1)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream)
+    rng = np.random.default_rng(77)
+    nb = sh.head_dim // 32
+    for layer in range(L):
+        blocks = []
+        for _ in range(2):
+            b = rng.integers(-127, 128, size=(sh.n_kv_heads, sh.seq_len, nb, 34), dtype=np.int16).astype(np.int8)
+            d = rng.uniform(0.005, 0.03, size=(sh.n_kv_heads, sh.seq_len, nb)).astype(np.float16)
+            b = b.view(np.uint8)
+            b[..., :2] = d.view(np.uint8).reshape(sh.n_kv_heads, sh.seq_len, nb, 2)
+            blocks.append(np.ascontiguousarray(b.reshape(sh.n_kv_heads, sh.seq_len, nb * 34)))
+        ctx.load_kv_q8(layer, 0, blocks[0], blocks[1])
+    g = torch.Generator(device="cuda")
+    g.manual_seed(78)
+    q = torch.randn((L, sh.n_heads, sh.head_dim), device="cuda", generator=g)
+    knew = torch.randn((L, sh.n_kv_heads, sh.head_dim), device="cuda", generator=g)
+    vnew = torch.randn((L, sh.n_kv_heads, sh.head_dim), device="cuda", generator=g)
+    out = torch.zeros_like(q)
+
+    def graph_of(fn):
+        gr = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream()
+        cs.wait_stream(stream)
+        with torch.cuda.stream(cs):
+            ctx.set_stream(cs)
+            with torch.cuda.graph(gr, stream=cs):
+                fn(cs)
+        stream.wait_stream(cs)
+        ctx.set_stream(stream)
+        return gr
+
+    def timed(gr, reps):
+        for _ in range(max(3, args.warmup)):
+            gr.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            gr.replay()
+        b.record(stream)
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    kgr = graph_of(lambda cs: [ctx.decode_dev(i % L, sh.pos, q[i % L], out[i % L], cs) for i in range(2 * L)])
+    kern_us = timed(kgr, 5) * 1e3 / (2 * L)
+    n0 = ctx.launch_count()
+    sgr = graph_of(lambda cs: [ctx.step_dev(i, sh.pos, q[i], knew[i], vnew[i], out[i], cs) for i in range(L)])
+    launches = ctx.launch_count() - n0
+    step_us = timed(sgr, max(args.steps, 5)) * 1e3 / L
+    ctx.check()
+    del kgr, sgr
+    ctx.close()
+    nbytes = 2 * (sh.pos + 1) * sh.n_kv_heads * (sh.head_dim + sh.head_dim // 16)
+    peak, peak_kind = measured_peaks()
+    return {"workload": WORKLOAD + " with a Q8_0 cache", "layers_cycled": L, "kernel": "decode_q8_kernel<128,4>",
+            "bytes_per_layer": nbytes, "kernel_us": round(kern_us, 3),
+            "kernel_gbs": round(nbytes / kern_us / 1e3, 1), "frac_of_hbm": round(nbytes / kern_us / 1e3 / peak, 4),
+            "peak_kind": peak_kind, "step_us_per_layer": round(step_us, 3),
+            "step_launches_per_layer": launches // L,
+            "tokens_per_s_32_layers": round(1e6 / (step_us * 32), 1)}
+
+
 def run_e2e(ctx, sh, world, args, torch):
     """l3p_attn_step per layer with pinned host buffers: H2D of q/k/v, append,
     decode, D2H of the output, every step."""
@@ -529,6 +608,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0-cache decode measurement")
+    ap.add_argument("--q8-only", action="store_true", help="Q8_0-cache decode measurement alone")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
     ap.add_argument("--layers", type=int, default=4)
     ap.add_argument("--prefill-only", action="store_true", help="prefill measurement alone (ncu case)")
@@ -541,6 +622,12 @@ def main():
         return run_reference_arm(args)
     if args.kernel_only:
         return run_kernel_only(args)
+    if args.q8_only:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps({"mode": "q8-only", **run_q8(args, torch)}), flush=True)
+        return 0
     if args.prefill_only:
         import torch
 

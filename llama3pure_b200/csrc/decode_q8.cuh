@@ -134,18 +134,28 @@ __global__ void q8_dequant_kernel(const int8_t* __restrict__ d8, const uint16_t*
   }
 }
 
+#ifndef L3P_Q8_WARPS
+#define L3P_Q8_WARPS 8  // warps per CTA
+#endif
+#ifndef L3P_Q8_ROWS
+#define L3P_Q8_ROWS 16  // rows per tile for head_dim <= 128 (half as many at 256)
+#endif
+#ifndef L3P_Q8_RING_KB
+#define L3P_Q8_RING_KB 192  // shared-memory ring per CTA
+#endif
+
 template <int HD, int GT>
 struct DecodeQ8Cfg {
   static_assert(HD == 64 || HD == 128 || HD == 256, "head_dim");
   static_assert(GT == 1 || GT == 2 || GT == 4 || GT == 8, "group");
-  static constexpr int kWarps = 8;
+  static constexpr int kWarps = L3P_Q8_WARPS;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kR = HD >= 256 ? 8 : 16;  // rows per tile (4 rows per pass, 8 lanes per row)
+  static constexpr int kR = HD >= 256 ? L3P_Q8_ROWS / 2 : L3P_Q8_ROWS;  // rows per tile (4 per pass, 8 lanes per row)
   static constexpr int kScB = HD / 16;           // scale bytes per row
   static constexpr int kTileKB = kR * HD;        // int8 bytes of a K (or V) tile
   static constexpr int kTileSB = kR * kScB;      // scale bytes of a K (or V) tile
   static constexpr int kStageBytes = 2 * (kTileKB + kTileSB);
-  static constexpr int kStagesRaw = (192 * 1024 / kWarps) / kStageBytes;
+  static constexpr int kStagesRaw = (L3P_Q8_RING_KB * 1024 / kWarps) / kStageBytes;
   static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > 8 ? 8 : kStagesRaw);
   static constexpr int kRingBytes = kWarps * kStages * kStageBytes;
   static constexpr int kSmemBytes = kRingBytes;
@@ -169,7 +179,8 @@ __device__ __forceinline__ void cp_async_small(void* smem_dst, const void* gmem_
 }
 
 template <int HD, int GT>
-__global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, 1) decode_q8_kernel(const DecodeArgs a) {
+__global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD, GT>::kCtasPerSm)
+    decode_q8_kernel(const DecodeArgs a) {
   using C = DecodeQ8Cfg<HD, GT>;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float* ring = reinterpret_cast<float*>(smem_raw);
@@ -226,36 +237,56 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, 1) decode_q8_ke
     }
   };
 
+  // q of the group, scaled (c:3264-3265 / c:3288-3289) and quantised to Q8_0
+  // (c:3310-3312) once per CTA by warp 0 into shared memory.  Warp 0 loads q
+  // before it issues any copy: behind the CTA's cache copies the small q loads
+  // would wait for HBM.  The q rows h0..h0+GT-1 are contiguous.
+  constexpr int kQV = GT * HD;                      // q values of the group
+  constexpr int kQN = kQV >= 512 ? 16 : kQV / 32;   // values per lane and pass
+  __shared__ __align__(16) uint32_t s_q8[kQV / 4];  // int8 q, packed
+  __shared__ float s_dq[kQV / 32];                  // block scales
   pdl_launch_dependents();
+  if (warp == 0) {
+    pdl_wait();
+    const float* qg = a.q + (long long)z * a.q_zstride + (long long)h0 * HD;
+#pragma unroll
+    for (int p = 0; p < kQV / (32 * kQN); ++p) {
+      const int base = p * 32 * kQN + lane * kQN;
+      float x[kQN];
+#pragma unroll
+      for (int i = 0; i < kQN; i += 2) {
+        const float2 t = *reinterpret_cast<const float2*>(qg + base + i);
+        x[i] = t.x * a.scale;
+        x[i + 1] = t.y * a.scale;
+      }
+      uint32_t w[(kQN + 3) / 4];
+      const uint16_t d = q8_quantize_lanes<kQN>(x, w);
+      if constexpr (kQN == 2) {
+        reinterpret_cast<uint16_t*>(s_q8)[base / 2] = (uint16_t)w[0];
+      } else {
+#pragma unroll
+        for (int i = 0; i < kQN / 4; ++i) s_q8[base / 4 + i] = w[i];
+      }
+      if (base % 32 == 0) s_dq[base / 32] = fp16_to_f32(d);
+    }
+  }
 #pragma unroll
   for (int i = 0; i < C::kStages - 1; ++i) {
     if (i < my_tiles) issue(i);
     cp_async_commit();
   }
   pdl_wait();
-
-  // q of the group, scaled (c:3264-3265 / c:3288-3289) and quantised to Q8_0
-  // (c:3310-3312) in the score layout: lane (rq, sg) holds values
-  // [sg*HD/8, (sg+1)*HD/8) of every q row and the scale of their block.
+  __syncthreads();  // s_q8 / s_dq written
+  // score layout: lane (rq, sg) holds values [sg*HD/8, (sg+1)*HD/8) of every
+  // q row and the scale of their block
   const int rq = lane >> 3, sg = lane & 7;
   uint32_t qw[GT][C::kKW];
   float dq[GT];
-  const float* qz = a.q + (long long)z * a.q_zstride;
 #pragma unroll
   for (int g = 0; g < GT; ++g) {
-    const float* qrow = qz + (long long)(h0 + g) * HD + sg * C::kKB;
-    float x[C::kKB];
 #pragma unroll
-    for (int i = 0; i < C::kKB; i += 4) {
-      const float4 t = *reinterpret_cast<const float4*>(qrow + i);
-      x[i] = t.x * a.scale;
-      x[i + 1] = t.y * a.scale;
-      x[i + 2] = t.z * a.scale;
-      x[i + 3] = t.w * a.scale;
-    }
-    // the 8 lanes of a row group hold the whole row; a block spans the aligned
-    // group of 32/kKB lanes (the reduction in q8_quantize_lanes)
-    dq[g] = fp16_to_f32(q8_quantize_lanes<C::kKB>(x, qw[g]));
+    for (int w = 0; w < C::kKW; ++w) qw[g][w] = s_q8[(g * HD + sg * C::kKB) / 4 + w];
+    dq[g] = s_dq[(g * HD + sg * C::kKB) / 32];
   }
 
   float my_m[GT], my_l[GT];

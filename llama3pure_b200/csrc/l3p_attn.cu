@@ -134,6 +134,7 @@ int decode_smem() {
 
 struct KernelInfo {
   DecodeFn fn = nullptr;
+  int threads = kDecodeThreads;
   int smem = 0;
   int rows = 8;
   int ctas_per_sm = 1;
@@ -145,6 +146,7 @@ KernelInfo kernel_for(int hd, int gt, bool q8 = false) {
 #define L3P_CASE8(H, T)                                   \
   if (hd == H && gt == T) {                               \
     k.fn = decode_q8_kernel<H, T>;                        \
+    k.threads = DecodeQ8Cfg<H, T>::kThreads;              \
     k.smem = DecodeQ8Cfg<H, T>::kSmemBytes;               \
     k.rows = DecodeQ8Cfg<H, T>::kR;                       \
     k.ctas_per_sm = DecodeQ8Cfg<H, T>::kCtasPerSm;        \
@@ -389,7 +391,7 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
     if (b.v_new) b.v_new = a.v_new + (long long)z0 * a.new_zstride;
     cudaLaunchConfig_t lc{};
     lc.gridDim = dim3(plan.nsplit, ctx->kvh_count * ctx->n_hg, zc);
-    lc.blockDim = dim3(kDecodeThreads, 1, 1);
+    lc.blockDim = dim3(ki.threads, 1, 1);
     lc.dynamicSmemBytes = ki.smem;
     lc.stream = s;
     cudaLaunchAttribute attr[2];
@@ -663,7 +665,7 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   for (int ci = 1; ci < 5; ++ci) {
     cudaLaunchConfig_t lc{};
     lc.gridDim = dim3(1 << ci, 1, 1);
-    lc.blockDim = dim3(kDecodeThreads, 1, 1);
+    lc.blockDim = dim3(ki.threads, 1, 1);
     lc.dynamicSmemBytes = ki.smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
