@@ -146,6 +146,7 @@ class CpuReference:
 
 
 def cpu_baseline(min_seconds: float = 10.0):
+    host_threads_for_reference()
     ref = CpuReference(layers=CONFIGS[WORKLOAD].n_layers)
     dts = []
     while sum(dts) < min_seconds or len(dts) < 3:
@@ -157,10 +158,19 @@ def cpu_baseline(min_seconds: float = 10.0):
     return out
 
 
+def host_threads_for_reference() -> None:
+    """torchrun sets OMP_NUM_THREADS=1 in every rank; the reference arm runs
+    on rank 0 alone and must use the host's cores (OpenMP reads the variable
+    when the reference library first loads, which happens after this)."""
+    if os.environ.get("OMP_NUM_THREADS") in (None, "1"):
+        os.environ["OMP_NUM_THREADS"] = str(os.cpu_count() or 1)
+
+
 def run_reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
+    host_threads_for_reference()
     ref = CpuReference(layers=CONFIGS[WORKLOAD].n_layers)
     for _ in range(args.warmup):
         ref.step()

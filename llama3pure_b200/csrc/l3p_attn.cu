@@ -179,10 +179,13 @@ KernelInfo kernel_for(int hd, int gt, bool q8 = false) {
 // estimate minimised is
 //   streaming: max(all bytes / ~5.3 TB/s, waves * share bytes / ~42 GB/s)
 //   + per-wave latency
-//   + cluster launch and merge (~2.5 us: cluster scheduling costs more than
-//     the merge through distributed shared memory saves at one cluster per unit)
+//   + cluster launch and merge (~5 us: cluster scheduling costs more than
+//     the merge through distributed shared memory saves, at one cluster per
+//     unit and at several)
 //   + global merge when a unit spans several clusters or has no cluster
-//     (fence, ticket and an L2 round trip, ~1.5 us, plus the partials' bytes)
+//     (fence, ticket and an L2 round trip, ~2.2 us, plus the partials' bytes
+//     read by the one merging CTA at ~60 GB/s: measured 2.8 us for 16 parts,
+//     4.5 us for 64, 6.6 us for 128 on one 8192-position KV head)
 // The bandwidth figures are what one launch sustains on B200 (a 64 MiB
 // stream reaches ~5.3 TB/s with 128 to 148 CTAs, i.e. up to ~42 GB/s per SM).
 struct Plan {
@@ -239,8 +242,8 @@ Plan plan_splits(const PlanLimits* ctx, long long P, long long units, int rows_p
         waves = (units * ns + slots - 1) / slots;
       const double share = (double)((n_tiles + ns - 1) / ns) * rows_per_tile * row_bytes;
       double cost = std::max(total_us, waves * share / 42e3) + waves * 1.0;
-      if (cs > 1) cost += 2.5;  // cluster launches measured ~2-3 us slower at 128 CTAs
-      if (global) cost += 1.5 + gparts * part_bytes / 400e3;
+      if (cs > 1) cost += 5.0;  // cluster launch and merge: measured ~5 us slower than plain plans at 64-128 CTAs
+      if (global) cost += 2.2 + gparts * part_bytes / 60e3;
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
         best.nsplit = ns;
