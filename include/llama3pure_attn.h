@@ -198,6 +198,60 @@ long long l3p_attn_launch_count(const l3p_attn_ctx* ctx);
  * benchmarks; no counterpart in the reference. */
 int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* nsplit, int* cluster);
 
+/* ---- The pre-attention step on the device -------------------------------
+ * The entry points above take q and k after RoPE.  These take them as the
+ * q/k projections produce them and perform the engines' steps between the
+ * projections and the cache write on the GPU, bit for bit (IEEE single
+ * precision, the reference's operation order, no fused multiply-adds):
+ *   Gemma3 QK-RMSNorm, rmsnorm_per_head (c:3150-3165) on every q and k head
+ *     with this layer's attn_q_norm / attn_k_norm weights, when the model is
+ *     Gemma3 and both weight arrays are given (c:3233-3236, c:3507-3512);
+ *   RoPE from per-layer cos/sin tables built exactly as malloc_run_state
+ *     builds them (c:381-421; Gemma3 SWA layers use the rope_theta_swa table,
+ *     c:456-468): NEOX pairs (i, i+head_dim/2) for Gemma3 (c:3254-3278),
+ *     consecutive pairs (2i, 2i+1) otherwise (c:3279-3296);
+ *   the K/V cache write (c:3299-3308, c:3562-3567).
+ * The attention scale is still applied by the attention itself (so the
+ * products are the reference's (x0*cos - x1*sin) * attn_scale). */
+typedef struct l3p_attn_rope_config {
+    float rope_theta;     /* Config.rope_theta (c:219); <= 0 => 1e6 for Gemma3, 5e5 otherwise (c:5127) */
+    float rope_theta_swa; /* Config.rope_theta_swa (c:227); <= 0 => 10000 (c:390) */
+    float rms_norm_eps;   /* Config.rms_norm_eps; <= 0 => 1e-5f (c:3198) */
+    const float* q_norm;  /* HOST [n_layers][head_dim] attn_q_norm weights (c:274), or NULL */
+    const float* k_norm;  /* HOST [n_layers][head_dim] attn_k_norm weights (c:275), or NULL */
+} l3p_attn_rope_config;
+
+/* Build the RoPE tables for positions [0, seq_len) on the host, as
+ * malloc_run_state does (c:381-421), copy them and the QK-norm weights to the
+ * device.  Call before any entry point below; calling it again replaces
+ * them.  Device memory: seq_len * head_dim * 4 bytes per table (two tables for
+ * Gemma3). */
+int l3p_attn_set_rope(l3p_attn_ctx* ctx, const l3p_attn_rope_config* rope);
+
+/* QK-norm and RoPE of n_tok tokens at positions [pos0, pos0+n_tok) of
+ * `layer` into q_out, k_out (same layouts as q: [n_tok][n_heads*head_dim],
+ * k: [n_tok][n_kv_heads*head_dim]; only the owned heads' rows are written).
+ * q_out is not multiplied by the attention scale.  No cache write. */
+int l3p_attn_rope_dev(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* q, const float* k,
+                      float* q_out, float* k_out, void* stream);
+
+/* l3p_attn_step / l3p_attn_step_dev with q, k straight from the projections
+ * (before QK-norm and RoPE); v is the V projection.  Two launches: the
+ * pre-attention kernel, then the decode (with overlap mode on, the decode
+ * streams the cached rows while the pre-attention kernel runs). */
+int l3p_attn_step_raw(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
+                      const float* v, float* out);
+int l3p_attn_step_raw_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
+                          const float* v, float* out, void* stream);
+
+/* l3p_attn_prefill / l3p_attn_prefill_dev with q, k straight from the
+ * projections: the pre-attention kernel writes the prompt's K/V rows into
+ * the cache itself, then the prefill attention runs. */
+int l3p_attn_prefill_raw(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,
+                         const float* k, const float* v, float* out);
+int l3p_attn_prefill_raw_dev(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,
+                             const float* k, const float* v, float* out, void* stream);
+
 /* Decode attention that allocates nothing.  No counterpart in the reference.
  *
  * For callers that own every byte of device memory themselves -- typically

@@ -53,6 +53,12 @@ EXPORTS = (
     "l3p_attn_launch_count",
     "l3p_attn_set_overlap",
     "l3p_attn_decode_plan",
+    "l3p_attn_set_rope",
+    "l3p_attn_rope_dev",
+    "l3p_attn_step_raw",
+    "l3p_attn_step_raw_dev",
+    "l3p_attn_prefill_raw",
+    "l3p_attn_prefill_raw_dev",
     "l3p_attn_decode_noalloc",
     "l3p_attn_noalloc_last_error",
 )
@@ -77,6 +83,18 @@ class AttnConfig(C.Structure):
         ("seq_begin", C.c_int),
         ("seq_count", C.c_int),
         ("kv_format", C.c_int),
+    ]
+
+
+class RopeConfig(C.Structure):
+    """Mirror of l3p_attn_rope_config."""
+
+    _fields_ = [
+        ("rope_theta", C.c_float),
+        ("rope_theta_swa", C.c_float),
+        ("rms_norm_eps", C.c_float),
+        ("q_norm", C.c_void_p),
+        ("k_norm", C.c_void_p),
     ]
 
 
@@ -127,6 +145,12 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_launch_count": (C.c_longlong, [vp]),
         "l3p_attn_set_overlap": (i, [vp, i]),
         "l3p_attn_decode_plan": (i, [vp, i, i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+        "l3p_attn_set_rope": (i, [vp, C.POINTER(RopeConfig)]),
+        "l3p_attn_rope_dev": (i, [vp, i, i, i, fp, fp, fp, fp, vp]),
+        "l3p_attn_step_raw": (i, [vp, i, i, fp, fp, fp, fp]),
+        "l3p_attn_step_raw_dev": (i, [vp, i, i, fp, fp, fp, fp, vp]),
+        "l3p_attn_prefill_raw": (i, [vp, i, i, i, fp, fp, fp, fp]),
+        "l3p_attn_prefill_raw_dev": (i, [vp, i, i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_decode_noalloc": (i, [C.POINTER(AttnConfig), i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_noalloc_last_error": (C.c_char_p, []),
     }
@@ -248,6 +272,15 @@ class AttnContext:
         self._ok(self.lib.l3p_attn_decode_plan(self.h, pos, n_slices, C.byref(ns), C.byref(cs)), "decode_plan")
         return ns.value, cs.value
 
+    def set_rope(self, rope_theta: float = 0.0, rope_theta_swa: float = 0.0, rms_norm_eps: float = 0.0,
+                 q_norm: np.ndarray | None = None, k_norm: np.ndarray | None = None) -> None:
+        """RoPE tables and QK-norm weights ([n_layers][head_dim] float32) for
+        the pre-attention entry points (l3p_attn_set_rope)."""
+        qn = None if q_norm is None else np.ascontiguousarray(q_norm, np.float32)
+        kn = None if k_norm is None else np.ascontiguousarray(k_norm, np.float32)
+        rc = RopeConfig(rope_theta, rope_theta_swa, rms_norm_eps, _host(qn), _host(kn))
+        self._ok(self.lib.l3p_attn_set_rope(self.h, C.byref(rc)), "set_rope")
+
     # -- host-pointer entry points ---------------------------------------------
     def load_kv(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
         self._ok(self.lib.l3p_attn_load_kv(self.h, layer, pos0, k.shape[1], _host(k), _host(v)), "load_kv")
@@ -299,6 +332,25 @@ class AttnContext:
                  "prefill")
         return out
 
+    def step_raw(self, layer: int, pos: int, q: np.ndarray, k_row: np.ndarray, v_row: np.ndarray,
+                 out: np.ndarray | None = None) -> np.ndarray:
+        """step() with q, k before QK-norm and RoPE."""
+        if out is None:
+            out = np.zeros((self.n_heads, self.head_dim), np.float32)
+        self._ok(self.lib.l3p_attn_step_raw(self.h, layer, pos, _host(q), _host(k_row), _host(v_row), _host(out)),
+                 "step_raw")
+        return out
+
+    def prefill_raw(self, layer: int, start_pos: int, q: np.ndarray, k: np.ndarray, v: np.ndarray,
+                    out: np.ndarray | None = None) -> np.ndarray:
+        """prefill() with q, k before QK-norm and RoPE."""
+        n = q.shape[0]
+        if out is None:
+            out = np.zeros((n, self.n_heads, self.head_dim), np.float32)
+        self._ok(self.lib.l3p_attn_prefill_raw(self.h, layer, start_pos, n, _host(q), _host(k), _host(v),
+                                               _host(out)), "prefill_raw")
+        return out
+
     # -- device-pointer entry points -------------------------------------------
     def kv_device_ptr(self, layer: int) -> tuple[int, int]:
         k, v = C.c_void_p(), C.c_void_p()
@@ -331,6 +383,18 @@ class AttnContext:
     def prefill_dev(self, layer, start_pos, n_tok, q, k, v, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_prefill_dev(self.h, layer, start_pos, n_tok, _dev(q), _dev(k), _dev(v), _dev(out),
                                                _stream(stream)), "prefill_dev")
+
+    def rope_dev(self, layer, pos0, n_tok, q, k, q_out, k_out, stream=None) -> None:
+        self._ok(self.lib.l3p_attn_rope_dev(self.h, layer, pos0, n_tok, _dev(q), _dev(k), _dev(q_out), _dev(k_out),
+                                            _stream(stream)), "rope_dev")
+
+    def step_raw_dev(self, layer, pos, q, k_row, v_row, out, stream=None) -> None:
+        self._ok(self.lib.l3p_attn_step_raw_dev(self.h, layer, pos, _dev(q), _dev(k_row), _dev(v_row), _dev(out),
+                                                _stream(stream)), "step_raw_dev")
+
+    def prefill_raw_dev(self, layer, start_pos, n_tok, q, k, v, out, stream=None) -> None:
+        self._ok(self.lib.l3p_attn_prefill_raw_dev(self.h, layer, start_pos, n_tok, _dev(q), _dev(k), _dev(v),
+                                                   _dev(out), _stream(stream)), "prefill_raw_dev")
 
 
 def decode_noalloc(cfg: AttnConfig, layer: int, pos: int, k_cache, v_cache, q, out, stream=None, lib=None) -> None:

@@ -105,6 +105,7 @@ struct DecodeArgs {
   int cluster;             // CTAs per thread-block cluster (1 = no cluster); divides nsplit
   int is_gemma3, swa_window, swa_pattern;
   int partial;
+  int new_pending;         // the cache row of pos is written by the kernel before this one on the stream
 };
 
 #ifndef L3P_DECODE_WARPS
@@ -473,6 +474,8 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
   const float* knew = fused ? a.k_new + (long long)z * a.new_zstride + (long long)kvh * HD : nullptr;
   const float* vnew = fused ? a.v_new + (long long)z * a.new_zstride + (long long)kvh * HD : nullptr;
   const int new_row = pos - lo;  // index of the new token's row in the range
+  // tiles holding the new row are copied only after the preceding kernel has finished
+  const bool wait_new = (fused || (a.new_pending && pos >= lo && pos < hi));
 
   // tiles of this warp: t = split + nsplit * (warp + kWarps * i)
   const int first = split + a.nsplit * warp;
@@ -513,7 +516,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
   for (int i = 0; i < C::kStages - 1; ++i) {
     if (i < my_tiles) {
       const int r0 = (first + i * step) * C::kR;
-      if (fused && !waited && new_row >= r0 && new_row < r0 + C::kR) {
+      if (wait_new && !waited && new_row >= r0 && new_row < r0 + C::kR) {
         pdl_wait();
         waited = true;
       }

@@ -270,9 +270,21 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
       if (base % 32 == 0) s_dq[base / 32] = fp16_to_f32(d);
     }
   }
+  // a tile holding the row of pos, when the kernel before this one writes it,
+  // is copied only after that kernel has finished
+  const bool wait_new = a.new_pending && pos >= lo && pos < hi;
+  const int new_row = pos - lo;
+  bool waited = warp == 0;
 #pragma unroll
   for (int i = 0; i < C::kStages - 1; ++i) {
-    if (i < my_tiles) issue(i);
+    if (i < my_tiles) {
+      const int r0 = (first + i * step) * C::kR;
+      if (wait_new && !waited && new_row >= r0 && new_row < r0 + C::kR) {
+        pdl_wait();
+        waited = true;
+      }
+      issue(i);
+    }
     cp_async_commit();
   }
   pdl_wait();

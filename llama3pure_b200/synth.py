@@ -104,6 +104,24 @@ def prefill_inputs(shape: AttnShape, layer: int, n_tok: int | None = None):
     return k, v, q
 
 
+def raw_qkv_inputs(shape: AttnShape, layer: int, n_tok: int):
+    """Projection outputs before QK-norm and RoPE, token-major: q
+    ``[n_tok][n_heads*hd]``, k, v ``[n_tok][n_kv*hd]``, and QK-norm weights
+    ``[n_layers][hd]`` for q and k drawn as 1 + 0.1*N(0, 1) (Gemma3 GGUF norm
+    weights already carry the +1, c:3148).  Generator: rng_for(seed + 1000,
+    layer); draw order k, v, q, q_norm, k_norm."""
+    g = rng_for(shape.seed + 1000, layer)
+    kvd, qd = shape.n_kv_heads * shape.head_dim, shape.n_heads * shape.head_dim
+    k = g.standard_normal((n_tok, kvd), dtype=np.float32)
+    v = g.standard_normal((n_tok, kvd), dtype=np.float32)
+    q = g.standard_normal((n_tok, qd), dtype=np.float32)
+    q_norm = (np.float32(1.0) + np.float32(0.1) * g.standard_normal((shape.n_layers, shape.head_dim),
+                                                                     dtype=np.float32)).astype(np.float32)
+    k_norm = (np.float32(1.0) + np.float32(0.1) * g.standard_normal((shape.n_layers, shape.head_dim),
+                                                                     dtype=np.float32)).astype(np.float32)
+    return q, k, v, q_norm, k_norm
+
+
 def sha256_arrays(*arrays: np.ndarray) -> str:
     h = hashlib.sha256()
     for a in arrays:
@@ -144,6 +162,7 @@ __all__ = [
     "rng_for",
     "decode_inputs",
     "prefill_inputs",
+    "raw_qkv_inputs",
     "sha256_arrays",
     "decode_kv_bytes",
     "prefill_flops",

@@ -376,3 +376,74 @@ int l3po_prefill(void* ctx, int layer, int start_pos, int n_tok, const float* q,
     if (skipped) *skipped = total;
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Pre-attention step: Gemma3 QK-RMSNorm and RoPE.                          */
+
+/* Per-head RMS norm in place: the sum of squares accumulated in index order,
+ * r = 1/sqrtf(mean + eps), x = w * (r * x)  (rmsnorm_per_head, c:3150-3165). */
+static void head_rmsnorm(float* x, const float* w, int hd, float inv_hd, float eps) {
+    float ss = 0.0f;
+    for (int j = 0; j < hd; ++j) ss += x[j] * x[j];
+    float r = 1.0f / sqrtf(ss * inv_hd + eps);
+    for (int j = 0; j < hd; ++j) x[j] = w[j] * (r * x[j]);
+}
+
+/* Rotate one head row by the (cos, sin) pairs of its position: NEOX pairs
+ * (i, i + hd/2) for Gemma3 (c:3254-3278), consecutive pairs (2i, 2i+1)
+ * otherwise (c:3279-3296).  No attention scale (applied by the attention). */
+static void head_rotate(float* x, const float* c, const float* s, int hd, int neox) {
+    int half = hd / 2;
+    for (int i = 0; i < half; ++i) {
+        int a = neox ? i : 2 * i;
+        int b = neox ? i + half : 2 * i + 1;
+        float v0 = x[a], v1 = x[b];
+        x[a] = v0 * c[i] - v1 * s[i];
+        x[b] = v0 * s[i] + v1 * c[i];
+    }
+}
+
+int l3po_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer, int pos0, int n_tok,
+              float* q, float* k) {
+    if (!cfg || !rope || !q || !k || n_tok < 0 || pos0 < 0 || layer < 0 || layer >= cfg->n_layers)
+        return -1;
+    int hd = cfg->head_dim, half = hd / 2, gemma = cfg->is_gemma3 != 0;
+    /* per-layer table choice (c:456-468) and the theta defaults (c:390, c:5127) */
+    int pat = cfg->swa_pattern;
+    int swa_layer = pat > 0 && layer % pat < pat - 1;
+    float theta;
+    if (gemma && swa_layer)
+        theta = rope->rope_theta_swa > 0.0f ? rope->rope_theta_swa : 10000.0f;
+    else
+        theta = rope->rope_theta > 0.0f ? rope->rope_theta : (gemma ? 1000000.0f : 500000.0f);
+    float eps = rope->rms_norm_eps > 0.0f ? rope->rms_norm_eps : 1e-5f;
+    float inv_hd = 1.0f / (float)hd;
+    int norm = gemma && rope->q_norm && rope->k_norm;
+    float* freq = (float*)malloc(sizeof(float) * 3 * (size_t)half);
+    if (!freq) return -4;
+    float* c = freq + half;
+    float* s = c + half;
+    /* inverse frequencies and angles as c:384-405 */
+    for (int i = 0; i < half; ++i) freq[i] = 1.0f / powf(theta, (float)(i * 2) / (float)hd);
+    size_t qd = (size_t)cfg->n_heads * hd, kvd = (size_t)cfg->n_kv_heads * hd;
+    for (int t = 0; t < n_tok; ++t) {
+        int pos = pos0 + t;
+        for (int i = 0; i < half; ++i) {
+            float ang = pos * freq[i];
+            c[i] = cosf(ang);
+            s[i] = sinf(ang);
+        }
+        for (int h = 0; h < cfg->n_heads; ++h) {
+            float* x = q + t * qd + (size_t)h * hd;
+            if (norm) head_rmsnorm(x, rope->q_norm + (size_t)layer * hd, hd, inv_hd, eps);
+            head_rotate(x, c, s, hd, gemma);
+        }
+        for (int h = 0; h < cfg->n_kv_heads; ++h) {
+            float* x = k + t * kvd + (size_t)h * hd;
+            if (norm) head_rmsnorm(x, rope->k_norm + (size_t)layer * hd, hd, inv_hd, eps);
+            head_rotate(x, c, s, hd, gemma);
+        }
+    }
+    free(freq);
+    return 0;
+}

@@ -52,6 +52,17 @@ typedef struct {
     int swa_pattern; /* 0 => no SWA layers */
 } l3p_oracle_cfg;
 
+/* Pre-attention step (the engines' code between the q/k projections and the
+ * cache write): Gemma3 QK-RMSNorm then RoPE, q left unscaled.  Fields as the
+ * library's l3p_attn_rope_config. */
+typedef struct {
+    float rope_theta;     /* <= 0 => 1e6 for Gemma3, 5e5 otherwise */
+    float rope_theta_swa; /* <= 0 => 10000 */
+    float rms_norm_eps;   /* <= 0 => 1e-5f */
+    const float* q_norm;  /* [n_layers][head_dim] or NULL */
+    const float* k_norm;  /* [n_layers][head_dim] or NULL */
+} l3p_oracle_rope;
+
 /* ---- restatement (oracle/l3p_oracle.c) ---- */
 void* l3po_create(const l3p_oracle_cfg* cfg, int mode);
 void l3po_destroy(void* ctx);
@@ -67,6 +78,10 @@ void l3po_q8_quantize(const float* src, uint8_t* dst, int count);
 float l3po_q8_dot(const uint8_t* a, const uint8_t* b, int count);
 void l3po_q8_accum(float* out, const uint8_t* v, float w, int count);
 void l3po_softmax(float* x, int n);
+/* In place on q [n_tok][n_heads*head_dim] and k [n_tok][n_kv_heads*head_dim]
+ * of tokens at positions pos0, pos0+1, ... of `layer`. */
+int l3po_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer, int pos0, int n_tok,
+              float* q, float* k);
 
 /* ---- reference harness (oracle/ref_harness.c -> oracle/_ref/) ---- */
 void* l3pref_create(const l3p_oracle_cfg* cfg, int mode);
@@ -82,6 +97,8 @@ void l3pref_q8_quantize(const float* src, uint8_t* dst, int count);
 float l3pref_q8_dot(const uint8_t* a, const uint8_t* b, int count);
 void l3pref_q8_accum(float* out, const uint8_t* v, float w, int count);
 void l3pref_softmax(float* x, int n);
+int l3pref_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer, int pos0, int n_tok,
+                float* q, float* k);
 int l3pref_threads(void);
 
 #ifdef __cplusplus

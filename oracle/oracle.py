@@ -25,6 +25,16 @@ MODE_Q8 = 1
 _LIBS: dict = {}
 
 
+class OracleRope(C.Structure):
+    _fields_ = [
+        ("rope_theta", C.c_float),
+        ("rope_theta_swa", C.c_float),
+        ("rms_norm_eps", C.c_float),
+        ("q_norm", C.POINTER(C.c_float)),
+        ("k_norm", C.POINTER(C.c_float)),
+    ]
+
+
 class OracleCfg(C.Structure):
     _fields_ = [
         ("n_layers", C.c_int),
@@ -80,6 +90,7 @@ def _load(impl: str, fast: bool):
         "q8_dot": (C.c_float, [C.c_void_p, C.c_void_p, C.c_int]),
         "q8_accum": (None, [fp, C.c_void_p, C.c_float, C.c_int]),
         "softmax": (None, [fp, C.c_int]),
+        "rope": (C.c_int, [C.POINTER(OracleCfg), C.POINTER(OracleRope), C.c_int, C.c_int, C.c_int, fp, fp]),
     }
     fns = {}
     for name, (res, args) in sig.items():
@@ -176,3 +187,25 @@ def primitives(impl: str = "port"):
 def threads(impl: str = "ref", fast: bool = True) -> int:
     fns = _load(impl, fast)[1]
     return int(fns["threads"]()) if "threads" in fns else 1
+
+
+def rope(shape, layer: int, pos0: int, q: np.ndarray, k: np.ndarray, rope_theta: float = 0.0,
+         rope_theta_swa: float = 0.0, rms_norm_eps: float = 0.0, q_norm=None, k_norm=None,
+         impl: str = "port", n_layers: int | None = None):
+    """The pre-attention step (QK-norm, RoPE; q unscaled) of tokens at pos0..
+
+    q: [n_tok][n_heads*head_dim], k: [n_tok][n_kv_heads*head_dim]; returns
+    rotated copies.  q_norm / k_norm: [n_layers][head_dim] or None."""
+    _, f = _load(impl, False)
+    q = np.array(q, np.float32, order="C", copy=True)
+    k = np.array(k, np.float32, order="C", copy=True)
+    nl = n_layers if n_layers is not None else max(layer + 1, getattr(shape, "n_layers", 1))
+    cfg = OracleCfg(nl, shape.n_heads, shape.n_kv_heads, shape.head_dim, max(pos0 + q.shape[0], 1), 0.0,
+                    shape.is_gemma3, shape.swa_window, shape.swa_pattern)
+    qn = None if q_norm is None else np.ascontiguousarray(q_norm, np.float32)
+    kn = None if k_norm is None else np.ascontiguousarray(k_norm, np.float32)
+    rc_ = OracleRope(rope_theta, rope_theta_swa, rms_norm_eps, _fptr(qn), _fptr(kn))
+    rc = f["rope"](C.byref(cfg), C.byref(rc_), layer, pos0, q.shape[0], _fptr(q), _fptr(k))
+    if rc:
+        raise RuntimeError(f"oracle rope rc={rc}")
+    return q, k

@@ -259,3 +259,73 @@ L3P_EXPORT int l3pref_threads(void) {
     return 1;
 #endif
 }
+
+/* Pre-attention step of c:3233-3296 (decode) / c:3507-3560 (prefill) for
+ * n_tok tokens: the reference's own rmsnorm_per_head (c:3150) and the cos/sin
+ * tables its malloc_run_state builds (c:381-421, per-layer choice c:456-468);
+ * the rotation loops are re-created without the attn_scale factor, which the
+ * attention applies afterwards. */
+L3P_EXPORT int l3pref_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer, int pos0,
+                           int n_tok, float* q, float* k) {
+    if (!cfg || !rope || !q || !k || n_tok < 0 || pos0 < 0 || layer < 0 || layer >= cfg->n_layers)
+        return -1;
+    Config p;
+    memset(&p, 0, sizeof(p));
+    p.n_layers = layer + 1;
+    p.n_heads = cfg->n_heads;
+    p.n_kv_heads = cfg->n_kv_heads;
+    p.head_dim = cfg->head_dim;
+    p.dim = cfg->n_heads * cfg->head_dim;
+    p.hidden_dim = 32;
+    p.vocab_size = 1;
+    p.seq_len = pos0 + n_tok > 1 ? pos0 + n_tok : 1;
+    p.is_gemma3 = cfg->is_gemma3;
+    p.swa_window = cfg->swa_window;
+    p.swa_pattern = cfg->swa_pattern;
+    p.rope_theta = rope->rope_theta > 0.0f ? rope->rope_theta : (cfg->is_gemma3 ? 1000000.0f : 500000.0f);
+    p.rope_theta_swa = rope->rope_theta_swa;
+    p.rms_norm_eps = rope->rms_norm_eps;
+    RunState s;
+    memset(&s, 0, sizeof(s));
+    malloc_run_state(&s, &p);
+    float eps = p.rms_norm_eps > 0 ? p.rms_norm_eps : 1e-5f; /* c:3198 */
+    int head_size = s.head_size, half = head_size / 2;
+    int q_dim = s.q_dim, kv_dim = s.kv_dim;
+    for (int b = 0; b < n_tok; ++b) {
+        int pos = pos0 + b;
+        float* q_arr = q + (size_t)b * q_dim;
+        float* k_arr = k + (size_t)b * kv_dim;
+        if (p.is_gemma3 && rope->q_norm && rope->k_norm) {
+            rmsnorm_per_head(q_arr, q_arr, (float*)rope->q_norm + layer * head_size, p.n_heads, head_size,
+                             s.inv_head_size, eps);
+            rmsnorm_per_head(k_arr, k_arr, (float*)rope->k_norm + layer * head_size, p.n_kv_heads, head_size,
+                             s.inv_head_size, eps);
+        }
+        float* rope_cos = s.rope_cos_layer[layer] + pos * half;
+        float* rope_sin = s.rope_sin_layer[layer] + pos * half;
+        if (p.is_gemma3) {
+            for (int h = 0; h < p.n_heads + p.n_kv_heads; h++) {
+                float* x = h < p.n_heads ? q_arr + h * head_size : k_arr + (h - p.n_heads) * head_size;
+                for (int i = 0; i < half; i++) {
+                    float v0 = x[i], v1 = x[i + half];
+                    x[i] = v0 * rope_cos[i] - v1 * rope_sin[i];
+                    x[i + half] = v0 * rope_sin[i] + v1 * rope_cos[i];
+                }
+            }
+        } else {
+            for (int i = 0; i < q_dim; i += 2) {
+                int j = (i % head_size) / 2;
+                float v0 = q_arr[i], v1 = q_arr[i + 1];
+                q_arr[i] = v0 * rope_cos[j] - v1 * rope_sin[j];
+                q_arr[i + 1] = v0 * rope_sin[j] + v1 * rope_cos[j];
+                if (i < kv_dim) {
+                    float k0 = k_arr[i], k1 = k_arr[i + 1];
+                    k_arr[i] = k0 * rope_cos[j] - k1 * rope_sin[j];
+                    k_arr[i + 1] = k0 * rope_sin[j] + k1 * rope_cos[j];
+                }
+            }
+        }
+    }
+    free_run_state(&s);
+    return 0;
+}

@@ -3,7 +3,8 @@
 Run in a container that has the reference source (it needs oracle/_ref/,
 built by `make -C oracle ref` from llama3pure-c-engine.c in place):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py          # both files
+    python tests/golden/make_golden.py rope     # rope_golden.npz only
 
 Each case records its geometry, the SHA-256 of its seeded inputs (so generator
 drift is caught) and the reference's attention output in both oracle modes:
@@ -30,6 +31,7 @@ from llama3pure_b200.synth import (  # noqa: E402
     AttnShape,
     decode_inputs,
     prefill_inputs,
+    raw_qkv_inputs,
     sha256_arrays,
 )
 
@@ -61,6 +63,45 @@ def prefill_cases():
                                           is_gemma3=1, swa_window=16, swa_pattern=6), 0),
         ("prefill_8b_2k_layer0", CONFIGS["llama31_8b_prefill_2k"], 0),
     ]
+
+
+def rope_cases():
+    """(name, shape, layer, pos0, n_tok, rope_theta, rope_theta_swa, rms_norm_eps, qk_norm)"""
+    c = CONFIGS
+    return [
+        ("l8b_pos8190", c["llama31_8b_decode_8k"], 0, 8190, 2, 0.0, 0.0, 0.0, False),
+        ("l1b_pos0_l3", c["llama32_1b_decode"], 3, 0, 5, 500000.0, 0.0, 0.0, False),
+        ("l8b_pos131071", c["llama31_8b_decode_128k"], 0, 131071, 1, 0.0, 0.0, 0.0, False),
+        ("gemma_swa_l0_norm", GEMMA_SWA, 0, 4094, 2, 1000000.0, 10000.0, 1e-6, True),
+        ("gemma_swa_l5_norm", GEMMA_SWA, 5, 4094, 2, 1000000.0, 10000.0, 1e-6, True),
+        ("gemma_l2_plain", c["gemma_2b_decode"], 2, 77, 3, 0.0, 0.0, 0.0, False),
+        ("gqa_hd64_theta1e4", AttnShape("gqa64", 2, 8, 2, 64, 512, pos=0, seed=21), 1, 100, 3,
+         10000.0, 0.0, 0.0, False),
+    ]
+
+
+def write_rope_golden():
+    """tests/golden/rope_golden.npz: the pre-attention step (QK-norm, RoPE) of
+    raw_qkv_inputs through the reference's own tables and rmsnorm_per_head."""
+    data = {}
+    names = []
+    for name, shape, layer, pos0, n_tok, th, th_swa, eps, norm in rope_cases():
+        q, k, v, qn, kn = raw_qkv_inputs(shape, layer, n_tok)
+        qr, kr = O.rope(shape, layer, pos0, q, k, th, th_swa, eps, qn if norm else None, kn if norm else None,
+                        impl="ref", n_layers=shape.n_layers)
+        data[f"{name}/q"] = qr
+        data[f"{name}/k"] = kr
+        data[f"{name}/sha256"] = np.array(sha256_arrays(q, k, v, qn, kn))
+        data[f"{name}/geom"] = np.array([shape.n_layers, shape.n_heads, shape.n_kv_heads, shape.head_dim,
+                                         shape.seq_len, shape.seed, layer, pos0, n_tok, shape.is_gemma3,
+                                         shape.swa_window, shape.swa_pattern, int(norm)], np.int64)
+        data[f"{name}/theta"] = np.array([th, th_swa, eps], np.float32)
+        names.append(name)
+        print("rope", name, "done", flush=True)
+    data["cases"] = np.array(names)
+    out_path = os.path.join(HERE, "rope_golden.npz")
+    np.savez_compressed(out_path, **data)
+    print("wrote", out_path, os.path.getsize(out_path), "bytes")
 
 
 def run_decode(shape: AttnShape, layer: int, append: bool, mode: int):
@@ -141,4 +182,10 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if not O.ref_available():
+        sys.exit("oracle/_ref/libl3p_ref.so missing: run `make -C oracle ref` where the reference source exists")
+    if sys.argv[1:] == ["rope"]:
+        write_rope_golden()
+    else:
+        main()
+        write_rope_golden()

@@ -162,3 +162,68 @@ def test_known_answer_dominant_score_selects_row():
     out, _ = o.decode(0, sh.pos, q)
     for kv in range(sh.n_kv_heads):
         np.testing.assert_allclose(out[kv * sh.kv_mul], v[kv, 7], rtol=1e-4, atol=1e-5)
+
+
+# ---- pre-attention step: QK-norm and RoPE -----------------------------------
+
+_ROPE_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "rope_golden.npz")
+
+
+def rope_case(g, name):
+    """(shape, layer, pos0, n_tok, theta, theta_swa, eps, norm) of a rope_golden.npz case."""
+    nl, hq, hkv, hd, cap, seed, layer, pos0, n_tok, gem, win, pat, norm = [int(x) for x in g[f"{name}/geom"]]
+    th, th_swa, eps = [float(x) for x in g[f"{name}/theta"]]
+    shape = AttnShape(name, nl, hq, hkv, hd, cap, pos=pos0, seed=seed, is_gemma3=gem, swa_window=win,
+                      swa_pattern=pat)
+    return shape, layer, pos0, n_tok, th, th_swa, eps, bool(norm)
+
+
+def _rope_names():
+    return [str(n) for n in np.load(_ROPE_GOLDEN)["cases"]]
+
+
+@pytest.mark.parametrize("name", _rope_names())
+def test_rope_matches_golden(name):
+    """The restatement reproduces the reference's tables, rmsnorm_per_head and
+    rotation loops bit for bit (golden from oracle/_ref)."""
+    from llama3pure_b200.synth import raw_qkv_inputs
+
+    g = np.load(_ROPE_GOLDEN)
+    shape, layer, pos0, n_tok, th, th_swa, eps, norm = rope_case(g, name)
+    q, k, v, qn, kn = raw_qkv_inputs(shape, layer, n_tok)
+    assert sha256_arrays(q, k, v, qn, kn) == str(g[f"{name}/sha256"]), "seeded generator drifted"
+    qr, kr = O.rope(shape, layer, pos0, q, k, th, th_swa, eps, qn if norm else None, kn if norm else None,
+                    impl="port", n_layers=shape.n_layers)
+    np.testing.assert_array_equal(qr.view(np.uint32), g[f"{name}/q"].view(np.uint32))
+    np.testing.assert_array_equal(kr.view(np.uint32), g[f"{name}/k"].view(np.uint32))
+    assert not np.array_equal(qr, q)  # something was rotated
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built (needs the reference source)")
+@pytest.mark.parametrize("gemma,norm,hd,layer", [(0, 0, 64, 0), (0, 0, 128, 3), (1, 1, 256, 0), (1, 1, 256, 5),
+                                                 (1, 0, 128, 4), (1, 1, 64, 11)])
+def test_rope_port_bit_identical_to_reference(gemma, norm, hd, layer):
+    rng = np.random.default_rng(hd * 7 + layer)
+    shape = AttnShape("r", 12, 8, 2, hd, 3000, is_gemma3=gemma, swa_window=128 if gemma else 0,
+                      swa_pattern=6 if gemma else 0)
+    n_tok, pos0 = 4, int(rng.integers(0, 2990))
+    q = (3 * rng.standard_normal((n_tok, 8 * hd))).astype(np.float32)
+    k = (3 * rng.standard_normal((n_tok, 2 * hd))).astype(np.float32)
+    qn = (1 + 0.2 * rng.standard_normal((12, hd))).astype(np.float32)
+    kn = (1 + 0.2 * rng.standard_normal((12, hd))).astype(np.float32)
+    args = (shape, layer, pos0, q, k, 0.0, 0.0, 1e-6, qn if norm else None, kn if norm else None)
+    a = O.rope(*args, impl="port", n_layers=12)
+    b = O.rope(*args, impl="ref", n_layers=12)
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x.view(np.uint32), y.view(np.uint32))
+
+
+def test_rope_position0_is_identity_without_norm():
+    """cos 0 = 1, sin 0 = 0: position 0 leaves q and k unchanged (c:402-404)."""
+    shape = AttnShape("p0", 1, 4, 2, 128, 8)
+    rng = np.random.default_rng(3)
+    q = rng.standard_normal((1, 4 * 128)).astype(np.float32)
+    k = rng.standard_normal((1, 2 * 128)).astype(np.float32)
+    qr, kr = O.rope(shape, 0, 0, q, k, impl="port")
+    np.testing.assert_array_equal(qr, q)
+    np.testing.assert_array_equal(kr, k)
