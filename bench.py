@@ -326,6 +326,41 @@ def run_ours(args):
     torch.cuda.synchronize()
     kern_ms = k0.elapsed_time(k1) / (3 * 2 * L)
     del kgraph
+
+    # the same step from the raw projections (l3p_attn_step_raw_dev: RoPE and
+    # the cache write on the device, then the decode), as a graph of L layers
+    raw = None
+    if not args.no_raw:
+        ctx.set_rope()
+        ctx.set_overlap(not args.no_overlap)
+        rgraph = torch.cuda.CUDAGraph()
+        rstream = torch.cuda.Stream()
+        rstream.wait_stream(stream)
+        n0 = ctx.launch_count()
+        with torch.cuda.stream(rstream):
+            ctx.set_stream(rstream)
+            with torch.cuda.graph(rgraph, stream=rstream):
+                for layer in range(L):
+                    ctx.step_raw_dev(layer, sh.pos, q[layer], knew[layer], vnew[layer], out[layer], rstream)
+        raw_launches = ctx.launch_count() - n0
+        stream.wait_stream(rstream)
+        ctx.set_stream(stream)
+        for _ in range(max(3, args.warmup)):
+            rgraph.replay()
+        torch.cuda.synchronize()
+        r0 = torch.cuda.Event(enable_timing=True)
+        r1 = torch.cuda.Event(enable_timing=True)
+        r0.record(stream)
+        for _ in range(args.steps):
+            rgraph.replay()
+        r1.record(stream)
+        torch.cuda.synchronize()
+        ctx.check()
+        raw_ms = r0.elapsed_time(r1) / args.steps
+        del rgraph
+        raw = {"api": "l3p_attn_step_raw_dev (QK-norm/RoPE + cache write + decode)",
+               "us_per_layer": round(raw_ms * 1e3 / L, 3), "launches_per_layer": raw_launches // L,
+               "post_rope_step_us_per_layer": round(ms / args.steps * 1e3 / L, 3)}
     if clocks:
         clk = clocks.stop()
     else:
@@ -389,6 +424,7 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": bytes_per_layer_rank, "traffic": args.traffic},
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "pre_attention_step": raw,
             "prefill": prefill,
             "q8_decode": q8,
             "clocks": clk,
@@ -497,9 +533,24 @@ def run_prefill(args, torch):
     ctx.check()
     ms = e0.elapsed_time(e1) / reps
     tflops = prefill_flops(sh) / (ms / 1e3) / 1e12
+    res = {"workload": "llama31_8b_prefill_2k", "ms_per_layer": round(ms, 4), "tflops": round(tflops, 2),
+           "flops_per_layer": prefill_flops(sh), "kernel": "prefill_tc_kernel (tcgen05 3xTF32) + prefill_prep_kernel"}
+    if not getattr(args, "no_raw", False):
+        # from the raw projections: RoPE + cache write in the pre-attention kernel
+        ctx.set_rope()
+        for i in range(args.warmup):
+            ctx.prefill_raw_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], stream)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(reps):
+            ctx.prefill_raw_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ctx.check()
+        res["raw_ms_per_layer"] = round(e0.elapsed_time(e1) / reps, 4)
+        res["raw_api"] = "l3p_attn_prefill_raw_dev (RoPE + cache write, then prep + attention)"
     ctx.close()
-    return {"workload": "llama31_8b_prefill_2k", "ms_per_layer": round(ms, 4), "tflops": round(tflops, 2),
-            "flops_per_layer": prefill_flops(sh), "kernel": "prefill_tc_kernel (tcgen05 3xTF32) + prefill_prep_kernel"}
+    return res
 
 
 def run_q8(args, torch, layers: int = 16):
@@ -566,6 +617,13 @@ def run_q8(args, torch, layers: int = 16):
     step_us = timed(sgr, max(args.steps, 5)) * 1e3 / L
     ctx.check()
     del kgr, sgr
+    raw_us = None
+    if not getattr(args, "no_raw", False):
+        ctx.set_rope()
+        rgr = graph_of(lambda cs: [ctx.step_raw_dev(i, sh.pos, q[i], knew[i], vnew[i], out[i], cs) for i in range(L)])
+        raw_us = round(timed(rgr, max(args.steps, 5)) * 1e3 / L, 3)
+        ctx.check()
+        del rgr
     ctx.close()
     nbytes = 2 * (sh.pos + 1) * sh.n_kv_heads * (sh.head_dim + sh.head_dim // 16)
     peak, peak_kind = measured_peaks()
@@ -573,7 +631,7 @@ def run_q8(args, torch, layers: int = 16):
             "bytes_per_layer": nbytes, "kernel_us": round(kern_us, 3),
             "kernel_gbs": round(nbytes / kern_us / 1e3, 1), "frac_of_hbm": round(nbytes / kern_us / 1e3 / peak, 4),
             "peak_kind": peak_kind, "step_us_per_layer": round(step_us, 3),
-            "step_launches_per_layer": launches // L,
+            "step_launches_per_layer": launches // L, "raw_step_us_per_layer": raw_us,
             "tokens_per_s_32_layers": round(1e6 / (step_us * 32), 1)}
 
 
@@ -619,6 +677,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0-cache decode measurement")
+    ap.add_argument("--no-raw", action="store_true", help="skip the raw-projection (RoPE on device) measurements")
     ap.add_argument("--q8-only", action="store_true", help="Q8_0-cache decode measurement alone")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
     ap.add_argument("--layers", type=int, default=4)

@@ -7,7 +7,9 @@
  * (c:3562-3612) and the four JS forward functions (llama3pure-js-engine.js:
  * 5099-5188, 5375-5457, 5624-5721, 5951-6041).  This library is the seam cut
  * at exactly those lines:
- *   upstream   post-RoPE q, k, v of one token (or a prompt batch) for layer l;
+ *   upstream   post-RoPE q, k, v of one token (or a prompt batch) for layer l
+ *              (or, through the *_raw entry points, q/k/v straight from the
+ *              projections: QK-norm, RoPE and the cache write then run here);
  *   downstream the attention output xb[n_heads*head_dim] fed to `wo`
  *              (c:3362, js:5191).
  *
@@ -225,7 +227,10 @@ typedef struct l3p_attn_rope_config {
  * malloc_run_state does (c:381-421), copy them and the QK-norm weights to the
  * device.  Call before any entry point below; calling it again replaces
  * them.  Device memory: seq_len * head_dim * 4 bytes per table (two tables for
- * Gemma3). */
+ * Gemma3), plus a buffer for the rotated q/k rows of one token.  The
+ * single-token entry points then allocate nothing (they may be captured in a
+ * CUDA graph); a prefill of more tokens than any before grows the buffer, so
+ * make one call of the largest size before capturing prefills. */
 int l3p_attn_set_rope(l3p_attn_ctx* ctx, const l3p_attn_rope_config* rope);
 
 /* QK-norm and RoPE of n_tok tokens at positions [pos0, pos0+n_tok) of

@@ -631,6 +631,11 @@ int launch_rope(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* 
 
 int ensure_rope_buf(l3p_attn_ctx* ctx, size_t floats, cudaStream_t s) {
   if (floats <= ctx->rope_buf_floats) return L3P_OK;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone)
+    return fail(ctx, L3P_E_INVAL,
+                "the rotated-row buffer must grow to %zu floats, which cannot happen during stream capture: "
+                "make one call of this size before capturing", floats);
   if (ctx->rope_buf) {
     L3P_CUDA(ctx, cudaStreamSynchronize(s));
     cudaFree(ctx->rope_buf);
@@ -937,7 +942,8 @@ L3P_API int l3p_attn_set_rope(l3p_attn_ctx* ctx, const l3p_attn_rope_config* rop
     L3P_CUDA(ctx, cudaMemcpy(ctx->qk_norm + n, rope->k_norm, n * sizeof(float), cudaMemcpyHostToDevice));
   }
   ctx->rms_eps = rope->rms_norm_eps > 0.f ? rope->rms_norm_eps : 1e-5f;
-  return L3P_OK;
+  // the single-token entry points never allocate (they may run inside a CUDA graph capture)
+  return ensure_rope_buf(ctx, (size_t)(ctx->cfg.n_heads + ctx->cfg.n_kv_heads) * hd, ctx->stream);
 }
 
 L3P_API int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* nsplit, int* cluster) {
