@@ -15,8 +15,10 @@ Printed on rank 0 as one JSON line:
              inputs resident in HBM, device time (CUDA events, max over ranks)
   e2e        the same metric through the host-pointer C ABI (l3p_attn_step
              per layer: pinned host q/k/v in, host output back, per step)
-  roofline   the decode kernel alone: algorithmic bytes per launch / average
-             launch time, against MEASURED_PEAKS.json's HBM copy bandwidth
+  roofline   the decode kernel: algorithmic bytes per launch / average launch
+             time over the timed region (every launch in it is this kernel),
+             against MEASURED_PEAKS.json's HBM copy bandwidth; the same kernel
+             timed in isolation (launches without overlap) beside it
   cpu_baseline  the reference's own CPU attention (oracle/_ref, compiled from
              llama3pure-c-engine.c with its OpenMP flags) on a bounded sample
 Multi-GPU (torchrun): each rank owns n_kv/N KV heads (head sharding, no
@@ -41,6 +43,10 @@ sys.path.insert(0, ROOT)
 from llama3pure_b200.synth import CONFIGS, decode_inputs  # noqa: E402
 
 WORKLOAD = "llama31_8b_decode_8k"
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode launch on this
+# workload (67.18 MB + 0.59 MB), from the ncu capture summarised in
+# profiles/decode_f32_kernel_llama31_8b_8k.md; --traffic overrides it
+NCU_TRAFFIC_PER_LAUNCH = 67.77e6
 METRIC = "decode-attn KV GB/s (fp32-equivalent), Llama-3.1-8B shapes, ctx 8K, 32 layers, append+decode per layer"
 
 
@@ -376,7 +382,9 @@ def run_ours(args):
     value = total_bytes / (ms / 1e3) / 1e9
     ms_step = ms / args.steps
     peak, peak_kind = measured_peaks()
-    achieved = bytes_per_layer_rank / (kern_ms / 1e3) / 1e9
+    # every launch of the timed region is the decode kernel (one per layer)
+    launch_ms = ms_step / launches_per_step
+    achieved = bytes_per_layer_rank / (launch_ms / 1e3) / 1e9
 
     # end to end through the host-pointer C ABI (rank 0 at N GPUs: every rank runs it)
     e2e = None
@@ -394,6 +402,9 @@ def run_ours(args):
     q8 = None
     if rank == 0 and world == 1 and not args.no_q8:
         q8 = run_q8(args, torch)
+    wo = None
+    if rank == 0 and world == 1 and not args.no_wo:
+        wo = run_wo(args, torch)
     prefill = None
     if rank == 0 and not args.no_prefill:
         prefill = run_prefill(args, torch)
@@ -419,12 +430,19 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "kernel": "decode_f32_kernel<128,4>", "kernel_us": round(kern_ms * 1e3, 3),
-                         "kernel_timing": "graph of 64 decode launches without overlap, CUDA events",
-                         "algorithmic_bytes_per_launch": bytes_per_layer_rank, "traffic": args.traffic},
+                         "kernel": "decode_f32_kernel<128,4>", "kernel_us": round(launch_ms * 1e3, 3),
+                         "kernel_timing": "timed region / its launches (one decode launch per layer, CUDA graph "
+                                          "with programmatic dependent launch, CUDA events)",
+                         "isolated_kernel_us": round(kern_ms * 1e3, 3),
+                         "isolated_frac": round(bytes_per_layer_rank / kern_ms / 1e6 / peak, 4),
+                         "isolated_timing": "graph of 64 decode launches without overlap, CUDA events",
+                         "algorithmic_bytes_per_launch": bytes_per_layer_rank,
+                         "traffic": args.traffic if args.traffic is not None else
+                         (NCU_TRAFFIC_PER_LAUNCH if world == 1 else None)},
             "e2e": e2e,
             "cpu_baseline": cpu,
             "pre_attention_step": raw,
+            "wo_projection": wo,
             "prefill": prefill,
             "q8_decode": q8,
             "clocks": clk,
@@ -635,6 +653,55 @@ def run_q8(args, torch, layers: int = 16):
             "tokens_per_s_32_layers": round(1e6 / (step_us * 32), 1)}
 
 
+def run_wo(args, torch, layers: int = 16):
+    """The wo projection (attention output -> dim) on the workload's geometry
+    (4096 x 4096) for each weight type: `layers` layers of random GGUF rows
+    cycled (more than L2 in total), the kernel alone timed over a CUDA graph of
+    2*layers launches without overlap."""
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.synth import wo_weights
+
+    sh = CONFIGS[WORKLOAD]
+    dim = cols = sh.n_heads * sh.head_dim
+    stream = torch.cuda.Stream()
+    peak, peak_kind = measured_peaks()
+    res = {"shape": f"{dim} x {cols}", "layers_cycled": layers, "peak_kind": peak_kind}
+    for name, wt, nbytes in (("q8_0", 8, cols // 32 * 34), ("q4_k", 12, cols // 256 * 144),
+                             ("q6_k", 14, cols // 256 * 210)):
+        ctx = AttnContext.for_shape(sh, n_layers=layers, seq_len=16)
+        ctx.set_stream(stream)
+        w = wo_weights(wt, dim, cols, seed=5)
+        for layer in range(layers):
+            ctx.set_wo(layer, wt, w)
+        x = torch.randn((layers, cols), device="cuda")
+        y = torch.zeros((layers, dim), device="cuda")
+        gr = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream()
+        cs.wait_stream(stream)
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(gr, stream=cs):
+                for i in range(2 * layers):
+                    ctx.wo_dev(i % layers, x[i % layers], y[i % layers], cs)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(cs)
+        reps = 5
+        for _ in range(reps):
+            gr.replay()
+        b.record(cs)
+        torch.cuda.synchronize()
+        ctx.check()
+        us = a.elapsed_time(b) * 1e3 / (reps * 2 * layers)
+        algo = dim * nbytes + cols * 4 + dim * 4  # GGUF weight bytes + x + y
+        res[name] = {"us": round(us, 3), "bytes": algo, "gbs": round(algo / us / 1e3, 1),
+                     "frac_of_hbm": round(algo / us / 1e3 / peak, 4)}
+        del gr
+        ctx.close()
+    return res
+
+
 def run_e2e(ctx, sh, world, args, torch):
     """l3p_attn_step per layer with pinned host buffers: H2D of q/k/v, append,
     decode, D2H of the output, every step."""
@@ -678,6 +745,8 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0-cache decode measurement")
     ap.add_argument("--no-raw", action="store_true", help="skip the raw-projection (RoPE on device) measurements")
+    ap.add_argument("--no-wo", action="store_true", help="skip the wo projection measurement")
+    ap.add_argument("--wo-only", action="store_true", help="wo projection measurement alone (ncu case)")
     ap.add_argument("--q8-only", action="store_true", help="Q8_0-cache decode measurement alone")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
     ap.add_argument("--layers", type=int, default=4)
@@ -696,6 +765,12 @@ def main():
 
         torch.cuda.set_device(0)
         print(json.dumps({"mode": "q8-only", **run_q8(args, torch)}), flush=True)
+        return 0
+    if args.wo_only:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps({"mode": "wo-only", **run_wo(args, torch)}), flush=True)
         return 0
     if args.prefill_only:
         import torch

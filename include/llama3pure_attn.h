@@ -257,6 +257,37 @@ int l3p_attn_prefill_raw(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok,
 int l3p_attn_prefill_raw_dev(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,
                              const float* k, const float* v, float* out, void* stream);
 
+/* ---- The wo projection: the attention output's consumer ----------------
+ * xb2 = Wo . xb (c:3362, js:5191) with the GGUF-quantised attn_output.weight,
+ * on the device.  The reference dequantises each weight row to fp32 and forms
+ * fp32 dot products (matmul_quantized -> matmul_deq_4row, c:2091-2176, for
+ * the types with a row dequantiser); the library multiplies the same values
+ * in a different summation order (within 1e-4 of the reference). */
+#define L3P_W_Q8_0 8  /* GGML_TYPE_Q8_0 (c:102): 34-byte blocks of 32 values */
+#define L3P_W_Q4_K 12 /* GGML_TYPE_Q4_K (c:106): 144-byte blocks of 256 values */
+#define L3P_W_Q6_K 14 /* GGML_TYPE_Q6_K (c:108): 210-byte blocks of 256 values */
+
+/* Hand layer `layer`'s attn_output.weight to the context: `dim` rows of
+ * n_heads*head_dim values in GGUF `type` blocks, as stored in the file
+ * (QuantizedTensor.data, c:2912).  The context copies the columns of the q
+ * heads it owns (tensor parallelism by head: with one context per GPU every
+ * GPU holds 1/N of the columns); they must fall on whole blocks, and at most
+ * 8192 owned columns (16384 for Q6_K). */
+int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* rows, int dim);
+
+/* xout[dim] = Wo[:, owned columns] . x[owned rows], x: [n_heads*head_dim] (the
+ * attention output; only the owned heads' rows are read).  With several
+ * contexts (GPUs) each xout is a partial sum; the engine adds them (an
+ * all-reduce, or a reduce-scatter when the next step is row-sharded). */
+int l3p_attn_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* xout);
+int l3p_attn_wo_dev(l3p_attn_ctx* ctx, int layer, const float* x, float* xout, void* stream);
+
+/* The engine's block from the q/k/v projections to wo's output in one host
+ * call (c:3233-3362: QK-norm, RoPE, cache write, attention, wo); needs
+ * l3p_attn_set_rope and l3p_attn_set_wo.  xout: [dim]. */
+int l3p_attn_step_raw_wo(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
+                         const float* v, float* xout);
+
 /* Decode attention that allocates nothing.  No counterpart in the reference.
  *
  * For callers that own every byte of device memory themselves -- typically

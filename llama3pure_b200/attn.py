@@ -59,6 +59,10 @@ EXPORTS = (
     "l3p_attn_step_raw_dev",
     "l3p_attn_prefill_raw",
     "l3p_attn_prefill_raw_dev",
+    "l3p_attn_set_wo",
+    "l3p_attn_wo",
+    "l3p_attn_wo_dev",
+    "l3p_attn_step_raw_wo",
     "l3p_attn_decode_noalloc",
     "l3p_attn_noalloc_last_error",
 )
@@ -151,6 +155,10 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_step_raw_dev": (i, [vp, i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_prefill_raw": (i, [vp, i, i, i, fp, fp, fp, fp]),
         "l3p_attn_prefill_raw_dev": (i, [vp, i, i, i, fp, fp, fp, fp, vp]),
+        "l3p_attn_set_wo": (i, [vp, i, i, vp, i]),
+        "l3p_attn_wo": (i, [vp, i, fp, fp]),
+        "l3p_attn_wo_dev": (i, [vp, i, fp, fp, vp]),
+        "l3p_attn_step_raw_wo": (i, [vp, i, i, fp, fp, fp, fp]),
         "l3p_attn_decode_noalloc": (i, [C.POINTER(AttnConfig), i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_noalloc_last_error": (C.c_char_p, []),
     }
@@ -212,6 +220,7 @@ class AttnContext:
         self.kv_head_begin = kv_head_begin
         self.kv_head_count = kv_head_count or (n_kv_heads - kv_head_begin)
         self.kv_mul = n_heads // n_kv_heads
+        self.wo_dim = 0  # rows of the wo weights once set_wo has run
         h = C.c_void_p()
         rc = self.lib.l3p_attn_create(C.byref(self.cfg), C.byref(h))
         if rc != L3P_OK:
@@ -280,6 +289,13 @@ class AttnContext:
         kn = None if k_norm is None else np.ascontiguousarray(k_norm, np.float32)
         rc = RopeConfig(rope_theta, rope_theta_swa, rms_norm_eps, _host(qn), _host(kn))
         self._ok(self.lib.l3p_attn_set_rope(self.h, C.byref(rc)), "set_rope")
+
+    def set_wo(self, layer: int, wtype: int, rows: np.ndarray) -> None:
+        """attn_output.weight of `layer`: uint8 GGUF rows [dim][row bytes]."""
+        if rows.dtype != np.uint8 or not rows.flags.c_contiguous:
+            raise TypeError("weight rows must be C-contiguous uint8")
+        self._ok(self.lib.l3p_attn_set_wo(self.h, layer, wtype, rows.ctypes.data, rows.shape[0]), "set_wo")
+        self.wo_dim = rows.shape[0]
 
     # -- host-pointer entry points ---------------------------------------------
     def load_kv(self, layer: int, pos0: int, k: np.ndarray, v: np.ndarray) -> None:
@@ -351,6 +367,17 @@ class AttnContext:
                                                _host(out)), "prefill_raw")
         return out
 
+    def wo(self, layer: int, x: np.ndarray) -> np.ndarray:
+        out = np.zeros(max(self.wo_dim, 1), np.float32)
+        self._ok(self.lib.l3p_attn_wo(self.h, layer, _host(x), _host(out)), "wo")
+        return out
+
+    def step_raw_wo(self, layer: int, pos: int, q: np.ndarray, k_row: np.ndarray, v_row: np.ndarray) -> np.ndarray:
+        out = np.zeros(max(self.wo_dim, 1), np.float32)
+        self._ok(self.lib.l3p_attn_step_raw_wo(self.h, layer, pos, _host(q), _host(k_row), _host(v_row), _host(out)),
+                 "step_raw_wo")
+        return out
+
     # -- device-pointer entry points -------------------------------------------
     def kv_device_ptr(self, layer: int) -> tuple[int, int]:
         k, v = C.c_void_p(), C.c_void_p()
@@ -383,6 +410,9 @@ class AttnContext:
     def prefill_dev(self, layer, start_pos, n_tok, q, k, v, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_prefill_dev(self.h, layer, start_pos, n_tok, _dev(q), _dev(k), _dev(v), _dev(out),
                                                _stream(stream)), "prefill_dev")
+
+    def wo_dev(self, layer, x, xout, stream=None) -> None:
+        self._ok(self.lib.l3p_attn_wo_dev(self.h, layer, _dev(x), _dev(xout), _stream(stream)), "wo_dev")
 
     def rope_dev(self, layer, pos0, n_tok, q, k, q_out, k_out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_rope_dev(self.h, layer, pos0, n_tok, _dev(q), _dev(k), _dev(q_out), _dev(k_out),

@@ -1,0 +1,246 @@
+// wo.cuh -- the attention output's consumer on the device (sm_100a): the
+// `wo` projection xout = Wo . xb with GGUF-quantised weights (c:3362,
+// js:5191), tensor-parallel by head.
+//
+// The reference dequantises four weight rows at a time to fp32 and forms
+// fp32 dot products with xb (matmul_quantized -> matmul_deq_4row,
+// c:2091-2176) for the types that have a row dequantiser; those are the types
+// here:
+//   Q8_0  (34-byte blocks of 32)   value = d * q8                 (c:691-702)
+//   Q4_K  (144-byte blocks of 256) value = d*sc_j * q4 - dmin*m_j (c:704-746)
+//   Q6_K  (210-byte blocks of 256) value = d * sc_k * (q6 - 32)   (c:873-902)
+// The products are the same; the summation order is not (per lane, then
+// across lanes and warps; scale factors applied per sub-block), which moves
+// results by a few ulps of the row sum, inside the 1e-4 contract.
+//
+// A context owns the q heads of its KV heads, so it holds the columns
+// [q_head0*hd, (q_head0+n_qh)*hd) of every row: its xout is the partial sum
+// over its heads, and one context per GPU gives the by-head tensor-parallel
+// split (the partials add up across GPUs).
+//
+// Device layout per layer (row-major, every row 16-byte aligned):
+//   Q8_0  int8 values [dim][C] and fp16 scales [dim][C/32]
+//   Q4_K  the GGUF blocks as they are, [dim][C/256][144]
+//   Q6_K  blocks padded to 224 bytes: ql 128 | qh 64 | scales 16 | d 2 | 14 spare
+//
+// GEMV decomposition.  A weight row is cut into column slices of 1024
+// values (Q8_0, Q4_K) or 2048 (Q6_K); lane l of a warp always covers the same
+// 32 or 64 columns of its slice, so it loads its x values ONCE into registers
+// and reuses them for every row.  The 8 warps of a CTA form wc column groups
+// (one slice each) x 8/wc row groups; a CTA takes a contiguous block of rows,
+// each warp streams its slice of its rows with kUnroll rows of loads in
+// flight, and the per-row partials of the column groups are added in shared
+// memory.  Weights do not depend on the kernel before this one, so with
+// programmatic dependent launch the first rows are requested before
+// griddepcontrol.wait and only x waits for the attention.
+#pragma once
+#include "decode_q8.cuh"
+
+namespace l3p {
+
+constexpr int kWoWarps = 8;
+constexpr int kWoUnroll = 4;  // rows of weight loads in flight per warp
+
+struct WoArgs {
+  const uint8_t* w;      // this layer's weight rows (format above), owned columns only
+  const uint16_t* wsc;   // Q8_0 scales [rows][C/32]
+  long long row_bytes;   // bytes of one weight row in `w`
+  int rows, C;           // output rows (dim), owned columns
+  int rows_per_cta;
+  int wc;                // column groups per CTA (power of two <= 8)
+  const float* x;        // owned columns of the attention output (x[0] = column q_head0*hd)
+  float* y;              // [rows]
+};
+
+// Per-format lane work: columns, loads and the dot product of one row.
+struct WoQ8 {
+  static constexpr int kSlice = 1024;  // columns per warp slice
+  static constexpr int kLaneCols = 32;
+  struct Raw {
+    uint4 a, b;
+    uint16_t d;
+  };
+  // lane's columns inside its slice: one Q8_0 block [32*lane, 32*lane+32)
+  __device__ static int col(int lane, int i) { return 32 * lane + i; }
+  __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
+    const int lane = threadIdx.x & 31;
+    const uint8_t* s = p.w + (long long)row * p.row_bytes + c0 + 32 * lane;
+    r.a = __ldg(reinterpret_cast<const uint4*>(s));
+    r.b = __ldg(reinterpret_cast<const uint4*>(s + 16));
+    r.d = __ldg(p.wsc + (long long)row * (p.C / 32) + c0 / 32 + lane);
+  }
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&)[2]) {
+    const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) s = fmaf((float)(int8_t)(w[i / 4] >> (8 * (i % 4))), x[i], s);
+    return fp16_to_f32(r.d) * s;
+  }
+  __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
+};
+
+struct WoQ4K {
+  static constexpr int kSlice = 1024;  // 4 blocks of 256
+  static constexpr int kLaneCols = 32;
+  struct Raw {
+    uint4 h;  // d, dmin, 12 scale bytes
+    uint4 q;  // 16 quant bytes: 16 low nibbles (sub-block 2p) and 16 high (sub-block 2p+1)
+  };
+  // lane = 8*block + c; quant bytes [16c, 16c+16) of the block hold values
+  // o+i of sub-blocks 2p (low nibble) and 2p+1 (high), p = c/2, o = 16*(c%2)
+  __device__ static int col(int lane, int i) {
+    const int b = lane >> 3, c = lane & 7, p = c >> 1, o = 16 * (c & 1);
+    return 256 * b + 64 * p + o + (i < 16 ? i : 32 + (i - 16));
+  }
+  __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
+    const int lane = threadIdx.x & 31;
+    const uint8_t* blk = p.w + (long long)row * p.row_bytes + (long long)(c0 / 256 + (lane >> 3)) * 144;
+    r.h = __ldg(reinterpret_cast<const uint4*>(blk));
+    r.q = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * (lane & 7)));
+  }
+  // byte k (0..11) of the packed scales, held in the words s0 s1 s2 (selects, no local memory)
+  __device__ static int sbyte(uint32_t s0, uint32_t s1, uint32_t s2, int k) {
+    const uint32_t w = k < 4 ? s0 : (k < 8 ? s1 : s2);
+    return (int)((w >> (8 * (k & 3))) & 0xffu);
+  }
+  // 6-bit scale and min of sub-block j from the 12 packed bytes (c:705-713)
+  __device__ static void scale_min(uint32_t s0, uint32_t s1, uint32_t s2, int j, int& sc, int& m) {
+    if (j < 4) {
+      sc = sbyte(s0, s1, s2, j) & 63;
+      m = sbyte(s0, s1, s2, j + 4) & 63;
+    } else {
+      sc = (sbyte(s0, s1, s2, j + 4) & 15) | ((sbyte(s0, s1, s2, j - 4) >> 6) << 4);
+      m = (sbyte(s0, s1, s2, j + 4) >> 4) | ((sbyte(s0, s1, s2, j) >> 6) << 4);
+    }
+  }
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&xs)[2]) {
+    const int lane = threadIdx.x & 31, p = (lane & 7) >> 1;
+    const float d = fp16_to_f32((uint16_t)(r.h.x & 0xffffu)), dmin = fp16_to_f32((uint16_t)(r.h.x >> 16));
+    int sc0, m0, sc1, m1;
+    scale_min(r.h.y, r.h.z, r.h.w, 2 * p, sc0, m0);
+    scale_min(r.h.y, r.h.z, r.h.w, 2 * p + 1, sc1, m1);
+    const uint32_t q[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
+    float lo = 0.f, hi = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t byte = (q[i / 4] >> (8 * (i % 4))) & 0xffu;
+      lo = fmaf((float)(byte & 15u), x[i], lo);
+      hi = fmaf((float)(byte >> 4), x[16 + i], hi);
+    }
+    return d * ((float)sc0 * lo + (float)sc1 * hi) - dmin * ((float)m0 * xs[0] + (float)m1 * xs[1]);
+  }
+  __device__ static void xsums(const float (&x)[kLaneCols], float (&xs)[2]) {
+    xs[0] = xs[1] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      xs[0] += x[i];
+      xs[1] += x[16 + i];
+    }
+  }
+};
+
+struct WoQ6K {
+  static constexpr int kSlice = 2048;  // 8 blocks of 256
+  static constexpr int kLaneCols = 64;
+  static constexpr int kBlockBytes = 224;
+  struct Raw {
+    uint4 l0, l1, h;  // ql[64h+16j..], ql[64h+32+16j..], qh[32h+16j..]
+    uint2 sc;         // scales [8h, 8h+8)
+    uint16_t d;
+  };
+  // lane = 4*block + 2*half + j: values l = 16j+i (i < 16) of the half at
+  // columns 128*half + l + {0, 32, 64, 96}
+  __device__ static int col(int lane, int i) {
+    const int b = lane >> 2, h = (lane >> 1) & 1, j = lane & 1;
+    return 256 * b + 128 * h + 16 * j + 32 * (i / 16) + (i % 16);
+  }
+  __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
+    const int lane = threadIdx.x & 31, h = (lane >> 1) & 1, j = lane & 1;
+    const uint8_t* blk = p.w + (long long)row * p.row_bytes + (long long)(c0 / 256 + (lane >> 2)) * kBlockBytes;
+    r.l0 = __ldg(reinterpret_cast<const uint4*>(blk + 64 * h + 16 * j));
+    r.l1 = __ldg(reinterpret_cast<const uint4*>(blk + 64 * h + 32 + 16 * j));
+    r.h = __ldg(reinterpret_cast<const uint4*>(blk + 128 + 32 * h + 16 * j));
+    r.sc = __ldg(reinterpret_cast<const uint2*>(blk + 192 + 8 * h));
+    r.d = __ldg(reinterpret_cast<const uint16_t*>(blk + 208));
+  }
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&)[2]) {
+    const int j = threadIdx.x & 1;
+    const uint32_t a[4] = {r.l0.x, r.l0.y, r.l0.z, r.l0.w};
+    const uint32_t b[4] = {r.l1.x, r.l1.y, r.l1.z, r.l1.w};
+    const uint32_t c[4] = {r.h.x, r.h.y, r.h.z, r.h.w};
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint32_t qa = (a[i / 4] >> (8 * (i % 4))) & 0xffu, qb = (b[i / 4] >> (8 * (i % 4))) & 0xffu;
+      const uint32_t qh = (c[i / 4] >> (8 * (i % 4))) & 0xffu;
+      s0 = fmaf((float)((int)((qa & 15u) | ((qh & 3u) << 4)) - 32), x[i], s0);
+      s1 = fmaf((float)((int)((qb & 15u) | (((qh >> 2) & 3u) << 4)) - 32), x[16 + i], s1);
+      s2 = fmaf((float)((int)((qa >> 4) | (((qh >> 4) & 3u) << 4)) - 32), x[32 + i], s2);
+      s3 = fmaf((float)((int)((qb >> 4) | (((qh >> 6) & 3u) << 4)) - 32), x[48 + i], s3);
+    }
+    const uint32_t sw[2] = {r.sc.x, r.sc.y};
+    auto sc = [&](int k) { return (float)(int8_t)(sw[k / 4] >> (8 * (k % 4))); };
+    return fp16_to_f32(r.d) * (sc(j) * s0 + sc(j + 2) * s1 + sc(j + 4) * s2 + sc(j + 6) * s3);
+  }
+  __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
+};
+
+// grid: ceil(rows / rows_per_cta) CTAs of kWoWarps warps; dynamic shared
+// memory: kWoWarps * rows_per_cta floats.
+template <class F>
+__global__ void __launch_bounds__(kWoWarps * 32) wo_gemv_kernel(const WoArgs p) {
+  extern __shared__ float red[];  // [wc][rows_per_cta]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int wcol = warp % p.wc, wrow = warp / p.wc, wr = kWoWarps / p.wc;
+  const int r_begin = blockIdx.x * p.rows_per_cta;
+  const int r_end = min(p.rows, r_begin + p.rows_per_cta);
+  const int c0 = wcol * F::kSlice;                         // this warp's slice
+  const bool active = c0 + F::col(lane, 0) < p.C;          // lanes past the owned columns idle
+  const int n_my = r_end - r_begin > wrow ? (r_end - r_begin - wrow + wr - 1) / wr : 0;
+
+  // weights first: they do not depend on the kernel before this one
+  pdl_launch_dependents();
+  typename F::Raw raw[kWoUnroll];
+#pragma unroll
+  for (int u = 0; u < kWoUnroll; ++u)
+    if (active && u < n_my) F::load(p, r_begin + wrow + wr * u, c0, raw[u]);
+  pdl_wait();
+  float x[F::kLaneCols];
+  float xs[2];
+  // the lane's columns come in runs of 16 consecutive values
+#pragma unroll
+  for (int i = 0; i < F::kLaneCols; i += 4) {
+    const float4 t = active ? __ldg(reinterpret_cast<const float4*>(p.x + c0 + F::col(lane, i)))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    x[i] = t.x;
+    x[i + 1] = t.y;
+    x[i + 2] = t.z;
+    x[i + 3] = t.w;
+  }
+  F::xsums(x, xs);
+
+  for (int t0 = 0; t0 < n_my; t0 += kWoUnroll) {
+    float acc[kWoUnroll];
+#pragma unroll
+    for (int u = 0; u < kWoUnroll; ++u) acc[u] = (active && t0 + u < n_my) ? F::dot(raw[u], x, xs) : 0.f;
+    // next rows' loads before the reductions
+#pragma unroll
+    for (int u = 0; u < kWoUnroll; ++u)
+      if (active && t0 + kWoUnroll + u < n_my) F::load(p, r_begin + wrow + wr * (t0 + kWoUnroll + u), c0, raw[u]);
+#pragma unroll
+    for (int u = 0; u < kWoUnroll; ++u) {
+      float v = acc[u];
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0 && t0 + u < n_my) red[wcol * p.rows_per_cta + wrow + wr * (t0 + u)] = v;
+    }
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < r_end - r_begin; r += blockDim.x) {
+    float s = 0.f;
+    for (int c = 0; c < p.wc; ++c) s += red[c * p.rows_per_cta + r];
+    p.y[r_begin + r] = s;
+  }
+}
+
+}  // namespace l3p

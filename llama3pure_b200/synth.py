@@ -122,6 +122,41 @@ def raw_qkv_inputs(shape: AttnShape, layer: int, n_tok: int):
     return q, k, v, q_norm, k_norm
 
 
+W_BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210)}  # GGUF type -> (values, bytes) per block
+
+
+def wo_weights(wtype: int, rows: int, cols: int, seed: int, scale: float = 0.02) -> np.ndarray:
+    """Random GGUF weight rows (uint8 [rows][cols/values*bytes]) of a Q8_0,
+    Q4_K or Q6_K tensor whose values are ~N(0, scale): every quant byte drawn
+    uniformly, every fp16 scale set so that the block spans about +-3 scale.
+    Generator: rng_for(seed + 2000, wtype)."""
+    n, nb = W_BLOCK[wtype]
+    g = rng_for(seed + 2000, wtype)
+    blocks = g.integers(0, 256, size=(rows, cols // n, nb), dtype=np.uint8)
+
+    def f16(a):
+        return np.ascontiguousarray(np.asarray(a, np.float16)).view(np.uint8).reshape(a.shape + (2,))
+
+    shp = (rows, cols // n)
+    if wtype == 8:
+        blocks[..., 0:2] = f16(g.uniform(2.0, 4.0, shp) * scale / 127.0)
+    elif wtype == 12:
+        # value = d*sc*q - dmin*m, q in 0..15, sc and m 6-bit
+        blocks[..., 0:2] = f16(g.uniform(0.5, 1.5, shp) * scale / 63.0 * 0.75)
+        blocks[..., 2:4] = f16(g.uniform(0.5, 1.5, shp) * scale / 63.0 * 0.75 * 7.5)
+    else:
+        # value = d*sc*(q-32), q 6-bit, sc int8
+        blocks[..., 208:210] = f16(g.uniform(0.5, 1.5, shp) * scale * 3.0 / (32.0 * 127.0))
+    return np.ascontiguousarray(blocks.reshape(rows, -1))
+
+
+def wo_input(cols: int, seed: int) -> np.ndarray:
+    """An attention output fed to wo: 0.3*N(0, 1) float32 [cols], generator
+    PCG64(SeedSequence([seed, 3000]))."""
+    g = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, 3000])))
+    return (np.float32(0.3) * g.standard_normal(cols, dtype=np.float32)).astype(np.float32)
+
+
 def sha256_arrays(*arrays: np.ndarray) -> str:
     h = hashlib.sha256()
     for a in arrays:
@@ -163,6 +198,8 @@ __all__ = [
     "decode_inputs",
     "prefill_inputs",
     "raw_qkv_inputs",
+    "wo_input",
+    "wo_weights",
     "sha256_arrays",
     "decode_kv_bytes",
     "prefill_flops",

@@ -447,3 +447,109 @@ int l3po_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer,
     free(freq);
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* The wo projection: weight rows dequantised, then fp32 dot products.      */
+
+#define QK_SUPER 256 /* values per K-quant super-block (c:121 QK_K) */
+
+long long l3po_w_row_bytes(int type, int cols) {
+    switch (type) {
+        case L3P_W_Q8_0: return (long long)(cols / 32) * 34;
+        case L3P_W_Q4_K: return (long long)(cols / QK_SUPER) * 144;
+        case L3P_W_Q6_K: return (long long)(cols / QK_SUPER) * 210;
+        default: return 0;
+    }
+}
+
+static uint16_t rd16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* Q8_0: value = int8 * d (dequantize_row_q8_0, c:691-702). */
+static void deq_q8_0(const uint8_t* src, float* dst, int cols) {
+    for (int b = 0; b < cols / 32; ++b) {
+        const uint8_t* blk = src + (size_t)b * 34;
+        float d = l3po_fp16_to_fp32(rd16(blk));
+        for (int j = 0; j < 32; ++j) dst[b * 32 + j] = (float)(int8_t)blk[2 + j] * d;
+    }
+}
+
+/* 6-bit scale and min number j (0..7) of a Q4_K block's 12 packed bytes:
+ * j < 4 in the low 6 bits of bytes j and j+4; j >= 4 split between the
+ * nibbles of byte j+4 and the top 2 bits of bytes j-4 and j (c:705-713). */
+static void k4_scale_min(const uint8_t* sc, int j, int* scale, int* min) {
+    if (j < 4) {
+        *scale = sc[j] & 63;
+        *min = sc[j + 4] & 63;
+    } else {
+        *scale = (sc[j + 4] & 15) | ((sc[j - 4] >> 6) << 4);
+        *min = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+}
+
+/* Q4_K: 8 sub-blocks of 32; sub-block j value = (d*scale_j) * nibble - dmin*min_j.
+ * Sub-blocks 2p and 2p+1 share 32 bytes: low nibbles, then high (c:715-746). */
+static void deq_q4_k(const uint8_t* src, float* dst, int cols) {
+    for (int b = 0; b < cols / QK_SUPER; ++b) {
+        const uint8_t* blk = src + (size_t)b * 144;
+        float d = l3po_fp16_to_fp32(rd16(blk)), dmin = l3po_fp16_to_fp32(rd16(blk + 2));
+        const uint8_t* sc = blk + 4;
+        const uint8_t* qs = blk + 16;
+        float* y = dst + (size_t)b * QK_SUPER;
+        for (int p = 0; p < 4; ++p) {
+            int s0, m0, s1, m1;
+            k4_scale_min(sc, 2 * p, &s0, &m0);
+            k4_scale_min(sc, 2 * p + 1, &s1, &m1);
+            float dl = d * s0, ml = dmin * m0, dh = d * s1, mh = dmin * m1;
+            for (int l = 0; l < 32; ++l) y[64 * p + l] = dl * (qs[32 * p + l] & 15) - ml;
+            for (int l = 0; l < 32; ++l) y[64 * p + 32 + l] = dh * (qs[32 * p + l] >> 4) - mh;
+        }
+    }
+}
+
+/* Q6_K: two halves of 128 values; value = d * scale * (6-bit q - 32), the 6
+ * bits from a nibble of ql and two bits of qh (c:873-902). */
+static void deq_q6_k(const uint8_t* src, float* dst, int cols) {
+    for (int b = 0; b < cols / QK_SUPER; ++b) {
+        const uint8_t* blk = src + (size_t)b * 210;
+        const uint8_t* ql = blk;
+        const uint8_t* qh = blk + 128;
+        const int8_t* sc = (const int8_t*)(blk + 192);
+        float d = l3po_fp16_to_fp32(rd16(blk + 208));
+        float* y = dst + (size_t)b * QK_SUPER;
+        for (int h = 0; h < 2; ++h) {
+            const uint8_t* l8 = ql + 64 * h;
+            const uint8_t* h8 = qh + 32 * h;
+            const int8_t* s8 = sc + 8 * h;
+            float* yh = y + 128 * h;
+            for (int l = 0; l < 32; ++l) {
+                int g = l / 16;
+                int v0 = ((l8[l] & 15) | (((h8[l] >> 0) & 3) << 4)) - 32;
+                int v1 = ((l8[l + 32] & 15) | (((h8[l] >> 2) & 3) << 4)) - 32;
+                int v2 = ((l8[l] >> 4) | (((h8[l] >> 4) & 3) << 4)) - 32;
+                int v3 = ((l8[l + 32] >> 4) | (((h8[l] >> 6) & 3) << 4)) - 32;
+                yh[l] = d * s8[g] * v0;
+                yh[l + 32] = d * s8[g + 2] * v1;
+                yh[l + 64] = d * s8[g + 4] * v2;
+                yh[l + 96] = d * s8[g + 6] * v3;
+            }
+        }
+    }
+}
+
+int l3po_matvec(int type, const void* w, int rows, int cols, const float* x, float* out) {
+    long long rb = l3po_w_row_bytes(type, cols);
+    if (rb <= 0 || !w || !x || !out || rows < 0) return -1;
+    float* buf = (float*)malloc(sizeof(float) * (size_t)cols);
+    if (!buf) return -4;
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t* row = (const uint8_t*)w + (size_t)r * rb;
+        if (type == L3P_W_Q8_0) deq_q8_0(row, buf, cols);
+        else if (type == L3P_W_Q4_K) deq_q4_k(row, buf, cols);
+        else deq_q6_k(row, buf, cols);
+        float s = 0.0f;
+        for (int j = 0; j < cols; ++j) s += buf[j] * x[j];
+        out[r] = s;
+    }
+    free(buf);
+    return 0;
+}

@@ -63,6 +63,11 @@ typedef struct {
     const float* k_norm;  /* [n_layers][head_dim] or NULL */
 } l3p_oracle_rope;
 
+/* Weight types of the wo projection (GGUF tensor types, ggml numbering). */
+#define L3P_W_Q8_0 8  /* 34-byte blocks of 32: fp16 d, 32 int8 */
+#define L3P_W_Q4_K 12 /* 144-byte blocks of 256: fp16 d, dmin, 12 scale bytes, 128 nibble bytes */
+#define L3P_W_Q6_K 14 /* 210-byte blocks of 256: 128 low-nibble, 64 high-bit, 16 int8 scales, fp16 d */
+
 /* ---- restatement (oracle/l3p_oracle.c) ---- */
 void* l3po_create(const l3p_oracle_cfg* cfg, int mode);
 void l3po_destroy(void* ctx);
@@ -82,6 +87,11 @@ void l3po_softmax(float* x, int n);
  * of tokens at positions pos0, pos0+1, ... of `layer`. */
 int l3po_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer, int pos0, int n_tok,
               float* q, float* k);
+/* Bytes of one weight row of `cols` values (0 for an unknown type). */
+long long l3po_w_row_bytes(int type, int cols);
+/* out[rows] = W x: each row dequantised to fp32, then summed in column order
+ * (matmul_deq_4row, c:2136-2176).  W: rows of l3po_w_row_bytes bytes. */
+int l3po_matvec(int type, const void* w, int rows, int cols, const float* x, float* out);
 
 /* ---- reference harness (oracle/ref_harness.c -> oracle/_ref/) ---- */
 void* l3pref_create(const l3p_oracle_cfg* cfg, int mode);
@@ -99,6 +109,7 @@ void l3pref_q8_accum(float* out, const uint8_t* v, float w, int count);
 void l3pref_softmax(float* x, int n);
 int l3pref_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer, int pos0, int n_tok,
                 float* q, float* k);
+int l3pref_matvec(int type, const void* w, int rows, int cols, const float* x, float* out);
 int l3pref_threads(void);
 
 #ifdef __cplusplus

@@ -91,6 +91,7 @@ def _load(impl: str, fast: bool):
         "q8_accum": (None, [fp, C.c_void_p, C.c_float, C.c_int]),
         "softmax": (None, [fp, C.c_int]),
         "rope": (C.c_int, [C.POINTER(OracleCfg), C.POINTER(OracleRope), C.c_int, C.c_int, C.c_int, fp, fp]),
+        "matvec": (C.c_int, [C.c_int, C.c_void_p, C.c_int, C.c_int, fp, fp]),
     }
     fns = {}
     for name, (res, args) in sig.items():
@@ -209,3 +210,26 @@ def rope(shape, layer: int, pos0: int, q: np.ndarray, k: np.ndarray, rope_theta:
     if rc:
         raise RuntimeError(f"oracle rope rc={rc}")
     return q, k
+
+
+W_Q8_0, W_Q4_K, W_Q6_K = 8, 12, 14
+W_BLOCK = {W_Q8_0: (32, 34), W_Q4_K: (256, 144), W_Q6_K: (256, 210)}  # values, bytes per block
+
+
+def w_row_bytes(wtype: int, cols: int) -> int:
+    n, b = W_BLOCK[wtype]
+    return cols // n * b
+
+
+def matvec(wtype: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray, impl: str = "port") -> np.ndarray:
+    """out[rows] = W x for GGUF weight rows (uint8 [rows][row bytes]), the
+    reference's dequantise-then-dot path (matmul_quantized, c:2091)."""
+    _, f = _load(impl, False)
+    w = np.ascontiguousarray(w, np.uint8)
+    assert w.size == rows * w_row_bytes(wtype, cols)
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty(rows, np.float32)
+    rc = f["matvec"](wtype, w.ctypes.data, rows, cols, _fptr(x), _fptr(out))
+    if rc:
+        raise RuntimeError(f"oracle matvec rc={rc}")
+    return out

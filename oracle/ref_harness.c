@@ -329,3 +329,34 @@ L3P_EXPORT int l3pref_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rop
     free_run_state(&s);
     return 0;
 }
+
+/* The wo projection through the reference's own matmul_quantized (c:2091)
+ * with a QuantizedTensor set up as load_quantized_tensor does (c:2912-2920)
+ * and the dequantisation / Q8_0 scratch main() allocates (c:5190-5200). */
+L3P_EXPORT int l3pref_matvec(int type, const void* w, int rows, int cols, const float* x, float* out) {
+    if (!w || !x || !out || rows <= 0 || cols <= 0) return -1;
+    ensure_fp16();
+    static int scratch_cols = 0;
+    if (cols > scratch_cols) {
+        free(q8_buf);
+        free(deq_buf);
+        q8_buf = (block_q8_0*)calloc((size_t)(cols + QK8_0 - 1) / QK8_0, sizeof(block_q8_0));
+        deq_buf_stride = 4 * cols;
+        deq_buf = (float*)calloc((size_t)omp_get_max_threads() * deq_buf_stride, sizeof(float));
+        if (!q8_buf || !deq_buf) return -4;
+        scratch_cols = cols;
+    }
+    QuantizedTensor qt;
+    memset(&qt, 0, sizeof(qt));
+    qt.data = (void*)w;
+    qt.type = (enum ggml_type)type;
+    qt.n_elements = rows * cols;
+    qt.rows = rows;
+    qt.cols = cols;
+    qt.row_size = get_row_size(cols, qt.type);
+    qt.q8_func = get_vec_dot_q8_func(qt.type);
+    qt.dot_func = get_vec_dot_func(qt.type);
+    qt.deq_func = get_deq_row_func(qt.type);
+    matmul_quantized(out, x, &qt);
+    return 0;
+}

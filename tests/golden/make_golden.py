@@ -3,8 +3,9 @@
 Run in a container that has the reference source (it needs oracle/_ref/,
 built by `make -C oracle ref` from llama3pure-c-engine.c in place):
 
-    python tests/golden/make_golden.py          # both files
+    python tests/golden/make_golden.py          # all three files
     python tests/golden/make_golden.py rope     # rope_golden.npz only
+    python tests/golden/make_golden.py wo       # wo_golden.npz only
 
 Each case records its geometry, the SHA-256 of its seeded inputs (so generator
 drift is caught) and the reference's attention output in both oracle modes:
@@ -33,6 +34,8 @@ from llama3pure_b200.synth import (  # noqa: E402
     prefill_inputs,
     raw_qkv_inputs,
     sha256_arrays,
+    wo_input,
+    wo_weights,
 )
 
 PREFILL_ROWS = (0, 1, 2, 31, 32, 33, 1023, 2047)
@@ -100,6 +103,37 @@ def write_rope_golden():
         print("rope", name, "done", flush=True)
     data["cases"] = np.array(names)
     out_path = os.path.join(HERE, "rope_golden.npz")
+    np.savez_compressed(out_path, **data)
+    print("wrote", out_path, os.path.getsize(out_path), "bytes")
+
+
+def wo_cases():
+    """(name, weight type, rows, cols, seed)"""
+    return [
+        ("q8_0_64x4096", O.W_Q8_0, 64, 4096, 1),
+        ("q8_0_37x2048", O.W_Q8_0, 37, 2048, 2),
+        ("q4_k_48x4096", O.W_Q4_K, 48, 4096, 3),
+        ("q4_k_9x2048", O.W_Q4_K, 9, 2048, 4),
+        ("q6_k_40x4096", O.W_Q6_K, 40, 4096, 5),
+        ("q6_k_7x2048", O.W_Q6_K, 7, 2048, 6),
+    ]
+
+
+def write_wo_golden():
+    """tests/golden/wo_golden.npz: the wo projection through the reference's
+    own matmul_quantized (dequantise rows, fp32 dots) for Q8_0, Q4_K, Q6_K."""
+    data = {}
+    names = []
+    for name, wt, rows, cols, seed in wo_cases():
+        w = wo_weights(wt, rows, cols, seed)
+        x = wo_input(cols, seed)
+        data[f"{name}/out"] = O.matvec(wt, w, rows, cols, x, impl="ref")
+        data[f"{name}/sha256"] = np.array(sha256_arrays(w, x))
+        data[f"{name}/geom"] = np.array([wt, rows, cols, seed], np.int64)
+        names.append(name)
+        print("wo", name, "done", flush=True)
+    data["cases"] = np.array(names)
+    out_path = os.path.join(HERE, "wo_golden.npz")
     np.savez_compressed(out_path, **data)
     print("wrote", out_path, os.path.getsize(out_path), "bytes")
 
@@ -186,6 +220,9 @@ if __name__ == "__main__":
         sys.exit("oracle/_ref/libl3p_ref.so missing: run `make -C oracle ref` where the reference source exists")
     if sys.argv[1:] == ["rope"]:
         write_rope_golden()
+    elif sys.argv[1:] == ["wo"]:
+        write_wo_golden()
     else:
         main()
         write_rope_golden()
+        write_wo_golden()

@@ -227,3 +227,41 @@ def test_rope_position0_is_identity_without_norm():
     qr, kr = O.rope(shape, 0, 0, q, k, impl="port")
     np.testing.assert_array_equal(qr, q)
     np.testing.assert_array_equal(kr, k)
+
+
+# ---- the wo projection -------------------------------------------------------
+
+_WO_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "wo_golden.npz")
+
+
+def _wo_names():
+    return [str(n) for n in np.load(_WO_GOLDEN)["cases"]]
+
+
+@pytest.mark.parametrize("name", _wo_names())
+def test_wo_matvec_matches_golden(name):
+    """Dequantise-then-dot of Q8_0 / Q4_K / Q6_K rows, bit for bit against the
+    reference's own matmul_quantized (golden from oracle/_ref)."""
+    from llama3pure_b200.synth import wo_input, wo_weights
+
+    g = np.load(_WO_GOLDEN)
+    wt, rows, cols, seed = [int(v) for v in g[f"{name}/geom"]]
+    w = wo_weights(wt, rows, cols, seed)
+    x = wo_input(cols, seed)
+    assert sha256_arrays(w, x) == str(g[f"{name}/sha256"]), "seeded generator drifted"
+    got = O.matvec(wt, w, rows, cols, x, impl="port")
+    np.testing.assert_array_equal(got.view(np.uint32), g[f"{name}/out"].view(np.uint32))
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built (needs the reference source)")
+@pytest.mark.parametrize("wt", [O.W_Q8_0, O.W_Q4_K, O.W_Q6_K])
+def test_wo_port_bit_identical_to_reference(wt):
+    from llama3pure_b200.synth import wo_weights
+
+    rng = np.random.default_rng(wt)
+    for rows, cols in ((5, 256), (33, 1024), (4, 8192)):
+        w = wo_weights(wt, rows, cols, seed=rows)
+        x = rng.standard_normal(cols).astype(np.float32)
+        a = O.matvec(wt, w, rows, cols, x, impl="port")
+        b = O.matvec(wt, w, rows, cols, x, impl="ref")
+        np.testing.assert_array_equal(a.view(np.uint32), b.view(np.uint32))
