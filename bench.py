@@ -367,6 +367,34 @@ def run_ours(args):
         raw = {"api": "l3p_attn_step_raw_dev (QK-norm/RoPE + cache write + decode)",
                "us_per_layer": round(raw_ms * 1e3 / L, 3), "launches_per_layer": raw_launches // L,
                "post_rope_step_us_per_layer": round(ms / args.steps * 1e3 / L, 3)}
+        if not args.no_wo and world == 1:
+            # and on to the wo projection (Q8_0 weights, 4096 x 4096 per layer)
+            from llama3pure_b200.synth import wo_weights
+
+            w = wo_weights(8, sh.n_heads * sh.head_dim, sh.n_heads * sh.head_dim, seed=3)
+            for layer in range(L):
+                ctx.set_wo(layer, 8, w)
+            xb2 = torch.zeros((L, sh.n_heads * sh.head_dim), device="cuda")
+            bgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(rstream):
+                ctx.set_stream(rstream)
+                with torch.cuda.graph(bgraph, stream=rstream):
+                    for layer in range(L):
+                        ctx.step_raw_dev(layer, sh.pos, q[layer], knew[layer], vnew[layer], out[layer], rstream)
+                        ctx.wo_dev(layer, out[layer], xb2[layer], rstream)
+            stream.wait_stream(rstream)
+            ctx.set_stream(stream)
+            for _ in range(max(3, args.warmup)):
+                bgraph.replay()
+            torch.cuda.synchronize()
+            r0.record(stream)
+            for _ in range(args.steps):
+                bgraph.replay()
+            r1.record(stream)
+            torch.cuda.synchronize()
+            ctx.check()
+            raw["with_wo_q8_0_us_per_layer"] = round(r0.elapsed_time(r1) / args.steps * 1e3 / L, 3)
+            del bgraph
     if clocks:
         clk = clocks.stop()
     else:
@@ -682,15 +710,16 @@ def run_wo(args, torch, layers: int = 16):
             with torch.cuda.graph(gr, stream=cs):
                 for i in range(2 * layers):
                     ctx.wo_dev(i % layers, x[i % layers], y[i % layers], cs)
-        for _ in range(3):
-            gr.replay()
-        torch.cuda.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(cs)
         reps = 5
-        for _ in range(reps):
-            gr.replay()
-        b.record(cs)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(cs):  # replays run on the current stream; time them there
+            for _ in range(3):
+                gr.replay()
+            torch.cuda.synchronize()
+            a.record(cs)
+            for _ in range(reps):
+                gr.replay()
+            b.record(cs)
         torch.cuda.synchronize()
         ctx.check()
         us = a.elapsed_time(b) * 1e3 / (reps * 2 * layers)

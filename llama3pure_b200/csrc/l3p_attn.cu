@@ -90,12 +90,13 @@ struct l3p_attn_ctx {
     int type = 0;  // 0 = not set
     int rows = 0;
     long long row_bytes = 0;
+    int sc_stride = 0;  // bytes per row of Q8_0 scales
     uint8_t* w = nullptr;
-    uint16_t* wsc = nullptr;
+    uint8_t* wsc = nullptr;
   };
   std::vector<WoLayer> wo;
   float* wo_x = nullptr;
-  int wo_ctas_per_sm[3] = {0, 0, 0};  // Q8_0, Q4_K, Q6_K
+  int wo_ctas_per_sm[6] = {0, 0, 0, 0, 0, 0};  // (Q8_0, Q4_K, Q6_K) x (4, 8 warps)
   std::string last_error;
 };
 
@@ -682,6 +683,7 @@ int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream
   a.w = L.w;
   a.wsc = L.wsc;
   a.row_bytes = L.row_bytes;
+  a.sc_stride = L.sc_stride;
   a.rows = L.rows;
   a.C = ctx->kvh_count * ctx->G * ctx->hd;
   a.x = x + (long long)ctx->cfg.kv_head_begin * ctx->G * ctx->hd;
@@ -691,29 +693,33 @@ int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream
   const int slices = (a.C + slice - 1) / slice;
   a.wc = 1;
   while (a.wc < slices) a.wc <<= 1;
-  const int per_sm = std::max(ctx->wo_ctas_per_sm[fi], 1);
-  const int target = ctx->num_sms * per_sm;
+  const int nw = a.wc <= 4 ? 4 : 8;  // warps per CTA
+  const int k = fi * 2 + (nw == 8);
+  // every SM holds as many CTAs as fit; a CTA takes a contiguous block of rows
+  const int target = ctx->num_sms * std::max(ctx->wo_ctas_per_sm[k], 1);
   a.rows_per_cta = std::max(1, (a.rows + target - 1) / target);
   const int grid = (a.rows + a.rows_per_cta - 1) / a.rows_per_cta;
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(grid, 1, 1);
-  lc.blockDim = dim3(kWoWarps * 32, 1, 1);
-  lc.dynamicSmemBytes = (size_t)kWoWarps * a.rows_per_cta * sizeof(float);
+  lc.blockDim = dim3(nw * 32, 1, 1);
+  lc.dynamicSmemBytes = (size_t)nw * a.rows_per_cta * sizeof(float);
   lc.stream = s;
   cudaLaunchAttribute attr[1];
   if (ctx->overlap) {
-    // weights are prefetched before griddepcontrol.wait; x is read after it
+    // weights are requested before griddepcontrol.wait; x is read after it
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
   }
-  if (fi == 0)
-    L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ8>, a));
-  else if (fi == 1)
-    L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ4K>, a));
-  else
-    L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ6K>, a));
+  switch (k) {
+    case 0: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ8, 4>, a)); break;
+    case 1: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ8, 8>, a)); break;
+    case 2: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ4K, 4>, a)); break;
+    case 3: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ4K, 8>, a)); break;
+    case 4: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ6K, 4>, a)); break;
+    default: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ6K, 8>, a)); break;
+  }
   ++ctx->launches;
   return L3P_OK;
 }
@@ -1034,17 +1040,19 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
   const uint8_t* src = static_cast<const uint8_t*>(rows);
   const size_t src_row = (size_t)(cols / vals) * bytes, nb = (size_t)C / vals, b0 = (size_t)c_lo / vals;
   // device layout of wo.cuh
-  std::vector<uint8_t> w;
-  std::vector<uint16_t> sc;
+  std::vector<uint8_t> w, sc;
   long long row_bytes;
+  int sc_stride = 0;
   if (type == L3P_W_Q8_0) {
     row_bytes = C;
+    sc_stride = (int)((nb * 2 + 15) / 16 * 16);
     w.resize((size_t)dim * C);
-    sc.resize((size_t)dim * nb);
+    sc.assign((size_t)dim * sc_stride, 0);
     for (int r = 0; r < dim; ++r)
       for (size_t b = 0; b < nb; ++b) {
         const uint8_t* blk = src + (size_t)r * src_row + (b0 + b) * bytes;
-        sc[(size_t)r * nb + b] = (uint16_t)(blk[0] | (blk[1] << 8));
+        sc[(size_t)r * sc_stride + 2 * b] = blk[0];  // fp16 scale, little-endian
+        sc[(size_t)r * sc_stride + 2 * b + 1] = blk[1];
         memcpy(&w[(size_t)r * C + b * 32], blk + 2, 32);
       }
   } else if (type == L3P_W_Q4_K) {
@@ -1067,12 +1075,13 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
       ctx->wo.clear();
       return fail(ctx, L3P_E_NOMEM, "wo input buffer allocation failed");
     }
-    // resident CTAs per SM of each format's kernel (grid sizing)
-    const void* fns[3] = {(const void*)wo_gemv_kernel<WoQ8>, (const void*)wo_gemv_kernel<WoQ4K>,
-                          (const void*)wo_gemv_kernel<WoQ6K>};
-    for (int i = 0; i < 3; ++i)
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctx->wo_ctas_per_sm[i], fns[i], kWoWarps * 32,
-                                                        (size_t)kWoWarps * 64 * sizeof(float)) != cudaSuccess) {
+    // resident CTAs per SM of each kernel (grid sizing)
+    const void* fns[6] = {(const void*)wo_gemv_kernel<WoQ8, 4>,  (const void*)wo_gemv_kernel<WoQ8, 8>,
+                          (const void*)wo_gemv_kernel<WoQ4K, 4>, (const void*)wo_gemv_kernel<WoQ4K, 8>,
+                          (const void*)wo_gemv_kernel<WoQ6K, 4>, (const void*)wo_gemv_kernel<WoQ6K, 8>};
+    for (int i = 0; i < 6; ++i)
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctx->wo_ctas_per_sm[i], fns[i], (i % 2 ? 8 : 4) * 32,
+                                                        (size_t)(i % 2 ? 8 : 4) * 64 * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
         ctx->wo_ctas_per_sm[i] = 1;
       }
@@ -1081,17 +1090,18 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
   cudaFree(L.w);
   cudaFree(L.wsc);
   L = l3p_attn_ctx::WoLayer();
-  if (cudaMalloc(&L.w, w.size()) != cudaSuccess || (!sc.empty() && cudaMalloc(&L.wsc, sc.size() * 2) != cudaSuccess)) {
+  if (cudaMalloc(&L.w, w.size()) != cudaSuccess || (!sc.empty() && cudaMalloc(&L.wsc, sc.size()) != cudaSuccess)) {
     cudaGetLastError();
     cudaFree(L.w);
     L = l3p_attn_ctx::WoLayer();
     return fail(ctx, L3P_E_NOMEM, "wo weight allocation of %zu bytes failed", w.size());
   }
   L3P_CUDA(ctx, cudaMemcpy(L.w, w.data(), w.size(), cudaMemcpyHostToDevice));
-  if (!sc.empty()) L3P_CUDA(ctx, cudaMemcpy(L.wsc, sc.data(), sc.size() * 2, cudaMemcpyHostToDevice));
+  if (!sc.empty()) L3P_CUDA(ctx, cudaMemcpy(L.wsc, sc.data(), sc.size(), cudaMemcpyHostToDevice));
   L.type = type;
   L.rows = dim;
   L.row_bytes = row_bytes;
+  L.sc_stride = sc_stride;
   return L3P_OK;
 }
 

@@ -19,62 +19,89 @@
 // split (the partials add up across GPUs).
 //
 // Device layout per layer (row-major, every row 16-byte aligned):
-//   Q8_0  int8 values [dim][C] and fp16 scales [dim][C/32]
+//   Q8_0  int8 values [dim][C] and fp16 scales [dim][sc_stride/2]
+//         (sc_stride = C/16 bytes rounded up to 16)
 //   Q4_K  the GGUF blocks as they are, [dim][C/256][144]
 //   Q6_K  blocks padded to 224 bytes: ql 128 | qh 64 | scales 16 | d 2 | 14 spare
 //
-// GEMV decomposition.  A weight row is cut into column slices of 1024
-// values (Q8_0, Q4_K) or 2048 (Q6_K); lane l of a warp always covers the same
-// 32 or 64 columns of its slice, so it loads its x values ONCE into registers
-// and reuses them for every row.  The 8 warps of a CTA form wc column groups
-// (one slice each) x 8/wc row groups; a CTA takes a contiguous block of rows,
-// each warp streams its slice of its rows with kUnroll rows of loads in
-// flight, and the per-row partials of the column groups are added in shared
-// memory.  Weights do not depend on the kernel before this one, so with
-// programmatic dependent launch the first rows are requested before
-// griddepcontrol.wait and only x waits for the attention.
+// Kernel.  A row is cut into column slices of 1024 values (Q8_0, Q4_K) or
+// 2048 (Q6_K); lane l of a warp always covers the same columns of its slice,
+// so it loads its x values once into registers and reuses them for every
+// row, and every warp-wide weight load is 512 contiguous bytes.  The NW warps
+// of a CTA form wc column groups (one slice each) x NW/wc row groups; a CTA
+// takes a contiguous block of rows, each warp keeps kUnroll rows of weight
+// loads in flight in registers, and the column groups' per-row partials are
+// added in shared memory.  CTAs are small (4 warps when the owned columns fit
+// 4 slices) and use little shared memory, so under programmatic dependent
+// launch they become resident beside the attention kernel's CTAs, request
+// their first rows while it finishes and wait (griddepcontrol.wait) only
+// before reading x.
+//
+// Integers become floats by placing them in the mantissa of 2^23 (one byte
+// permute) and subtracting 2^23 plus the offset (one add): exact, and on the
+// full-rate pipes (an int-to-float conversion per value would run at a
+// quarter of the rate and bound the kernel).
 #pragma once
 #include "decode_q8.cuh"
 
 namespace l3p {
 
-constexpr int kWoWarps = 8;
-constexpr int kWoUnroll = 4;  // rows of weight loads in flight per warp
-
 struct WoArgs {
-  const uint8_t* w;      // this layer's weight rows (format above), owned columns only
-  const uint16_t* wsc;   // Q8_0 scales [rows][C/32]
-  long long row_bytes;   // bytes of one weight row in `w`
-  int rows, C;           // output rows (dim), owned columns
+  const uint8_t* w;     // this layer's weight rows (format above), owned columns only
+  const uint8_t* wsc;   // Q8_0 scales, sc_stride bytes per row
+  long long row_bytes;  // bytes of one weight row in `w`
+  int sc_stride;        // bytes of one row of Q8_0 scales (0 for the K-quants)
+  int rows, C;          // output rows (dim), owned columns
   int rows_per_cta;
-  int wc;                // column groups per CTA (power of two <= 8)
-  const float* x;        // owned columns of the attention output (x[0] = column q_head0*hd)
-  float* y;              // [rows]
+  int wc;               // column groups per CTA (power of two <= warps)
+  const float* x;       // owned columns of the attention output (x[0] = column q_head0*hd)
+  float* y;             // [rows]
 };
 
-// Per-format lane work: columns, loads and the dot product of one row.
+// Byte i (0..3) of w as the float 2^23 + byte: exact for every byte.
+__device__ __forceinline__ float byte_f(uint32_t w, int i) {
+  return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)i));
+}
+constexpr float kTwo23 = 8388608.f;
+
+// Per-format lane work: the lane's columns, its loads of one row's slice and
+// the dot product.
 struct WoQ8 {
   static constexpr int kSlice = 1024;  // columns per warp slice
   static constexpr int kLaneCols = 32;
+  static constexpr int kUnroll = 8;
   struct Raw {
     uint4 a, b;
-    uint16_t d;
+    uint16_t d0, d1;
   };
-  // lane's columns inside its slice: one Q8_0 block [32*lane, 32*lane+32)
-  __device__ static int col(int lane, int i) { return 32 * lane + i; }
+  // lane l: columns [16l, 16l+16) and [512+16l, 512+16l+16) of its slice
+  __device__ static int col(int lane, int i) { return (i < 16 ? 16 * lane : 512 + 16 * lane - 16) + i; }
   __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
     const int lane = threadIdx.x & 31;
-    const uint8_t* s = p.w + (long long)row * p.row_bytes + c0 + 32 * lane;
+    const uint8_t* s = p.w + (long long)row * p.row_bytes + c0 + 16 * lane;
+    const uint16_t* sc = reinterpret_cast<const uint16_t*>(p.wsc + (long long)row * p.sc_stride) + c0 / 32 + lane / 2;
     r.a = __ldg(reinterpret_cast<const uint4*>(s));
-    r.b = __ldg(reinterpret_cast<const uint4*>(s + 16));
-    r.d = __ldg(p.wsc + (long long)row * (p.C / 32) + c0 / 32 + lane);
+    r.d0 = __ldg(sc);
+    // the owned columns may end inside the slice's second half
+    if (c0 + 512 + 16 * lane < p.C) {
+      r.b = __ldg(reinterpret_cast<const uint4*>(s + 512));
+      r.d1 = __ldg(sc + 16);
+    } else {
+      r.b = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // zeros after the bias flip
+      r.d1 = 0;
+    }
   }
   __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&)[2]) {
-    const uint32_t w[8] = {r.a.x, r.a.y, r.a.z, r.a.w, r.b.x, r.b.y, r.b.z, r.b.w};
-    float s = 0.f;
+    // int8 q: (q ^ 0x80) is q + 128 as an unsigned byte
+    const uint32_t wa[4] = {r.a.x ^ 0x80808080u, r.a.y ^ 0x80808080u, r.a.z ^ 0x80808080u, r.a.w ^ 0x80808080u};
+    const uint32_t wb[4] = {r.b.x ^ 0x80808080u, r.b.y ^ 0x80808080u, r.b.z ^ 0x80808080u, r.b.w ^ 0x80808080u};
+    float s[4] = {0.f, 0.f, 0.f, 0.f}, t[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int i = 0; i < 32; ++i) s = fmaf((float)(int8_t)(w[i / 4] >> (8 * (i % 4))), x[i], s);
-    return fp16_to_f32(r.d) * s;
+    for (int i = 0; i < 16; ++i) {
+      s[i % 4] = fmaf(byte_f(wa[i / 4], i % 4) - (kTwo23 + 128.f), x[i], s[i % 4]);
+      t[i % 4] = fmaf(byte_f(wb[i / 4], i % 4) - (kTwo23 + 128.f), x[16 + i], t[i % 4]);
+    }
+    return fp16_to_f32(r.d0) * ((s[0] + s[1]) + (s[2] + s[3])) + fp16_to_f32(r.d1) * ((t[0] + t[1]) + (t[2] + t[3]));
   }
   __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
 };
@@ -82,6 +109,7 @@ struct WoQ8 {
 struct WoQ4K {
   static constexpr int kSlice = 1024;  // 4 blocks of 256
   static constexpr int kLaneCols = 32;
+  static constexpr int kUnroll = 8;
   struct Raw {
     uint4 h;  // d, dmin, 12 scale bytes
     uint4 q;  // 16 quant bytes: 16 low nibbles (sub-block 2p) and 16 high (sub-block 2p+1)
@@ -120,14 +148,15 @@ struct WoQ4K {
     scale_min(r.h.y, r.h.z, r.h.w, 2 * p, sc0, m0);
     scale_min(r.h.y, r.h.z, r.h.w, 2 * p + 1, sc1, m1);
     const uint32_t q[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
-    float lo = 0.f, hi = 0.f;
+    float lo[2] = {0.f, 0.f}, hi[2] = {0.f, 0.f};
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const uint32_t byte = (q[i / 4] >> (8 * (i % 4))) & 0xffu;
-      lo = fmaf((float)(byte & 15u), x[i], lo);
-      hi = fmaf((float)(byte >> 4), x[16 + i], hi);
+      const uint32_t l4 = q[i / 4] & 0x0f0f0f0fu, h4 = (q[i / 4] >> 4) & 0x0f0f0f0fu;
+      lo[i % 2] = fmaf(byte_f(l4, i % 4) - kTwo23, x[i], lo[i % 2]);
+      hi[i % 2] = fmaf(byte_f(h4, i % 4) - kTwo23, x[16 + i], hi[i % 2]);
     }
-    return d * ((float)sc0 * lo + (float)sc1 * hi) - dmin * ((float)m0 * xs[0] + (float)m1 * xs[1]);
+    return d * ((float)sc0 * (lo[0] + lo[1]) + (float)sc1 * (hi[0] + hi[1])) -
+           dmin * ((float)m0 * xs[0] + (float)m1 * xs[1]);
   }
   __device__ static void xsums(const float (&x)[kLaneCols], float (&xs)[2]) {
     xs[0] = xs[1] = 0.f;
@@ -142,6 +171,7 @@ struct WoQ4K {
 struct WoQ6K {
   static constexpr int kSlice = 2048;  // 8 blocks of 256
   static constexpr int kLaneCols = 64;
+  static constexpr int kUnroll = 4;
   static constexpr int kBlockBytes = 224;
   struct Raw {
     uint4 l0, l1, h;  // ql[64h+16j..], ql[64h+32+16j..], qh[32h+16j..]
@@ -170,13 +200,20 @@ struct WoQ6K {
     const uint32_t c[4] = {r.h.x, r.h.y, r.h.z, r.h.w};
     float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const uint32_t qa = (a[i / 4] >> (8 * (i % 4))) & 0xffu, qb = (b[i / 4] >> (8 * (i % 4))) & 0xffu;
-      const uint32_t qh = (c[i / 4] >> (8 * (i % 4))) & 0xffu;
-      s0 = fmaf((float)((int)((qa & 15u) | ((qh & 3u) << 4)) - 32), x[i], s0);
-      s1 = fmaf((float)((int)((qb & 15u) | (((qh >> 2) & 3u) << 4)) - 32), x[16 + i], s1);
-      s2 = fmaf((float)((int)((qa >> 4) | (((qh >> 4) & 3u) << 4)) - 32), x[32 + i], s2);
-      s3 = fmaf((float)((int)((qb >> 4) | (((qh >> 6) & 3u) << 4)) - 32), x[48 + i], s3);
+    for (int k = 0; k < 4; ++k) {
+      // four 6-bit values per byte lane: low/high nibbles of ql with bit pairs of qh (c:885-888)
+      const uint32_t q0 = (a[k] & 0x0f0f0f0fu) | ((c[k] & 0x03030303u) << 4);
+      const uint32_t q1 = (b[k] & 0x0f0f0f0fu) | (((c[k] >> 2) & 0x03030303u) << 4);
+      const uint32_t q2 = ((a[k] >> 4) & 0x0f0f0f0fu) | (((c[k] >> 4) & 0x03030303u) << 4);
+      const uint32_t q3 = ((b[k] >> 4) & 0x0f0f0f0fu) | (((c[k] >> 6) & 0x03030303u) << 4);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = 4 * k + e;
+        s0 = fmaf(byte_f(q0, e) - (kTwo23 + 32.f), x[i], s0);
+        s1 = fmaf(byte_f(q1, e) - (kTwo23 + 32.f), x[16 + i], s1);
+        s2 = fmaf(byte_f(q2, e) - (kTwo23 + 32.f), x[32 + i], s2);
+        s3 = fmaf(byte_f(q3, e) - (kTwo23 + 32.f), x[48 + i], s3);
+      }
     }
     const uint32_t sw[2] = {r.sc.x, r.sc.y};
     auto sc = [&](int k) { return (float)(int8_t)(sw[k / 4] >> (8 * (k % 4))); };
@@ -185,33 +222,34 @@ struct WoQ6K {
   __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
 };
 
-// grid: ceil(rows / rows_per_cta) CTAs of kWoWarps warps; dynamic shared
-// memory: kWoWarps * rows_per_cta floats.
-template <class F>
-__global__ void __launch_bounds__(kWoWarps * 32) wo_gemv_kernel(const WoArgs p) {
+// grid: ceil(rows / rows_per_cta) CTAs of NW warps; dynamic shared memory:
+// NW * rows_per_cta floats.
+template <class F, int NW>
+__global__ void __launch_bounds__(NW * 32) wo_gemv_kernel(const WoArgs p) {
   extern __shared__ float red[];  // [wc][rows_per_cta]
+  constexpr int U = F::kUnroll;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int wcol = warp % p.wc, wrow = warp / p.wc, wr = kWoWarps / p.wc;
+  const int wcol = warp % p.wc, wrow = warp / p.wc, wr = NW / p.wc;
   const int r_begin = blockIdx.x * p.rows_per_cta;
   const int r_end = min(p.rows, r_begin + p.rows_per_cta);
-  const int c0 = wcol * F::kSlice;                         // this warp's slice
-  const bool active = c0 + F::col(lane, 0) < p.C;          // lanes past the owned columns idle
+  const int c0 = wcol * F::kSlice;                 // this warp's slice
+  const bool active = c0 + F::col(lane, 0) < p.C;  // lanes past the owned columns idle
   const int n_my = r_end - r_begin > wrow ? (r_end - r_begin - wrow + wr - 1) / wr : 0;
 
   // weights first: they do not depend on the kernel before this one
   pdl_launch_dependents();
-  typename F::Raw raw[kWoUnroll];
+  typename F::Raw raw[U];
 #pragma unroll
-  for (int u = 0; u < kWoUnroll; ++u)
+  for (int u = 0; u < U; ++u)
     if (active && u < n_my) F::load(p, r_begin + wrow + wr * u, c0, raw[u]);
   pdl_wait();
   float x[F::kLaneCols];
   float xs[2];
-  // the lane's columns come in runs of 16 consecutive values
+  // the lane's columns come in runs of 16 consecutive values (x = 0 past C)
 #pragma unroll
   for (int i = 0; i < F::kLaneCols; i += 4) {
-    const float4 t = active ? __ldg(reinterpret_cast<const float4*>(p.x + c0 + F::col(lane, i)))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+    const int c = c0 + F::col(lane, i);
+    const float4 t = c < p.C ? __ldg(reinterpret_cast<const float4*>(p.x + c)) : make_float4(0.f, 0.f, 0.f, 0.f);
     x[i] = t.x;
     x[i + 1] = t.y;
     x[i + 2] = t.z;
@@ -219,16 +257,16 @@ __global__ void __launch_bounds__(kWoWarps * 32) wo_gemv_kernel(const WoArgs p) 
   }
   F::xsums(x, xs);
 
-  for (int t0 = 0; t0 < n_my; t0 += kWoUnroll) {
-    float acc[kWoUnroll];
+  for (int t0 = 0; t0 < n_my; t0 += U) {
+    float acc[U];
 #pragma unroll
-    for (int u = 0; u < kWoUnroll; ++u) acc[u] = (active && t0 + u < n_my) ? F::dot(raw[u], x, xs) : 0.f;
-    // next rows' loads before the reductions
+    for (int u = 0; u < U; ++u) acc[u] = (active && t0 + u < n_my) ? F::dot(raw[u], x, xs) : 0.f;
+    // the next rows' loads before the reductions
 #pragma unroll
-    for (int u = 0; u < kWoUnroll; ++u)
-      if (active && t0 + kWoUnroll + u < n_my) F::load(p, r_begin + wrow + wr * (t0 + kWoUnroll + u), c0, raw[u]);
+    for (int u = 0; u < U; ++u)
+      if (active && t0 + U + u < n_my) F::load(p, r_begin + wrow + wr * (t0 + U + u), c0, raw[u]);
 #pragma unroll
-    for (int u = 0; u < kWoUnroll; ++u) {
+    for (int u = 0; u < U; ++u) {
       float v = acc[u];
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);

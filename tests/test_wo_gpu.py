@@ -105,6 +105,40 @@ def test_wo_head_shards_sum_to_the_whole(n_shards, tname):
     _check(total, want, f"sum of {n_shards} shards")
 
 
+@pytest.mark.parametrize("n_kv,G,hd", [(3, 4, 64), (1, 4, 64), (5, 2, 128), (3, 8, 128)])
+def test_wo_q8_0_owned_columns_not_a_slice_multiple(n_kv, G, hd):
+    """Owned column counts that end inside a 1024-value slice (768, 256,
+    1280, 3072): the lanes past the end read nothing."""
+    torch = _torch()
+    cols, dim = n_kv * G * hd, 384
+    w = wo_weights(O.W_Q8_0, dim, cols, seed=cols)
+    x = wo_input(cols, seed=7)
+    with AttnContext(1, n_kv * G, n_kv, hd, 16) as ctx:
+        ctx.set_wo(0, O.W_Q8_0, w)
+        dx = torch.from_numpy(x).cuda()
+        dy = torch.full((dim,), float("nan"), device="cuda")
+        ctx.wo_dev(0, dx, dy)
+        ctx.check()
+        _check(dy.cpu().numpy(), O.matvec(O.W_Q8_0, w, dim, cols, x), f"{cols} columns")
+
+
+@pytest.mark.parametrize("tname", list(TYPES))
+def test_wo_wide_rows_use_eight_column_groups(tname):
+    """8192 owned columns (64 heads of 128): eight slices of Q8_0/Q4_K, four
+    of Q6_K, i.e. the 8-warp CTAs."""
+    torch = _torch()
+    cols, dim, wt = 8192, 300, TYPES[tname]
+    w = wo_weights(wt, dim, cols, seed=77)
+    x = wo_input(cols, seed=78)
+    with AttnContext(1, 64, 8, 128, 16) as ctx:
+        ctx.set_wo(0, wt, w)
+        dx = torch.from_numpy(x).cuda()
+        dy = torch.full((dim,), float("nan"), device="cuda")
+        ctx.wo_dev(0, dx, dy)
+        ctx.check()
+        _check(dy.cpu().numpy(), O.matvec(wt, w, dim, cols, x), f"{tname} 8192 columns")
+
+
 @pytest.mark.parametrize("tname", ["q8_0", "q6_k"])
 @pytest.mark.parametrize("sname", ["l8b", "gemma"])
 def test_step_raw_wo_is_the_engines_block(sname, tname):
