@@ -484,6 +484,125 @@ def run_ours(args):
     return 0
 
 
+def run_long(args):
+    """Llama-3.1-8B shapes at position 131071 of a
+    131072-entry fp32 cache (1 GiB of K+V per layer, K rows x 0.5), 32 layers,
+    split over the ranks as head groups x sequence parts (--seq-parts).  Per
+    layer each rank runs the partial decode over its positions; ranks sharing
+    a head group all-gather their (m, l, o) triples over NCCL and merge them
+    with the LSE kernel.  One JSON line on rank 0 (device time, max over
+    ranks)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.shard import plan_shards
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    sh = CONFIGS["llama31_8b_decode_128k"]
+    L, P, hd = sh.n_layers, sh.pos + 1, sh.head_dim
+    seq_parts = args.seq_parts if args.seq_parts > 0 else 1
+    shards = plan_shards(sh.n_kv_heads, sh.seq_len, world, seq_parts)
+    me = shards[rank]
+    ctx = AttnContext.for_shape(sh, device=local, kv_head_begin=me.kv_head_begin, kv_head_count=me.kv_head_count,
+                                seq_begin=me.seq_begin, seq_count=me.seq_count)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    ctx.set_stream(stream)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(2000 + rank)
+    for layer in range(L):
+        kp, vp = ctx.kv_device_ptr(layer)
+        kt = torch.as_tensor(DevView(kp, (me.kv_head_count, me.seq_count, hd)), device="cuda")
+        vt = torch.as_tensor(DevView(vp, (me.kv_head_count, me.seq_count, hd)), device="cuda")
+        kt.normal_(generator=g).mul_(sh.k_scale)
+        vt.normal_(generator=g)
+    q = torch.randn((L, sh.n_heads * hd), device="cuda", generator=g)
+    out = torch.zeros_like(q)
+    part_o = torch.zeros((L, sh.n_heads * hd), device="cuda")
+    part_ml = torch.zeros((L, sh.n_heads * 2), device="cuda")
+    gat_o = torch.zeros((L, world, sh.n_heads * hd), device="cuda")
+    gat_ml = torch.zeros((L, world, sh.n_heads * 2), device="cuda")
+    r0 = me.kv_head_begin * sh.kv_mul
+    nr = me.kv_head_count * sh.kv_mul
+    g0 = me.head_group * seq_parts  # first rank of this head group
+
+    def step(s):
+        for layer in range(L):
+            if seq_parts == 1:
+                ctx.decode_dev(layer, sh.pos, q[layer], out[layer], s)
+                continue
+            ctx.decode_partial_dev(layer, sh.pos, q[layer], part_o[layer], part_ml[layer], s)
+            dist.all_gather_into_tensor(gat_o[layer], part_o[layer])
+            dist.all_gather_into_tensor(gat_ml[layer], part_ml[layer])
+            ctx.lse_merge_dev(seq_parts, sh.n_heads, r0, nr, gat_o[layer, g0], gat_ml[layer, g0], out[layer], s)
+
+    for _ in range(args.warmup):
+        step(stream)
+    torch.cuda.synchronize()
+    ctx.check()
+    # a CUDA graph when the step holds no collective (every rank takes the same branch)
+    graph = None
+    if not args.no_graph and seq_parts == 1:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step(stream)
+
+    def run_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step(stream)
+
+    for _ in range(args.warmup):
+        run_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        run_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    ctx.check()
+    total_bytes = 2 * P * sh.n_kv_heads * hd * 4 * L * args.steps
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        gbs = total_bytes / (ms / 1e3) / 1e9
+        print(json.dumps({
+            "metric": "decode-attn KV GB/s (fp32-equivalent), Llama-3.1-8B shapes, ctx 128K, 32 layers",
+            "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "us_per_layer": round(ms / args.steps * 1e3 / L, 2),
+            "tokens_per_s": round(1e3 / (ms / args.steps), 2), "higher_is_better": True, "scaling": "strong",
+            "dtype": "f32", "data": "synthetic (on-device N(0,1), K x 0.5)",
+            "config": {"workload": "llama31_8b_decode_128k", "head_groups": world // seq_parts,
+                       "seq_parts": seq_parts, "exchange": "NCCL all-gather + LSE merge" if seq_parts > 1 else "none",
+                       "launch": "cuda graph" if graph is not None else "stream"},
+            "frac_of_hbm_per_gpu": round(gbs / world / peak, 4), "peak_kind": peak_kind,
+        }), flush=True)
+    del graph
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def run_kernel_only(args):
     """Decode kernel alone on `--layers` layers of the workload (a small case
     for ncu captures: layers x 64 MiB of KV, still larger than L2)."""
@@ -776,6 +895,8 @@ def main():
     ap.add_argument("--no-raw", action="store_true", help="skip the raw-projection (RoPE on device) measurements")
     ap.add_argument("--no-wo", action="store_true", help="skip the wo projection measurement")
     ap.add_argument("--wo-only", action="store_true", help="wo projection measurement alone (ncu case)")
+    ap.add_argument("--long", action="store_true", help="BASELINE configs[2] (128K context) over --gpus ranks")
+    ap.add_argument("--seq-parts", type=int, default=1, help="--long: sequence parts per head group")
     ap.add_argument("--q8-only", action="store_true", help="Q8_0-cache decode measurement alone")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
     ap.add_argument("--layers", type=int, default=4)
@@ -789,6 +910,8 @@ def main():
         return run_reference_arm(args)
     if args.kernel_only:
         return run_kernel_only(args)
+    if args.long:
+        return run_long(args)
     if args.q8_only:
         import torch
 
