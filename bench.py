@@ -535,10 +535,22 @@ def run_long(args):
     nr = me.kv_head_count * sh.kv_mul
     g0 = me.head_group * seq_parts  # first rank of this head group
 
+    nvlink = seq_parts > 1 and args.xchg == "nvlink"
+    if nvlink:
+        # the members of this head group map each other's exchange regions
+        h = ctx.seq_group_export(seq_parts, me.seq_part)
+        hs = [None] * world
+        dist.all_gather_object(hs, h)
+        ctx.seq_group_import(hs[g0:g0 + seq_parts])
+        ctx.set_overlap(True)
+
     def step(s):
         for layer in range(L):
             if seq_parts == 1:
                 ctx.decode_dev(layer, sh.pos, q[layer], out[layer], s)
+                continue
+            if nvlink:
+                ctx.decode_seq_dev(layer, sh.pos, q[layer], out[layer], s)
                 continue
             ctx.decode_partial_dev(layer, sh.pos, q[layer], part_o[layer], part_ml[layer], s)
             dist.all_gather_into_tensor(gat_o[layer], part_o[layer])
@@ -551,7 +563,7 @@ def run_long(args):
     ctx.check()
     # a CUDA graph when the step holds no collective (every rank takes the same branch)
     graph = None
-    if not args.no_graph and seq_parts == 1:
+    if not args.no_graph and (seq_parts == 1 or nvlink):
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=stream):
             step(stream)
@@ -591,7 +603,10 @@ def run_long(args):
             "tokens_per_s": round(1e3 / (ms / args.steps), 2), "higher_is_better": True, "scaling": "strong",
             "dtype": "f32", "data": "synthetic (on-device N(0,1), K x 0.5)",
             "config": {"workload": "llama31_8b_decode_128k", "head_groups": world // seq_parts,
-                       "seq_parts": seq_parts, "exchange": "NCCL all-gather + LSE merge" if seq_parts > 1 else "none",
+                       "seq_parts": seq_parts,
+                       "exchange": ("none" if seq_parts == 1 else
+                                    "peer reads over NVLink inside the merge kernel (l3p_attn_decode_seq_dev)"
+                                    if nvlink else "NCCL all-gather + LSE merge kernel"),
                        "launch": "cuda graph" if graph is not None else "stream"},
             "frac_of_hbm_per_gpu": round(gbs / world / peak, 4), "peak_kind": peak_kind,
         }), flush=True)
@@ -897,6 +912,8 @@ def main():
     ap.add_argument("--wo-only", action="store_true", help="wo projection measurement alone (ncu case)")
     ap.add_argument("--long", action="store_true", help="BASELINE configs[2] (128K context) over --gpus ranks")
     ap.add_argument("--seq-parts", type=int, default=1, help="--long: sequence parts per head group")
+    ap.add_argument("--xchg", default="nvlink", choices=["nvlink", "nccl"],
+                    help="--long: exchange of the sequence parts' partials")
     ap.add_argument("--q8-only", action="store_true", help="Q8_0-cache decode measurement alone")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
     ap.add_argument("--layers", type=int, default=4)

@@ -288,6 +288,28 @@ int l3p_attn_wo_dev(l3p_attn_ctx* ctx, int layer, const float* x, float* xout, v
 int l3p_attn_step_raw_wo(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
                          const float* v, float* xout);
 
+/* ---- Sequence groups over NVLink -----------------------------------------
+ * The contexts that own the same KV heads and consecutive position ranges of
+ * one sequence (one per GPU; seq_begin/seq_count) form a group of n_parts.
+ * Instead of all-gathering partial triples through a collective library, each
+ * member exports a small exchange region (CUDA IPC), imports the others', and
+ * then one l3p_attn_decode_seq_dev per member per layer computes the partial
+ * attention over its positions, publishes it, waits (bounded; L3P_E_TIMEOUT
+ * through l3p_attn_check if a member never arrives) for the others' and
+ * merges the group's triples, reading the peers' over NVLink.  Every member
+ * must call it for the same layers and positions in the same order.  No
+ * counterpart in the reference. */
+/* Allocate the exchange region and write its cudaIpcMemHandle (64 bytes) to
+ * *handle; n_parts members (2..16), this context is member `part`. */
+int l3p_attn_seq_group_export(l3p_attn_ctx* ctx, int n_parts, int part, void* handle);
+/* Map the other members' regions: handles = the n_parts 64-byte handles of
+ * the group in member order (this context's own entry is ignored). */
+int l3p_attn_seq_group_import(l3p_attn_ctx* ctx, const void* handles);
+/* Decode attention at `pos` over the whole group's positions; out: the owned
+ * q heads' rows of [n_heads*head_dim], on every member. */
+int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* out,
+                            void* stream);
+
 /* Decode attention that allocates nothing.  No counterpart in the reference.
  *
  * For callers that own every byte of device memory themselves -- typically

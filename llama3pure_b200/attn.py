@@ -63,6 +63,9 @@ EXPORTS = (
     "l3p_attn_wo",
     "l3p_attn_wo_dev",
     "l3p_attn_step_raw_wo",
+    "l3p_attn_seq_group_export",
+    "l3p_attn_seq_group_import",
+    "l3p_attn_decode_seq_dev",
     "l3p_attn_decode_noalloc",
     "l3p_attn_noalloc_last_error",
 )
@@ -159,6 +162,9 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_wo": (i, [vp, i, fp, fp]),
         "l3p_attn_wo_dev": (i, [vp, i, fp, fp, vp]),
         "l3p_attn_step_raw_wo": (i, [vp, i, i, fp, fp, fp, fp]),
+        "l3p_attn_seq_group_export": (i, [vp, i, i, vp]),
+        "l3p_attn_seq_group_import": (i, [vp, vp]),
+        "l3p_attn_decode_seq_dev": (i, [vp, i, i, fp, fp, vp]),
         "l3p_attn_decode_noalloc": (i, [C.POINTER(AttnConfig), i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_noalloc_last_error": (C.c_char_p, []),
     }
@@ -410,6 +416,21 @@ class AttnContext:
     def prefill_dev(self, layer, start_pos, n_tok, q, k, v, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_prefill_dev(self.h, layer, start_pos, n_tok, _dev(q), _dev(k), _dev(v), _dev(out),
                                                _stream(stream)), "prefill_dev")
+
+    def seq_group_export(self, n_parts: int, part: int) -> bytes:
+        """This member's 64-byte exchange-region handle (share it with the group)."""
+        h = (C.c_ubyte * 64)()
+        self._ok(self.lib.l3p_attn_seq_group_export(self.h, n_parts, part, C.byref(h)), "seq_group_export")
+        return bytes(h)
+
+    def seq_group_import(self, handles) -> None:
+        """Map the members' regions: `handles` in member order."""
+        buf = b"".join(handles)
+        self._ok(self.lib.l3p_attn_seq_group_import(self.h, C.c_char_p(buf)), "seq_group_import")
+
+    def decode_seq_dev(self, layer, pos, q, out, stream=None) -> None:
+        self._ok(self.lib.l3p_attn_decode_seq_dev(self.h, layer, pos, _dev(q), _dev(out), _stream(stream)),
+                 "decode_seq_dev")
 
     def wo_dev(self, layer, x, xout, stream=None) -> None:
         self._ok(self.lib.l3p_attn_wo_dev(self.h, layer, _dev(x), _dev(xout), _stream(stream)), "wo_dev")

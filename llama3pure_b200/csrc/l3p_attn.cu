@@ -19,6 +19,7 @@
 #include "prefill_tc.cuh"
 #include "rope.cuh"
 #include "wo.cuh"
+#include "seq_xchg.cuh"
 #include "llama3pure_attn.h"
 
 using namespace l3p;
@@ -97,6 +98,14 @@ struct l3p_attn_ctx {
   std::vector<WoLayer> wo;
   float* wo_x = nullptr;
   int wo_ctas_per_sm[6] = {0, 0, 0, 0, 0, 0};  // (Q8_0, Q4_K, Q6_K) x (4, 8 warps)
+  // sequence group over NVLink (l3p_attn_seq_group_*): this context's exchange
+  // region (flags, then per-layer partial slots; seq_xchg.cuh), the members'
+  // regions mapped into this process, and the step counter
+  int xg_parts = 0, xg_part = 0;
+  bool xg_ready = false;
+  uint8_t* xg_region = nullptr;
+  void* xg_peer[kXchgMaxParts] = {};
+  long long xg_slot_floats = 0;
   std::string last_error;
 };
 
@@ -520,6 +529,9 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
     cudaFree(w.wsc);
   }
   cudaFree(ctx->wo_x);
+  for (int p = 0; p < ctx->xg_parts; ++p)
+    if (p != ctx->xg_part && ctx->xg_peer[p]) cudaIpcCloseMemHandle(ctx->xg_peer[p]);
+  cudaFree(ctx->xg_region);
     }
     ctx->pf_img = nullptr;
     ctx->pf_img_floats = 0;
@@ -1255,6 +1267,95 @@ L3P_API int l3p_attn_wo_dev(l3p_attn_ctx* ctx, int layer, const float* x, float*
   if (int rc = check_aligned(ctx, {x, xout})) return rc;
   DeviceScope dev(ctx->cfg.device);
   return launch_wo(ctx, layer, x, xout, pick_stream(ctx, stream));
+}
+
+// ==========================================================================
+// Sequence groups over NVLink
+
+L3P_API int l3p_attn_seq_group_export(l3p_attn_ctx* ctx, int n_parts, int part, void* handle) {
+  if (!ctx || !handle) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (n_parts < 2 || n_parts > kXchgMaxParts || part < 0 || part >= n_parts)
+    return fail(ctx, L3P_E_INVAL, "sequence group of %d parts (2..%d), part %d", n_parts, kXchgMaxParts, part);
+  DeviceScope dev(ctx->cfg.device);
+  if (!ctx->xg_region) {
+    // per layer: [n_heads][hd] partial outputs then [n_heads][2] (m, l), padded to 16 bytes
+    ctx->xg_slot_floats = ((long long)ctx->cfg.n_heads * (ctx->hd + 2) + 3) / 4 * 4;
+    const size_t bytes = kXchgFlagBytes + (size_t)ctx->cfg.n_layers * ctx->xg_slot_floats * sizeof(float);
+    if (cudaMalloc(&ctx->xg_region, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      ctx->xg_region = nullptr;
+      return fail(ctx, L3P_E_NOMEM, "exchange region of %zu bytes", bytes);
+    }
+    L3P_CUDA(ctx, cudaMemset(ctx->xg_region, 0, bytes));
+  }
+  ctx->xg_parts = n_parts;
+  ctx->xg_part = part;
+  ctx->xg_ready = false;
+  L3P_CUDA(ctx, cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), ctx->xg_region));
+  return L3P_OK;
+}
+
+L3P_API int l3p_attn_seq_group_import(l3p_attn_ctx* ctx, const void* handles) {
+  if (!ctx || !handles) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (!ctx->xg_region) return fail(ctx, L3P_E_INVAL, "l3p_attn_seq_group_export has not been called");
+  DeviceScope dev(ctx->cfg.device);
+  const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int p = 0; p < ctx->xg_parts; ++p) {
+    if (p == ctx->xg_part) {
+      ctx->xg_peer[p] = ctx->xg_region;
+      continue;
+    }
+    if (ctx->xg_peer[p]) continue;
+    L3P_CUDA(ctx, cudaIpcOpenMemHandle(&ctx->xg_peer[p], h[p], cudaIpcMemLazyEnablePeerAccess));
+  }
+  ctx->xg_ready = true;
+  return L3P_OK;
+}
+
+L3P_API int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* out,
+                                    void* stream) {
+  if (!ctx || !q || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_layer(ctx, layer)) return rc;
+  if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
+  if (!ctx->xg_ready) return fail(ctx, L3P_E_INVAL, "sequence group not connected (export, then import)");
+  if (int rc = check_aligned(ctx, {q, out})) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  const long long slot = (long long)layer * ctx->xg_slot_floats;
+  float* mine = reinterpret_cast<float*>(ctx->xg_region + kXchgFlagBytes) + slot;
+  // the partial attention over this context's positions, into its own slot
+  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, q, nullptr, mine, mine + (long long)ctx->cfg.n_heads * ctx->hd,
+                             s, nullptr, nullptr, true))
+    return rc;
+  XchgArgs a{};
+  for (int p = 0; p < ctx->xg_parts; ++p) {
+    uint8_t* base = static_cast<uint8_t*>(ctx->xg_peer[p]);
+    a.parts[p] = reinterpret_cast<const float*>(base + kXchgFlagBytes) + slot;
+    a.peer_flags[p] = reinterpret_cast<unsigned*>(base);
+  }
+  a.my_flags = reinterpret_cast<unsigned*>(ctx->xg_region);
+  a.n_parts = ctx->xg_parts;
+  a.part = ctx->xg_part;
+  a.hd = ctx->hd;
+  a.n_heads = ctx->cfg.n_heads;
+  a.row_begin = ctx->cfg.kv_head_begin * ctx->G;
+  a.n_rows = ctx->kvh_count * ctx->G;
+  a.out = out;
+  a.err = ctx->err_dev;
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(1, 1, 1);
+  lc.blockDim = dim3(kXchgThreads, 1, 1);
+  lc.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (ctx->overlap) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+  }
+  L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, seq_merge_kernel, a));
+  ++ctx->launches;
+  return L3P_OK;
 }
 
 L3P_API int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v) {
