@@ -310,6 +310,21 @@ int l3p_attn_seq_group_import(l3p_attn_ctx* ctx, const void* handles);
 int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* out,
                             void* stream);
 
+/* ---- Tensor-parallel wo over NVLink ----------------------------------------
+ * Head-sharded contexts (one per GPU) each hold the wo columns of their heads,
+ * so their projections are partial sums.  Members of a group of n_members
+ * export (64-byte CUDA IPC handle of a small exchange region for `dim`-row
+ * projections) and import each other's regions once; then
+ * l3p_attn_wo_allreduce_dev writes every member's partial straight into every
+ * member's memory (peer stores) and adds the members' partials in member order
+ * -- the all-reduce of xb2 without a collective library, and the same bits on
+ * every member.  Two launches per call; every member calls it for the same
+ * layers in the same order.  No counterpart in the reference. */
+int l3p_attn_tp_group_export(l3p_attn_ctx* ctx, int n_members, int member, int dim, void* handle);
+int l3p_attn_tp_group_import(l3p_attn_ctx* ctx, const void* handles);
+/* xout[dim] = sum over the group of Wo[:, member's columns] . x[member's rows]. */
+int l3p_attn_wo_allreduce_dev(l3p_attn_ctx* ctx, int layer, const float* x, float* xout, void* stream);
+
 /* Decode attention that allocates nothing.  No counterpart in the reference.
  *
  * For callers that own every byte of device memory themselves -- typically

@@ -12,6 +12,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import sys
 
 import numpy as np
 
@@ -66,6 +67,9 @@ EXPORTS = (
     "l3p_attn_seq_group_export",
     "l3p_attn_seq_group_import",
     "l3p_attn_decode_seq_dev",
+    "l3p_attn_tp_group_export",
+    "l3p_attn_tp_group_import",
+    "l3p_attn_wo_allreduce_dev",
     "l3p_attn_decode_noalloc",
     "l3p_attn_noalloc_last_error",
 )
@@ -165,6 +169,9 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_seq_group_export": (i, [vp, i, i, vp]),
         "l3p_attn_seq_group_import": (i, [vp, vp]),
         "l3p_attn_decode_seq_dev": (i, [vp, i, i, fp, fp, vp]),
+        "l3p_attn_tp_group_export": (i, [vp, i, i, i, vp]),
+        "l3p_attn_tp_group_import": (i, [vp, vp]),
+        "l3p_attn_wo_allreduce_dev": (i, [vp, i, fp, fp, vp]),
         "l3p_attn_decode_noalloc": (i, [C.POINTER(AttnConfig), i, i, fp, fp, fp, fp, vp]),
         "l3p_attn_noalloc_last_error": (C.c_char_p, []),
     }
@@ -207,6 +214,18 @@ def _stream(s) -> int | None:
         return None
     h = s if isinstance(s, int) else s.cuda_stream  # torch.cuda.Stream
     return h if h != 0 else CUDA_STREAM_LEGACY
+
+
+def _dev_stream(s) -> int | None:
+    """Stream of a *_dev call: the given one, else torch's current stream when
+    torch drives CUDA in this process (the device tensors were produced there,
+    so the call is ordered after them), else the context's own stream."""
+    if s is not None:
+        return _stream(s)
+    torch = sys.modules.get("torch")
+    if torch is not None and torch.cuda.is_initialized():
+        return _stream(torch.cuda.current_stream())
+    return None
 
 
 class AttnContext:
@@ -391,31 +410,31 @@ class AttnContext:
         return k.value, v.value
 
     def kv_append_dev(self, layer, pos, k, v, stream=None) -> None:
-        self._ok(self.lib.l3p_attn_kv_append_dev(self.h, layer, pos, _dev(k), _dev(v), _stream(stream)),
+        self._ok(self.lib.l3p_attn_kv_append_dev(self.h, layer, pos, _dev(k), _dev(v), _dev_stream(stream)),
                  "kv_append_dev")
 
     def decode_dev(self, layer, pos, q, out, stream=None) -> None:
-        self._ok(self.lib.l3p_attn_decode_dev(self.h, layer, pos, _dev(q), _dev(out), _stream(stream)), "decode_dev")
+        self._ok(self.lib.l3p_attn_decode_dev(self.h, layer, pos, _dev(q), _dev(out), _dev_stream(stream)), "decode_dev")
 
     def step_dev(self, layer, pos, q, k_row, v_row, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_step_dev(self.h, layer, pos, _dev(q), _dev(k_row), _dev(v_row), _dev(out),
-                                            _stream(stream)), "step_dev")
+                                            _dev_stream(stream)), "step_dev")
 
     def decode_layers_dev(self, layer0, n_layers, pos, q, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_decode_layers_dev(self.h, layer0, n_layers, pos, _dev(q), _dev(out),
-                                                     _stream(stream)), "decode_layers_dev")
+                                                     _dev_stream(stream)), "decode_layers_dev")
 
     def decode_partial_dev(self, layer, pos, q, part_o, part_ml, stream=None) -> None:
         self._ok(self.lib.l3p_attn_decode_partial_dev(self.h, layer, pos, _dev(q), _dev(part_o), _dev(part_ml),
-                                                      _stream(stream)), "decode_partial_dev")
+                                                      _dev_stream(stream)), "decode_partial_dev")
 
     def lse_merge_dev(self, n_parts, rows_per_part, row_begin, n_rows, parts_o, parts_ml, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_lse_merge_dev(self.h, n_parts, rows_per_part, row_begin, n_rows, _dev(parts_o),
-                                                 _dev(parts_ml), _dev(out), _stream(stream)), "lse_merge_dev")
+                                                 _dev(parts_ml), _dev(out), _dev_stream(stream)), "lse_merge_dev")
 
     def prefill_dev(self, layer, start_pos, n_tok, q, k, v, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_prefill_dev(self.h, layer, start_pos, n_tok, _dev(q), _dev(k), _dev(v), _dev(out),
-                                               _stream(stream)), "prefill_dev")
+                                               _dev_stream(stream)), "prefill_dev")
 
     def seq_group_export(self, n_parts: int, part: int) -> bytes:
         """This member's 64-byte exchange-region handle (share it with the group)."""
@@ -429,23 +448,35 @@ class AttnContext:
         self._ok(self.lib.l3p_attn_seq_group_import(self.h, C.c_char_p(buf)), "seq_group_import")
 
     def decode_seq_dev(self, layer, pos, q, out, stream=None) -> None:
-        self._ok(self.lib.l3p_attn_decode_seq_dev(self.h, layer, pos, _dev(q), _dev(out), _stream(stream)),
+        self._ok(self.lib.l3p_attn_decode_seq_dev(self.h, layer, pos, _dev(q), _dev(out), _dev_stream(stream)),
                  "decode_seq_dev")
 
+    def tp_group_export(self, n_members: int, member: int, dim: int) -> bytes:
+        h = (C.c_ubyte * 64)()
+        self._ok(self.lib.l3p_attn_tp_group_export(self.h, n_members, member, dim, C.byref(h)), "tp_group_export")
+        return bytes(h)
+
+    def tp_group_import(self, handles) -> None:
+        self._ok(self.lib.l3p_attn_tp_group_import(self.h, C.c_char_p(b"".join(handles))), "tp_group_import")
+
+    def wo_allreduce_dev(self, layer, x, xout, stream=None) -> None:
+        self._ok(self.lib.l3p_attn_wo_allreduce_dev(self.h, layer, _dev(x), _dev(xout), _dev_stream(stream)),
+                 "wo_allreduce_dev")
+
     def wo_dev(self, layer, x, xout, stream=None) -> None:
-        self._ok(self.lib.l3p_attn_wo_dev(self.h, layer, _dev(x), _dev(xout), _stream(stream)), "wo_dev")
+        self._ok(self.lib.l3p_attn_wo_dev(self.h, layer, _dev(x), _dev(xout), _dev_stream(stream)), "wo_dev")
 
     def rope_dev(self, layer, pos0, n_tok, q, k, q_out, k_out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_rope_dev(self.h, layer, pos0, n_tok, _dev(q), _dev(k), _dev(q_out), _dev(k_out),
-                                            _stream(stream)), "rope_dev")
+                                            _dev_stream(stream)), "rope_dev")
 
     def step_raw_dev(self, layer, pos, q, k_row, v_row, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_step_raw_dev(self.h, layer, pos, _dev(q), _dev(k_row), _dev(v_row), _dev(out),
-                                                _stream(stream)), "step_raw_dev")
+                                                _dev_stream(stream)), "step_raw_dev")
 
     def prefill_raw_dev(self, layer, start_pos, n_tok, q, k, v, out, stream=None) -> None:
         self._ok(self.lib.l3p_attn_prefill_raw_dev(self.h, layer, start_pos, n_tok, _dev(q), _dev(k), _dev(v),
-                                                   _dev(out), _stream(stream)), "prefill_raw_dev")
+                                                   _dev(out), _dev_stream(stream)), "prefill_raw_dev")
 
 
 def decode_noalloc(cfg: AttnConfig, layer: int, pos: int, k_cache, v_cache, q, out, stream=None, lib=None) -> None:
@@ -454,7 +485,7 @@ def decode_noalloc(cfg: AttnConfig, layer: int, pos: int, k_cache, v_cache, q, o
     array; overlapping calls race)."""
     lib = lib or load_library()
     rc = lib.l3p_attn_decode_noalloc(C.byref(cfg), layer, pos, _dev(k_cache), _dev(v_cache), _dev(q), _dev(out),
-                                     _stream(stream))
+                                     _dev_stream(stream))
     if rc != L3P_OK:
         msg = lib.l3p_attn_noalloc_last_error()
         raise AttnError(rc, f"decode_noalloc: {msg.decode() if msg else ''}")

@@ -106,6 +106,12 @@ struct l3p_attn_ctx {
   uint8_t* xg_region = nullptr;
   void* xg_peer[kXchgMaxParts] = {};
   long long xg_slot_floats = 0;
+  // tensor-parallel group over NVLink (l3p_attn_tp_group_*): flags, step
+  // counter, then two slots of [members][dim] partial projections
+  int tp_members = 0, tp_member = 0, tp_dim = 0;
+  bool tp_ready = false;
+  uint8_t* tp_region = nullptr;
+  void* tp_peer[kXchgMaxParts] = {};
   std::string last_error;
 };
 
@@ -532,6 +538,9 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
   for (int p = 0; p < ctx->xg_parts; ++p)
     if (p != ctx->xg_part && ctx->xg_peer[p]) cudaIpcCloseMemHandle(ctx->xg_peer[p]);
   cudaFree(ctx->xg_region);
+  for (int p = 0; p < ctx->tp_members; ++p)
+    if (p != ctx->tp_member && ctx->tp_peer[p]) cudaIpcCloseMemHandle(ctx->tp_peer[p]);
+  cudaFree(ctx->tp_region);
     }
     ctx->pf_img = nullptr;
     ctx->pf_img_floats = 0;
@@ -689,9 +698,17 @@ int check_rope(l3p_attn_ctx* ctx) {
 }
 
 // The wo GEMV of `layer` (wo.cuh): y[dim] = W[:, owned columns] . x[owned columns].
-int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream_t s) {
+int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream_t s, bool tp = false) {
   const l3p_attn_ctx::WoLayer& L = ctx->wo[layer];
   WoArgs a{};
+  if (tp) {
+    // partial rows into every member's exchange slots (seq_xchg.cuh)
+    a.tp_members = ctx->tp_members;
+    a.tp_member = ctx->tp_member;
+    for (int m = 0; m < ctx->tp_members; ++m)
+      a.tp_slots[m] = reinterpret_cast<float*>(static_cast<uint8_t*>(ctx->tp_peer[m]) + kXchgFlagBytes);
+    a.tp_step = reinterpret_cast<const unsigned*>(ctx->tp_region) + 16;
+  }
   a.w = L.w;
   a.wsc = L.wsc;
   a.row_bytes = L.row_bytes;
@@ -1354,6 +1371,84 @@ L3P_API int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const
     lc.numAttrs = 1;
   }
   L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, seq_merge_kernel, a));
+  ++ctx->launches;
+  return L3P_OK;
+}
+
+L3P_API int l3p_attn_tp_group_export(l3p_attn_ctx* ctx, int n_members, int member, int dim, void* handle) {
+  if (!ctx || !handle) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (n_members < 2 || n_members > kXchgMaxParts || member < 0 || member >= n_members || dim <= 0 || dim % 4)
+    return fail(ctx, L3P_E_INVAL, "tensor-parallel group of %d members (2..%d), member %d, dim %d (multiple of 4)",
+                n_members, kXchgMaxParts, member, dim);
+  DeviceScope dev(ctx->cfg.device);
+  if (ctx->tp_region && (ctx->tp_members != n_members || ctx->tp_dim != dim))
+    return fail(ctx, L3P_E_INVAL, "the tensor-parallel group is already set up with another shape");
+  if (!ctx->tp_region) {
+    const size_t bytes = kXchgFlagBytes + 2ull * n_members * dim * sizeof(float);
+    if (cudaMalloc(&ctx->tp_region, bytes) != cudaSuccess) {
+      cudaGetLastError();
+      ctx->tp_region = nullptr;
+      return fail(ctx, L3P_E_NOMEM, "tensor-parallel exchange region of %zu bytes", bytes);
+    }
+    L3P_CUDA(ctx, cudaMemset(ctx->tp_region, 0, bytes));
+  }
+  ctx->tp_members = n_members;
+  ctx->tp_member = member;
+  ctx->tp_dim = dim;
+  ctx->tp_ready = false;
+  L3P_CUDA(ctx, cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), ctx->tp_region));
+  return L3P_OK;
+}
+
+L3P_API int l3p_attn_tp_group_import(l3p_attn_ctx* ctx, const void* handles) {
+  if (!ctx || !handles) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (!ctx->tp_region) return fail(ctx, L3P_E_INVAL, "l3p_attn_tp_group_export has not been called");
+  DeviceScope dev(ctx->cfg.device);
+  const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int p = 0; p < ctx->tp_members; ++p) {
+    if (p == ctx->tp_member) {
+      ctx->tp_peer[p] = ctx->tp_region;
+      continue;
+    }
+    if (ctx->tp_peer[p]) continue;
+    L3P_CUDA(ctx, cudaIpcOpenMemHandle(&ctx->tp_peer[p], h[p], cudaIpcMemLazyEnablePeerAccess));
+  }
+  ctx->tp_ready = true;
+  return L3P_OK;
+}
+
+L3P_API int l3p_attn_wo_allreduce_dev(l3p_attn_ctx* ctx, int layer, const float* x, float* xout, void* stream) {
+  if (!ctx || !x || !xout) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
+  if (int rc = check_wo(ctx, layer)) return rc;
+  if (!ctx->tp_ready) return fail(ctx, L3P_E_INVAL, "tensor-parallel group not connected (export, then import)");
+  if (ctx->wo[layer].rows != ctx->tp_dim)
+    return fail(ctx, L3P_E_INVAL, "wo of layer %d has %d rows, the group was set up for %d", layer,
+                ctx->wo[layer].rows, ctx->tp_dim);
+  if (int rc = check_aligned(ctx, {x, xout})) return rc;
+  DeviceScope dev(ctx->cfg.device);
+  cudaStream_t s = pick_stream(ctx, stream);
+  if (int rc = launch_wo(ctx, layer, x, nullptr, s, true)) return rc;
+  TpArgs a{};
+  for (int m = 0; m < ctx->tp_members; ++m) a.peer_flags[m] = static_cast<unsigned*>(ctx->tp_peer[m]);
+  a.my_flags = reinterpret_cast<unsigned*>(ctx->tp_region);
+  a.my_slots = reinterpret_cast<const float*>(ctx->tp_region + kXchgFlagBytes);
+  a.n_members = ctx->tp_members;
+  a.member = ctx->tp_member;
+  a.dim = ctx->tp_dim;
+  a.out = xout;
+  a.err = ctx->err_dev;
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = dim3(1, 1, 1);
+  lc.blockDim = dim3(kTpThreads, 1, 1);
+  lc.stream = s;
+  cudaLaunchAttribute attr[1];
+  if (ctx->overlap) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+  }
+  L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, tp_sum_kernel, a));
   ++ctx->launches;
   return L3P_OK;
 }

@@ -56,6 +56,12 @@ struct WoArgs {
   int wc;               // column groups per CTA (power of two <= warps)
   const float* x;       // owned columns of the attention output (x[0] = column q_head0*hd)
   float* y;             // [rows]
+  // tensor-parallel group (seq_xchg.cuh): instead of y, store the partial into
+  // row band `member` of slot (step+1)&1 of every member's exchange slots,
+  // step = *tp_step (read after griddepcontrol.wait)
+  int tp_members, tp_member;
+  float* tp_slots[16];  // every member's [2][tp_members][rows] slots (own included)
+  const unsigned* tp_step;
 };
 
 // Byte i (0..3) of w as the float 2^23 + byte: exact for every byte.
@@ -274,10 +280,21 @@ __global__ void __launch_bounds__(NW * 32) wo_gemv_kernel(const WoArgs p) {
     }
   }
   __syncthreads();
+  if (p.tp_members == 0) {
+    for (int r = threadIdx.x; r < r_end - r_begin; r += blockDim.x) {
+      float s = 0.f;
+      for (int c = 0; c < p.wc; ++c) s += red[c * p.rows_per_cta + r];
+      p.y[r_begin + r] = s;
+    }
+    return;
+  }
+  // tensor-parallel: the row band of this member in every member's next slot
+  const unsigned next = (*p.tp_step + 1u) & 1u;
+  const size_t band = ((size_t)next * p.tp_members + p.tp_member) * p.rows + r_begin;
   for (int r = threadIdx.x; r < r_end - r_begin; r += blockDim.x) {
     float s = 0.f;
     for (int c = 0; c < p.wc; ++c) s += red[c * p.rows_per_cta + r];
-    p.y[r_begin + r] = s;
+    for (int m = 0; m < p.tp_members; ++m) p.tp_slots[m][band + r] = s;
   }
 }
 
