@@ -395,6 +395,44 @@ def run_ours(args):
             ctx.check()
             raw["with_wo_q8_0_us_per_layer"] = round(r0.elapsed_time(r1) / args.steps * 1e3 / L, 3)
             del bgraph
+        if not args.no_wo and world > 1:
+            # the tensor-parallel block: every rank's partial wo summed over NVLink (Q8_0, 4096 x 4096)
+            from llama3pure_b200.synth import wo_weights
+
+            dim = sh.n_heads * sh.head_dim
+            w = wo_weights(8, dim, dim, seed=3)
+            for layer in range(L):
+                ctx.set_wo(layer, 8, w)
+            h = ctx.tp_group_export(world, rank, dim)
+            hs = [None] * world
+            dist.all_gather_object(hs, h)
+            ctx.tp_group_import(hs)
+            xb2 = torch.zeros((L, dim), device="cuda")
+            bgraph = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(rstream):
+                ctx.set_stream(rstream)
+                with torch.cuda.graph(bgraph, stream=rstream):
+                    for layer in range(L):
+                        ctx.step_raw_dev(layer, sh.pos, q[layer], knew[layer], vnew[layer], out[layer], rstream)
+                        ctx.wo_allreduce_dev(layer, out[layer], xb2[layer], rstream)
+            stream.wait_stream(rstream)
+            ctx.set_stream(stream)
+            for _ in range(max(3, args.warmup)):
+                bgraph.replay()
+            torch.cuda.synchronize()
+            dist.barrier()
+            torch.cuda.synchronize()
+            r0.record(stream)
+            for _ in range(args.steps):
+                bgraph.replay()
+            r1.record(stream)
+            torch.cuda.synchronize()
+            ctx.check()
+            t = torch.tensor([r0.elapsed_time(r1)], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            raw["with_wo_allreduce_q8_0_us_per_layer"] = round(t.item() / args.steps * 1e3 / L, 3)
+            raw["wo_allreduce"] = "partial wo per rank, summed over NVLink peer stores (l3p_attn_wo_allreduce_dev)"
+            del bgraph
     if clocks:
         clk = clocks.stop()
     else:
