@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -63,6 +65,12 @@ struct l3p_attn_ctx {
   // device error word in mapped pinned host memory
   int* err_host = nullptr;
   int* err_dev = nullptr;
+  // completion word of the host-pointer decode calls (mapped pinned memory,
+  // written by the launch's last output writer) and its device-side counter
+  unsigned* done_host = nullptr;
+  unsigned* done_dev = nullptr;
+  unsigned* done_ctr = nullptr;
+  unsigned done_seq = 0;
   long long launches = 0;
   // clusters of 2^i CTAs of this context's decode kernel that fit on the GPU at once
   int max_clusters[5] = {0, 0, 0, 0, 0};
@@ -370,7 +378,7 @@ int read_err(l3p_attn_ctx* ctx) {
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
                   const float* q, float* out, float* part_o, float* part_ml, cudaStream_t s,
                   const float* k_new = nullptr, const float* v_new = nullptr, bool allow_overlap = false,
-                  bool new_pending = false) {
+                  bool new_pending = false, bool signal_host = false) {
   const KernelInfo ki = kernel_for(ctx->hd, ctx->GT, ctx->q8);
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
   if (ctx->q8 && k_new) return fail(ctx, L3P_E_INVAL, "fused append needs an fp32 cache");
@@ -424,6 +432,13 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   a.swa_pattern = ctx->cfg.swa_pattern;
   a.partial = part_o != nullptr;
   a.new_pending = new_pending ? 1 : 0;
+  if (signal_host && nz <= 65535) {
+    // the host waits on done_host instead of synchronising the stream
+    a.done_ctr = ctx->done_ctr;
+    a.done_flag = ctx->done_dev;
+    a.done_value = ++ctx->done_seq;
+    a.done_writers = (unsigned)(units * (plan.cluster > 1 ? plan.cluster : 1));
+  }
 
   for (int z0 = 0; z0 < nz; z0 += 65535) {
     const int zc = std::min(nz - z0, 65535);
@@ -887,6 +902,14 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
     return bail(L3P_E_CUDA, "error word allocation failed");
   }
   *ctx->err_host = 0;
+  if (cudaHostAlloc(&ctx->done_host, sizeof(unsigned), cudaHostAllocMapped) != cudaSuccess ||
+      cudaHostGetDevicePointer(&ctx->done_dev, ctx->done_host, 0) != cudaSuccess ||
+      cudaMalloc(&ctx->done_ctr, sizeof(unsigned)) != cudaSuccess) {
+    cudaGetLastError();
+    return bail(L3P_E_CUDA, "completion word allocation failed");
+  }
+  *ctx->done_host = 0;
+  if (cudaMemset(ctx->done_ctr, 0, sizeof(unsigned)) != cudaSuccess) return bail(L3P_E_CUDA, "counter memset failed");
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(L3P_E_CUDA, "stream creation failed");
   ctx->own_stream = true;
@@ -955,6 +978,8 @@ L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
   cudaFree(ctx->pf_img);
   if (ctx->hst) cudaFreeHost(ctx->hst);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
+  if (ctx->done_host) cudaFreeHost(ctx->done_host);
+  cudaFree(ctx->done_ctr);
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -1472,6 +1497,23 @@ int finish_host_call(l3p_attn_ctx* ctx) {
   return read_err(ctx);
 }
 
+// Wait for a decode launched with signal_host: spin on the mapped completion
+// word (the launch's last output writer stores done_seq into it) instead of a
+// stream synchronisation, which costs a few microseconds more per call.  A
+// launch that failed never stores it: after 10 s the stream is synchronised
+// and its error reported.
+int finish_host_decode(l3p_attn_ctx* ctx) {
+  const unsigned want = ctx->done_seq;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (unsigned long long i = 1;; ++i) {
+    if (*reinterpret_cast<volatile unsigned*>(ctx->done_host) == want) break;
+    if ((i & 4095u) == 0 && std::chrono::steady_clock::now() - t0 > std::chrono::seconds(10))
+      return finish_host_call(ctx);
+  }
+  std::atomic_thread_fence(std::memory_order_acquire);
+  return read_err(ctx);
+}
+
 // rows of the q/out arrays this context owns: [row_lo, row_hi) in head_dim units
 void owned_rows(const l3p_attn_ctx* ctx, int* row_lo, int* row_hi) {
   *row_lo = ctx->cfg.kv_head_begin * ctx->G;
@@ -1508,10 +1550,11 @@ L3P_API int l3p_attn_decode(l3p_attn_ctx* ctx, int layer, int pos, const float* 
   const size_t row0 = (size_t)r0 * ctx->hd, nrow = (size_t)(r1 - r0) * ctx->hd;
   memcpy(ctx->hst + row0, q + row0, nrow * 4);
   L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf + row0, ctx->hst + row0, nrow * 4, cudaMemcpyHostToDevice, ctx->stream));
-  // the kernel writes the output into mapped pinned memory
-  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + qd, nullptr, nullptr, ctx->stream))
+  // the kernel writes the output into mapped pinned memory and signals it
+  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + qd, nullptr, nullptr, ctx->stream,
+                             nullptr, nullptr, false, false, true))
     return rc;
-  if (int rc = finish_host_call(ctx)) return rc;
+  if (int rc = finish_host_decode(ctx)) return rc;
   memcpy(out + row0, ctx->hst + qd + row0, nrow * 4);
   return L3P_OK;
 }
@@ -1537,13 +1580,14 @@ L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q,
   L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, ctx->hst, in * 4, cudaMemcpyHostToDevice, ctx->stream));
   if (ctx->q8) {
     if (int rc = launch_append(ctx, layer, pos, 1, ctx->st_buf + qd, ctx->st_buf + qd + kvd, ctx->stream)) return rc;
-    if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr, ctx->stream))
+    if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr, ctx->stream,
+                               nullptr, nullptr, false, false, true))
       return rc;
   } else if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr,
-                                    ctx->stream, ctx->st_buf + qd, ctx->st_buf + qd + kvd)) {
+                                    ctx->stream, ctx->st_buf + qd, ctx->st_buf + qd + kvd, false, false, true)) {
     return rc;
   }
-  if (int rc = finish_host_call(ctx)) return rc;
+  if (int rc = finish_host_decode(ctx)) return rc;
   memcpy(out + row0, ctx->hst + in + row0, nrow * 4);
   return L3P_OK;
 }
