@@ -833,8 +833,12 @@ def run_q8(args, torch, layers: int = 16):
     sgr = graph_of(lambda cs: [ctx.step_dev(i, sh.pos, q[i], knew[i], vnew[i], out[i], cs) for i in range(L)])
     launches = ctx.launch_count() - n0
     step_us = timed(sgr, max(args.steps, 5)) * 1e3 / L
+    # the same step with programmatic dependent launch (as the headline step)
+    ctx.set_overlap(not args.no_overlap)
+    ogr = graph_of(lambda cs: [ctx.step_dev(i, sh.pos, q[i], knew[i], vnew[i], out[i], cs) for i in range(L)])
+    step_overlap_us = timed(ogr, max(args.steps, 5)) * 1e3 / L
     ctx.check()
-    del kgr, sgr
+    del kgr, sgr, ogr
     raw_us = None
     if not getattr(args, "no_raw", False):
         ctx.set_rope()
@@ -849,7 +853,8 @@ def run_q8(args, torch, layers: int = 16):
             "bytes_per_layer": nbytes, "kernel_us": round(kern_us, 3),
             "kernel_gbs": round(nbytes / kern_us / 1e3, 1), "frac_of_hbm": round(nbytes / kern_us / 1e3 / peak, 4),
             "peak_kind": peak_kind, "step_us_per_layer": round(step_us, 3),
-            "step_launches_per_layer": launches // L, "raw_step_us_per_layer": raw_us,
+            "step_launches_per_layer": launches // L, "step_overlap_us_per_layer": round(step_overlap_us, 3),
+            "raw_step_us_per_layer": raw_us,
             "tokens_per_s_32_layers": round(1e6 / (step_us * 32), 1)}
 
 

@@ -10,6 +10,7 @@ import glob
 import os
 import shutil
 import subprocess
+import tempfile
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
@@ -41,19 +42,30 @@ def up_to_date(out: str = LIB_PATH) -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, out: str = LIB_PATH, extra: list[str] | None = None) -> str:
-    """Build the shared library if any source is newer; return its path."""
+    """Build the shared library if any source is newer; return its path.  The
+    translation units compile in parallel into a temporary directory, then
+    link into `out`."""
     if not force and up_to_date(out):
         return out
     units = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    cmd = [
-        nvcc(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17",
-        "-Xcompiler", "-fPIC,-fvisibility=hidden", "-shared",
-        "-I", INCLUDE, "-I", CSRC,
-        "-o", out + ".tmp", *units, *(extra or []),
-    ]
-    if verbose:
-        print(" ".join(cmd), flush=True)
-    subprocess.run(cmd, check=True)
+    flags = [*ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+             "-I", INCLUDE, "-I", CSRC, *(extra or [])]
+    with tempfile.TemporaryDirectory() as tmp:
+        objs, procs = [], []
+        for u in units:
+            obj = os.path.join(tmp, os.path.basename(u) + ".o")
+            cmd = [nvcc(), *flags, "-c", u, "-o", obj]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            procs.append(subprocess.Popen(cmd))
+            objs.append(obj)
+        failed = [u for u, p in zip(units, procs) if p.wait() != 0]
+        if failed:
+            raise subprocess.CalledProcessError(1, f"nvcc -c {' '.join(failed)}")
+        link = [nvcc(), *ARCH_FLAGS, "-shared", "-o", out + ".tmp", *objs]
+        if verbose:
+            print(" ".join(link), flush=True)
+        subprocess.run(link, check=True)
     os.replace(out + ".tmp", out)
     return out
 

@@ -1,0 +1,183 @@
+// ctx.h -- the library context and the helpers its translation units share
+// (l3p_attn.cu, l3p_preattn.cu, l3p_wo.cu, l3p_groups.cu).  Private: not part
+// of the C ABI.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <initializer_list>
+#include <string>
+#include <vector>
+
+#include "limits.cuh"
+#include "llama3pure_attn.h"
+
+#define L3P_API extern "C" __attribute__((visibility("default")))
+
+struct l3p_attn_ctx {
+  l3p_attn_config cfg{};
+  int hd = 0, G = 0, GT = 1, n_hg = 1;
+  int kvh_count = 0, seq_count = 0;
+  float scale = 1.f;
+  int num_sms = 148;
+  float* kc = nullptr;  // fp32 cache: [n_layers][kvh_count][seq_count][hd]
+  float* vc = nullptr;
+  bool q8 = false;      // Q8_0 cache (kv_format L3P_KV_Q8_0) instead of kc/vc:
+  int8_t* k8 = nullptr;  //   int8 values, same layout as kc
+  int8_t* v8 = nullptr;
+  uint16_t* ksc = nullptr;  //   fp16 block scales [n_layers][kvh_count][seq_count][hd/32]
+  uint16_t* vsc = nullptr;
+  long long layer_elems = 0, head_elems = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  // split-K scratch: partial outputs, (m, l) pairs and per-unit tickets
+  float* ws_o = nullptr;
+  float* ws_ml = nullptr;
+  unsigned* counters = nullptr;
+  long long ws_o_floats = 0, ws_ml_floats = 0, n_counters = 0;
+  // device staging for the host-pointer entry points
+  float* st_buf = nullptr;
+  size_t st_floats = 0;
+  // pinned, device-mapped host staging for the single-token host calls: the
+  // inputs cross in one copy and the kernel writes the output straight into it
+  float* hst = nullptr;
+  float* hst_dev = nullptr;
+  size_t hst_floats = 0;
+  // prefill: pre-split K/V tile images for the tensor-core kernel
+  float* pf_img = nullptr;
+  size_t pf_img_floats = 0;
+  bool prefill_tc = false;  // head_dim 128 uses the tcgen05 kernel (L3P_PREFILL_PATH=ffma forces the other)
+  int prefill_cg = 1;       // CTAs per tcgen05 prefill unit: 2 (CTA pairs) when the GQA group is even
+  // device error word in mapped pinned host memory
+  int* err_host = nullptr;
+  int* err_dev = nullptr;
+  // completion word of the host-pointer decode calls (mapped pinned memory,
+  // written by the launch's last output writer) and its device-side counter
+  unsigned* done_host = nullptr;
+  unsigned* done_dev = nullptr;
+  unsigned* done_ctr = nullptr;
+  unsigned done_seq = 0;
+  long long launches = 0;
+  // clusters of 2^i CTAs of this context's decode kernel that fit on the GPU at once
+  int max_clusters[5] = {0, 0, 0, 0, 0};
+  // L3P_DECODE_PLAN="nsplit:cluster" pins the decomposition (tests use it to
+  // exercise every merge path); 0 = automatic
+  int force_nsplit = 0, force_cluster = 0;
+  // overlap mode: decode launches carry programmatic stream serialisation
+  bool overlap = false;
+  // split scratch is used in kScratchSlots rotating slices so that launches
+  // overlapping on the GPU never share partials or tickets
+  unsigned long long launch_seq = 0;
+  // pre-attention step (l3p_attn_set_rope): (cos, sin) per position and pair,
+  // [seq_len][hd/2], for dense layers and for Gemma3 SWA layers (the same
+  // array when the model has one table), QK-norm weights [2][n_layers][hd]
+  // (q then k; null = no QK-norm) and the rotated rows of the raw entry points
+  float2* rope_tab = nullptr;
+  float2* rope_tab_swa = nullptr;
+  float* qk_norm = nullptr;
+  float rms_eps = 1e-5f;
+  float* rope_buf = nullptr;
+  size_t rope_buf_floats = 0;
+  // wo projection (l3p_attn_set_wo): per layer the owned columns of the
+  // weight rows in the device layout of wo.cuh, and the attention output
+  // buffer of the combined host call
+  struct WoLayer {
+    int type = 0;  // 0 = not set
+    int rows = 0;
+    long long row_bytes = 0;
+    int sc_stride = 0;  // bytes per row of Q8_0 scales
+    uint8_t* w = nullptr;
+    uint8_t* wsc = nullptr;
+  };
+  std::vector<WoLayer> wo;
+  float* wo_x = nullptr;
+  int wo_ctas_per_sm[6] = {0, 0, 0, 0, 0, 0};  // (Q8_0, Q4_K, Q6_K) x (4, 8 warps)
+  // sequence group over NVLink (l3p_attn_seq_group_*): this context's exchange
+  // region (flags, then per-layer partial slots; seq_xchg.cuh), the members'
+  // regions mapped into this process, and the step counter
+  int xg_parts = 0, xg_part = 0;
+  bool xg_ready = false;
+  uint8_t* xg_region = nullptr;
+  void* xg_peer[l3p::kXchgMaxParts] = {};
+  long long xg_slot_floats = 0;
+  // tensor-parallel group over NVLink (l3p_attn_tp_group_*): flags, step
+  // counter, then two slots of [members][dim] partial projections
+  int tp_members = 0, tp_member = 0, tp_dim = 0;
+  bool tp_ready = false;
+  uint8_t* tp_region = nullptr;
+  void* tp_peer[l3p::kXchgMaxParts] = {};
+  std::string last_error;
+};
+
+namespace l3p_api {
+
+// Records the message of a failing entry point and returns its code.
+inline int fail(l3p_attn_ctx* ctx, int code, const char* fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->last_error = buf;
+  }
+  return code;
+}
+
+#define L3P_CUDA(ctx, call)                                                                  \
+  do {                                                                                       \
+    cudaError_t e_ = (call);                                                                 \
+    if (e_ != cudaSuccess)                                                                   \
+      return l3p_api::fail((ctx), L3P_E_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
+                           __LINE__);                                                        \
+  } while (0)
+
+// Makes the context's device current for the duration of an entry point and
+// restores the caller's device afterwards.
+struct DeviceScope {
+  int prev = -1;
+  bool changed = false;
+  explicit DeviceScope(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) changed = cudaSetDevice(dev) == cudaSuccess;
+  }
+  ~DeviceScope() {
+    if (changed) cudaSetDevice(prev);
+  }
+};
+
+inline cudaStream_t pick_stream(l3p_attn_ctx* ctx, void* s) { return s ? static_cast<cudaStream_t>(s) : ctx->stream; }
+
+// l3p_attn.cu
+int check_aligned(l3p_attn_ctx* ctx, std::initializer_list<const void*> ptrs);
+int ensure_staging(l3p_attn_ctx* ctx, size_t floats);
+int ensure_host_staging(l3p_attn_ctx* ctx, size_t floats);
+int check_layer(l3p_attn_ctx* ctx, int layer);
+int check_pos_full(l3p_attn_ctx* ctx, int pos);
+int read_err(l3p_attn_ctx* ctx);
+int finish_host_call(l3p_attn_ctx* ctx);
+int finish_host_decode(l3p_attn_ctx* ctx);
+void owned_rows(const l3p_attn_ctx* ctx, int* row_lo, int* row_hi);
+// Decode core shared by the single-layer, multi-layer, prefill and partial
+// entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
+int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz, const float* q,
+                  float* out, float* part_o, float* part_ml, cudaStream_t s, const float* k_new = nullptr,
+                  const float* v_new = nullptr, bool allow_overlap = false, bool new_pending = false,
+                  bool signal_host = false);
+int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v, cudaStream_t s);
+int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
+                      cudaStream_t s);
+
+// l3p_preattn.cu
+int check_rope(l3p_attn_ctx* ctx);
+int step_raw_core(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k, const float* v, float* out,
+                  cudaStream_t s, bool allow_overlap);
+int prefill_raw_core(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, const float* k,
+                     const float* v, float* out, cudaStream_t s);
+
+// l3p_wo.cu
+int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream_t s, bool tp = false);
+int check_wo(l3p_attn_ctx* ctx, int layer);
+
+}  // namespace l3p_api

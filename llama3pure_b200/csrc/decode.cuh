@@ -768,7 +768,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
 
 // Token K/V rows -> head-major cache rows.  k, v: [n_tok][src_stride] with
 // KV head h at offset h*HD; grid (n_tok, kvh_count), HD/4 threads.
-__global__ void kv_append_kernel(float* __restrict__ kc, float* __restrict__ vc, long long head_stride,
+static __global__ void kv_append_kernel(float* __restrict__ kc, float* __restrict__ vc, long long head_stride,
                                  int hd, const float* __restrict__ k, const float* __restrict__ v,
                                  long long src_stride, int kv_head_begin, int row0) {
   const int tok = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
@@ -780,7 +780,7 @@ __global__ void kv_append_kernel(float* __restrict__ kc, float* __restrict__ vc,
 
 // Log-sum-exp merge of n_parts partial triples.  parts_o: [n_parts][rows][hd],
 // parts_ml: [n_parts][rows][2]; one CTA per output row.
-__global__ void lse_merge_kernel(int n_parts, int rows, int row_begin, int hd, const float* __restrict__ parts_o,
+static __global__ void lse_merge_kernel(int n_parts, int rows, int row_begin, int hd, const float* __restrict__ parts_o,
                                  const float* __restrict__ parts_ml, float* __restrict__ out) {
   const int row = row_begin + blockIdx.x;
   float M = -INFINITY;

@@ -104,7 +104,7 @@ __global__ void kv_append_q8_kernel(int8_t* __restrict__ k8, int8_t* __restrict_
 
 // Cache rows -> the reference's 34-byte blocks (fp16 scale little-endian, then
 // 32 int8), [rows][HD/32 * 34] bytes; one thread per block.
-__global__ void q8_blocks_kernel(const int8_t* __restrict__ d8, const uint16_t* __restrict__ dsc, long long n_blocks,
+static __global__ void q8_blocks_kernel(const int8_t* __restrict__ d8, const uint16_t* __restrict__ dsc, long long n_blocks,
                                  uint8_t* __restrict__ out) {
   for (long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x; b < n_blocks; b += (long long)gridDim.x * blockDim.x) {
     uint8_t* o = out + b * 34;
@@ -116,7 +116,7 @@ __global__ void q8_blocks_kernel(const int8_t* __restrict__ d8, const uint16_t* 
 }
 
 // The reference's 34-byte blocks -> cache rows (inverse of q8_blocks_kernel).
-__global__ void q8_unblock_kernel(const uint8_t* __restrict__ in, long long n_blocks, int8_t* __restrict__ d8,
+static __global__ void q8_unblock_kernel(const uint8_t* __restrict__ in, long long n_blocks, int8_t* __restrict__ d8,
                                   uint16_t* __restrict__ dsc) {
   for (long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x; b < n_blocks; b += (long long)gridDim.x * blockDim.x) {
     const uint8_t* s = in + b * 34;
@@ -126,7 +126,7 @@ __global__ void q8_unblock_kernel(const uint8_t* __restrict__ in, long long n_bl
 }
 
 // Cache rows -> fp32 values d * int8 (exact), [blocks * 32]; one thread per block.
-__global__ void q8_dequant_kernel(const int8_t* __restrict__ d8, const uint16_t* __restrict__ dsc, long long n_blocks,
+static __global__ void q8_dequant_kernel(const int8_t* __restrict__ d8, const uint16_t* __restrict__ dsc, long long n_blocks,
                                   float* __restrict__ out) {
   for (long long b = (long long)blockIdx.x * blockDim.x + threadIdx.x; b < n_blocks; b += (long long)gridDim.x * blockDim.x) {
     const float d = fp16_to_f32(dsc[b]);

@@ -1,5 +1,7 @@
 // l3p_attn.cu -- the C ABI of libllama3pure_attn.so (include/llama3pure_attn.h):
-// context, device KV cache, launch planning and the host-pointer wrappers.
+// context, device KV cache, launch planning, decode / append / prefill and
+// their host-pointer wrappers.  The pre-attention step is in l3p_preattn.cu,
+// the wo projection in l3p_wo.cu, the NVLink groups in l3p_groups.cu.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -16,156 +18,21 @@
 #include <string>
 #include <vector>
 
+#include "ctx.h"
 #include "decode.cuh"
 #include "decode_q8.cuh"
 #include "prefill_tc.cuh"
-#include "rope.cuh"
-#include "wo.cuh"
-#include "seq_xchg.cuh"
-#include "llama3pure_attn.h"
 
 using namespace l3p;
+using namespace l3p_api;
 
-#define L3P_API extern "C" __attribute__((visibility("default")))
 
-struct l3p_attn_ctx {
-  l3p_attn_config cfg{};
-  int hd = 0, G = 0, GT = 1, n_hg = 1;
-  int kvh_count = 0, seq_count = 0;
-  float scale = 1.f;
-  int num_sms = 148;
-  float* kc = nullptr;  // fp32 cache: [n_layers][kvh_count][seq_count][hd]
-  float* vc = nullptr;
-  bool q8 = false;      // Q8_0 cache (kv_format L3P_KV_Q8_0) instead of kc/vc:
-  int8_t* k8 = nullptr;  //   int8 values, same layout as kc
-  int8_t* v8 = nullptr;
-  uint16_t* ksc = nullptr;  //   fp16 block scales [n_layers][kvh_count][seq_count][hd/32]
-  uint16_t* vsc = nullptr;
-  long long layer_elems = 0, head_elems = 0;
-  cudaStream_t stream = nullptr;
-  bool own_stream = false;
-  // split-K scratch: partial outputs, (m, l) pairs and per-unit tickets
-  float* ws_o = nullptr;
-  float* ws_ml = nullptr;
-  unsigned* counters = nullptr;
-  long long ws_o_floats = 0, ws_ml_floats = 0, n_counters = 0;
-  // device staging for the host-pointer entry points
-  float* st_buf = nullptr;
-  size_t st_floats = 0;
-  // pinned, device-mapped host staging for the single-token host calls: the
-  // inputs cross in one copy and the kernel writes the output straight into it
-  float* hst = nullptr;
-  float* hst_dev = nullptr;
-  size_t hst_floats = 0;
-  // prefill: pre-split K/V tile images for the tensor-core kernel
-  float* pf_img = nullptr;
-  size_t pf_img_floats = 0;
-  bool prefill_tc = false;  // head_dim 128 uses the tcgen05 kernel (L3P_PREFILL_PATH=ffma forces the other)
-  int prefill_cg = 1;       // CTAs per tcgen05 prefill unit: 2 (CTA pairs) when the GQA group is even
-  // device error word in mapped pinned host memory
-  int* err_host = nullptr;
-  int* err_dev = nullptr;
-  // completion word of the host-pointer decode calls (mapped pinned memory,
-  // written by the launch's last output writer) and its device-side counter
-  unsigned* done_host = nullptr;
-  unsigned* done_dev = nullptr;
-  unsigned* done_ctr = nullptr;
-  unsigned done_seq = 0;
-  long long launches = 0;
-  // clusters of 2^i CTAs of this context's decode kernel that fit on the GPU at once
-  int max_clusters[5] = {0, 0, 0, 0, 0};
-  // L3P_DECODE_PLAN="nsplit:cluster" pins the decomposition (tests use it to
-  // exercise every merge path); 0 = automatic
-  int force_nsplit = 0, force_cluster = 0;
-  // overlap mode: decode launches carry programmatic stream serialisation
-  bool overlap = false;
-  // split scratch is used in kScratchSlots rotating slices so that launches
-  // overlapping on the GPU never share partials or tickets
-  unsigned long long launch_seq = 0;
-  // pre-attention step (l3p_attn_set_rope): (cos, sin) per position and pair,
-  // [seq_len][hd/2], for dense layers and for Gemma3 SWA layers (the same
-  // array when the model has one table), QK-norm weights [2][n_layers][hd]
-  // (q then k; null = no QK-norm) and the rotated rows of the raw entry points
-  float2* rope_tab = nullptr;
-  float2* rope_tab_swa = nullptr;
-  float* qk_norm = nullptr;
-  float rms_eps = 1e-5f;
-  float* rope_buf = nullptr;
-  size_t rope_buf_floats = 0;
-  // wo projection (l3p_attn_set_wo): per layer the owned columns of the
-  // weight rows in the device layout of wo.cuh, and the attention output
-  // buffer of the combined host call
-  struct WoLayer {
-    int type = 0;  // 0 = not set
-    int rows = 0;
-    long long row_bytes = 0;
-    int sc_stride = 0;  // bytes per row of Q8_0 scales
-    uint8_t* w = nullptr;
-    uint8_t* wsc = nullptr;
-  };
-  std::vector<WoLayer> wo;
-  float* wo_x = nullptr;
-  int wo_ctas_per_sm[6] = {0, 0, 0, 0, 0, 0};  // (Q8_0, Q4_K, Q6_K) x (4, 8 warps)
-  // sequence group over NVLink (l3p_attn_seq_group_*): this context's exchange
-  // region (flags, then per-layer partial slots; seq_xchg.cuh), the members'
-  // regions mapped into this process, and the step counter
-  int xg_parts = 0, xg_part = 0;
-  bool xg_ready = false;
-  uint8_t* xg_region = nullptr;
-  void* xg_peer[kXchgMaxParts] = {};
-  long long xg_slot_floats = 0;
-  // tensor-parallel group over NVLink (l3p_attn_tp_group_*): flags, step
-  // counter, then two slots of [members][dim] partial projections
-  int tp_members = 0, tp_member = 0, tp_dim = 0;
-  bool tp_ready = false;
-  uint8_t* tp_region = nullptr;
-  void* tp_peer[kXchgMaxParts] = {};
-  std::string last_error;
-};
-
-namespace {
+namespace l3p_api {
 
 constexpr long long kWsOFloats = 8ll << 20;  // 32 MiB of split partials
 constexpr long long kCounters = 1 << 16;
 constexpr int kScratchSlots = 4;
 constexpr int kDecodeThreads = L3P_DECODE_WARPS * 32;  // DecodeCfg<*, *>::kThreads
-
-int fail(l3p_attn_ctx* ctx, int code, const char* fmt, ...) {
-  if (ctx) {
-    char buf[512];
-    va_list ap;
-    va_start(ap, fmt);
-    vsnprintf(buf, sizeof buf, fmt, ap);
-    va_end(ap);
-    ctx->last_error = buf;
-  }
-  return code;
-}
-
-#define L3P_CUDA(ctx, call)                                                                  \
-  do {                                                                                       \
-    cudaError_t e_ = (call);                                                                 \
-    if (e_ != cudaSuccess)                                                                   \
-      return fail((ctx), L3P_E_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
-                  __LINE__);                                                                 \
-  } while (0)
-
-// Makes the context's device current for the duration of an entry point and
-// restores the caller's device afterwards.
-struct DeviceScope {
-  int prev = -1;
-  bool changed = false;
-  explicit DeviceScope(int dev) {
-    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) changed = cudaSetDevice(dev) == cudaSuccess;
-  }
-  ~DeviceScope() {
-    if (changed) cudaSetDevice(prev);
-  }
-};
-
-cudaStream_t pick_stream(l3p_attn_ctx* ctx, void* s) {
-  return s ? static_cast<cudaStream_t>(s) : ctx->stream;
-}
 
 // --------------------------------------------------------------------------
 // Kernel table: one instantiation per (head_dim, q heads per CTA).
@@ -377,8 +244,7 @@ int read_err(l3p_attn_ctx* ctx) {
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
                   const float* q, float* out, float* part_o, float* part_ml, cudaStream_t s,
-                  const float* k_new = nullptr, const float* v_new = nullptr, bool allow_overlap = false,
-                  bool new_pending = false, bool signal_host = false) {
+                  const float* k_new, const float* v_new, bool allow_overlap, bool new_pending, bool signal_host) {
   const KernelInfo ki = kernel_for(ctx->hd, ctx->GT, ctx->q8);
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
   if (ctx->q8 && k_new) return fail(ctx, L3P_E_INVAL, "fused append needs an fp32 cache");
@@ -614,167 +480,6 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
   return L3P_OK;
 }
 
-// The pre-attention kernel (rope.cuh) over n_tok tokens at positions
-// [pos0, pos0+n_tok) of `layer`: rotated q rows to q_out, rotated k rows to
-// k_out when given, and the K (rotated) and V rows into the cache when
-// to_cache.
-int launch_rope(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* q, const float* k, const float* v,
-                float* q_out, float* k_out, bool to_cache, cudaStream_t s) {
-  RopeArgs a{};
-  a.q = q;
-  a.k = k;
-  a.v = v;
-  a.q_stride = (long long)ctx->cfg.n_heads * ctx->hd;
-  a.kv_stride = (long long)ctx->cfg.n_kv_heads * ctx->hd;
-  a.q_out = q_out;
-  a.k_out = k_out;
-  if (to_cache) {
-    const long long off = (long long)layer * ctx->layer_elems;
-    if (ctx->q8) {
-      a.k8 = ctx->k8 + off;
-      a.v8 = ctx->v8 + off;
-      a.ksc = ctx->ksc + off / 32;
-      a.vsc = ctx->vsc + off / 32;
-    } else {
-      a.kc = ctx->kc + off;
-      a.vc = ctx->vc + off;
-    }
-  }
-  a.head_stride = ctx->head_elems;
-  a.row0 = pos0 - ctx->cfg.seq_begin;
-  a.cap = ctx->seq_count;
-  // per-layer table choice of c:456-468: Gemma3 SWA layers use the rope_theta_swa table
-  const int pat = ctx->cfg.swa_pattern;
-  const bool swa_layer = pat > 0 && layer % pat < pat - 1;
-  a.tab = (ctx->cfg.is_gemma3 && swa_layer) ? ctx->rope_tab_swa : ctx->rope_tab;
-  a.q_norm = ctx->qk_norm ? ctx->qk_norm + (long long)layer * ctx->hd : nullptr;
-  a.k_norm = ctx->qk_norm ? ctx->qk_norm + ((long long)ctx->cfg.n_layers + layer) * ctx->hd : nullptr;
-  a.eps = ctx->rms_eps;
-  a.inv_hd = 1.0f / (float)ctx->hd;  // s->inv_head_size, c:437
-  a.pos0 = pos0;
-  a.n_tok = n_tok;
-  a.q_head0 = ctx->cfg.kv_head_begin * ctx->G;
-  a.n_qh = ctx->kvh_count * ctx->G;
-  a.kv_head0 = ctx->cfg.kv_head_begin;
-  a.n_kvh = ctx->kvh_count;
-  a.neox = ctx->cfg.is_gemma3 ? 1 : 0;
-  cudaLaunchConfig_t lc{};
-  lc.gridDim = dim3(n_tok, (a.n_qh + a.n_kvh + kRopeWarps - 1) / kRopeWarps, 1);
-  lc.blockDim = dim3(kRopeWarps * 32, 1, 1);
-  lc.stream = s;
-  cudaLaunchAttribute attr[1];
-  if (ctx->overlap) {
-    // the kernel reads nothing before its griddepcontrol.wait, so it may always overlap
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-  }
-  switch (ctx->hd) {
-    case 64:
-      L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, rope_qkv_kernel<64>, a));
-      break;
-    case 128:
-      L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, rope_qkv_kernel<128>, a));
-      break;
-    default:
-      L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, rope_qkv_kernel<256>, a));
-      break;
-  }
-  ++ctx->launches;
-  return L3P_OK;
-}
-
-int ensure_rope_buf(l3p_attn_ctx* ctx, size_t floats, cudaStream_t s) {
-  if (floats <= ctx->rope_buf_floats) return L3P_OK;
-  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(s, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone)
-    return fail(ctx, L3P_E_INVAL,
-                "the rotated-row buffer must grow to %zu floats, which cannot happen during stream capture: "
-                "make one call of this size before capturing", floats);
-  if (ctx->rope_buf) {
-    L3P_CUDA(ctx, cudaStreamSynchronize(s));
-    cudaFree(ctx->rope_buf);
-  }
-  ctx->rope_buf = nullptr;
-  ctx->rope_buf_floats = 0;
-  const size_t want = std::max(floats, (size_t)1 << 16);
-  if (cudaMalloc(&ctx->rope_buf, want * sizeof(float)) != cudaSuccess) {
-    cudaGetLastError();
-    return fail(ctx, L3P_E_NOMEM, "rotated-row buffer allocation of %zu floats failed", want);
-  }
-  ctx->rope_buf_floats = want;
-  return L3P_OK;
-}
-
-int check_rope(l3p_attn_ctx* ctx) {
-  if (!ctx->rope_tab) return fail(ctx, L3P_E_INVAL, "l3p_attn_set_rope has not been called on this context");
-  return L3P_OK;
-}
-
-// The wo GEMV of `layer` (wo.cuh): y[dim] = W[:, owned columns] . x[owned columns].
-int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream_t s, bool tp = false) {
-  const l3p_attn_ctx::WoLayer& L = ctx->wo[layer];
-  WoArgs a{};
-  if (tp) {
-    // partial rows into every member's exchange slots (seq_xchg.cuh)
-    a.tp_members = ctx->tp_members;
-    a.tp_member = ctx->tp_member;
-    for (int m = 0; m < ctx->tp_members; ++m)
-      a.tp_slots[m] = reinterpret_cast<float*>(static_cast<uint8_t*>(ctx->tp_peer[m]) + kXchgFlagBytes);
-    a.tp_step = reinterpret_cast<const unsigned*>(ctx->tp_region) + 16;
-  }
-  a.w = L.w;
-  a.wsc = L.wsc;
-  a.row_bytes = L.row_bytes;
-  a.sc_stride = L.sc_stride;
-  a.rows = L.rows;
-  a.C = ctx->kvh_count * ctx->G * ctx->hd;
-  a.x = x + (long long)ctx->cfg.kv_head_begin * ctx->G * ctx->hd;
-  a.y = y;
-  const int fi = L.type == L3P_W_Q8_0 ? 0 : L.type == L3P_W_Q4_K ? 1 : 2;
-  const int slice = L.type == L3P_W_Q6_K ? WoQ6K::kSlice : WoQ8::kSlice;
-  const int slices = (a.C + slice - 1) / slice;
-  a.wc = 1;
-  while (a.wc < slices) a.wc <<= 1;
-  const int nw = a.wc <= 4 ? 4 : 8;  // warps per CTA
-  const int k = fi * 2 + (nw == 8);
-  // every SM holds as many CTAs as fit; a CTA takes a contiguous block of rows
-  const int target = ctx->num_sms * std::max(ctx->wo_ctas_per_sm[k], 1);
-  a.rows_per_cta = std::max(1, (a.rows + target - 1) / target);
-  const int grid = (a.rows + a.rows_per_cta - 1) / a.rows_per_cta;
-  cudaLaunchConfig_t lc{};
-  lc.gridDim = dim3(grid, 1, 1);
-  lc.blockDim = dim3(nw * 32, 1, 1);
-  lc.dynamicSmemBytes = (size_t)nw * a.rows_per_cta * sizeof(float);
-  lc.stream = s;
-  cudaLaunchAttribute attr[1];
-  if (ctx->overlap) {
-    // weights are requested before griddepcontrol.wait; x is read after it
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-  }
-  switch (k) {
-    case 0: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ8, 4>, a)); break;
-    case 1: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ8, 8>, a)); break;
-    case 2: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ4K, 4>, a)); break;
-    case 3: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ4K, 8>, a)); break;
-    case 4: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ6K, 4>, a)); break;
-    default: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ6K, 8>, a)); break;
-  }
-  ++ctx->launches;
-  return L3P_OK;
-}
-
-int check_wo(l3p_attn_ctx* ctx, int layer) {
-  if (int rc = check_layer(ctx, layer)) return rc;
-  if (ctx->wo.empty() || ctx->wo[layer].type == 0)
-    return fail(ctx, L3P_E_INVAL, "l3p_attn_set_wo has not been called for layer %d", layer);
-  return L3P_OK;
-}
-
 int check_pos_full(l3p_attn_ctx* ctx, int pos) {
   if (pos < 0 || pos >= ctx->cfg.seq_len)
     return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
@@ -786,37 +491,7 @@ int check_pos_full(l3p_attn_ctx* ctx, int pos) {
   return L3P_OK;
 }
 
-// One token's pre-attention step and decode (step_raw entry points).
-int step_raw_core(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k, const float* v, float* out,
-                  cudaStream_t s, bool allow_overlap) {
-  const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
-  if (int rc = ensure_rope_buf(ctx, qd + kvd, s)) return rc;
-  float* rq = ctx->rope_buf;
-  float* rk = rq + qd;
-  if (ctx->q8) {
-    // the pre-attention kernel quantises the rows into the cache; the decode
-    // copies the row of pos only after that kernel has finished
-    if (int rc = launch_rope(ctx, layer, pos, 1, q, k, v, rq, nullptr, true, s)) return rc;
-    return launch_decode(ctx, layer, 0, pos, 0, 1, rq, out, nullptr, nullptr, s, nullptr, nullptr, allow_overlap,
-                         true);
-  }
-  // fp32: the decode takes the rotated K row and V from their producers and stores them (fused append)
-  if (int rc = launch_rope(ctx, layer, pos, 1, q, k, nullptr, rq, rk, false, s)) return rc;
-  return launch_decode(ctx, layer, 0, pos, 0, 1, rq, out, nullptr, nullptr, s, rk, v, allow_overlap);
-}
-
-// A prompt's pre-attention step (K/V rows into the cache) and prefill attention.
-int prefill_raw_core(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, const float* k,
-                     const float* v, float* out, cudaStream_t s) {
-  const size_t nq = (size_t)ctx->cfg.n_heads * ctx->hd * n_tok;
-  if (int rc = ensure_rope_buf(ctx, nq, s)) return rc;
-  float* rq = ctx->rope_buf;
-  if (int rc = launch_rope(ctx, layer, start_pos, n_tok, q, k, v, rq, nullptr, true, s)) return rc;
-  if (ctx->prefill_tc) return launch_prefill_tc(ctx, layer, start_pos, n_tok, rq, out, s);
-  return launch_decode(ctx, layer, 0, start_pos, 1, n_tok, rq, out, nullptr, nullptr, s);
-}
-
-}  // namespace
+}  // namespace l3p_api
 
 // ==========================================================================
 // Lifecycle
@@ -1017,148 +692,6 @@ L3P_API int l3p_attn_set_overlap(l3p_attn_ctx* ctx, int enable) {
   return L3P_OK;
 }
 
-L3P_API int l3p_attn_set_rope(l3p_attn_ctx* ctx, const l3p_attn_rope_config* rope) {
-  if (!ctx || !rope) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  const int hd = ctx->hd, half = hd / 2, n_pos = ctx->cfg.seq_len, L = ctx->cfg.n_layers;
-  const bool gemma = ctx->cfg.is_gemma3 != 0;
-  // defaults of c:5127 (rope_theta), c:390 (rope_theta_swa), c:3198 (eps)
-  const float theta = rope->rope_theta > 0.f ? rope->rope_theta : (gemma ? 1000000.0f : 500000.0f);
-  const float theta_swa = rope->rope_theta_swa > 0.f ? rope->rope_theta_swa : 10000.0f;
-  // the tables of malloc_run_state (c:381-421), the same single-precision
-  // library calls in the same order
-  auto build = [&](float th, std::vector<float2>& tab) {
-    std::vector<float> freq(half);
-    for (int i = 0; i < half; i++) freq[i] = 1.0f / powf(th, (float)(i * 2) / (float)hd);
-    tab.resize((size_t)n_pos * half);
-    for (int pos = 0; pos < n_pos; pos++) {
-      float2* row = tab.data() + (size_t)pos * half;
-      for (int i = 0; i < half; i++) {
-        const float val = pos * freq[i];
-        row[i] = make_float2(cosf(val), sinf(val));
-      }
-    }
-  };
-  std::vector<float2> tab, tab_swa;
-  build(theta, tab);
-  if (gemma) build(theta_swa, tab_swa);
-  DeviceScope dev(ctx->cfg.device);
-  L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-  if (ctx->rope_tab_swa != ctx->rope_tab) cudaFree(ctx->rope_tab_swa);
-  cudaFree(ctx->rope_tab);
-  cudaFree(ctx->qk_norm);
-  ctx->rope_tab = ctx->rope_tab_swa = nullptr;
-  ctx->qk_norm = nullptr;
-  const size_t tab_bytes = tab.size() * sizeof(float2);
-  if (cudaMalloc(&ctx->rope_tab, tab_bytes) != cudaSuccess ||
-      (gemma && cudaMalloc(&ctx->rope_tab_swa, tab_bytes) != cudaSuccess)) {
-    cudaGetLastError();
-    cudaFree(ctx->rope_tab);
-    ctx->rope_tab = ctx->rope_tab_swa = nullptr;
-    return fail(ctx, L3P_E_NOMEM, "RoPE table allocation of %zu bytes failed", tab_bytes);
-  }
-  if (!gemma) ctx->rope_tab_swa = ctx->rope_tab;
-  L3P_CUDA(ctx, cudaMemcpy(ctx->rope_tab, tab.data(), tab_bytes, cudaMemcpyHostToDevice));
-  if (gemma) L3P_CUDA(ctx, cudaMemcpy(ctx->rope_tab_swa, tab_swa.data(), tab_bytes, cudaMemcpyHostToDevice));
-  // QK-norm only for Gemma3 with both weight arrays (c:3233, c:3507)
-  if (gemma && rope->q_norm && rope->k_norm) {
-    const size_t n = (size_t)L * hd;
-    if (cudaMalloc(&ctx->qk_norm, 2 * n * sizeof(float)) != cudaSuccess) {
-      cudaGetLastError();
-      ctx->qk_norm = nullptr;
-      return fail(ctx, L3P_E_NOMEM, "QK-norm weight allocation failed");
-    }
-    L3P_CUDA(ctx, cudaMemcpy(ctx->qk_norm, rope->q_norm, n * sizeof(float), cudaMemcpyHostToDevice));
-    L3P_CUDA(ctx, cudaMemcpy(ctx->qk_norm + n, rope->k_norm, n * sizeof(float), cudaMemcpyHostToDevice));
-  }
-  ctx->rms_eps = rope->rms_norm_eps > 0.f ? rope->rms_norm_eps : 1e-5f;
-  // the single-token entry points never allocate (they may run inside a CUDA graph capture)
-  return ensure_rope_buf(ctx, (size_t)(ctx->cfg.n_heads + ctx->cfg.n_kv_heads) * hd, ctx->stream);
-}
-
-L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* rows, int dim) {
-  if (!ctx || !rows || dim <= 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
-  if (int rc = check_layer(ctx, layer)) return rc;
-  int vals, bytes;  // values and bytes per GGUF block
-  switch (type) {
-    case L3P_W_Q8_0: vals = 32, bytes = 34; break;
-    case L3P_W_Q4_K: vals = 256, bytes = 144; break;
-    case L3P_W_Q6_K: vals = 256, bytes = 210; break;
-    default: return fail(ctx, L3P_E_UNSUPPORTED, "wo weight type %d (Q8_0 = 8, Q4_K = 12, Q6_K = 14 are supported)", type);
-  }
-  const int hd = ctx->hd, cols = ctx->cfg.n_heads * hd;
-  const int c_lo = ctx->cfg.kv_head_begin * ctx->G * hd, C = ctx->kvh_count * ctx->G * hd;
-  const int max_c = 8 * (type == L3P_W_Q6_K ? WoQ6K::kSlice : WoQ8::kSlice);
-  if (cols % vals || c_lo % vals || C % vals || C > max_c)
-    return fail(ctx, L3P_E_UNSUPPORTED, "owned wo columns [%d, %d) do not fall on %d-value blocks or exceed %d", c_lo,
-                c_lo + C, vals, max_c);
-  const uint8_t* src = static_cast<const uint8_t*>(rows);
-  const size_t src_row = (size_t)(cols / vals) * bytes, nb = (size_t)C / vals, b0 = (size_t)c_lo / vals;
-  // device layout of wo.cuh
-  std::vector<uint8_t> w, sc;
-  long long row_bytes;
-  int sc_stride = 0;
-  if (type == L3P_W_Q8_0) {
-    row_bytes = C;
-    sc_stride = (int)((nb * 2 + 15) / 16 * 16);
-    w.resize((size_t)dim * C);
-    sc.assign((size_t)dim * sc_stride, 0);
-    for (int r = 0; r < dim; ++r)
-      for (size_t b = 0; b < nb; ++b) {
-        const uint8_t* blk = src + (size_t)r * src_row + (b0 + b) * bytes;
-        sc[(size_t)r * sc_stride + 2 * b] = blk[0];  // fp16 scale, little-endian
-        sc[(size_t)r * sc_stride + 2 * b + 1] = blk[1];
-        memcpy(&w[(size_t)r * C + b * 32], blk + 2, 32);
-      }
-  } else if (type == L3P_W_Q4_K) {
-    row_bytes = (long long)nb * 144;
-    w.resize((size_t)dim * row_bytes);
-    for (int r = 0; r < dim; ++r) memcpy(&w[(size_t)r * row_bytes], src + (size_t)r * src_row + b0 * 144, nb * 144);
-  } else {
-    row_bytes = (long long)nb * WoQ6K::kBlockBytes;
-    w.assign((size_t)dim * row_bytes, 0);
-    for (int r = 0; r < dim; ++r)
-      for (size_t b = 0; b < nb; ++b)
-        memcpy(&w[(size_t)r * row_bytes + b * WoQ6K::kBlockBytes], src + (size_t)r * src_row + (b0 + b) * 210, 210);
-  }
-  DeviceScope dev(ctx->cfg.device);
-  L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
-  if (ctx->wo.empty()) {
-    ctx->wo.resize(ctx->cfg.n_layers);
-    if (cudaMalloc(&ctx->wo_x, (size_t)cols * sizeof(float)) != cudaSuccess) {
-      cudaGetLastError();
-      ctx->wo.clear();
-      return fail(ctx, L3P_E_NOMEM, "wo input buffer allocation failed");
-    }
-    // resident CTAs per SM of each kernel (grid sizing)
-    const void* fns[6] = {(const void*)wo_gemv_kernel<WoQ8, 4>,  (const void*)wo_gemv_kernel<WoQ8, 8>,
-                          (const void*)wo_gemv_kernel<WoQ4K, 4>, (const void*)wo_gemv_kernel<WoQ4K, 8>,
-                          (const void*)wo_gemv_kernel<WoQ6K, 4>, (const void*)wo_gemv_kernel<WoQ6K, 8>};
-    for (int i = 0; i < 6; ++i)
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctx->wo_ctas_per_sm[i], fns[i], (i % 2 ? 8 : 4) * 32,
-                                                        (size_t)(i % 2 ? 8 : 4) * 64 * sizeof(float)) != cudaSuccess) {
-        cudaGetLastError();
-        ctx->wo_ctas_per_sm[i] = 1;
-      }
-  }
-  l3p_attn_ctx::WoLayer& L = ctx->wo[layer];
-  cudaFree(L.w);
-  cudaFree(L.wsc);
-  L = l3p_attn_ctx::WoLayer();
-  if (cudaMalloc(&L.w, w.size()) != cudaSuccess || (!sc.empty() && cudaMalloc(&L.wsc, sc.size()) != cudaSuccess)) {
-    cudaGetLastError();
-    cudaFree(L.w);
-    L = l3p_attn_ctx::WoLayer();
-    return fail(ctx, L3P_E_NOMEM, "wo weight allocation of %zu bytes failed", w.size());
-  }
-  L3P_CUDA(ctx, cudaMemcpy(L.w, w.data(), w.size(), cudaMemcpyHostToDevice));
-  if (!sc.empty()) L3P_CUDA(ctx, cudaMemcpy(L.wsc, sc.data(), sc.size(), cudaMemcpyHostToDevice));
-  L.type = type;
-  L.rows = dim;
-  L.row_bytes = row_bytes;
-  L.sc_stride = sc_stride;
-  return L3P_OK;
-}
-
 L3P_API int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* nsplit, int* cluster) {
   if (!ctx || n_slices <= 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
   const KernelInfo ki = kernel_for(ctx->hd, ctx->GT, ctx->q8);
@@ -1264,220 +797,6 @@ L3P_API int l3p_attn_prefill_dev(l3p_attn_ctx* ctx, int layer, int start_pos, in
   return launch_decode(ctx, layer, 0, start_pos, 1, n_tok, q, out, nullptr, nullptr, s);
 }
 
-L3P_API int l3p_attn_rope_dev(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* q, const float* k,
-                              float* q_out, float* k_out, void* stream) {
-  if (!ctx || !q || !k || !q_out || !k_out || n_tok < 0)
-    return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
-  if (int rc = check_layer(ctx, layer)) return rc;
-  if (pos0 < 0 || pos0 + n_tok > ctx->cfg.seq_len)
-    return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", pos0, pos0 + n_tok, ctx->cfg.seq_len);
-  if (int rc = check_aligned(ctx, {q, k, q_out, k_out})) return rc;
-  if (int rc = check_rope(ctx)) return rc;
-  if (n_tok == 0) return L3P_OK;
-  DeviceScope dev(ctx->cfg.device);
-  return launch_rope(ctx, layer, pos0, n_tok, q, k, nullptr, q_out, k_out, false, pick_stream(ctx, stream));
-}
-
-L3P_API int l3p_attn_step_raw_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
-                                  const float* v, float* out, void* stream) {
-  if (!ctx || !q || !k || !v || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (int rc = check_layer(ctx, layer)) return rc;
-  if (int rc = check_pos_full(ctx, pos)) return rc;
-  if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
-  if (int rc = check_rope(ctx)) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  return step_raw_core(ctx, layer, pos, q, k, v, out, pick_stream(ctx, stream), true);
-}
-
-L3P_API int l3p_attn_prefill_raw_dev(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,
-                                     const float* k, const float* v, float* out, void* stream) {
-  if (!ctx || !q || !k || !v || !out || n_tok < 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
-  if (int rc = check_layer(ctx, layer)) return rc;
-  if (n_tok == 0) return L3P_OK;
-  if (start_pos < 0 || start_pos + n_tok > ctx->cfg.seq_len)
-    return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", start_pos, start_pos + n_tok, ctx->cfg.seq_len);
-  if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
-  if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
-  if (int rc = check_rope(ctx)) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  return prefill_raw_core(ctx, layer, start_pos, n_tok, q, k, v, out, pick_stream(ctx, stream));
-}
-
-L3P_API int l3p_attn_wo_dev(l3p_attn_ctx* ctx, int layer, const float* x, float* xout, void* stream) {
-  if (!ctx || !x || !xout) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (int rc = check_wo(ctx, layer)) return rc;
-  if (int rc = check_aligned(ctx, {x, xout})) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  return launch_wo(ctx, layer, x, xout, pick_stream(ctx, stream));
-}
-
-// ==========================================================================
-// Sequence groups over NVLink
-
-L3P_API int l3p_attn_seq_group_export(l3p_attn_ctx* ctx, int n_parts, int part, void* handle) {
-  if (!ctx || !handle) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (n_parts < 2 || n_parts > kXchgMaxParts || part < 0 || part >= n_parts)
-    return fail(ctx, L3P_E_INVAL, "sequence group of %d parts (2..%d), part %d", n_parts, kXchgMaxParts, part);
-  DeviceScope dev(ctx->cfg.device);
-  if (!ctx->xg_region) {
-    // per layer: [n_heads][hd] partial outputs then [n_heads][2] (m, l), padded to 16 bytes
-    ctx->xg_slot_floats = ((long long)ctx->cfg.n_heads * (ctx->hd + 2) + 3) / 4 * 4;
-    const size_t bytes = kXchgFlagBytes + (size_t)ctx->cfg.n_layers * ctx->xg_slot_floats * sizeof(float);
-    if (cudaMalloc(&ctx->xg_region, bytes) != cudaSuccess) {
-      cudaGetLastError();
-      ctx->xg_region = nullptr;
-      return fail(ctx, L3P_E_NOMEM, "exchange region of %zu bytes", bytes);
-    }
-    L3P_CUDA(ctx, cudaMemset(ctx->xg_region, 0, bytes));
-  }
-  ctx->xg_parts = n_parts;
-  ctx->xg_part = part;
-  ctx->xg_ready = false;
-  L3P_CUDA(ctx, cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), ctx->xg_region));
-  return L3P_OK;
-}
-
-L3P_API int l3p_attn_seq_group_import(l3p_attn_ctx* ctx, const void* handles) {
-  if (!ctx || !handles) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (!ctx->xg_region) return fail(ctx, L3P_E_INVAL, "l3p_attn_seq_group_export has not been called");
-  DeviceScope dev(ctx->cfg.device);
-  const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
-  for (int p = 0; p < ctx->xg_parts; ++p) {
-    if (p == ctx->xg_part) {
-      ctx->xg_peer[p] = ctx->xg_region;
-      continue;
-    }
-    if (ctx->xg_peer[p]) continue;
-    L3P_CUDA(ctx, cudaIpcOpenMemHandle(&ctx->xg_peer[p], h[p], cudaIpcMemLazyEnablePeerAccess));
-  }
-  ctx->xg_ready = true;
-  return L3P_OK;
-}
-
-L3P_API int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, float* out,
-                                    void* stream) {
-  if (!ctx || !q || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (int rc = check_layer(ctx, layer)) return rc;
-  if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
-  if (!ctx->xg_ready) return fail(ctx, L3P_E_INVAL, "sequence group not connected (export, then import)");
-  if (int rc = check_aligned(ctx, {q, out})) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  cudaStream_t s = pick_stream(ctx, stream);
-  const long long slot = (long long)layer * ctx->xg_slot_floats;
-  float* mine = reinterpret_cast<float*>(ctx->xg_region + kXchgFlagBytes) + slot;
-  // the partial attention over this context's positions, into its own slot
-  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, q, nullptr, mine, mine + (long long)ctx->cfg.n_heads * ctx->hd,
-                             s, nullptr, nullptr, true))
-    return rc;
-  XchgArgs a{};
-  for (int p = 0; p < ctx->xg_parts; ++p) {
-    uint8_t* base = static_cast<uint8_t*>(ctx->xg_peer[p]);
-    a.parts[p] = reinterpret_cast<const float*>(base + kXchgFlagBytes) + slot;
-    a.peer_flags[p] = reinterpret_cast<unsigned*>(base);
-  }
-  a.my_flags = reinterpret_cast<unsigned*>(ctx->xg_region);
-  a.n_parts = ctx->xg_parts;
-  a.part = ctx->xg_part;
-  a.hd = ctx->hd;
-  a.n_heads = ctx->cfg.n_heads;
-  a.row_begin = ctx->cfg.kv_head_begin * ctx->G;
-  a.n_rows = ctx->kvh_count * ctx->G;
-  a.out = out;
-  a.err = ctx->err_dev;
-  cudaLaunchConfig_t lc{};
-  lc.gridDim = dim3(1, 1, 1);
-  lc.blockDim = dim3(kXchgThreads, 1, 1);
-  lc.stream = s;
-  cudaLaunchAttribute attr[1];
-  if (ctx->overlap) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-  }
-  L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, seq_merge_kernel, a));
-  ++ctx->launches;
-  return L3P_OK;
-}
-
-L3P_API int l3p_attn_tp_group_export(l3p_attn_ctx* ctx, int n_members, int member, int dim, void* handle) {
-  if (!ctx || !handle) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (n_members < 2 || n_members > kXchgMaxParts || member < 0 || member >= n_members || dim <= 0 || dim % 4)
-    return fail(ctx, L3P_E_INVAL, "tensor-parallel group of %d members (2..%d), member %d, dim %d (multiple of 4)",
-                n_members, kXchgMaxParts, member, dim);
-  DeviceScope dev(ctx->cfg.device);
-  if (ctx->tp_region && (ctx->tp_members != n_members || ctx->tp_dim != dim))
-    return fail(ctx, L3P_E_INVAL, "the tensor-parallel group is already set up with another shape");
-  if (!ctx->tp_region) {
-    const size_t bytes = kXchgFlagBytes + 2ull * n_members * dim * sizeof(float);
-    if (cudaMalloc(&ctx->tp_region, bytes) != cudaSuccess) {
-      cudaGetLastError();
-      ctx->tp_region = nullptr;
-      return fail(ctx, L3P_E_NOMEM, "tensor-parallel exchange region of %zu bytes", bytes);
-    }
-    L3P_CUDA(ctx, cudaMemset(ctx->tp_region, 0, bytes));
-  }
-  ctx->tp_members = n_members;
-  ctx->tp_member = member;
-  ctx->tp_dim = dim;
-  ctx->tp_ready = false;
-  L3P_CUDA(ctx, cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), ctx->tp_region));
-  return L3P_OK;
-}
-
-L3P_API int l3p_attn_tp_group_import(l3p_attn_ctx* ctx, const void* handles) {
-  if (!ctx || !handles) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (!ctx->tp_region) return fail(ctx, L3P_E_INVAL, "l3p_attn_tp_group_export has not been called");
-  DeviceScope dev(ctx->cfg.device);
-  const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
-  for (int p = 0; p < ctx->tp_members; ++p) {
-    if (p == ctx->tp_member) {
-      ctx->tp_peer[p] = ctx->tp_region;
-      continue;
-    }
-    if (ctx->tp_peer[p]) continue;
-    L3P_CUDA(ctx, cudaIpcOpenMemHandle(&ctx->tp_peer[p], h[p], cudaIpcMemLazyEnablePeerAccess));
-  }
-  ctx->tp_ready = true;
-  return L3P_OK;
-}
-
-L3P_API int l3p_attn_wo_allreduce_dev(l3p_attn_ctx* ctx, int layer, const float* x, float* xout, void* stream) {
-  if (!ctx || !x || !xout) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (int rc = check_wo(ctx, layer)) return rc;
-  if (!ctx->tp_ready) return fail(ctx, L3P_E_INVAL, "tensor-parallel group not connected (export, then import)");
-  if (ctx->wo[layer].rows != ctx->tp_dim)
-    return fail(ctx, L3P_E_INVAL, "wo of layer %d has %d rows, the group was set up for %d", layer,
-                ctx->wo[layer].rows, ctx->tp_dim);
-  if (int rc = check_aligned(ctx, {x, xout})) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  cudaStream_t s = pick_stream(ctx, stream);
-  if (int rc = launch_wo(ctx, layer, x, nullptr, s, true)) return rc;
-  TpArgs a{};
-  for (int m = 0; m < ctx->tp_members; ++m) a.peer_flags[m] = static_cast<unsigned*>(ctx->tp_peer[m]);
-  a.my_flags = reinterpret_cast<unsigned*>(ctx->tp_region);
-  a.my_slots = reinterpret_cast<const float*>(ctx->tp_region + kXchgFlagBytes);
-  a.n_members = ctx->tp_members;
-  a.member = ctx->tp_member;
-  a.dim = ctx->tp_dim;
-  a.out = xout;
-  a.err = ctx->err_dev;
-  cudaLaunchConfig_t lc{};
-  lc.gridDim = dim3(1, 1, 1);
-  lc.blockDim = dim3(kTpThreads, 1, 1);
-  lc.stream = s;
-  cudaLaunchAttribute attr[1];
-  if (ctx->overlap) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-  }
-  L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, tp_sum_kernel, a));
-  ++ctx->launches;
-  return L3P_OK;
-}
-
 L3P_API int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v) {
   if (!ctx) return L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
@@ -1490,7 +809,7 @@ L3P_API int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, floa
 // ==========================================================================
 // Host-pointer entry points: stage through device memory, synchronise.
 
-namespace {
+namespace l3p_api {
 
 int finish_host_call(l3p_attn_ctx* ctx) {
   L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
@@ -1520,7 +839,7 @@ void owned_rows(const l3p_attn_ctx* ctx, int* row_lo, int* row_hi) {
   *row_hi = (ctx->cfg.kv_head_begin + ctx->kvh_count) * ctx->G;
 }
 
-}  // namespace
+}  // namespace l3p_api
 
 L3P_API int l3p_attn_kv_append(l3p_attn_ctx* ctx, int layer, int pos, const float* k, const float* v) {
   if (!ctx || !k || !v) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
@@ -1623,107 +942,6 @@ L3P_API int l3p_attn_prefill(l3p_attn_ctx* ctx, int layer, int start_pos, int n_
   L3P_CUDA(ctx, cudaMemcpy2DAsync(out + (size_t)r0 * ctx->hd, qd * 4, dout + (size_t)r0 * ctx->hd, qd * 4,
                                   (size_t)(r1 - r0) * ctx->hd * 4, n_tok, cudaMemcpyDeviceToHost, ctx->stream));
   return finish_host_call(ctx);
-}
-
-L3P_API int l3p_attn_step_raw(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
-                              const float* v, float* out) {
-  if (!ctx || !q || !k || !v || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (int rc = check_layer(ctx, layer)) return rc;
-  if (int rc = check_pos_full(ctx, pos)) return rc;
-  if (int rc = check_rope(ctx)) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
-  const size_t in = qd + 2 * kvd;  // staged inputs: q | k | v
-  if (int rc = ensure_staging(ctx, in)) return rc;
-  if (int rc = ensure_host_staging(ctx, in + qd)) return rc;
-  int r0, r1;
-  owned_rows(ctx, &r0, &r1);
-  const size_t row0 = (size_t)r0 * ctx->hd, nrow = (size_t)(r1 - r0) * ctx->hd;
-  memcpy(ctx->hst + row0, q + row0, nrow * 4);
-  memcpy(ctx->hst + qd, k, kvd * 4);
-  memcpy(ctx->hst + qd + kvd, v, kvd * 4);
-  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, ctx->hst, in * 4, cudaMemcpyHostToDevice, ctx->stream));
-  if (int rc = step_raw_core(ctx, layer, pos, ctx->st_buf, ctx->st_buf + qd, ctx->st_buf + qd + kvd,
-                             ctx->hst_dev + in, ctx->stream, false))
-    return rc;
-  if (int rc = finish_host_call(ctx)) return rc;
-  memcpy(out + row0, ctx->hst + in + row0, nrow * 4);
-  return L3P_OK;
-}
-
-L3P_API int l3p_attn_prefill_raw(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q,
-                                 const float* k, const float* v, float* out) {
-  if (!ctx || !q || !k || !v || !out || n_tok < 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
-  if (int rc = check_layer(ctx, layer)) return rc;
-  if (n_tok == 0) return L3P_OK;
-  if (start_pos < 0 || start_pos + n_tok > ctx->cfg.seq_len)
-    return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", start_pos, start_pos + n_tok, ctx->cfg.seq_len);
-  if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
-  if (int rc = check_rope(ctx)) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
-  const size_t nq = qd * n_tok, nkv = kvd * n_tok;
-  if (int rc = ensure_staging(ctx, 2 * nq + 2 * nkv)) return rc;
-  float* dq = ctx->st_buf;
-  float* dout = dq + nq;
-  float* dk = dout + nq;
-  float* dv = dk + nkv;
-  L3P_CUDA(ctx, cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, ctx->stream));
-  L3P_CUDA(ctx, cudaMemcpyAsync(dk, k, nkv * 4, cudaMemcpyHostToDevice, ctx->stream));
-  L3P_CUDA(ctx, cudaMemcpyAsync(dv, v, nkv * 4, cudaMemcpyHostToDevice, ctx->stream));
-  if (int rc = prefill_raw_core(ctx, layer, start_pos, n_tok, dq, dk, dv, dout, ctx->stream)) return rc;
-  int r0, r1;
-  owned_rows(ctx, &r0, &r1);
-  L3P_CUDA(ctx, cudaMemcpy2DAsync(out + (size_t)r0 * ctx->hd, qd * 4, dout + (size_t)r0 * ctx->hd, qd * 4,
-                                  (size_t)(r1 - r0) * ctx->hd * 4, n_tok, cudaMemcpyDeviceToHost, ctx->stream));
-  return finish_host_call(ctx);
-}
-
-L3P_API int l3p_attn_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* xout) {
-  if (!ctx || !x || !xout) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (int rc = check_wo(ctx, layer)) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, dim = ctx->wo[layer].rows;
-  if (int rc = ensure_host_staging(ctx, qd + dim)) return rc;
-  int r0, r1;
-  owned_rows(ctx, &r0, &r1);
-  const size_t row0 = (size_t)r0 * ctx->hd, nrow = (size_t)(r1 - r0) * ctx->hd;
-  memcpy(ctx->hst + row0, x + row0, nrow * 4);
-  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->wo_x + row0, ctx->hst + row0, nrow * 4, cudaMemcpyHostToDevice, ctx->stream));
-  // the kernel writes xout into mapped pinned memory
-  if (int rc = launch_wo(ctx, layer, ctx->wo_x, ctx->hst_dev + qd, ctx->stream)) return rc;
-  if (int rc = finish_host_call(ctx)) return rc;
-  memcpy(xout, ctx->hst + qd, dim * 4);
-  return L3P_OK;
-}
-
-L3P_API int l3p_attn_step_raw_wo(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
-                                 const float* v, float* xout) {
-  if (!ctx || !q || !k || !v || !xout) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
-  if (int rc = check_layer(ctx, layer)) return rc;
-  if (int rc = check_pos_full(ctx, pos)) return rc;
-  if (int rc = check_rope(ctx)) return rc;
-  if (int rc = check_wo(ctx, layer)) return rc;
-  DeviceScope dev(ctx->cfg.device);
-  const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
-  const size_t dim = ctx->wo[layer].rows;
-  const size_t in = qd + 2 * kvd;  // staged inputs: q | k | v
-  if (int rc = ensure_staging(ctx, in)) return rc;
-  if (int rc = ensure_host_staging(ctx, in + dim)) return rc;
-  int r0, r1;
-  owned_rows(ctx, &r0, &r1);
-  const size_t row0 = (size_t)r0 * ctx->hd, nrow = (size_t)(r1 - r0) * ctx->hd;
-  memcpy(ctx->hst + row0, q + row0, nrow * 4);
-  memcpy(ctx->hst + qd, k, kvd * 4);
-  memcpy(ctx->hst + qd + kvd, v, kvd * 4);
-  L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, ctx->hst, in * 4, cudaMemcpyHostToDevice, ctx->stream));
-  if (int rc = step_raw_core(ctx, layer, pos, ctx->st_buf, ctx->st_buf + qd, ctx->st_buf + qd + kvd, ctx->wo_x,
-                             ctx->stream, false))
-    return rc;
-  if (int rc = launch_wo(ctx, layer, ctx->wo_x, ctx->hst_dev + in, ctx->stream)) return rc;
-  if (int rc = finish_host_call(ctx)) return rc;
-  memcpy(xout, ctx->hst + in, dim * 4);
-  return L3P_OK;
 }
 
 L3P_API int l3p_attn_load_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, const float* k, const float* v) {

@@ -30,12 +30,9 @@
 // slower member still reads.
 #pragma once
 #include "decode.cuh"
+#include "limits.cuh"
 
 namespace l3p {
-
-constexpr int kXchgMaxParts = 16;
-
-constexpr int kXchgFlagBytes = 256;  // flags and step counter ahead of the partial slots
 
 struct XchgArgs {
   const float* parts[kXchgMaxParts];    // this layer's slot in every member's region (own included)
@@ -58,7 +55,7 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
 
 // grid: ONE CTA of kXchgThreads threads (warp w merges q heads w, w + warps, ...).
 constexpr int kXchgThreads = 512;
-__global__ void __launch_bounds__(kXchgThreads) seq_merge_kernel(const XchgArgs a) {
+static __global__ void __launch_bounds__(kXchgThreads) seq_merge_kernel(const XchgArgs a) {
   pdl_launch_dependents();
   pdl_wait();  // this GPU's partials are written
   __shared__ int s_ok;
@@ -155,7 +152,7 @@ struct TpArgs {
   int* err;
 };
 
-__global__ void __launch_bounds__(kTpThreads) tp_sum_kernel(const TpArgs a) {
+static __global__ void __launch_bounds__(kTpThreads) tp_sum_kernel(const TpArgs a) {
   pdl_launch_dependents();
   pdl_wait();  // the projection's peer stores are complete
   __shared__ int s_ok;

@@ -43,6 +43,7 @@
 // quarter of the rate and bound the kernel).
 #pragma once
 #include "decode_q8.cuh"
+#include "limits.cuh"
 
 namespace l3p {
 
@@ -60,7 +61,7 @@ struct WoArgs {
   // row band `member` of slot (step+1)&1 of every member's exchange slots,
   // step = *tp_step (read after griddepcontrol.wait)
   int tp_members, tp_member;
-  float* tp_slots[16];  // every member's [2][tp_members][rows] slots (own included)
+  float* tp_slots[kXchgMaxParts];  // every member's [2][tp_members][rows] slots (own included)
   const unsigned* tp_step;
 };
 
