@@ -149,6 +149,17 @@ struct DeviceScope {
 
 inline cudaStream_t pick_stream(l3p_attn_ctx* ctx, void* s) { return s ? static_cast<cudaStream_t>(s) : ctx->stream; }
 
+// With overlap mode, a launch may start while the kernel before it on the
+// stream still runs (programmatic dependent launch); every kernel so launched
+// reads nothing the earlier kernel writes before its griddepcontrol.wait.
+inline void pdl_attr(const l3p_attn_ctx* ctx, cudaLaunchConfig_t& lc, cudaLaunchAttribute (&attr)[1]) {
+  if (!ctx->overlap) return;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+}
+
 // l3p_attn.cu
 int check_aligned(l3p_attn_ctx* ctx, std::initializer_list<const void*> ptrs);
 int ensure_staging(l3p_attn_ctx* ctx, size_t floats);
@@ -165,7 +176,10 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
                   float* out, float* part_o, float* part_ml, cudaStream_t s, const float* k_new = nullptr,
                   const float* v_new = nullptr, bool allow_overlap = false, bool new_pending = false,
                   bool signal_host = false);
-int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v, cudaStream_t s);
+// Cache rows of n_tok tokens.  trigger_early lets the next kernel launch
+// before the rows are written; it must then wait for them itself.
+int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v, cudaStream_t s,
+                  bool trigger_early = false);
 int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
                       cudaStream_t s);
 

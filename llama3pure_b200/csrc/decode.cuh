@@ -768,10 +768,15 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
 
 // Token K/V rows -> head-major cache rows.  k, v: [n_tok][src_stride] with
 // KV head h at offset h*HD; grid (n_tok, kvh_count), HD/4 threads.
+// trigger_early: let the next kernel launch at once (it must itself wait
+// before reading the rows written here, as decode does with new_pending);
+// otherwise it launches when this grid completes.
 static __global__ void kv_append_kernel(float* __restrict__ kc, float* __restrict__ vc, long long head_stride,
                                  int hd, const float* __restrict__ k, const float* __restrict__ v,
-                                 long long src_stride, int kv_head_begin, int row0) {
+                                 long long src_stride, int kv_head_begin, int row0, int trigger_early) {
   const int tok = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+  if (trigger_early) pdl_launch_dependents();
+  pdl_wait();  // the rows come from the kernel before this one
   const long long src = (long long)tok * src_stride + (long long)(kv_head_begin + h) * hd + 4 * t;
   const long long dst = (long long)h * head_stride + (long long)(row0 + tok) * hd + 4 * t;
   *reinterpret_cast<float4*>(kc + dst) = *reinterpret_cast<const float4*>(k + src);

@@ -78,9 +78,12 @@ __device__ __forceinline__ uint16_t q8_quantize_lanes(const float (&x)[N], uint3
 template <int HD>
 __global__ void kv_append_q8_kernel(int8_t* __restrict__ k8, int8_t* __restrict__ v8, uint16_t* __restrict__ ksc,
                                     uint16_t* __restrict__ vsc, long long head_stride, const float* __restrict__ k,
-                                    const float* __restrict__ v, long long src_stride, int kv_head_begin, int row0) {
+                                    const float* __restrict__ v, long long src_stride, int kv_head_begin, int row0,
+                                    int trigger_early) {
   constexpr int N = HD / 32;
   const int tok = blockIdx.x, h = blockIdx.y, lane = threadIdx.x;
+  if (trigger_early) pdl_launch_dependents();  // as kv_append_kernel
+  pdl_wait();  // the rows come from the kernel before this one
   const long long src = (long long)tok * src_stride + (long long)(kv_head_begin + h) * HD + lane * N;
   const long long row = (long long)h * head_stride / HD + row0 + tok;  // row index in the cache
 #pragma unroll

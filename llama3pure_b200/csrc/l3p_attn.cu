@@ -348,25 +348,34 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
 // of the destination head block; grid.y heads of head_elems values each.
 int launch_append_q8(l3p_attn_ctx* ctx, int8_t* k8, int8_t* v8, uint16_t* ksc, uint16_t* vsc, dim3 grid,
                      const float* k, const float* v, long long src_stride, int kv_head_begin, int row0,
-                     cudaStream_t s) {
+                     cudaStream_t s, int trigger_early) {
+  cudaLaunchConfig_t lc{};
+  lc.gridDim = grid;
+  lc.blockDim = dim3(32, 1, 1);
+  lc.stream = s;
+  cudaLaunchAttribute attr[1];
+  pdl_attr(ctx, lc, attr);
+  const long long hs = ctx->head_elems;
   switch (ctx->hd) {
     case 64:
-      kv_append_q8_kernel<64><<<grid, 32, 0, s>>>(k8, v8, ksc, vsc, ctx->head_elems, k, v, src_stride, kv_head_begin, row0);
+      L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kv_append_q8_kernel<64>, k8, v8, ksc, vsc, hs, k, v, src_stride,
+                                       kv_head_begin, row0, trigger_early));
       break;
     case 128:
-      kv_append_q8_kernel<128><<<grid, 32, 0, s>>>(k8, v8, ksc, vsc, ctx->head_elems, k, v, src_stride, kv_head_begin, row0);
+      L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kv_append_q8_kernel<128>, k8, v8, ksc, vsc, hs, k, v, src_stride,
+                                       kv_head_begin, row0, trigger_early));
       break;
     default:
-      kv_append_q8_kernel<256><<<grid, 32, 0, s>>>(k8, v8, ksc, vsc, ctx->head_elems, k, v, src_stride, kv_head_begin, row0);
+      L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kv_append_q8_kernel<256>, k8, v8, ksc, vsc, hs, k, v, src_stride,
+                                       kv_head_begin, row0, trigger_early));
       break;
   }
   ++ctx->launches;
-  L3P_CUDA(ctx, cudaGetLastError());
   return L3P_OK;
 }
 
 int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v,
-                  cudaStream_t s) {
+                  cudaStream_t s, bool trigger_early) {
   // clip the tokens to the owned position range
   const int own_lo = ctx->cfg.seq_begin, own_hi = ctx->cfg.seq_begin + ctx->seq_count;
   const int t_lo = std::max(pos0, own_lo), t_hi = std::min(pos0 + n_tok, own_hi);
@@ -382,16 +391,20 @@ int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float
       // quantise the rows into the Q8_0 cache (quantize_to_q8_0_cache, c:1535-1570)
       if (int rc = launch_append_q8(ctx, ctx->k8 + off, ctx->v8 + off, ctx->ksc + off / 32, ctx->vsc + off / 32, grid,
                                     ks + (long long)(t0 - t_lo) * src_stride, vs + (long long)(t0 - t_lo) * src_stride,
-                                    src_stride, ctx->cfg.kv_head_begin, t0 - own_lo, s))
+                                    src_stride, ctx->cfg.kv_head_begin, t0 - own_lo, s, trigger_early ? 1 : 0))
         return rc;
       continue;
     }
-    kv_append_kernel<<<grid, ctx->hd / 4, 0, s>>>(ctx->kc + off, ctx->vc + off, ctx->head_elems, ctx->hd,
-                                                   ks + (long long)(t0 - t_lo) * src_stride,
-                                                   vs + (long long)(t0 - t_lo) * src_stride, src_stride,
-                                                   ctx->cfg.kv_head_begin, t0 - own_lo);
+    cudaLaunchConfig_t lc{};
+    lc.gridDim = grid;
+    lc.blockDim = dim3(ctx->hd / 4, 1, 1);
+    lc.stream = s;
+    cudaLaunchAttribute attr[1];
+    pdl_attr(ctx, lc, attr);
+    L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kv_append_kernel, ctx->kc + off, ctx->vc + off, ctx->head_elems, ctx->hd,
+                                     ks + (long long)(t0 - t_lo) * src_stride, vs + (long long)(t0 - t_lo) * src_stride,
+                                     src_stride, ctx->cfg.kv_head_begin, t0 - own_lo, trigger_early ? 1 : 0));
     ++ctx->launches;
-    L3P_CUDA(ctx, cudaGetLastError());
   }
   return L3P_OK;
 }
@@ -736,8 +749,9 @@ L3P_API int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float
   if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
   if (ctx->q8) {
-    // the new row must be quantised before it is attended to (c:3299-3312): two launches
-    if (int rc = launch_append(ctx, layer, pos, 1, k, v, pick_stream(ctx, stream))) return rc;
+    // the new row must be quantised before it is attended to (c:3299-3312): two launches;
+    // the decode streams the cached rows meanwhile and copies the new row after its wait
+    if (int rc = launch_append(ctx, layer, pos, 1, k, v, pick_stream(ctx, stream), true)) return rc;
     return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), nullptr,
                          nullptr, true, true);
   }
@@ -966,7 +980,7 @@ L3P_API int l3p_attn_load_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, 
         const int nt = std::min(hi - lo - t0, 65535);
         if (int rc = launch_append_q8(ctx, ctx->k8 + off, ctx->v8 + off, ctx->ksc + off / 32, ctx->vsc + off / 32,
                                       dim3(nt, 1), ctx->st_buf + (size_t)t0 * row, ctx->st_buf + n + (size_t)t0 * row,
-                                      (long long)row, 0, lo - ctx->cfg.seq_begin + t0, ctx->stream))
+                                      (long long)row, 0, lo - ctx->cfg.seq_begin + t0, ctx->stream, 0))
           return rc;
       }
     }

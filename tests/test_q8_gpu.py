@@ -246,3 +246,44 @@ def test_fp32_only_entry_points_refuse_a_q8_cache():
     with AttnContext(1, 8, 2, 128, 64) as ctx:
         with pytest.raises(AttnError):
             ctx.read_kv_q8(0, 0, 4)
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_step_dev_layer_chain_in_a_graph(overlap):
+    """Consecutive layers of step_dev (append, then decode) captured in a CUDA
+    graph: with programmatic dependent launch the decode starts streaming
+    while the append runs and copies the new row only after its wait."""
+    import torch
+
+    sh = CONFIGS["llama31_8b_decode_8k"].with_(seq_len=1024, pos=1023, n_layers=4)
+    ks, vs, qs = [], [], []
+    with AttnContext.for_shape(sh, kv_format=Q8) as ctx:
+        for layer in range(sh.n_layers):
+            k, v, q = decode_inputs(sh.with_(seed=60 + layer), layer)
+            ctx.load_kv(layer, 0, np.ascontiguousarray(k[:, : sh.pos]), np.ascontiguousarray(v[:, : sh.pos]))
+            ks.append(k)
+            vs.append(v)
+            qs.append(q)
+        dq = torch.from_numpy(np.stack([q.reshape(-1) for q in qs])).cuda()
+        dk = torch.from_numpy(np.stack([np.ascontiguousarray(k[:, sh.pos]).reshape(-1) for k in ks])).cuda()
+        dv = torch.from_numpy(np.stack([np.ascontiguousarray(v[:, sh.pos]).reshape(-1) for v in vs])).cuda()
+        out = torch.zeros_like(dq)
+        ctx.set_overlap(overlap)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for layer in range(sh.n_layers):
+                    ctx.step_dev(layer, sh.pos, dq[layer], dk[layer], dv[layer], out[layer], s)
+            g.replay()
+        torch.cuda.synchronize()
+        ctx.check()
+        got = out.cpu().numpy()
+        del g
+    for layer in range(sh.n_layers):
+        o = O.Oracle(sh, O.MODE_Q8, "port", n_layers=layer + 1)
+        o.load_kv(layer, 0, ks[layer], vs[layer])
+        want, _ = o.decode(layer, sh.pos, qs[layer])
+        o.close()
+        _check(got[layer].reshape(want.shape), want, f"q8 step_dev chain layer {layer} overlap={overlap}")
