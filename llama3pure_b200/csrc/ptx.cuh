@@ -16,6 +16,16 @@ enum : int { kErrTimeout = 1, kErrBadArg = 2 };
 // lets the kernel finish without the data.
 constexpr uint32_t kMaxWaitProbes = 1u << 24;
 
+// Waits on another GPU (the NVLink groups) are bounded by time, not probes:
+// a member that never arrives costs this long, then the error word is set.
+constexpr unsigned long long kGroupWaitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -20,7 +20,8 @@
 //   1. (after griddepcontrol.wait: the partials are complete) advances the
 //      step counter and stores the step into flags[me] of every peer -- a
 //      release store at system scope;
-//   2. waits (bounded) until every peer's step has arrived in its own flags;
+//   2. waits (at most kGroupWaitNs) until every peer's step has arrived in its
+//      own flags, else sets kErrTimeout in the error word and returns;
 //   3. for each owned q head reads the n_parts triples -- its own locally, the
 //      peers' over NVLink -- and writes the log-sum-exp merge to `out`.
 // The step counter lives on the device, so a captured CUDA graph replays
@@ -69,10 +70,10 @@ static __global__ void __launch_bounds__(kXchgThreads) seq_merge_kernel(const Xc
     int ok = 1;
     for (int s = 0; s < a.n_parts && ok; ++s) {
       if (s == a.part) continue;
-      uint32_t i = 0;
+      const unsigned long long t0 = globaltimer_ns();
       // steps only grow: a member already further on has published this step too
       while ((int)(ld_acquire_sys(a.my_flags + s) - e) < 0) {
-        if (++i >= kMaxWaitProbes) {
+        if (globaltimer_ns() - t0 > kGroupWaitNs) {
           *reinterpret_cast<volatile int*>(a.err) = kErrTimeout;
           ok = 0;
           break;
@@ -167,9 +168,9 @@ static __global__ void __launch_bounds__(kTpThreads) tp_sum_kernel(const TpArgs 
     int ok = 1;
     for (int s = 0; s < a.n_members && ok; ++s) {
       if (s == a.member) continue;
-      uint32_t i = 0;
+      const unsigned long long t0 = globaltimer_ns();
       while ((int)(ld_acquire_sys(a.my_flags + s) - e) < 0) {
-        if (++i >= kMaxWaitProbes) {
+        if (globaltimer_ns() - t0 > kGroupWaitNs) {
           *reinterpret_cast<volatile int*>(a.err) = kErrTimeout;
           ok = 0;
           break;
