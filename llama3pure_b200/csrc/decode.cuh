@@ -62,6 +62,11 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src,
                : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 // Programmatic dependent launch: let the next kernel of the stream start
 // launching, and wait for the previous kernel's results (no-ops when the
 // launch carries no programmatic dependency).
@@ -112,6 +117,10 @@ struct DecodeArgs {
   unsigned* done_ctr;
   unsigned* done_flag;
   unsigned done_value, done_writers;
+  // mergers of the global stage (no cluster): the last merge_k parts to
+  // finish each merge 1/merge_k of the output; > 1 only for launches whose
+  // CTAs are all resident at once (a merger waits for the unit's last part)
+  int merge_k;
 };
 
 // A CTA that has written its share of the launch's outputs: the last such CTA
@@ -254,7 +263,46 @@ struct DecodeMergeSmem {
   float rw[kMaxCluster][GT];  // cluster merge weights
   float M[GT], L[GT];
   int last;
+  int mk;  // mergers of the global stage
 };
+
+// One batch of the global merge: fold parts sp0, sp0 + stride, ... (up to
+// kMergeBatch of them, those < n_parts) of one q head's float4 into the
+// running (M, L, O).  ml2 points at the head's (m, l) of part 0 ([part][GT]
+// float2), o4 at its float4 of part 0 ([part][GT*HD/4] float4).  All loads are
+// issued before any is used.
+template <int GT, int HD>
+__device__ __forceinline__ void merge_part_batch(const float2* ml2, const float4* o4, int sp0, int stride,
+                                                 int n_parts, float& M, float& L, float4& O) {
+  float2 ml[kMergeBatch];
+  float4 v[kMergeBatch];
+#pragma unroll
+  for (int j = 0; j < kMergeBatch; ++j) {
+    const int sp = sp0 + j * stride;
+    ml[j] = sp < n_parts ? __ldcg(ml2 + (long long)sp * GT) : make_float2(-INFINITY, 0.f);
+    v[j] = sp < n_parts ? __ldcg(o4 + (long long)sp * (GT * HD / 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float Mb = M;
+#pragma unroll
+  for (int j = 0; j < kMergeBatch; ++j) Mb = fmaxf(Mb, ml[j].x);
+  if (Mb == -INFINITY) return;
+  const float r = fast_exp2(M - Mb);  // rescale what was accumulated so far
+  L *= r;
+  O.x *= r;
+  O.y *= r;
+  O.z *= r;
+  O.w *= r;
+#pragma unroll
+  for (int j = 0; j < kMergeBatch; ++j) {
+    const float w = fast_exp2(ml[j].x - Mb);  // 0 for empty partials (m = -inf)
+    L = fmaf(ml[j].y, w, L);
+    O.x = fmaf(v[j].x, w, O.x);
+    O.y = fmaf(v[j].y, w, O.y);
+    O.z = fmaf(v[j].z, w, O.z);
+    O.w = fmaf(v[j].w, w, O.w);
+  }
+  M = Mb;
+}
 
 // Everything after the position loop of a decode kernel: merge the W warps of
 // the CTA (their running (m, l) already in ms.m / ms.l, their accumulators in
@@ -329,6 +377,7 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
   int n_parts = a.nsplit;  // partials the global stage merges
   int part = split;
   int rank = 0, cs = 1;
+  int mergers = 1;  // CTAs of the global stage that each merge a slice, without a cluster
   if (a.cluster > 1) {
     // ---- cluster stage: the CTAs of a cluster merge through distributed shared memory ----
     cg::cluster_group cluster = cg::this_cluster();
@@ -401,63 +450,115 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) s_last = atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts - 1);
+    if (threadIdx.x == 0 && a.merge_k <= 1) {
+      s_last = atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts - 1);
+      ms.mk = 1;
+    } else if (threadIdx.x == 0) {
+      // the last merge_k arrivals become mergers 0 .. merge_k-1; all but the
+      // last wait (bounded) until every part has arrived
+      const int k = a.merge_k;
+      const int t = (int)atomicAdd(&a.counters[unit], 1u);
+      int j = t - (n_parts - k);
+      if (j >= 0 && t != n_parts - 1) {
+        const unsigned long long t0 = globaltimer_ns();
+        while ((int)ld_acquire_gpu(&a.counters[unit]) < n_parts) {
+          if (globaltimer_ns() - t0 > kGroupWaitNs) {
+            *reinterpret_cast<volatile int*>(a.err) = kErrTimeout;
+            j = -1;
+            break;
+          }
+          __nanosleep(32);
+        }
+      }
+      s_last = j >= 0 ? j + 1 : 0;  // 0: not a merger
+      ms.mk = k;
+    }
     __syncthreads();
+    rank = s_last - 1;
+    cs = mergers = ms.mk;
   }
   if (!s_last) return;
   __threadfence();
 
   // ---- global stage: the last part to finish merges all n_parts partials ----
-  // (with a cluster, each rank of the last cluster merges its slice).  Every
-  // thread fetches the (m, l) pairs of its q head and its float4 of each
-  // partial in one batch, so the stage costs a single L2 round trip.
+  // (with a cluster, each rank of the last cluster merges its slice; without,
+  // each of the last merge_k parts).  A merger's thread takes one float4 of
+  // the slice and fetches the (m, l) pairs and float4s of kMergeBatch parts in
+  // one batch, so 16 parts cost a single L2 round trip.  With several mergers
+  // the slice is small, so its threads also split the parts into pg groups
+  // (thread t: float4 t % slice4, parts t / slice4 + pg * i) whose partial
+  // merges combine in shared memory: ceil(n_parts / (pg * kMergeBatch)) round
+  // trips.  (Splitting the parts of a single merger measured slower.)
   const long long slot0 = (long long)unit * n_parts;
   const int slice4 = GT * HD / 4 / cs;
+  int pg = 1;
+  if (mergers > 1)  // pg * slice4 <= T: one float4 and part group per thread
+    while (2 * pg * slice4 <= T && pg * kMergeBatch < n_parts) pg *= 2;
   const float2* ml2 = reinterpret_cast<const float2*>(a.ws_ml) + slot0 * GT;  // [n_parts][GT]
   const float4* o4 = reinterpret_cast<const float4*>(a.ws_o + slot0 * GT * HD);
-  for (int t = threadIdx.x; t < slice4; t += T) {
-    const int idx4 = rank * slice4 + t;
+  if (pg == 1) {
+    for (int t = threadIdx.x; t < slice4; t += T) {
+      const int idx4 = rank * slice4 + t;
+      const int g = (idx4 * 4) / HD;
+      float M = -INFINITY, L = 0.f;
+      float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp0 = 0; sp0 < n_parts; sp0 += kMergeBatch)
+        merge_part_batch<GT, HD>(ml2 + g, o4 + idx4, sp0, 1, n_parts, M, L, O);
+      const float inv = (a.partial && !(L > 0.f)) ? 0.f : 1.f / L;
+      *reinterpret_cast<float4*>(out_base + idx4 * 4) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+      if (ml_base && (idx4 * 4) % HD == 0) {
+        ml_base[2 * g] = M;
+        ml_base[2 * g + 1] = L;
+      }
+    }
+  } else {
+    float4* s_o = reinterpret_cast<float4*>(ring);           // [pg][slice4] group merges
+    float2* s_ml = reinterpret_cast<float2*>(ring + 4 * T);  // [pg][slice4] their (M, L)
+    const int t = threadIdx.x;
+    const bool on = t < slice4 * pg;
+    const int f = t % slice4, grp = t / slice4;
+    const int idx4 = rank * slice4 + f;
     const int g = (idx4 * 4) / HD;
     float M = -INFINITY, L = 0.f;
     float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp0 = 0; sp0 < n_parts; sp0 += kMergeBatch) {
-      float2 ml[kMergeBatch];
-      float4 v[kMergeBatch];
-#pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j) {
-        const int sp = sp0 + j;
-        ml[j] = sp < n_parts ? __ldcg(ml2 + (long long)sp * GT + g) : make_float2(-INFINITY, 0.f);
-        v[j] = sp < n_parts ? __ldcg(o4 + (long long)sp * (GT * HD / 4) + idx4) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      float Mb = M;
-#pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j) Mb = fmaxf(Mb, ml[j].x);
-      if (Mb == -INFINITY) continue;
-      const float r = fast_exp2(M - Mb);  // rescale what was accumulated so far
-      L *= r;
-      O.x *= r;
-      O.y *= r;
-      O.z *= r;
-      O.w *= r;
-#pragma unroll
-      for (int j = 0; j < kMergeBatch; ++j) {
-        const float w = fast_exp2(ml[j].x - Mb);  // 0 for empty partials (m = -inf)
-        L = fmaf(ml[j].y, w, L);
-        O.x = fmaf(v[j].x, w, O.x);
-        O.y = fmaf(v[j].y, w, O.y);
-        O.z = fmaf(v[j].z, w, O.z);
-        O.w = fmaf(v[j].w, w, O.w);
-      }
-      M = Mb;
+    for (int sp0 = grp; on && sp0 < n_parts; sp0 += pg * kMergeBatch)
+      merge_part_batch<GT, HD>(ml2 + g, o4 + idx4, sp0, pg, n_parts, M, L, O);
+    if (on) {
+      s_o[grp * slice4 + f] = O;
+      s_ml[grp * slice4 + f] = make_float2(M, L);
     }
-    const float inv = (a.partial && !(L > 0.f)) ? 0.f : 1.f / L;
-    *reinterpret_cast<float4*>(out_base + idx4 * 4) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-    if (ml_base && (idx4 * 4) % HD == 0) {
-      ml_base[2 * g] = M;
-      ml_base[2 * g + 1] = L;
+    __syncthreads();
+    if (on && grp == 0) {
+      for (int q = 1; q < pg; ++q) {
+        const float2 ml = s_ml[q * slice4 + f];
+        const float Mb = fmaxf(M, ml.x);
+        if (Mb == -INFINITY) continue;
+        const float r0 = fast_exp2(M - Mb), r1 = fast_exp2(ml.x - Mb);
+        const float4 o = s_o[q * slice4 + f];
+        L = L * r0 + ml.y * r1;
+        O.x = O.x * r0 + o.x * r1;
+        O.y = O.y * r0 + o.y * r1;
+        O.z = O.z * r0 + o.z * r1;
+        O.w = O.w * r0 + o.w * r1;
+        M = Mb;
+      }
+      const float inv = (a.partial && !(L > 0.f)) ? 0.f : 1.f / L;
+      *reinterpret_cast<float4*>(out_base + idx4 * 4) = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+      if (ml_base && (idx4 * 4) % HD == 0) {
+        ml_base[2 * g] = M;
+        ml_base[2 * g + 1] = L;
+      }
     }
   }
-  if (rank == 0 && threadIdx.x == 0) a.counters[unit] = 0u;  // ticket ready for the next launch
+  // ticket ready for the next launch: with several mergers the last one to
+  // finish resets it (each adds one more after its merge)
+  if (threadIdx.x == 0) {
+    if (mergers <= 1) {
+      if (rank == 0) a.counters[unit] = 0u;
+    } else if (atomicAdd(&a.counters[unit], 1u) == (unsigned)(n_parts + mergers - 1)) {
+      a.counters[unit] = 0u;
+    }
+  }
   decode_signal_done(a);
 }
 

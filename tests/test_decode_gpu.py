@@ -159,7 +159,8 @@ def test_errors_are_reported_not_fatal():
         ctx.decode(1, 3, q)  # the context stays usable
 
 
-@pytest.mark.parametrize("plan", ["1:1", "5:1", "16:1", "16:16", "32:16", "24:8", "8:2", "64:4"])
+@pytest.mark.parametrize("plan", ["1:1", "5:1", "16:1", "16:16", "32:16", "24:8", "8:2", "64:4", "48:1", "79:1",
+                                  "128:1"])
 @pytest.mark.parametrize("name", ["llama31_8b_decode_8k", "gemma_2b_decode"])
 def test_every_merge_path(monkeypatch, plan, name):
     """Pin the split-K decomposition (single CTA, global last-arriver merge,
@@ -172,6 +173,23 @@ def test_every_merge_path(monkeypatch, plan, name):
         got = _gpu_step(ctx, sh, 0, k, v, q)
     want, _ = _oracle(sh, 0, k, v, q)
     _check(got, want, f"{name} plan {plan}")
+
+
+@pytest.mark.parametrize("plan", ["79:1", "128:1"])
+def test_several_mergers_across_launches(monkeypatch, plan):
+    """One KV head split 79 or 128 ways fits one wave, so the last four parts
+    to finish each merge a quarter of the output; the unit's ticket must be
+    back at zero for every following launch (several positions in a row)."""
+    monkeypatch.setenv("L3P_DECODE_PLAN", plan)
+    sh = CONFIGS["gemma_2b_decode"].with_(pos=2047, seq_len=2048)
+    k, v, q = decode_inputs(sh, 0)
+    with AttnContext.for_shape(sh, n_layers=1) as ctx:
+        ctx.load_kv(0, 0, k, v)
+        for pos in (2047, 1500, 2047, 1024):
+            got = ctx.decode(0, pos, q)
+            want, _ = _oracle(sh.with_(pos=pos), 0, k, v, q)
+            _check(got, want, f"plan {plan} pos {pos}")
+        ctx.check()
 
 
 def test_default_plans_are_reported():
