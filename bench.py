@@ -917,10 +917,18 @@ def run_e2e(ctx, sh, world, args, torch):
     vh = torch.randn((L, sh.n_kv_heads, sh.head_dim)).pin_memory().numpy()
     oh = torch.zeros((L, sh.n_heads, sh.head_dim)).pin_memory().numpy()
     ctx.set_stream(None)
+    # the C-ABI call itself, with the buffers' addresses taken once (the
+    # AttnContext.step wrapper re-validates its numpy arguments on every call,
+    # which costs the Python loop ~4 us per layer)
+    fn, h, pos = ctx.lib.l3p_attn_step, ctx.h, sh.pos
+    args = [(layer, qh[layer].ctypes.data, kh[layer].ctypes.data, vh[layer].ctypes.data, oh[layer].ctypes.data)
+            for layer in range(L)]
 
     def step():
-        for layer in range(L):
-            ctx.step(layer, sh.pos, qh[layer], kh[layer], vh[layer], oh[layer])
+        for layer, qp, kp, vp, op in args:
+            rc = fn(h, layer, pos, qp, kp, vp, op)
+            if rc:
+                ctx._ok(rc, "l3p_attn_step")
 
     for _ in range(max(3, args.warmup)):
         step()

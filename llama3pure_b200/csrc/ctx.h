@@ -53,12 +53,6 @@ struct l3p_attn_ctx {
   // device error word in mapped pinned host memory
   int* err_host = nullptr;
   int* err_dev = nullptr;
-  // completion word of the host-pointer decode calls (mapped pinned memory,
-  // written by the launch's last output writer) and its device-side counter
-  unsigned* done_host = nullptr;
-  unsigned* done_dev = nullptr;
-  unsigned* done_ctr = nullptr;
-  unsigned done_seq = 0;
   long long launches = 0;
   // clusters of 2^i CTAs of this context's decode kernel that fit on the GPU at once
   int max_clusters[5] = {0, 0, 0, 0, 0};
@@ -168,14 +162,12 @@ int check_layer(l3p_attn_ctx* ctx, int layer);
 int check_pos_full(l3p_attn_ctx* ctx, int pos);
 int read_err(l3p_attn_ctx* ctx);
 int finish_host_call(l3p_attn_ctx* ctx);
-int finish_host_decode(l3p_attn_ctx* ctx);
 void owned_rows(const l3p_attn_ctx* ctx, int* row_lo, int* row_hi);
 // Decode core shared by the single-layer, multi-layer, prefill and partial
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz, const float* q,
                   float* out, float* part_o, float* part_ml, cudaStream_t s, const float* k_new = nullptr,
-                  const float* v_new = nullptr, bool allow_overlap = false, bool new_pending = false,
-                  bool signal_host = false);
+                  const float* v_new = nullptr, bool allow_overlap = false, bool new_pending = false);
 // Cache rows of n_tok tokens.  trigger_early lets the next kernel launch
 // before the rows are written; it must then wait for them itself.
 int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v, cudaStream_t s,

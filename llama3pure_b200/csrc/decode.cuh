@@ -111,32 +111,11 @@ struct DecodeArgs {
   int is_gemma3, swa_window, swa_pattern;
   int partial;
   int new_pending;         // the cache row of pos is written by the kernel before this one on the stream
-  // optional completion signal for a waiting host: every CTA that writes final
-  // outputs counts itself on done_ctr; the last of done_writers stores
-  // done_value into done_flag (mapped host memory) after a system-scope fence
-  unsigned* done_ctr;
-  unsigned* done_flag;
-  unsigned done_value, done_writers;
   // mergers of the global stage (no cluster): the last merge_k parts to
   // finish each merge 1/merge_k of the output; > 1 only for launches whose
   // CTAs are all resident at once (a merger waits for the unit's last part)
   int merge_k;
 };
-
-// A CTA that has written its share of the launch's outputs: the last such CTA
-// tells the host that the launch's results are in place.
-__device__ __forceinline__ void decode_signal_done(const DecodeArgs& a) {
-  if (a.done_flag == nullptr) return;
-  __syncthreads();  // every thread's output stores precede the count
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    if (atomicAdd(a.done_ctr, 1u) + 1u == a.done_writers) {
-      *a.done_ctr = 0u;
-      __threadfence_system();
-      asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.done_flag), "r"(a.done_value) : "memory");
-    }
-  }
-}
 
 #ifndef L3P_DECODE_WARPS
 #define L3P_DECODE_WARPS 8  // warps per CTA
@@ -370,7 +349,6 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
       ml_base[2 * threadIdx.x] = s_cm[threadIdx.x];
       ml_base[2 * threadIdx.x + 1] = s_cl[threadIdx.x];
     }
-    decode_signal_done(a);
     return;
   }
 
@@ -430,7 +408,6 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
     }
     if (last_stage) {
       cluster.sync();  // no CTA leaves while another still reads its shared memory
-      decode_signal_done(a);
       return;
     }
     __threadfence();
@@ -559,7 +536,6 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
       a.counters[unit] = 0u;
     }
   }
-  decode_signal_done(a);
 }
 
 template <int HD, int GT>
