@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <deque>
 #include <initializer_list>
 #include <string>
 #include <vector>
@@ -64,6 +65,9 @@ struct l3p_attn_ctx {
   // split scratch is used in kScratchSlots rotating slices so that launches
   // overlapping on the GPU never share partials or tickets
   unsigned long long launch_seq = 0;
+  // cache rows stored by the fused append of recent decode launches, per
+  // layer: (launch_seq of the launch, position); see launch_decode
+  std::vector<std::deque<std::pair<unsigned long long, int>>> recent_stores;
   // pre-attention step (l3p_attn_set_rope): (cos, sin) per position and pair,
   // [seq_len][hd/2], for dense layers and for Gemma3 SWA layers (the same
   // array when the model has one table), QK-norm weights [2][n_layers][hd]
@@ -167,11 +171,9 @@ void owned_rows(const l3p_attn_ctx* ctx, int* row_lo, int* row_hi);
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz, const float* q,
                   float* out, float* part_o, float* part_ml, cudaStream_t s, const float* k_new = nullptr,
-                  const float* v_new = nullptr, bool allow_overlap = false, bool new_pending = false);
-// Cache rows of n_tok tokens.  trigger_early lets the next kernel launch
-// before the rows are written; it must then wait for them itself.
-int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v, cudaStream_t s,
-                  bool trigger_early = false);
+                  const float* v_new = nullptr, bool allow_overlap = false);
+// Cache rows of n_tok tokens.  The next kernel launches when the rows are written.
+int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v, cudaStream_t s);
 int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
                       cudaStream_t s);
 

@@ -80,10 +80,10 @@ __device__ __forceinline__ void cp_async_wait() {
 struct DecodeArgs {
   const float* kc;         // K cache, all layers: [n_layers][kvh_count][cap][HD]
   float* vc;               // V cache, same layout
-  const int8_t* k8;        // Q8_0 cache (decode_q8_kernel): int8 values, same layout as kc
-  const int8_t* v8;
-  const uint16_t* ksc;     // fp16 block scales: [n_layers][kvh_count][cap][HD/32]
-  const uint16_t* vsc;
+  int8_t* k8;              // Q8_0 cache (decode_q8_kernel): int8 values, same layout as kc
+  int8_t* v8;              //   (written only by the fused append)
+  uint16_t* ksc;           // fp16 block scales: [n_layers][kvh_count][cap][HD/32]
+  uint16_t* vsc;
   float* kc_w;             // writable alias of kc (fused append)
   long long layer_stride;  // kvh_count * cap * HD
   long long head_stride;   // cap * HD
@@ -110,11 +110,13 @@ struct DecodeArgs {
   int cluster;             // CTAs per thread-block cluster (1 = no cluster); divides nsplit
   int is_gemma3, swa_window, swa_pattern;
   int partial;
-  int new_pending;         // the cache row of pos is written by the kernel before this one on the stream
   // mergers of the global stage (no cluster): the last merge_k parts to
   // finish each merge 1/merge_k of the output; > 1 only for launches whose
   // CTAs are all resident at once (a merger waits for the unit's last part)
   int merge_k;
+  // cache rows of positions >= wait_pos may still be being stored by an
+  // earlier launch in flight: copied only after griddepcontrol.wait (INT_MAX: none)
+  int wait_pos;
 };
 
 #ifndef L3P_DECODE_WARPS
@@ -576,7 +578,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
   const float* vnew = fused ? a.v_new + (long long)z * a.new_zstride + (long long)kvh * HD : nullptr;
   const int new_row = pos - lo;  // index of the new token's row in the range
   // tiles holding the new row are copied only after the preceding kernel has finished
-  const bool wait_new = (fused || (a.new_pending && pos >= lo && pos < hi));
+  const bool wait_new = fused;
 
   // tiles of this warp: t = split + nsplit * (warp + kWarps * i)
   const int first = split + a.nsplit * warp;
@@ -607,17 +609,20 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
     }
   };
 
-  // Start the stream before anything else.  Cached rows [start_t, pos) were
-  // written by earlier launches; q and the new row come from the kernel that
-  // precedes this one, so with programmatic dependent launch they are read
-  // only after pdl_wait() (a tile holding the new row waits first).
+  // Start the stream before anything else.  q and the new row come from the
+  // kernel that precedes this one, and rows from a.wait_pos on may still be
+  // being stored by an earlier launch of this layer that is in flight, so
+  // with programmatic dependent launch they are read only after pdl_wait():
+  // a warp's tiles come in increasing row order, so from its first tile that
+  // reaches wait_row on, it waits first.
   pdl_launch_dependents();
+  const int wait_row = min(wait_new ? new_row : INT_MAX, a.wait_pos - lo);
   bool waited = false;
 #pragma unroll
   for (int i = 0; i < C::kStages - 1; ++i) {
     if (i < my_tiles) {
       const int r0 = (first + i * step) * C::kR;
-      if (wait_new && !waited && new_row >= r0 && new_row < r0 + C::kR) {
+      if (!waited && r0 + C::kR > wait_row) {
         pdl_wait();
         waited = true;
       }
@@ -844,15 +849,12 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
 }
 
 // Token K/V rows -> head-major cache rows.  k, v: [n_tok][src_stride] with
-// KV head h at offset h*HD; grid (n_tok, kvh_count), HD/4 threads.
-// trigger_early: let the next kernel launch at once (it must itself wait
-// before reading the rows written here, as decode does with new_pending);
-// otherwise it launches when this grid completes.
+// KV head h at offset h*HD; grid (n_tok, kvh_count), HD/4 threads.  The next
+// kernel launches when this grid completes (it may read these rows at once).
 static __global__ void kv_append_kernel(float* __restrict__ kc, float* __restrict__ vc, long long head_stride,
                                  int hd, const float* __restrict__ k, const float* __restrict__ v,
-                                 long long src_stride, int kv_head_begin, int row0, int trigger_early) {
+                                 long long src_stride, int kv_head_begin, int row0) {
   const int tok = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
-  if (trigger_early) pdl_launch_dependents();
   pdl_wait();  // the rows come from the kernel before this one
   const long long src = (long long)tok * src_stride + (long long)(kv_head_begin + h) * hd + 4 * t;
   const long long dst = (long long)h * head_stride + (long long)(row0 + tok) * hd + 4 * t;

@@ -73,35 +73,48 @@ __device__ __forceinline__ uint16_t q8_quantize_lanes(const float (&x)[N], uint3
   return fp32_to_fp16_trunc(d);
 }
 
+// One row of HD values quantised by a warp: lane holds values
+// [lane*HD/32, (lane+1)*HD/32) of src; returns the scale of the lane's block.
+template <int HD>
+__device__ __forceinline__ uint16_t q8_quantize_row(const float* src, int lane, uint32_t (&w)[(HD / 32 + 3) / 4]) {
+  constexpr int N = HD / 32;
+  float x[N];
+#pragma unroll
+  for (int i = 0; i < N; ++i) x[i] = src[lane * N + i];
+  return q8_quantize_lanes<N>(x, w);
+}
+
+// Store a row quantised by q8_quantize_row: its int8 values at dst8 (the row's
+// first byte) and its block scales at dsc (the row's first scale); global or
+// shared memory.
+template <int HD>
+__device__ __forceinline__ void q8_store_row(int8_t* dst8, uint16_t* dsc, int lane, const uint32_t (&w)[(HD / 32 + 3) / 4],
+                                             uint16_t d) {
+  constexpr int N = HD / 32;
+  if constexpr (N == 2) {
+    *reinterpret_cast<uint16_t*>(dst8 + lane * N) = (uint16_t)w[0];
+  } else {
+#pragma unroll
+    for (int i = 0; i < N / 4; ++i) reinterpret_cast<uint32_t*>(dst8 + lane * N)[i] = w[i];
+  }
+  if ((lane * N) % 32 == 0) dsc[lane * N / 32] = d;
+}
+
 // Token K/V rows -> Q8_0 cache rows: one warp per (token, owned KV head) row,
 // HD/32 values per lane.  k, v: [n_tok][src_stride] with KV head h at h*HD.
 template <int HD>
 __global__ void kv_append_q8_kernel(int8_t* __restrict__ k8, int8_t* __restrict__ v8, uint16_t* __restrict__ ksc,
                                     uint16_t* __restrict__ vsc, long long head_stride, const float* __restrict__ k,
-                                    const float* __restrict__ v, long long src_stride, int kv_head_begin, int row0,
-                                    int trigger_early) {
-  constexpr int N = HD / 32;
+                                    const float* __restrict__ v, long long src_stride, int kv_head_begin, int row0) {
   const int tok = blockIdx.x, h = blockIdx.y, lane = threadIdx.x;
-  if (trigger_early) pdl_launch_dependents();  // as kv_append_kernel
   pdl_wait();  // the rows come from the kernel before this one
-  const long long src = (long long)tok * src_stride + (long long)(kv_head_begin + h) * HD + lane * N;
+  const long long src = (long long)tok * src_stride + (long long)(kv_head_begin + h) * HD;
   const long long row = (long long)h * head_stride / HD + row0 + tok;  // row index in the cache
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
-    const float* s = (which ? v : k) + src;
-    float x[N];
-#pragma unroll
-    for (int i = 0; i < N; ++i) x[i] = s[i];
-    uint32_t w[(N + 3) / 4];
-    const uint16_t d = q8_quantize_lanes<N>(x, w);
-    int8_t* dst8 = (which ? v8 : k8) + row * HD + lane * N;
-    if constexpr (N == 2) {
-      *reinterpret_cast<uint16_t*>(dst8) = (uint16_t)w[0];
-    } else {
-#pragma unroll
-      for (int i = 0; i < N / 4; ++i) reinterpret_cast<uint32_t*>(dst8)[i] = w[i];
-    }
-    if ((lane * N) % 32 == 0) (which ? vsc : ksc)[row * (HD / 32) + lane * N / 32] = d;
+    uint32_t w[(HD / 32 + 3) / 4];
+    const uint16_t d = q8_quantize_row<HD>((which ? v : k) + src, lane, w);
+    q8_store_row<HD>((which ? v8 : k8) + row * HD, (which ? vsc : ksc) + row * (HD / 32), lane, w, d);
   }
 }
 
@@ -146,6 +159,9 @@ static __global__ void q8_dequant_kernel(const int8_t* __restrict__ d8, const ui
 #ifndef L3P_Q8_RING_KB
 #define L3P_Q8_RING_KB 192  // shared-memory ring per CTA
 #endif
+#ifndef L3P_Q8_CTAS_PER_SM
+#define L3P_Q8_CTAS_PER_SM 1  // resident CTAs per SM the launch bounds ask for
+#endif
 
 template <int HD, int GT>
 struct DecodeQ8Cfg {
@@ -160,13 +176,16 @@ struct DecodeQ8Cfg {
   static constexpr int kStageBytes = 2 * (kTileKB + kTileSB);
   static constexpr int kStagesRaw = (L3P_Q8_RING_KB * 1024 / kWarps) / kStageBytes;
   static constexpr int kStages = kStagesRaw < 2 ? 2 : (kStagesRaw > 8 ? 8 : kStagesRaw);
-  static constexpr int kRingBytes = kWarps * kStages * kStageBytes;
+  // the ring doubles as the warps' merge buffer: at least (kWarps + 1) * GT * HD floats
+  static constexpr int kRingBytes = kWarps * kStages * kStageBytes > (kWarps + 1) * GT * HD * 4
+                                        ? kWarps * kStages * kStageBytes
+                                        : (kWarps + 1) * GT * HD * 4;
   static constexpr int kSmemBytes = kRingBytes;
   static constexpr int kEPL = HD / 32;  // values of a V row per lane
   static constexpr int kKB = HD / 8;    // K bytes per lane in the score phase (8 lanes per row)
   static constexpr int kKW = kKB / 4;   // ... as 32-bit words
   static constexpr int kLanesPerBlock = 32 / kKB;  // lanes sharing one 32-value block in the score phase
-  static constexpr int kCtasPerSm = 1;
+  static constexpr int kCtasPerSm = L3P_Q8_CTAS_PER_SM;
   static_assert(kTileKB % 512 == 0, "K tile copies cover the warp");
   static_assert(kStageBytes % 16 == 0, "stage alignment");
   static_assert((kWarps + 1) * GT * HD * 4 <= kRingBytes, "merge buffer fits in the ring");
@@ -218,6 +237,16 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
   const int step = a.nsplit * C::kWarps;
   const int my_tiles = n_tiles > first ? (n_tiles - first + step - 1) / step : 0;
   unsigned char* wring = smem_raw + warp * C::kStages * C::kStageBytes;
+
+  // Fused append (k_new set): the warp whose tile holds the new row quantises
+  // the token's K and V rows itself (the bytes kv_append_q8_kernel writes,
+  // c:3299-3312) and attends to them from registers; in the units of q-head
+  // group 0 it also stores them into the cache.
+  const bool fused = a.k_new != nullptr && pos >= lo && pos < hi;
+  const int new_row = pos - lo;
+  const int new_tile = new_row / C::kR;
+  const bool own_new = fused && new_tile >= first && (new_tile - first) % step == 0;  // warp-uniform
+  const int new_i = own_new ? (new_tile - first) / step : -1;
 
   // stage: [K int8 tile][V int8 tile][K scales][V scales]
   auto issue = [&](int i) {
@@ -273,16 +302,15 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
       if (base % 32 == 0) s_dq[base / 32] = fp16_to_f32(d);
     }
   }
-  // a tile holding the row of pos, when the kernel before this one writes it,
-  // is copied only after that kernel has finished
-  const bool wait_new = a.new_pending && pos >= lo && pos < hi;
-  const int new_row = pos - lo;
+  // cached rows [lo, pos) come from earlier launches (those from a.wait_pos
+  // on are copied after the wait, as in decode_f32_kernel); the row of pos,
+  // when fused, replaces its stale copy in the stage after the copy lands
+  const int wait_row = a.wait_pos - lo;
   bool waited = warp == 0;
 #pragma unroll
   for (int i = 0; i < C::kStages - 1; ++i) {
     if (i < my_tiles) {
-      const int r0 = (first + i * step) * C::kR;
-      if (wait_new && !waited && new_row >= r0 && new_row < r0 + C::kR) {
+      if (!waited && (first + i * step) * C::kR + C::kR > wait_row) {
         pdl_wait();
         waited = true;
       }
@@ -291,6 +319,19 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
     cp_async_commit();
   }
   pdl_wait();
+  constexpr int kNW = (HD / 32 + 3) / 4;  // packed int8 words of a lane's share of a row
+  uint32_t nkw[kNW], nvw[kNW];
+  uint16_t nkd = 0, nvd = 0;
+  if (own_new) {
+    const long long src = (long long)z * a.new_zstride + (long long)kvh * HD;
+    nkd = q8_quantize_row<HD>(a.k_new + src, lane, nkw);
+    nvd = q8_quantize_row<HD>(a.v_new + src, lane, nvw);
+    if (hg == 0) {
+      const long long crow = row0 + new_row;  // cache row of pos
+      q8_store_row<HD>(a.k8 + crow * HD, a.ksc + crow * (HD / 32), lane, nkw, nkd);
+      q8_store_row<HD>(a.v8 + crow * HD, a.vsc + crow * (HD / 32), lane, nvw, nvd);
+    }
+  }
   __syncthreads();  // s_q8 / s_dq written
   // score layout: lane (rq, sg) holds values [sg*HD/8, (sg+1)*HD/8) of every
   // q row and the scale of their block
@@ -320,7 +361,16 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
     cp_async_commit();
     cp_async_wait<C::kStages - 1>();
     __syncwarp();
-    const unsigned char* st = wring + (i % C::kStages) * C::kStageBytes;
+    unsigned char* stw = wring + (i % C::kStages) * C::kStageBytes;
+    if (i == new_i) {  // the stage holds the cache's old row of pos: put the token's row in its place
+      const int r = new_row - (first + i * step) * C::kR;
+      q8_store_row<HD>(reinterpret_cast<int8_t*>(stw) + r * HD,
+                       reinterpret_cast<uint16_t*>(stw + 2 * C::kTileKB) + r * (HD / 32), lane, nkw, nkd);
+      q8_store_row<HD>(reinterpret_cast<int8_t*>(stw) + C::kTileKB + r * HD,
+                       reinterpret_cast<uint16_t*>(stw + 2 * C::kTileKB + C::kTileSB) + r * (HD / 32), lane, nvw, nvd);
+      __syncwarp();
+    }
+    const unsigned char* st = stw;
     const int8_t* kt = reinterpret_cast<const int8_t*>(st);
     const int8_t* vt = kt + C::kTileKB;
     const uint16_t* kst = reinterpret_cast<const uint16_t*>(st + 2 * C::kTileKB);
@@ -411,28 +461,40 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
 #pragma unroll
         for (int g = 0; g < GT; ++g) pr[g] = sp[r * GT + g];
       }
-      float vx[C::kEPL];
+      // int8 -> fp32 exactly, two values per instruction: byte b + 128 as the
+      // low mantissa byte of 2^23, minus 2^23 + 128
+      float2 vx[C::kEPL / 2];
       float dv[(C::kEPL + 3) / 4];
+      const float2 kBias = make_float2(-8388736.0f, -8388736.0f);
       if constexpr (HD == 64) {
-        const uint32_t t = *reinterpret_cast<const uint16_t*>(vt + r * HD + 2 * lane);
-        vx[0] = (float)(int8_t)(t & 0xff);
-        vx[1] = (float)(int8_t)(t >> 8);
+        const uint32_t t = *reinterpret_cast<const uint16_t*>(vt + r * HD + 2 * lane) ^ 0x8080u;
+        vx[0] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(t, 0x4B000000u, 0x7540)),
+                                       __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7541))),
+                           kBias);
         dv[0] = fp16_to_f32(vst[r * (HD / 32) + lane / 16]);
       } else {
 #pragma unroll
         for (int c = 0; c < HD / 128; ++c) {
-          const uint32_t t = *reinterpret_cast<const uint32_t*>(vt + r * HD + c * 128 + 4 * lane);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) vx[4 * c + j] = (float)(int8_t)((t >> (8 * j)) & 0xff);
+          const uint32_t t = *reinterpret_cast<const uint32_t*>(vt + r * HD + c * 128 + 4 * lane) ^ 0x80808080u;
+          vx[2 * c] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(t, 0x4B000000u, 0x7540)),
+                                             __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7541))),
+                                 kBias);
+          vx[2 * c + 1] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(t, 0x4B000000u, 0x7542)),
+                                                 __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7543))),
+                                     kBias);
           dv[c] = fp16_to_f32(vst[r * (HD / 32) + c * 4 + lane / 8]);
         }
       }
+      // acc += v * (block scale * weight), as c:1605; the packed FMA rounds
+      // each half like fmaf
 #pragma unroll
       for (int g = 0; g < GT; ++g) {
 #pragma unroll
-        for (int e = 0; e < C::kEPL; ++e) {
-          const float sw = dv[e / 4] * pr[g];  // block scale * weight, as c:1605
-          acc[g][e] = fmaf(vx[e], sw, acc[g][e]);
+        for (int e = 0; e < C::kEPL; e += 2) {
+          const float sw = dv[e / 4] * pr[g];
+          const float2 r2 = __ffma2_rn(vx[e / 2], make_float2(sw, sw), make_float2(acc[g][e], acc[g][e + 1]));
+          acc[g][e] = r2.x;
+          acc[g][e + 1] = r2.y;
         }
       }
     }

@@ -5,6 +5,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -249,10 +250,9 @@ int read_err(l3p_attn_ctx* ctx) {
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
                   const float* q, float* out, float* part_o, float* part_ml, cudaStream_t s,
-                  const float* k_new, const float* v_new, bool allow_overlap, bool new_pending) {
+                  const float* k_new, const float* v_new, bool allow_overlap) {
   const KernelInfo ki = kernel_for(ctx->hd, ctx->GT, ctx->q8);
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
-  if (ctx->q8 && k_new) return fail(ctx, L3P_E_INVAL, "fused append needs an fp32 cache");
   // longest attended range over the slices (upper bound; the kernel clips per slice)
   const int pos_max = pos0 + (nz - 1) * pos_step;
   const long long lo = ctx->cfg.seq_begin;
@@ -261,7 +261,24 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   const long long units = (long long)nz * ctx->kvh_count * ctx->n_hg;
   const PlanLimits lim = limits_of(ctx);
   const Plan plan = plan_splits(&lim, P, units, ki.rows, ki.ctas_per_sm);
-  const int slot = (int)(ctx->launch_seq++ % kScratchSlots);
+  // Rows a fused append of an earlier launch may still be storing.  Under
+  // programmatic dependent launch every launch of a chain but the newest is
+  // resident at once (each has triggered, and none of its CTAs exits before
+  // the launch before it completes), and a decode CTA holds a whole SM's
+  // shared memory, so a store more than num_sms * ctas_per_sm decode launches
+  // back has landed; the window doubles that.  The kernel copies the rows from
+  // wait_pos on only after griddepcontrol.wait.
+  const unsigned long long window = 2ull * ctx->num_sms * ki.ctas_per_sm + 2;
+  int wait_pos = INT_MAX;
+  for (int z = 0; z < (layer_step ? nz : 1); ++z) {
+    auto& d = ctx->recent_stores[layer0 + z * layer_step];
+    while (!d.empty() && ctx->launch_seq - d.front().first > window) d.pop_front();
+    for (const auto& e : d) wait_pos = std::min(wait_pos, e.second);
+  }
+  const unsigned long long seq = ctx->launch_seq++;
+  const int slot = (int)(seq % kScratchSlots);
+  if (k_new)  // this launch stores the row of pos0 + z*pos_step of each slice's layer
+    for (int z = 0; z < nz; ++z) ctx->recent_stores[layer0 + z * layer_step].emplace_back(seq, pos0 + z * pos_step);
 
   DecodeArgs a{};
   a.kc = ctx->kc;
@@ -302,9 +319,9 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   a.swa_window = ctx->cfg.swa_window;
   a.swa_pattern = ctx->cfg.swa_pattern;
   a.partial = part_o != nullptr;
-  a.new_pending = new_pending ? 1 : 0;
   // several mergers for the global stage when every CTA of the launch is
   // resident at once (a merger waits for its unit's last part)
+  a.wait_pos = wait_pos;
   a.merge_k = 1;
   const long long grid_ctas = (long long)plan.nsplit * units;
   if (plan.cluster == 1 && plan.nsplit >= kMergersFrom && nz <= 65535 &&
@@ -353,7 +370,7 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
 // of the destination head block; grid.y heads of head_elems values each.
 int launch_append_q8(l3p_attn_ctx* ctx, int8_t* k8, int8_t* v8, uint16_t* ksc, uint16_t* vsc, dim3 grid,
                      const float* k, const float* v, long long src_stride, int kv_head_begin, int row0,
-                     cudaStream_t s, int trigger_early) {
+                     cudaStream_t s) {
   cudaLaunchConfig_t lc{};
   lc.gridDim = grid;
   lc.blockDim = dim3(32, 1, 1);
@@ -364,15 +381,15 @@ int launch_append_q8(l3p_attn_ctx* ctx, int8_t* k8, int8_t* v8, uint16_t* ksc, u
   switch (ctx->hd) {
     case 64:
       L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kv_append_q8_kernel<64>, k8, v8, ksc, vsc, hs, k, v, src_stride,
-                                       kv_head_begin, row0, trigger_early));
+                                       kv_head_begin, row0));
       break;
     case 128:
       L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kv_append_q8_kernel<128>, k8, v8, ksc, vsc, hs, k, v, src_stride,
-                                       kv_head_begin, row0, trigger_early));
+                                       kv_head_begin, row0));
       break;
     default:
       L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kv_append_q8_kernel<256>, k8, v8, ksc, vsc, hs, k, v, src_stride,
-                                       kv_head_begin, row0, trigger_early));
+                                       kv_head_begin, row0));
       break;
   }
   ++ctx->launches;
@@ -380,7 +397,7 @@ int launch_append_q8(l3p_attn_ctx* ctx, int8_t* k8, int8_t* v8, uint16_t* ksc, u
 }
 
 int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v,
-                  cudaStream_t s, bool trigger_early) {
+                  cudaStream_t s) {
   // clip the tokens to the owned position range
   const int own_lo = ctx->cfg.seq_begin, own_hi = ctx->cfg.seq_begin + ctx->seq_count;
   const int t_lo = std::max(pos0, own_lo), t_hi = std::min(pos0 + n_tok, own_hi);
@@ -396,7 +413,7 @@ int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float
       // quantise the rows into the Q8_0 cache (quantize_to_q8_0_cache, c:1535-1570)
       if (int rc = launch_append_q8(ctx, ctx->k8 + off, ctx->v8 + off, ctx->ksc + off / 32, ctx->vsc + off / 32, grid,
                                     ks + (long long)(t0 - t_lo) * src_stride, vs + (long long)(t0 - t_lo) * src_stride,
-                                    src_stride, ctx->cfg.kv_head_begin, t0 - own_lo, s, trigger_early ? 1 : 0))
+                                    src_stride, ctx->cfg.kv_head_begin, t0 - own_lo, s))
         return rc;
       continue;
     }
@@ -408,7 +425,7 @@ int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float
     pdl_attr(ctx, lc, attr);
     L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kv_append_kernel, ctx->kc + off, ctx->vc + off, ctx->head_elems, ctx->hd,
                                      ks + (long long)(t0 - t_lo) * src_stride, vs + (long long)(t0 - t_lo) * src_stride,
-                                     src_stride, ctx->cfg.kv_head_begin, t0 - own_lo, trigger_early ? 1 : 0));
+                                     src_stride, ctx->cfg.kv_head_begin, t0 - own_lo));
     ++ctx->launches;
   }
   return L3P_OK;
@@ -538,6 +555,7 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   ctx->G = c.n_heads / c.n_kv_heads;
   ctx->GT = (ctx->G % 8 == 0) ? 8 : (ctx->G % 4 == 0) ? 4 : (ctx->G % 2 == 0) ? 2 : 1;
   ctx->n_hg = ctx->G / ctx->GT;
+  ctx->recent_stores.resize(c.n_layers);
   ctx->kvh_count = kvh_count;
   ctx->seq_count = seq_count;
   if (const char* plan = getenv("L3P_DECODE_PLAN")) {
@@ -743,13 +761,8 @@ L3P_API int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
   DeviceScope dev(ctx->cfg.device);
-  if (ctx->q8) {
-    // the new row must be quantised before it is attended to (c:3299-3312): two launches;
-    // the decode streams the cached rows meanwhile and copies the new row after its wait
-    if (int rc = launch_append(ctx, layer, pos, 1, k, v, pick_stream(ctx, stream), true)) return rc;
-    return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), nullptr,
-                         nullptr, true, true);
-  }
+  // one launch: the decode stores the new row (quantised first for a Q8_0
+  // cache, c:3299-3312) and attends to it from its producer's copy
   return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), k, v, true);
 }
 
@@ -892,15 +905,9 @@ L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q,
   // one host->device copy of all inputs; the kernel writes the output into
   // mapped pinned memory, so no device->host copy follows
   L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, ctx->hst, in * 4, cudaMemcpyHostToDevice, ctx->stream));
-  if (ctx->q8) {
-    if (int rc = launch_append(ctx, layer, pos, 1, ctx->st_buf + qd, ctx->st_buf + qd + kvd, ctx->stream)) return rc;
-    if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr, ctx->stream,
-                               nullptr, nullptr))
-      return rc;
-  } else if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr,
-                                    ctx->stream, ctx->st_buf + qd, ctx->st_buf + qd + kvd)) {
+  if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr, ctx->stream,
+                             ctx->st_buf + qd, ctx->st_buf + qd + kvd))
     return rc;
-  }
   if (int rc = finish_host_call(ctx)) return rc;
   memcpy(out + row0, ctx->hst + in + row0, nrow * 4);
   return L3P_OK;
@@ -961,7 +968,7 @@ L3P_API int l3p_attn_load_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, 
         const int nt = std::min(hi - lo - t0, 65535);
         if (int rc = launch_append_q8(ctx, ctx->k8 + off, ctx->v8 + off, ctx->ksc + off / 32, ctx->vsc + off / 32,
                                       dim3(nt, 1), ctx->st_buf + (size_t)t0 * row, ctx->st_buf + n + (size_t)t0 * row,
-                                      (long long)row, 0, lo - ctx->cfg.seq_begin + t0, ctx->stream, 0))
+                                      (long long)row, 0, lo - ctx->cfg.seq_begin + t0, ctx->stream))
           return rc;
       }
     }
@@ -1230,6 +1237,7 @@ L3P_API int l3p_attn_decode_noalloc(const l3p_attn_config* cfg, int layer, int p
   a.is_gemma3 = c.is_gemma3;
   a.swa_window = c.swa_window;
   a.swa_pattern = c.swa_pattern;
+  a.wait_pos = INT_MAX;  // plain stream order: every earlier store has landed
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(plan.nsplit, kvh_count * n_hg, 1);
   lc.blockDim = dim3(kDecodeThreads, 1, 1);

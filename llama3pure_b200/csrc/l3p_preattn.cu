@@ -120,14 +120,8 @@ int step_raw_core(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const f
   if (int rc = ensure_rope_buf(ctx, qd + kvd, s)) return rc;
   float* rq = ctx->rope_buf;
   float* rk = rq + qd;
-  if (ctx->q8) {
-    // the pre-attention kernel quantises the rows into the cache; the decode
-    // copies the row of pos only after that kernel has finished
-    if (int rc = launch_rope(ctx, layer, pos, 1, q, k, v, rq, nullptr, true, s)) return rc;
-    return launch_decode(ctx, layer, 0, pos, 0, 1, rq, out, nullptr, nullptr, s, nullptr, nullptr, allow_overlap,
-                         true);
-  }
-  // fp32: the decode takes the rotated K row and V from their producers and stores them (fused append)
+  // the decode takes the rotated K row and V from their producers and stores
+  // them (fused append; quantised first for a Q8_0 cache)
   if (int rc = launch_rope(ctx, layer, pos, 1, q, k, nullptr, rq, rk, false, s)) return rc;
   return launch_decode(ctx, layer, 0, pos, 0, 1, rq, out, nullptr, nullptr, s, rk, v, allow_overlap);
 }

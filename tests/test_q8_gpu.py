@@ -250,9 +250,9 @@ def test_fp32_only_entry_points_refuse_a_q8_cache():
 
 @pytest.mark.parametrize("overlap", [False, True])
 def test_step_dev_layer_chain_in_a_graph(overlap):
-    """Consecutive layers of step_dev (append, then decode) captured in a CUDA
-    graph: with programmatic dependent launch the decode starts streaming
-    while the append runs and copies the new row only after its wait."""
+    """Consecutive layers of step_dev (one launch each: the decode quantises
+    and stores the new row itself) captured in a CUDA graph, with and without
+    programmatic dependent launch between the layers."""
     import torch
 
     sh = CONFIGS["llama31_8b_decode_8k"].with_(seq_len=1024, pos=1023, n_layers=4)
@@ -287,3 +287,58 @@ def test_step_dev_layer_chain_in_a_graph(overlap):
         want, _ = o.decode(layer, sh.pos, qs[layer])
         o.close()
         _check(got[layer].reshape(want.shape), want, f"q8 step_dev chain layer {layer} overlap={overlap}")
+
+
+@pytest.mark.parametrize("kv_format", [0, Q8])
+@pytest.mark.parametrize("plan", ["auto", "1:1", "3:1"])
+def test_same_layer_consecutive_positions_under_overlap(monkeypatch, kv_format, plan):
+    """One layer stepped at positions p, p+1, ... back to back in a CUDA graph
+    with programmatic dependent launch, across tile boundaries (8 rows for
+    fp32, 16 for Q8_0): each step's launch may start while the previous one
+    still runs, and copies the cache row the previous one stored; that store
+    must land first.  Every output matches the oracle and the cache holds the
+    appended rows (Q8_0: the reference quantiser's bytes)."""
+    import torch
+
+    if plan != "auto":
+        monkeypatch.setenv("L3P_DECODE_PLAN", plan)
+    sh = AttnShape("samelayer", 1, 8, 2, 128, 64, pos=60, seed=71)
+    p0, n = 13, 20  # positions 13..32 cross the boundaries at 16, 24 and 32
+    k, v, q = decode_inputs(sh, 0)
+    qs = np.random.default_rng(72).standard_normal((n, sh.n_heads, sh.head_dim)).astype(np.float32)
+    with AttnContext.for_shape(sh, n_layers=1, kv_format=kv_format) as ctx:
+        ctx.load_kv(0, 0, np.ascontiguousarray(k[:, :p0]), np.ascontiguousarray(v[:, :p0]))
+        dq = torch.from_numpy(qs).cuda()
+        dk = torch.from_numpy(np.ascontiguousarray(k[:, p0:p0 + n].transpose(1, 0, 2))).cuda()
+        dv = torch.from_numpy(np.ascontiguousarray(v[:, p0:p0 + n].transpose(1, 0, 2))).cuda()
+        out = torch.zeros_like(dq)
+        ctx.set_overlap(True)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(n):
+                    ctx.step_dev(0, p0 + i, dq[i], dk[i], dv[i], out[i], s)
+            g.replay()
+        torch.cuda.synchronize()
+        ctx.check()
+        got = out.cpu().numpy()
+        if kv_format == Q8:
+            kb, vb = ctx.read_kv_q8(0, p0, n)
+        else:
+            kc, vc = ctx.read_kv(0, p0, n)
+        del g
+    if kv_format == Q8:
+        np.testing.assert_array_equal(kb, _oracle_blocks(k[:, p0:p0 + n]))
+        np.testing.assert_array_equal(vb, _oracle_blocks(v[:, p0:p0 + n]))
+    else:
+        np.testing.assert_array_equal(kc, k[:, p0:p0 + n])
+        np.testing.assert_array_equal(vc, v[:, p0:p0 + n])
+    mode = O.MODE_Q8 if kv_format == Q8 else O.MODE_F32
+    o = O.Oracle(sh, mode, "port", n_layers=1)
+    o.load_kv(0, 0, k, v)
+    for i in range(n):
+        want, _ = o.decode(0, p0 + i, qs[i])
+        _check(got[i], want, f"kv_format {kv_format} plan {plan} pos {p0 + i}")
+    o.close()
