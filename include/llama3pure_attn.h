@@ -114,7 +114,8 @@ int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const f
                   const float* v, float* out);
 /* Device form of l3p_attn_step: ONE kernel launch that takes the new K/V row
  * straight from k, v ([n_kv_heads*head_dim]), uses it for position pos and
- * stores it into the cache. */
+ * stores it into the cache (an L3P_KV_Q8_0 cache: quantised first, the bytes
+ * of kv_append, c:3299-3312). */
 int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k,
                       const float* v, float* out, void* stream);
 
