@@ -921,11 +921,11 @@ def run_e2e(ctx, sh, world, args, torch):
     # AttnContext.step wrapper re-validates its numpy arguments on every call,
     # which costs the Python loop ~4 us per layer)
     fn, h, pos = ctx.lib.l3p_attn_step, ctx.h, sh.pos
-    args = [(layer, qh[layer].ctypes.data, kh[layer].ctypes.data, vh[layer].ctypes.data, oh[layer].ctypes.data)
-            for layer in range(L)]
+    calls = [(layer, qh[layer].ctypes.data, kh[layer].ctypes.data, vh[layer].ctypes.data, oh[layer].ctypes.data)
+             for layer in range(L)]
 
     def step():
-        for layer, qp, kp, vp, op in args:
+        for layer, qp, kp, vp, op in calls:
             rc = fn(h, layer, pos, qp, kp, vp, op)
             if rc:
                 ctx._ok(rc, "l3p_attn_step")
