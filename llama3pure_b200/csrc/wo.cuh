@@ -70,6 +70,11 @@ __device__ __forceinline__ float byte_f(uint32_t w, int i) {
   return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7540u | (uint32_t)i));
 }
 constexpr float kTwo23 = 8388608.f;
+// Bytes i and i+1 of w, minus `bias`, as two exact floats: two byte permutes
+// and one packed subtraction.
+__device__ __forceinline__ float2 byte_pair(uint32_t w, int i, float bias) {
+  return __fadd2_rn(make_float2(byte_f(w, i), byte_f(w, i + 1)), make_float2(-bias, -bias));
+}
 
 // Per-format lane work: the lane's columns, its loads of one row's slice and
 // the dot product.
@@ -102,13 +107,16 @@ struct WoQ8 {
     // int8 q: (q ^ 0x80) is q + 128 as an unsigned byte
     const uint32_t wa[4] = {r.a.x ^ 0x80808080u, r.a.y ^ 0x80808080u, r.a.z ^ 0x80808080u, r.a.w ^ 0x80808080u};
     const uint32_t wb[4] = {r.b.x ^ 0x80808080u, r.b.y ^ 0x80808080u, r.b.z ^ 0x80808080u, r.b.w ^ 0x80808080u};
-    float s[4] = {0.f, 0.f, 0.f, 0.f}, t[4] = {0.f, 0.f, 0.f, 0.f};
+    // packed pairs (i, i+1): two products per FFMA2, each rounded like fmaf
+    float2 s[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)}, t[2] = {s[0], s[1]};
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      s[i % 4] = fmaf(byte_f(wa[i / 4], i % 4) - (kTwo23 + 128.f), x[i], s[i % 4]);
-      t[i % 4] = fmaf(byte_f(wb[i / 4], i % 4) - (kTwo23 + 128.f), x[16 + i], t[i % 4]);
+    for (int i = 0; i < 16; i += 2) {
+      s[(i / 2) % 2] = __ffma2_rn(byte_pair(wa[i / 4], i % 4, kTwo23 + 128.f), make_float2(x[i], x[i + 1]), s[(i / 2) % 2]);
+      t[(i / 2) % 2] =
+          __ffma2_rn(byte_pair(wb[i / 4], i % 4, kTwo23 + 128.f), make_float2(x[16 + i], x[17 + i]), t[(i / 2) % 2]);
     }
-    return fp16_to_f32(r.d0) * ((s[0] + s[1]) + (s[2] + s[3])) + fp16_to_f32(r.d1) * ((t[0] + t[1]) + (t[2] + t[3]));
+    return fp16_to_f32(r.d0) * ((s[0].x + s[1].x) + (s[0].y + s[1].y)) +
+           fp16_to_f32(r.d1) * ((t[0].x + t[1].x) + (t[0].y + t[1].y));
   }
   __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
 };
@@ -155,14 +163,14 @@ struct WoQ4K {
     scale_min(r.h.y, r.h.z, r.h.w, 2 * p, sc0, m0);
     scale_min(r.h.y, r.h.z, r.h.w, 2 * p + 1, sc1, m1);
     const uint32_t q[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
-    float lo[2] = {0.f, 0.f}, hi[2] = {0.f, 0.f};
+    float2 lo = make_float2(0.f, 0.f), hi = lo;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 16; i += 2) {
       const uint32_t l4 = q[i / 4] & 0x0f0f0f0fu, h4 = (q[i / 4] >> 4) & 0x0f0f0f0fu;
-      lo[i % 2] = fmaf(byte_f(l4, i % 4) - kTwo23, x[i], lo[i % 2]);
-      hi[i % 2] = fmaf(byte_f(h4, i % 4) - kTwo23, x[16 + i], hi[i % 2]);
+      lo = __ffma2_rn(byte_pair(l4, i % 4, kTwo23), make_float2(x[i], x[i + 1]), lo);
+      hi = __ffma2_rn(byte_pair(h4, i % 4, kTwo23), make_float2(x[16 + i], x[17 + i]), hi);
     }
-    return d * ((float)sc0 * (lo[0] + lo[1]) + (float)sc1 * (hi[0] + hi[1])) -
+    return d * ((float)sc0 * (lo.x + lo.y) + (float)sc1 * (hi.x + hi.y)) -
            dmin * ((float)m0 * xs[0] + (float)m1 * xs[1]);
   }
   __device__ static void xsums(const float (&x)[kLaneCols], float (&xs)[2]) {
@@ -205,7 +213,7 @@ struct WoQ6K {
     const uint32_t a[4] = {r.l0.x, r.l0.y, r.l0.z, r.l0.w};
     const uint32_t b[4] = {r.l1.x, r.l1.y, r.l1.z, r.l1.w};
     const uint32_t c[4] = {r.h.x, r.h.y, r.h.z, r.h.w};
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+    float2 s0 = make_float2(0.f, 0.f), s1 = s0, s2 = s0, s3 = s0;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       // four 6-bit values per byte lane: low/high nibbles of ql with bit pairs of qh (c:885-888)
@@ -214,17 +222,18 @@ struct WoQ6K {
       const uint32_t q2 = ((a[k] >> 4) & 0x0f0f0f0fu) | (((c[k] >> 4) & 0x03030303u) << 4);
       const uint32_t q3 = ((b[k] >> 4) & 0x0f0f0f0fu) | (((c[k] >> 6) & 0x03030303u) << 4);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 4; e += 2) {
         const int i = 4 * k + e;
-        s0 = fmaf(byte_f(q0, e) - (kTwo23 + 32.f), x[i], s0);
-        s1 = fmaf(byte_f(q1, e) - (kTwo23 + 32.f), x[16 + i], s1);
-        s2 = fmaf(byte_f(q2, e) - (kTwo23 + 32.f), x[32 + i], s2);
-        s3 = fmaf(byte_f(q3, e) - (kTwo23 + 32.f), x[48 + i], s3);
+        s0 = __ffma2_rn(byte_pair(q0, e, kTwo23 + 32.f), make_float2(x[i], x[i + 1]), s0);
+        s1 = __ffma2_rn(byte_pair(q1, e, kTwo23 + 32.f), make_float2(x[16 + i], x[17 + i]), s1);
+        s2 = __ffma2_rn(byte_pair(q2, e, kTwo23 + 32.f), make_float2(x[32 + i], x[33 + i]), s2);
+        s3 = __ffma2_rn(byte_pair(q3, e, kTwo23 + 32.f), make_float2(x[48 + i], x[49 + i]), s3);
       }
     }
     const uint32_t sw[2] = {r.sc.x, r.sc.y};
     auto sc = [&](int k) { return (float)(int8_t)(sw[k / 4] >> (8 * (k % 4))); };
-    return fp16_to_f32(r.d) * (sc(j) * s0 + sc(j + 2) * s1 + sc(j + 4) * s2 + sc(j + 6) * s3);
+    return fp16_to_f32(r.d) * (sc(j) * (s0.x + s0.y) + sc(j + 2) * (s1.x + s1.y) + sc(j + 4) * (s2.x + s2.y) +
+                               sc(j + 6) * (s3.x + s3.y));
   }
   __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
 };
