@@ -195,6 +195,13 @@ int l3p_attn_set_overlap(l3p_attn_ctx* ctx, int enable);
  * (the benchmark reports it per step).  No counterpart in the reference. */
 long long l3p_attn_launch_count(const l3p_attn_ctx* ctx);
 
+/* The architecture the library's kernels were compiled for, as the CUDA
+ * runtime reports it for the decode kernel on `device`: *binary = SASS
+ * version (100 for sm_100a), *ptx = PTX version (0 when the image carries no
+ * PTX).  Fails with L3P_E_CUDA when the device cannot run the image.  A
+ * runtime check of the build; no counterpart in the reference. */
+int l3p_attn_device_arch(int device, int* binary, int* ptx);
+
 /* The split-K decomposition a decode launch at `pos` over `n_slices` layers
  * (or prefill tokens) would use: CTAs per KV-head group (*nsplit) and CTAs
  * per thread-block cluster (*cluster).  Introspection for tests and
@@ -351,7 +358,11 @@ int l3p_attn_wo_allreduce_dev(l3p_attn_ctx* ctx, int layer, const float* x, floa
  * head, q-head group) units; a plan is chosen within 2 MiB of partials).
  * The first call on each device looks up the array's device address and sets
  * the kernel's shared-memory attribute; make that first call before any stream
- * capture.  Every call uses the same array: calls whose kernels may overlap on
+ * capture.  That set-up is kept for the life of the process: after a
+ * cudaDeviceReset (or a release and re-creation of the device's primary
+ * context) this entry point must not be called on that device again.  `layer`
+ * must lie in [0, n_layers) (any layer >= 0 when n_layers is 0), else
+ * L3P_E_RANGE.  Every call uses the same array: calls whose kernels may overlap on
  * the GPU (other streams, other host threads) race and must be serialised by
  * the caller.  l3p_attn_noalloc_last_error() describes the last failure of the
  * calling thread. */

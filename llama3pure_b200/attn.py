@@ -52,6 +52,7 @@ EXPORTS = (
     "l3p_attn_read_kv_q8",
     "l3p_attn_kv_device_ptr",
     "l3p_attn_launch_count",
+    "l3p_attn_device_arch",
     "l3p_attn_set_overlap",
     "l3p_attn_decode_plan",
     "l3p_attn_set_rope",
@@ -154,6 +155,7 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_read_kv_q8": (i, [vp, i, i, i, fp, fp]),
         "l3p_attn_kv_device_ptr": (i, [vp, i, C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)]),
         "l3p_attn_launch_count": (C.c_longlong, [vp]),
+        "l3p_attn_device_arch": (i, [i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "l3p_attn_set_overlap": (i, [vp, i]),
         "l3p_attn_decode_plan": (i, [vp, i, i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "l3p_attn_set_rope": (i, [vp, C.POINTER(RopeConfig)]),

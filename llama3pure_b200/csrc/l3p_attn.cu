@@ -442,21 +442,6 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
     if (ctx->pf_img) {
       L3P_CUDA(ctx, cudaStreamSynchronize(s));
       cudaFree(ctx->pf_img);
-  if (ctx->rope_tab_swa != ctx->rope_tab) cudaFree(ctx->rope_tab_swa);
-  cudaFree(ctx->rope_tab);
-  cudaFree(ctx->qk_norm);
-  cudaFree(ctx->rope_buf);
-  for (auto& w : ctx->wo) {
-    cudaFree(w.w);
-    cudaFree(w.wsc);
-  }
-  cudaFree(ctx->wo_x);
-  for (int p = 0; p < ctx->xg_parts; ++p)
-    if (p != ctx->xg_part && ctx->xg_peer[p]) cudaIpcCloseMemHandle(ctx->xg_peer[p]);
-  cudaFree(ctx->xg_region);
-  for (int p = 0; p < ctx->tp_members; ++p)
-    if (p != ctx->tp_member && ctx->tp_peer[p]) cudaIpcCloseMemHandle(ctx->tp_peer[p]);
-  cudaFree(ctx->tp_region);
     }
     ctx->pf_img = nullptr;
     ctx->pf_img_floats = 0;
@@ -679,6 +664,21 @@ L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
   cudaFree(ctx->counters);
   cudaFree(ctx->st_buf);
   cudaFree(ctx->pf_img);
+  if (ctx->rope_tab_swa != ctx->rope_tab) cudaFree(ctx->rope_tab_swa);
+  cudaFree(ctx->rope_tab);
+  cudaFree(ctx->qk_norm);
+  cudaFree(ctx->rope_buf);
+  for (auto& w : ctx->wo) {
+    cudaFree(w.w);
+    cudaFree(w.wsc);
+  }
+  cudaFree(ctx->wo_x);
+  for (int p = 0; p < ctx->xg_parts; ++p)
+    if (p != ctx->xg_part && ctx->xg_peer[p]) cudaIpcCloseMemHandle(ctx->xg_peer[p]);
+  cudaFree(ctx->xg_region);
+  for (int p = 0; p < ctx->tp_members; ++p)
+    if (p != ctx->tp_member && ctx->tp_peer[p]) cudaIpcCloseMemHandle(ctx->tp_peer[p]);
+  cudaFree(ctx->tp_region);
   if (ctx->hst) cudaFreeHost(ctx->hst);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -711,6 +711,19 @@ L3P_API int l3p_attn_set_stream(l3p_attn_ctx* ctx, void* stream) {
 }
 
 L3P_API long long l3p_attn_launch_count(const l3p_attn_ctx* ctx) { return ctx ? ctx->launches : -1; }
+
+L3P_API int l3p_attn_device_arch(int device, int* binary, int* ptx) {
+  if (!binary || !ptx) return L3P_E_INVAL;
+  DeviceScope dev(device);
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, decode_f32_kernel<128, 4>) != cudaSuccess) {
+    cudaGetLastError();
+    return L3P_E_CUDA;
+  }
+  *binary = fa.binaryVersion;
+  *ptx = fa.ptxVersion;
+  return L3P_OK;
+}
 
 L3P_API int l3p_attn_set_overlap(l3p_attn_ctx* ctx, int enable) {
   if (!ctx) return L3P_E_INVAL;
@@ -1093,6 +1106,12 @@ L3P_API int l3p_attn_load_kv_q8(l3p_attn_ctx* ctx, int layer, int pos0, int n_po
 // The caller passes the KV cache, q and out; the split-K partials and the
 // per-unit tickets live in the fixed array below, which every GPU that loads
 // this library holds until the process exits.
+//
+// The per-device set-up below (the array's device address, the kernel's
+// shared-memory attribute) is cached for the life of the process: it assumes
+// the device's primary context lives as long as the process does.  A caller
+// that resets a device (cudaDeviceReset) or releases and re-creates its
+// primary context must not call this entry point on that device afterwards.
 
 namespace {
 
@@ -1144,6 +1163,10 @@ L3P_API int l3p_attn_decode_noalloc(const l3p_attn_config* cfg, int layer, int p
   if (c.seq_begin != 0 || (c.seq_count != 0 && c.seq_count != c.seq_len))
     return noalloc_fail(L3P_E_INVAL, "the no-allocation decode needs the whole sequence (seq_begin 0)");
   if (pos < 0 || pos >= c.seq_len) return noalloc_fail(L3P_E_RANGE, "pos %d outside [0, %d)", pos, c.seq_len);
+  // the layer picks the sliding-window rule (l % swa_pattern); as the context
+  // entry points, reject one outside [0, n_layers) (n_layers 0: no upper bound)
+  if (layer < 0 || (c.n_layers > 0 && layer >= c.n_layers))
+    return noalloc_fail(L3P_E_RANGE, "layer %d outside [0, %d)", layer, c.n_layers);
   for (const void* p : {(const void*)k_cache, (const void*)v_cache, (const void*)q, (const void*)out})
     if (!aligned16(p)) return noalloc_fail(L3P_E_INVAL, "device pointer %p is not 16-byte aligned", p);
   const int hd = c.head_dim;

@@ -1,8 +1,8 @@
 """Wire libllama3pure_attn.so into the reference C engine (test infrastructure).
 
 Reads llama3pure-c-engine.c where it lies and writes a copy in which the
-engine's attention blocks call the library, exactly as INTEGRATION.md tells
-an engine maintainer to do:
+engine's attention blocks call the library, the integration an engine
+maintainer makes:
 
   transformer()          c:3232-3359 (QK-norm, RoPE, cache write, attention)
                          -> l3p_attn_step_raw

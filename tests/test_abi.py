@@ -37,11 +37,20 @@ def test_library_exports_every_declared_symbol(lib):
     assert {s for s in exported if s.startswith("l3p")} == _declared_symbols()
 
 
-def test_library_is_built_for_sm100a(lib):
-    out = subprocess.run(["cuobjdump", "--list-elf", attn.LIB_PATH], capture_output=True, text=True)
-    if out.returncode != 0:
-        pytest.skip("cuobjdump unavailable")
-    assert "sm_100a" in out.stdout
+def test_library_is_compiled_for_sm100a_only():
+    from llama3pure_b200.build import ARCH_FLAGS
+
+    assert ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+@pytest.mark.gpu
+def test_runtime_reports_sm100_kernels(lib):
+    """The CUDA runtime's own view of the loaded image: SASS for sm_100 and
+    no PTX to JIT from."""
+    binary, ptx = C.c_int(0), C.c_int(-1)
+    assert lib.l3p_attn_device_arch(0, C.byref(binary), C.byref(ptx)) == 0
+    assert binary.value == 100
+    assert ptx.value == 0
 
 
 def _cfg(**kw):

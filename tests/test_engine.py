@@ -1,5 +1,6 @@
-"""The reference C engine wired to libllama3pure_attn.so (the integration of
-INTEGRATION.md, built by tests/engine/Makefile where the reference source is).
+"""The reference C engine wired to libllama3pure_attn.so (the engine
+maintainer's integration, built by tests/engine/Makefile where the reference
+source is).
 
 The reference engine's own forward pass (transformer_prefill + transformer,
 llama3pure-c-engine.c:3190, c:3439) runs twice on the same synthetic Q8_0

@@ -89,3 +89,30 @@ def test_prefill_device_entry_point_matches_host():
         torch.cuda.synchronize()
         ctx.check()
     np.testing.assert_allclose(out.cpu().numpy(), host, rtol=1e-6, atol=1e-7)
+
+
+def test_prefill_image_growth_keeps_rope_tables_and_wo_weights():
+    """A prefill longer than any before it regrows the tensor-core image
+    buffer; the RoPE tables and wo weights set earlier must stay valid (a raw
+    step and the projection after the growth match the oracle's chain)."""
+    from llama3pure_b200.synth import raw_qkv_inputs, wo_weights
+
+    sh = AttnShape("pf_grow", 1, 8, 2, 128, 520, pos=511, seed=15)
+    k, v, q = prefill_inputs(sh, 0)
+    qr, kr, vr, _, _ = raw_qkv_inputs(sh, 0, 1)
+    pos, cols = 512, sh.n_heads * sh.head_dim
+    w = wo_weights(8, 256, cols, seed=4)
+    with AttnContext.for_shape(sh, n_layers=1) as ctx:
+        ctx.set_rope()
+        ctx.set_wo(0, 8, w)
+        ctx.prefill(0, 0, q[:64], k[:64], v[:64])      # image sized for 64 keys
+        ctx.prefill(0, 64, q[64:], k[64:], v[64:])     # grows it to 512 keys
+        att = ctx.step_raw(0, pos, qr[0].copy(), kr[0].copy(), vr[0].copy())
+        xb2 = ctx.wo(0, att.reshape(-1).copy())
+    q_rot, k_rot = O.rope(sh, 0, pos, qr, kr, n_layers=1)
+    o = O.Oracle(sh, O.MODE_F32, "port", n_layers=1)
+    o.load_kv(0, 0, np.ascontiguousarray(k.transpose(1, 0, 2)), np.ascontiguousarray(v.transpose(1, 0, 2)))
+    want, _ = o.decode(0, pos, q_rot.reshape(-1), k_rot.reshape(-1).copy(), vr.reshape(-1).copy())
+    o.close()
+    _check(att.reshape(-1), want.reshape(-1), "raw step after image growth")
+    _check(xb2, O.matvec(8, w, 256, cols, np.ascontiguousarray(att.reshape(-1))), "wo after image growth")
