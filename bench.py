@@ -19,6 +19,15 @@ Printed on rank 0 as one JSON line:
              time over the timed region (every launch in it is this kernel),
              against MEASURED_PEAKS.json's HBM copy bandwidth; the same kernel
              timed in isolation (launches without overlap) beside it
+  exchange   (N > 1) the head-sharded block's exchange per layer: the
+             tensor-parallel wo sum over NVLink, timed inside the step
+  configs    BASELINE configs[0], [2], [3] at this GPU count (us/layer,
+             tokens/s, fraction of HBM per GPU); prefill = configs[4] with the
+             heads sharded over the ranks
+  parity     every multi-GPU data path (KV-head shards, sequence parts merged
+             over NVLink and over NCCL, the tensor-parallel wo sum) on seeded
+             inputs against the CPU oracle, outside the timed regions; a
+             mismatch makes the run exit 1
   cpu_baseline  the reference's own CPU attention (oracle/_ref, compiled from
              llama3pure-c-engine.c with its OpenMP flags) on a bounded sample
 Multi-GPU (torchrun): each rank owns n_kv/N KV heads (head sharding, no
@@ -116,24 +125,25 @@ class ClockSampler:
 class CpuReference:
     """The reference's own decode attention (Q8_0 cache as shipped, OpenMP
     over KV heads as at llama3pure-c-engine.c:3327-3328) on `layers` layers of
-    the workload, each timed call = append row pos + attend, per layer."""
+    the workload, each timed call = append row pos + attend, per layer.
+    fast: True = the harness built -march=x86-64-v3, "v4" = -march=x86-64-v4."""
 
-    def __init__(self, layers: int = 2):
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import oracle as O
-
-        self.kind = "reference" if O.ref_available(fast=True) else "port"
+    def __init__(self, layers: int = 2, fast=True):
+        O = oracle_module()
+        self.kind = "reference" if O.ref_available(fast=fast) else "port"
         self.impl = "ref" if self.kind == "reference" else "port"
+        self.fast = fast if self.kind == "reference" else True
         self.sh = sh = CONFIGS[WORKLOAD]
         self.layers = layers
-        self.o = O.Oracle(sh, O.MODE_Q8, self.impl, fast=True, n_layers=layers)
+        self.o = O.Oracle(sh, O.MODE_Q8, self.impl, fast=self.fast, n_layers=layers)
         self.rows = []
         for layer in range(layers):
             k, v, q = decode_inputs(sh, layer)
             self.o.load_kv(layer, 0, k[:, : sh.pos], v[:, : sh.pos])
             self.rows.append((q, np.ascontiguousarray(k[:, sh.pos]), np.ascontiguousarray(v[:, sh.pos])))
             del k, v
-        self.threads = min(O.threads(self.impl, fast=True), sh.n_kv_heads)
+        self.omp_threads = O.threads(self.impl, fast=self.fast)
+        self.threads = min(self.omp_threads, sh.n_kv_heads)
         self.bytes_per_layer = 2 * (sh.pos + 1) * sh.n_kv_heads * sh.head_dim * 4
         self.o.decode(0, sh.pos, *self.rows[0])  # warm
 
@@ -151,15 +161,62 @@ class CpuReference:
         self.o.close()
 
 
+def oracle_module():
+    """The CPU oracle / reference harness (test infrastructure): bench.py runs
+    it only as the timed CPU baseline and as the parity leg's checker."""
+    p = os.path.join(ROOT, "oracle")
+    if p not in sys.path:
+        sys.path.insert(0, p)
+    import oracle as O
+
+    return O
+
+
+BUILD_FLAGS = {True: "-Ofast -fopenmp -march=x86-64-v3", "v4": "-Ofast -fopenmp -march=x86-64-v4"}
+
+
+def pick_reference_build():
+    """The reference harness build to time on this host: x86-64-v3, or
+    x86-64-v4 (AVX-512) when the CPU has it and it is faster on a 4-layer
+    sample.  (The reference's own flag is -march=native, Makefile:33; the
+    harness is compiled where the reference source is, not on this host.)
+    Returns (fast, {build: GB/s on the sample})."""
+    O = oracle_module()
+    cands = [True] + (["v4"] if O.ref_available("v4") and O.cpu_has_v4() else [])
+    if not O.ref_available(True) or len(cands) == 1:
+        return True, {}
+    gbs = {}
+    for c in cands:
+        r = CpuReference(layers=4, fast=c)
+        t = min(r.step() for _ in range(3))
+        gbs[c] = r.bytes_per_layer * r.layers / t / 1e9
+        r.close()
+    best = max(gbs, key=gbs.get)
+    return best, {BUILD_FLAGS[c]: round(v, 2) for c, v in gbs.items()}
+
+
+def cpu_facts(ref: CpuReference, sample_gbs: dict) -> dict:
+    O = oracle_module()
+    return {"host_cpus": os.cpu_count(), "cpu_model": O.cpu_model(), "omp_threads": ref.omp_threads,
+            "threads_used": ref.threads,
+            "threads_note": "the reference parallelises decode attention over KV heads only "
+                            "(llama3pure-c-engine.c:3327-3328): at most n_kv_heads = 8 threads work",
+            "build": BUILD_FLAGS.get(ref.fast, "-Ofast -fopenmp -march=x86-64-v3") +
+                     (" (reference harness, llama3pure-c-engine.c compiled in place)" if ref.kind == "reference"
+                      else " (restated port)"),
+            "builds_sampled_gbs": sample_gbs}
+
+
 def cpu_baseline(min_seconds: float = 10.0):
     host_threads_for_reference()
-    ref = CpuReference(layers=CONFIGS[WORKLOAD].n_layers)
+    fast, sampled = pick_reference_build()
+    ref = CpuReference(layers=CONFIGS[WORKLOAD].n_layers, fast=fast)
     dts = []
     while sum(dts) < min_seconds or len(dts) < 3:
         dts.append(ref.step())
     gbs = ref.bytes_per_layer * ref.layers * len(dts) / sum(dts) / 1e9
     out = {"value": round(gbs, 3), "unit": "GB/s", "cores": ref.threads, "kind": ref.kind,
-           "sample": ref.describe(len(dts), sum(dts))}
+           "sample": ref.describe(len(dts), sum(dts)), **cpu_facts(ref, sampled)}
     ref.close()
     return out
 
@@ -177,7 +234,8 @@ def run_reference_arm(args):
     if rank != 0:
         return 0
     host_threads_for_reference()
-    ref = CpuReference(layers=CONFIGS[WORKLOAD].n_layers)
+    fast, sampled = pick_reference_build()
+    ref = CpuReference(layers=CONFIGS[WORKLOAD].n_layers, fast=fast)
     for _ in range(args.warmup):
         ref.step()
     dts = [ref.step() for _ in range(args.steps)]
@@ -190,7 +248,7 @@ def run_reference_arm(args):
         "config": {"workload": WORKLOAD, "layers_per_step": ref.layers, "pos": ref.sh.pos,
                    "note": "every step is the full 32-layer workload"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": ref.threads, "kind": ref.kind,
-                         "sample": ref.describe(len(dts), sum(dts))},
+                         "sample": ref.describe(len(dts), sum(dts)), **cpu_facts(ref, sampled)},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     ref.close()
@@ -208,6 +266,540 @@ class DevView:
     def __init__(self, ptr: int, shape):
         self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False),
                                          "version": 3, "strides": None}
+
+
+class Job:
+    """The job's ranks: torch, the process group (or None) and timing helpers."""
+
+    def __init__(self, torch, dist, world: int, rank: int, local: int):
+        self.torch, self.dist, self.world, self.rank, self.local = torch, dist, world, rank, local
+
+    def max(self, *vals):
+        if self.world == 1:
+            return list(vals)
+        t = self.torch.tensor(list(vals), device="cuda", dtype=self.torch.float64)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return t.tolist()
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def graph(self, fn):
+        """CUDA graph of fn(stream), captured on a side stream."""
+        torch = self.torch
+        g = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream()
+        cs.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cs):
+            with torch.cuda.graph(g, stream=cs):
+                fn(cs)
+        torch.cuda.current_stream().wait_stream(cs)
+        return g
+
+    def time_graph(self, g, reps: int, warmup: int = 3) -> float:
+        """ms per replay, max over ranks (ranks start together after a barrier)."""
+        torch = self.torch
+        s = torch.cuda.current_stream()
+        for _ in range(warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        self.barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(s)
+        for _ in range(reps):
+            g.replay()
+        b.record(s)
+        torch.cuda.synchronize()
+        return self.max(a.elapsed_time(b) / reps)[0]
+
+    def fill_cache(self, ctx, n_layers: int, heads: int, rows: int, hd: int, seed: int, k_scale: float = 1.0,
+                   n_rows: int | None = None):
+        """N(0,1) rows [0, n_rows) of every owned cache row block, on the device."""
+        torch = self.torch
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)
+        for layer in range(n_layers):
+            kp, vp = ctx.kv_device_ptr(layer)
+            kt = torch.as_tensor(DevView(kp, (heads, rows, hd)), device="cuda")
+            vt = torch.as_tensor(DevView(vp, (heads, rows, hd)), device="cuda")
+            kt[:, : n_rows or rows].normal_(generator=g)
+            if k_scale != 1.0:
+                kt.mul_(k_scale)
+            vt[:, : n_rows or rows].normal_(generator=g)
+        return g
+
+
+def _peak():
+    import json
+
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p.get("bf16_tflops", 0.0)), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def _decode_record(us_per_layer: float, L: int, bytes_per_layer_job: float, bytes_per_layer_rank: float,
+                   world: int, peak: float):
+    return {"us_per_layer": round(us_per_layer, 3), "tokens_per_s": round(1e6 / (us_per_layer * L), 1),
+            "job_gbs": round(bytes_per_layer_job / us_per_layer / 1e3, 1),
+            "frac_of_hbm_per_gpu": round(bytes_per_layer_rank / us_per_layer / 1e3 / peak, 4)}
+
+
+# --------------------------------------------------------------------------
+# configs[0]: Llama-3.2-1B shapes, 16 layers, 1024 positions, head_dim 64
+
+
+def config1(job: Job, reps: int):
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.shard import plan_shards
+    from llama3pure_b200.synth import CONFIGS
+
+    torch = job.torch
+    sh = CONFIGS["llama32_1b_decode"]
+    L, P, hd = sh.n_layers, sh.pos + 1, sh.head_dim
+    me = plan_shards(sh.n_kv_heads, sh.seq_len, job.world, 1)[job.rank]
+    hk = me.kv_head_count
+    peak, _, pk = _peak()
+    res = {"workload": sh.name, "n_layers": L, "kv_positions": P, "head_dim": hd,
+           "parallelism": f"kv-head shards x{job.world} ({hk} KV heads per GPU)", "peak_kind": pk}
+    with AttnContext.for_shape(sh, device=job.local, kv_head_begin=me.kv_head_begin, kv_head_count=hk) as ctx:
+        g = job.fill_cache(ctx, L, hk, sh.seq_len, hd, 3000 + job.rank)
+        q = torch.randn((L, sh.n_heads * hd), device="cuda", generator=g)
+        kn = torch.randn((L, sh.n_kv_heads * hd), device="cuda", generator=g)
+        vn = torch.randn((L, sh.n_kv_heads * hd), device="cuda", generator=g)
+        out = torch.zeros_like(q)
+        ctx.set_overlap(True)
+        n0 = ctx.launch_count()
+        gs = job.graph(lambda s: [ctx.step_dev(l, sh.pos, q[l], kn[l], vn[l], out[l], s) for l in range(L)])
+        step_launches = ctx.launch_count() - n0
+        gd = job.graph(lambda s: [ctx.decode_dev(l, sh.pos, q[l], out[l], s) for l in range(L)])
+        n0 = ctx.launch_count()
+        gb = job.graph(lambda s: ctx.decode_layers_dev(0, L, sh.pos, q, out, s))
+        batched_launches = ctx.launch_count() - n0
+        step_ms = job.time_graph(gs, reps)
+        dec_ms = job.time_graph(gd, reps)
+        bat_ms = job.time_graph(gb, reps)
+        ctx.check()
+        plan = ctx.decode_plan(sh.pos)
+        del gs, gd, gb
+    rank_b = 2 * P * hk * hd * 4
+    job_b = rank_b * job.world
+    res["per_call_step"] = {"api": "l3p_attn_step_dev per layer (append + decode), graph + programmatic "
+                                   "dependent launch", "launches_per_layer": step_launches // L,
+                            **_decode_record(step_ms * 1e3 / L, L, job_b, rank_b, job.world, peak)}
+    res["per_call_decode"] = {"api": "l3p_attn_decode_dev per layer, graph + programmatic dependent launch",
+                              **_decode_record(dec_ms * 1e3 / L, L, job_b, rank_b, job.world, peak)}
+    res["layer_batched"] = {"api": "l3p_attn_decode_layers_dev: all 16 layers in one launch",
+                            "launches_per_step": batched_launches,
+                            **_decode_record(bat_ms * 1e3 / L, L, job_b, rank_b, job.world, peak)}
+    res["split_k"] = {"ctas_per_kv_head": plan[0], "cluster": plan[1]}
+    res["bytes_per_layer"] = job_b
+    return res
+
+
+# --------------------------------------------------------------------------
+# configs[2]: 131072 cached positions, 1 GiB of K+V per layer, 32 layers
+
+
+def config3(job: Job, reps: int, seq_parts_list=(1, 2)):
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.shard import plan_shards
+    from llama3pure_b200.synth import CONFIGS
+
+    torch = job.torch
+    sh = CONFIGS["llama31_8b_decode_128k"]
+    L, P, hd = sh.n_layers, sh.pos + 1, sh.head_dim
+    peak, _, pk = _peak()
+    job_b = 2 * P * sh.n_kv_heads * hd * 4
+    res = {"workload": sh.name, "n_layers": L, "kv_positions": P, "bytes_per_layer": job_b, "peak_kind": pk,
+           "decompositions": []}
+    for sp in seq_parts_list:
+        if job.world % sp or sh.n_kv_heads % (job.world // sp) or (sp > 1 and job.world < 2):
+            continue
+        me = plan_shards(sh.n_kv_heads, sh.seq_len, job.world, sp)[job.rank]
+        g0 = me.head_group * sp
+        with AttnContext.for_shape(sh, device=job.local, kv_head_begin=me.kv_head_begin,
+                                   kv_head_count=me.kv_head_count, seq_begin=me.seq_begin,
+                                   seq_count=me.seq_count) as ctx:
+            g = job.fill_cache(ctx, L, me.kv_head_count, me.seq_count, hd, 4000 + job.rank, k_scale=sh.k_scale)
+            q = torch.randn((L, sh.n_heads * hd), device="cuda", generator=g)
+            out = torch.zeros_like(q)
+            if sp > 1:
+                h = ctx.seq_group_export(sp, me.seq_part)
+                hs = [None] * job.world
+                job.dist.all_gather_object(hs, h)
+                ctx.seq_group_import(hs[g0:g0 + sp])
+            ctx.set_overlap(True)
+            if sp > 1:
+                gr = job.graph(lambda s: [ctx.decode_seq_dev(l, sh.pos, q[l], out[l], s) for l in range(L)])
+            else:
+                gr = job.graph(lambda s: [ctx.decode_dev(l, sh.pos, q[l], out[l], s) for l in range(L)])
+            ms = job.time_graph(gr, reps)
+            ctx.check()
+            del gr
+            rank_b = 2 * me.seq_count * me.kv_head_count * hd * 4
+        rec = {"head_groups": job.world // sp, "seq_parts": sp,
+               "exchange": "none" if sp == 1 else "partial triples read from the peers over NVLink in the merge "
+                                                  "kernel (l3p_attn_decode_seq_dev)",
+               **_decode_record(ms * 1e3 / L, L, job_b, rank_b, job.world, peak)}
+        res["decompositions"].append(rec)
+    best = min(res["decompositions"], key=lambda r: r["us_per_layer"])
+    res["best"] = {k: best[k] for k in ("head_groups", "seq_parts", "us_per_layer", "tokens_per_s",
+                                        "frac_of_hbm_per_gpu")}
+    return res
+
+
+# --------------------------------------------------------------------------
+# configs[3]: Gemma-2B shapes, 18 layers, 8 q heads, 1 KV head, head_dim 256
+
+
+def config4(job: Job, reps: int):
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.synth import CONFIGS
+
+    torch = job.torch
+    sh = CONFIGS["gemma_2b_decode"]
+    L, P, hd = sh.n_layers, sh.pos + 1, sh.head_dim
+    W = job.world
+    b, e = sh.seq_len * job.rank // W, sh.seq_len * (job.rank + 1) // W
+    peak, _, pk = _peak()
+    res = {"workload": sh.name, "n_layers": L, "kv_positions": P, "head_dim": hd, "peak_kind": pk,
+           "parallelism": "one GPU" if W == 1 else f"{W} sequence parts of the single KV head over NVLink "
+                                                   "(l3p_attn_decode_seq_dev)"}
+    with AttnContext.for_shape(sh, device=job.local, seq_begin=b, seq_count=e - b) as ctx:
+        g = job.fill_cache(ctx, L, 1, e - b, hd, 5000 + job.rank)
+        q = torch.randn((L, sh.n_heads * hd), device="cuda", generator=g)
+        kn = torch.randn((L, hd), device="cuda", generator=g)
+        vn = torch.randn((L, hd), device="cuda", generator=g)
+        out = torch.zeros_like(q)
+        if W > 1:
+            h = ctx.seq_group_export(W, job.rank)
+            hs = [None] * W
+            job.dist.all_gather_object(hs, h)
+            ctx.seq_group_import(hs)
+        ctx.set_overlap(True)
+        if W > 1:
+            gd = job.graph(lambda s: [ctx.decode_seq_dev(l, sh.pos, q[l], out[l], s) for l in range(L)])
+            gs = None
+        else:
+            gd = job.graph(lambda s: [ctx.decode_dev(l, sh.pos, q[l], out[l], s) for l in range(L)])
+            gs = job.graph(lambda s: [ctx.step_dev(l, sh.pos, q[l], kn[l], vn[l], out[l], s) for l in range(L)])
+        dec_ms = job.time_graph(gd, reps)
+        step_ms = job.time_graph(gs, reps) if gs is not None else None
+        ctx.check()
+        del gd, gs
+    job_b = 2 * P * hd * 4
+    rank_b = 2 * (e - b) * hd * 4
+    res["decode"] = {"api": "l3p_attn_decode_dev" if W == 1 else "l3p_attn_decode_seq_dev",
+                     **_decode_record(dec_ms * 1e3 / L, L, job_b, rank_b, W, peak)}
+    if step_ms is not None:
+        res["step"] = {"api": "l3p_attn_step_dev (append + decode)",
+                       **_decode_record(step_ms * 1e3 / L, L, job_b, rank_b, W, peak)}
+    res["bytes_per_layer"] = job_b
+    return res
+
+
+# --------------------------------------------------------------------------
+# configs[4]: causal prefill, 2048 tokens, heads sharded by KV-head group
+
+
+def measure_tf32_peak(torch):
+    """Dense TF32 tensor throughput of this GPU, measured live: an fp32
+    torch.matmul (cuBLAS) with TF32 enabled, 8192^3, best of 5 (2*N^3 flops).
+    The 3xTF32 prefill roofline is a third of it."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    n = 8192
+    a = torch.randn((n, n), device="cuda")
+    b = torch.randn((n, n), device="cuda")
+    c = a @ b
+    best = 1e9
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        c = a @ b
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c
+    return 2 * n ** 3 / (best / 1e3) / 1e12
+
+
+def config5(job: Job, reps: int, raw: bool = True):
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.shard import plan_shards
+    from llama3pure_b200.synth import CONFIGS, prefill_flops
+
+    torch = job.torch
+    sh = CONFIGS["llama31_8b_prefill_2k"]
+    S, hd = sh.pos + 1, sh.head_dim
+    L = 4  # layers cycled (16 MiB of K/V each)
+    me = plan_shards(sh.n_kv_heads, sh.seq_len, job.world, 1)[job.rank]
+    with AttnContext.for_shape(sh, n_layers=L, device=job.local, kv_head_begin=me.kv_head_begin,
+                               kv_head_count=me.kv_head_count) as ctx:
+        g = torch.Generator(device="cuda")
+        g.manual_seed(6000 + job.rank)
+        q = torch.randn((L, S, sh.n_heads, hd), device="cuda", generator=g)
+        k = torch.randn((L, S, sh.n_kv_heads, hd), device="cuda", generator=g)
+        v = torch.randn((L, S, sh.n_kv_heads, hd), device="cuda", generator=g)
+        out = torch.zeros_like(q)
+        s = torch.cuda.current_stream()
+
+        def timed(fn):
+            for i in range(3):
+                fn(i % L)
+            torch.cuda.synchronize()
+            job.barrier()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for i in range(reps):
+                fn(i % L)
+            e1.record(s)
+            torch.cuda.synchronize()
+            return job.max(e0.elapsed_time(e1) / reps)[0]
+
+        n0 = ctx.launch_count()
+        ctx.prefill_dev(0, 0, S, q[0], k[0], v[0], out[0], s)
+        launches = ctx.launch_count() - n0
+        ms = timed(lambda i: ctx.prefill_dev(i, 0, S, q[i], k[i], v[i], out[i], s))
+        raw_ms = None
+        if raw:
+            ctx.set_rope()
+            raw_ms = timed(lambda i: ctx.prefill_raw_dev(i, 0, S, q[i], k[i], v[i], out[i], s))
+        ctx.check()
+    flops = prefill_flops(sh)
+    tflops = flops / (ms / 1e3) / 1e12
+    tf32 = measure_tf32_peak(torch)
+    _, bf16, _ = _peak()
+    res = {"workload": sh.name, "tokens": S, "head_dim": hd, "ms_per_layer": round(ms, 4),
+           "tflops": round(tflops, 2), "flops_per_layer": flops, "launches_per_layer": launches,
+           "parallelism": f"kv-head shards x{job.world} ({me.kv_head_count} KV heads, "
+                          f"{me.kv_head_count * sh.kv_mul} q heads per GPU)",
+           "kernel": "prefill_tc_kernel (tcgen05 3xTF32) + prefill_prep_kernel + kv_append_kernel",
+           "tf32_dense_tflops_measured": round(tf32, 1),
+           "tf32_how": "torch.matmul fp32 with allow_tf32 (cuBLAS), 8192^3, best of 5, this GPU, this run",
+           "roofline_3xtf32_tflops_per_gpu": round(tf32 / 3, 1),
+           "frac_of_3xtf32_per_gpu": round(tflops / job.world / (tf32 / 3), 4)}
+    if bf16 > 0:
+        # TF32 dense peak taken as half the driver-measured bf16 burst peak
+        res["frac_of_3xtf32_from_half_bf16_per_gpu"] = round(tflops / job.world / (bf16 / 2 / 3), 4)
+    if raw_ms is not None:
+        res["raw_ms_per_layer"] = round(raw_ms, 4)
+        res["raw_api"] = "l3p_attn_prefill_raw_dev (RoPE + cache write, then prep + attention)"
+    res["tokens_per_s_32_layers"] = round(S / (ms * 32 / 1e3), 1)
+    return res
+
+
+def prefill_other_head_dims(job: Job, reps: int, tf32: float):
+    """Causal prefill of 2048 tokens at the other two head sizes on one GPU:
+    Llama-3.2-1B shapes (head_dim 64, the tcgen05 kernel) and Gemma-2B shapes
+    (head_dim 256, MQA: the decode kernel in token mode, one grid slice per
+    token -- Q hi and O alone would fill the tensor memory at head_dim 256)."""
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.synth import CONFIGS, prefill_flops
+
+    torch = job.torch
+    res = {}
+    for name, base, path in (("llama32_1b_hd64", CONFIGS["llama32_1b_decode"], "prefill_tc_kernel<1,64> (tcgen05 3xTF32)"),
+                             ("gemma_2b_hd256", CONFIGS["gemma_2b_decode"],
+                              "decode_f32_kernel<256,8> in token mode (FFMA, fp32)")):
+        sh = base.with_(seq_len=2048, pos=2047, n_layers=2)
+        S, hd = 2048, sh.head_dim
+        with AttnContext.for_shape(sh, device=job.local) as ctx:
+            g = torch.Generator(device="cuda")
+            g.manual_seed(7000)
+            L = 2
+            q = torch.randn((L, S, sh.n_heads, hd), device="cuda", generator=g)
+            k = torch.randn((L, S, sh.n_kv_heads, hd), device="cuda", generator=g)
+            v = torch.randn((L, S, sh.n_kv_heads, hd), device="cuda", generator=g)
+            out = torch.zeros_like(q)
+            s = torch.cuda.current_stream()
+            for i in range(3):
+                ctx.prefill_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], s)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for i in range(reps):
+                ctx.prefill_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], s)
+            e1.record(s)
+            torch.cuda.synchronize()
+            ctx.check()
+            ms = e0.elapsed_time(e1) / reps
+        flops = prefill_flops(sh)
+        tflops = flops / (ms / 1e3) / 1e12
+        res[name] = {"shape": f"{sh.n_heads} q heads / {sh.n_kv_heads} KV heads, head_dim {hd}, 2048 tokens",
+                     "path": path, "ms_per_layer": round(ms, 4), "tflops": round(tflops, 2), "flops_per_layer": flops,
+                     "frac_of_3xtf32": round(tflops / (tf32 / 3), 4)}
+    # the FFMA path's own ceiling: fp32 FMA issue of every SM at the clock the GPU reports
+    props = torch.cuda.get_device_properties(job.local)
+    clock_ghz = getattr(props, "clock_rate", 0) / 1e6 or 1.965
+    ffma = props.multi_processor_count * 128 * 2 * clock_ghz / 1e3
+    res["gemma_2b_hd256"]["frac_of_ffma_peak"] = round(res["gemma_2b_hd256"]["tflops"] / ffma, 4)
+    res["ffma_peak_tflops"] = round(ffma, 1)
+    res["ffma_peak_how"] = "SMs x 128 fp32 FMA lanes x 2 flop x the SM clock the device reports"
+    return res
+
+
+# --------------------------------------------------------------------------
+# parity leg: seeded inputs (BASELINE generator) through every multi-GPU path
+
+
+def _cmp(got, want):
+    from llama3pure_b200.synth import tolerance_ok
+
+    ok, ma, mr = tolerance_ok(got, want)
+    return {"ok": ok, "max_abs": float(f"{ma:.3e}"), "max_rel": float(f"{mr:.3e}")}
+
+
+def _worst(recs):
+    """One record for several compared outputs (all ranks, repeated calls)."""
+    return {"ok": all(r["ok"] for r in recs), "max_abs": max(r["max_abs"] for r in recs),
+            "max_rel": max(r["max_rel"] for r in recs), "outputs_compared": len(recs)}
+
+
+def parity_leg(job: Job):
+    """Returns {path: {ok, max_abs, max_rel, ...}} on rank 0 (None elsewhere)."""
+    from llama3pure_b200.attn import AttnContext
+    from llama3pure_b200.shard import plan_shards
+    from llama3pure_b200.synth import CONFIGS, decode_inputs, wo_input, wo_weights
+
+    torch, dist, W, rank = job.torch, job.dist, job.world, job.rank
+    O = oracle_module() if rank == 0 else None
+    res = {}
+
+    def gather(arr):
+        """Every rank's numpy array, on rank 0."""
+        if W == 1:
+            return [arr]
+        out = [None] * W
+        dist.all_gather_object(out, arr)
+        return out if rank == 0 else None
+
+    # KV-head shards: configs[1] layer 0 (seed 1), append of row 8191 + decode,
+    # through the host C ABI (l3p_attn_step) on every rank; rows concatenated
+    sh = CONFIGS["llama31_8b_decode_8k"]
+    k, v, q = decode_inputs(sh, 0)
+    me = plan_shards(sh.n_kv_heads, sh.seq_len, W, 1)[rank]
+    with AttnContext.for_shape(sh, n_layers=1, device=job.local, kv_head_begin=me.kv_head_begin,
+                               kv_head_count=me.kv_head_count) as ctx:
+        ctx.load_kv(0, 0, np.ascontiguousarray(k[:, : sh.pos]), np.ascontiguousarray(v[:, : sh.pos]))
+        out = ctx.step(0, sh.pos, q, np.ascontiguousarray(k[:, sh.pos]), np.ascontiguousarray(v[:, sh.pos]))
+        r0, r1 = ctx.owned_rows
+    parts = gather((r0, r1, out[r0:r1].copy()))
+    if rank == 0:
+        full = np.full((sh.n_heads, sh.head_dim), np.nan, np.float32)
+        for a, b, rows in parts:
+            full[a:b] = rows
+        o = O.Oracle(sh, O.MODE_F32, "port", n_layers=1)
+        o.load_kv(0, 0, k, v)
+        want, _ = o.decode(0, sh.pos, q)
+        o.close()
+        res["kv_head_shards"] = {"workload": sh.name + " layer 0 (append + decode, l3p_attn_step)",
+                                 "ranks": W, **_cmp(full, want.reshape(full.shape))}
+    del k, v
+
+    # sequence parts of one KV head: configs[3] layer 0 (seed 3) split over the ranks
+    gs = CONFIGS["gemma_2b_decode"]
+    k, v, q = decode_inputs(gs, 0)
+    want = None
+    if rank == 0:
+        o = O.Oracle(gs, O.MODE_F32, "port", n_layers=1)
+        o.load_kv(0, 0, k, v)
+        want, _ = o.decode(0, gs.pos, q)
+        o.close()
+        want = want.reshape(gs.n_heads, gs.head_dim)
+    if W > 1:
+        b, e = gs.seq_len * rank // W, gs.seq_len * (rank + 1) // W
+        with AttnContext.for_shape(gs, n_layers=1, device=job.local, seq_begin=b, seq_count=e - b) as ctx:
+            ctx.load_kv(0, b, np.ascontiguousarray(k[:, b:e]), np.ascontiguousarray(v[:, b:e]))
+            dq = torch.from_numpy(q.reshape(-1).copy()).cuda()
+            # over NVLink peer memory, three steps (device step counter, slot reuse)
+            h = ctx.seq_group_export(W, rank)
+            hs = [None] * W
+            dist.all_gather_object(hs, h)
+            ctx.seq_group_import(hs)
+            outs = []
+            for _ in range(3):
+                dout = torch.zeros_like(dq)
+                ctx.decode_seq_dev(0, gs.pos, dq, dout)
+                outs.append(dout)
+            ctx.check()
+            nv = [o_.cpu().numpy().reshape(gs.n_heads, gs.head_dim) for o_ in outs]
+            # NCCL all-gather of the partial triples + the LSE merge kernel
+            po = torch.zeros(gs.n_heads * gs.head_dim, device="cuda")
+            pml = torch.zeros(gs.n_heads * 2, device="cuda")
+            ctx.decode_partial_dev(0, gs.pos, dq, po, pml)
+            go = torch.zeros((W, po.numel()), device="cuda")
+            gml = torch.zeros((W, pml.numel()), device="cuda")
+            dist.all_gather_into_tensor(go, po)
+            dist.all_gather_into_tensor(gml, pml)
+            mout = torch.zeros_like(dq)
+            ctx.lse_merge_dev(W, gs.n_heads, 0, gs.n_heads, go, gml, mout)
+            ctx.check()
+            nc = mout.cpu().numpy().reshape(gs.n_heads, gs.head_dim)
+        all_nv, all_nc = gather(nv), gather(nc)
+        if rank == 0:
+            res["seq_parts_nvlink_merge"] = {
+                "workload": gs.name + f" layer 0, {W} sequence parts (l3p_attn_decode_seq_dev, 3 steps)",
+                **_worst([_cmp(x, want) for outs_r in all_nv for x in outs_r])}
+            res["seq_parts_nccl_lse_merge"] = {
+                "workload": gs.name + f" layer 0, {W} sequence parts (decode_partial_dev + NCCL all-gather + "
+                                      "lse_merge_dev)",
+                **_worst([_cmp(x, want) for x in all_nc])}
+    else:
+        with AttnContext.for_shape(gs, n_layers=1, device=job.local) as ctx:
+            ctx.load_kv(0, 0, k, v)
+            got = ctx.decode(0, gs.pos, q)
+        res["gemma_mqa_decode"] = {"workload": gs.name + " layer 0 (one GPU)", **_cmp(got, want)}
+    del k, v
+
+    # the wo projection: 4096 x 4096 (Llama-3.1-8B), three GGUF types; at N > 1
+    # the tensor-parallel sum over NVLink on every rank, two steps
+    dim = cols = sh.n_heads * sh.head_dim
+    x = wo_input(cols, seed=7)
+    for name, wt in (("q8_0", 8), ("q4_k", 12), ("q6_k", 14)):
+        w = wo_weights(wt, dim, cols, seed=6)
+        with AttnContext.for_shape(sh, n_layers=1, seq_len=16, device=job.local, kv_head_begin=me.kv_head_begin,
+                                   kv_head_count=me.kv_head_count) as ctx:
+            ctx.set_wo(0, wt, w)
+            dx = torch.from_numpy(x).cuda()
+            outs = []
+            if W > 1:
+                h = ctx.tp_group_export(W, rank, dim)
+                hs = [None] * W
+                dist.all_gather_object(hs, h)
+                ctx.tp_group_import(hs)
+                for _ in range(2):
+                    y = torch.zeros(dim, device="cuda")
+                    ctx.wo_allreduce_dev(0, dx, y)
+                    outs.append(y)
+            else:
+                y = torch.zeros(dim, device="cuda")
+                ctx.wo_dev(0, dx, y)
+                outs.append(y)
+            ctx.check()
+            got = [o_.cpu().numpy() for o_ in outs]
+        allg = gather(got)
+        if rank == 0:
+            want = O.matvec(wt, w, dim, cols, x)
+            key = f"tp_wo_sum_{name}" if W > 1 else f"wo_{name}"
+            res[key] = {"workload": f"wo {dim} x {cols} {name}" +
+                                    (" (l3p_attn_wo_allreduce_dev, 2 steps, every rank)" if W > 1 else " (l3p_attn_wo_dev)"),
+                        **_worst([_cmp(g_, want) for r_ in allg for g_ in r_])}
+    if rank == 0:
+        res["tolerance"] = "|gpu - oracle| <= 1e-4 + 1e-4*|oracle| element-wise (fp32 oracle, f32 mode)"
+        res["all_ok"] = all(r["ok"] for r in res.values() if isinstance(r, dict))
+    return res if rank == 0 else None
+
+
+# --------------------------------------------------------------------------
+# the headline line
 
 
 def run_ours(args):
@@ -336,6 +928,7 @@ def run_ours(args):
     # the same step from the raw projections (l3p_attn_step_raw_dev: RoPE and
     # the cache write on the device, then the decode), as a graph of L layers
     raw = None
+    exchange = None
     if not args.no_raw:
         ctx.set_rope()
         ctx.set_overlap(not args.no_overlap)
@@ -367,72 +960,42 @@ def run_ours(args):
         raw = {"api": "l3p_attn_step_raw_dev (QK-norm/RoPE + cache write + decode)",
                "us_per_layer": round(raw_ms * 1e3 / L, 3), "launches_per_layer": raw_launches // L,
                "post_rope_step_us_per_layer": round(ms / args.steps * 1e3 / L, 3)}
-        if not args.no_wo and world == 1:
-            # and on to the wo projection (Q8_0 weights, 4096 x 4096 per layer)
-            from llama3pure_b200.synth import wo_weights
-
-            w = wo_weights(8, sh.n_heads * sh.head_dim, sh.n_heads * sh.head_dim, seed=3)
-            for layer in range(L):
-                ctx.set_wo(layer, 8, w)
-            xb2 = torch.zeros((L, sh.n_heads * sh.head_dim), device="cuda")
-            bgraph = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(rstream):
-                ctx.set_stream(rstream)
-                with torch.cuda.graph(bgraph, stream=rstream):
-                    for layer in range(L):
-                        ctx.step_raw_dev(layer, sh.pos, q[layer], knew[layer], vnew[layer], out[layer], rstream)
-                        ctx.wo_dev(layer, out[layer], xb2[layer], rstream)
-            stream.wait_stream(rstream)
-            ctx.set_stream(stream)
-            for _ in range(max(3, args.warmup)):
-                bgraph.replay()
-            torch.cuda.synchronize()
-            r0.record(stream)
-            for _ in range(args.steps):
-                bgraph.replay()
-            r1.record(stream)
-            torch.cuda.synchronize()
-            ctx.check()
-            raw["with_wo_q8_0_us_per_layer"] = round(r0.elapsed_time(r1) / args.steps * 1e3 / L, 3)
-            del bgraph
-        if not args.no_wo and world > 1:
-            # the tensor-parallel block: every rank's partial wo summed over NVLink (Q8_0, 4096 x 4096)
+        if not args.no_wo:
+            # and on to the wo projection (Q8_0 weights, 4096 x 4096 per layer): at N = 1 the
+            # local projection; at N > 1 each rank's partial over its heads, then (a) left
+            # partial and (b) summed over NVLink on every rank -- (b) - (a) is the exchange
             from llama3pure_b200.synth import wo_weights
 
             dim = sh.n_heads * sh.head_dim
             w = wo_weights(8, dim, dim, seed=3)
             for layer in range(L):
                 ctx.set_wo(layer, 8, w)
-            h = ctx.tp_group_export(world, rank, dim)
-            hs = [None] * world
-            dist.all_gather_object(hs, h)
-            ctx.tp_group_import(hs)
             xb2 = torch.zeros((L, dim), device="cuda")
-            bgraph = torch.cuda.CUDAGraph()
-            with torch.cuda.stream(rstream):
-                ctx.set_stream(rstream)
-                with torch.cuda.graph(bgraph, stream=rstream):
-                    for layer in range(L):
-                        ctx.step_raw_dev(layer, sh.pos, q[layer], knew[layer], vnew[layer], out[layer], rstream)
-                        ctx.wo_allreduce_dev(layer, out[layer], xb2[layer], rstream)
-            stream.wait_stream(rstream)
+            job = Job(torch, dist, world, rank, local)
             ctx.set_stream(stream)
-            for _ in range(max(3, args.warmup)):
-                bgraph.replay()
-            torch.cuda.synchronize()
-            dist.barrier()
-            torch.cuda.synchronize()
-            r0.record(stream)
-            for _ in range(args.steps):
-                bgraph.replay()
-            r1.record(stream)
-            torch.cuda.synchronize()
+            bgraph = job.graph(lambda s: [(ctx.step_raw_dev(l, sh.pos, q[l], knew[l], vnew[l], out[l], s),
+                                           ctx.wo_dev(l, out[l], xb2[l], s)) for l in range(L)])
+            wo_ms = job.time_graph(bgraph, args.steps, max(3, args.warmup))
             ctx.check()
-            t = torch.tensor([r0.elapsed_time(r1)], device="cuda")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            raw["with_wo_allreduce_q8_0_us_per_layer"] = round(t.item() / args.steps * 1e3 / L, 3)
-            raw["wo_allreduce"] = "partial wo per rank, summed over NVLink peer stores (l3p_attn_wo_allreduce_dev)"
             del bgraph
+            raw["with_wo_q8_0_us_per_layer"] = round(wo_ms * 1e3 / L, 3)
+            if world > 1:
+                h = ctx.tp_group_export(world, rank, dim)
+                hs = [None] * world
+                dist.all_gather_object(hs, h)
+                ctx.tp_group_import(hs)
+                agraph = job.graph(lambda s: [(ctx.step_raw_dev(l, sh.pos, q[l], knew[l], vnew[l], out[l], s),
+                                               ctx.wo_allreduce_dev(l, out[l], xb2[l], s)) for l in range(L)])
+                ar_ms = job.time_graph(agraph, args.steps, max(3, args.warmup))
+                ctx.check()
+                del agraph
+                raw["with_wo_allreduce_q8_0_us_per_layer"] = round(ar_ms * 1e3 / L, 3)
+                raw["wo_allreduce"] = ("each rank's partial wo over its heads, summed over NVLink peer memory "
+                                       "(l3p_attn_wo_allreduce_dev)")
+                exchange = {"us_per_layer": round((ar_ms - wo_ms) * 1e3 / L, 3),
+                            "what": "the tensor-parallel wo sum of the head-sharded step: 16 KiB partial per rank, "
+                                    "reduce-scattered and all-gathered over NVLink inside the projection; "
+                                    "= with_wo_allreduce - with_wo (same graph without the sum)"}
     if clocks:
         clk = clocks.stop()
     else:
@@ -451,8 +1014,9 @@ def run_ours(args):
     # every launch of the timed region is the decode kernel (one per layer)
     launch_ms = ms_step / launches_per_step
     achieved = bytes_per_layer_rank / (launch_ms / 1e3) / 1e9
+    split_k = dict(zip(("ctas_per_kv_head", "cluster"), ctx.decode_plan(sh.pos)))
 
-    # end to end through the host-pointer C ABI (rank 0 at N GPUs: every rank runs it)
+    # end to end through the host-pointer C ABI (every rank runs it; max over ranks)
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(ctx, sh, world, args, torch)
@@ -461,6 +1025,26 @@ def run_ours(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e["ms_per_step"] = t.item()
             e2e["value"] = round(bytes_per_layer_rank * world * L / (e2e["ms_per_step"] / 1e3) / 1e9, 3)
+    del graph
+    ctx.close()
+
+    # every BASELINE configuration at this GPU count, then the parity leg
+    job = Job(torch, dist, world, rank, local)
+    configs = None
+    if not args.no_configs:
+        reps = max(args.steps // 2, 5)
+        configs = {"llama32_1b_decode": config1(job, reps),
+                   "llama31_8b_decode_128k": config3(job, max(reps // 2, 3)),
+                   "gemma_2b_decode": config4(job, reps)}
+    prefill = None
+    if not args.no_prefill:
+        prefill = config5(job, max(args.steps // 2, 4), raw=not args.no_raw)
+        if world == 1:
+            prefill["other_head_dims"] = prefill_other_head_dims(job, max(args.steps // 4, 3),
+                                                                 prefill["tf32_dense_tflops_measured"])
+    parity = None
+    if not args.no_parity:
+        parity = parity_leg(job)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -471,25 +1055,21 @@ def run_ours(args):
     wo = None
     if rank == 0 and world == 1 and not args.no_wo:
         wo = run_wo(args, torch)
-    prefill = None
-    if rank == 0 and not args.no_prefill:
-        prefill = run_prefill(args, torch)
-        tf32 = measure_tf32_peak(torch)
-        prefill["tf32_dense_tflops_measured"] = round(tf32, 1)
-        prefill["roofline_3xtf32_tflops"] = round(tf32 / 3, 1)
-        prefill["frac_of_3xtf32"] = round(prefill["tflops"] / (tf32 / 3), 4)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded N(0,1) fp32 q/K/V, generated on device)",
+            "data": ("synthetic: the timed caches and q/k/v are N(0,1) fp32 from torch's device generator "
+                     "(Philox, seed 1000 + rank); the parity leg uses the BASELINE generator (numpy PCG64, "
+                     "SeedSequence([seed, layer]))"),
             "config": {"workload": WORKLOAD, "n_layers": L, "n_heads": sh.n_heads, "n_kv_heads": sh.n_kv_heads,
                        "head_dim": sh.head_dim, "pos": sh.pos, "kv_positions": P,
                        "parallelism": f"kv-head shards x{world}",
-                       "launch": ("cuda graph" if graph else "stream") + ("" if args.no_overlap else " + programmatic dependent launch"),
-                       "split_k": dict(zip(("ctas_per_kv_head", "cluster"), ctx.decode_plan(sh.pos))),
+                       "launch": ("cuda graph" if not args.no_graph else "stream") +
+                                 ("" if args.no_overlap else " + programmatic dependent launch"),
+                       "split_k": split_k,
                        "l2": "inputs larger than L2 (2 GiB KV per step vs 126 MB L2)"},
             "us_per_layer": round(ms_step * 1e3 / L, 3),
             "tokens_per_s": round(1e3 / ms_step, 2),
@@ -505,8 +1085,12 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": bytes_per_layer_rank,
                          "traffic": args.traffic if args.traffic is not None else
                          (NCU_TRAFFIC_PER_LAUNCH if world == 1 else None)},
+            "exchange_us_per_layer": exchange["us_per_layer"] if exchange else None,
+            "exchange": exchange,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "parity": parity,
+            "configs": configs,
             "pre_attention_step": raw,
             "wo_projection": wo,
             "prefill": prefill,
@@ -514,12 +1098,15 @@ def run_ours(args):
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
-    del graph
-    ctx.close()
+    rc = 0
+    if rank == 0 and parity is not None and not parity["all_ok"]:
+        print("parity leg FAILED: " + json.dumps({k: r for k, r in parity.items()
+                                                  if isinstance(r, dict) and not r["ok"]}), file=sys.stderr)
+        rc = 1
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    return 0
+    return rc
 
 
 def run_long(args):
@@ -696,79 +1283,6 @@ def run_kernel_only(args):
                       "gbs": round(nbytes / us / 1e3, 1)}), flush=True)
     ctx.close()
     return 0
-
-
-def measure_tf32_peak(torch):
-    """Dense TF32 tensor throughput of this GPU, measured live: an fp32
-    torch.matmul with TF32 enabled, 8192^3, best of 5 (2*N^3 flops).  The
-    3xTF32 prefill roofline is a third of it."""
-    prev = torch.backends.cuda.matmul.allow_tf32
-    torch.backends.cuda.matmul.allow_tf32 = True
-    n = 8192
-    a = torch.randn((n, n), device="cuda")
-    b = torch.randn((n, n), device="cuda")
-    c = a @ b
-    best = 1e9
-    for _ in range(5):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        c = a @ b
-        e1.record()
-        torch.cuda.synchronize()
-        best = min(best, e0.elapsed_time(e1))
-    torch.backends.cuda.matmul.allow_tf32 = prev
-    del a, b, c
-    return 2 * n ** 3 / (best / 1e3) / 1e12
-
-
-def run_prefill(args, torch):
-    """Causal prefill of BASELINE configs[4] (Llama-3.1-8B shapes, 2048
-    tokens, one layer per launch) through l3p_attn_prefill_dev."""
-    from llama3pure_b200.attn import AttnContext
-    from llama3pure_b200.synth import prefill_flops
-
-    sh = CONFIGS["llama31_8b_prefill_2k"]
-    S = sh.pos + 1
-    L = 4  # layers cycled (16 MiB of K/V each)
-    ctx = AttnContext.for_shape(sh, n_layers=L)
-    stream = torch.cuda.current_stream()
-    g = torch.Generator(device="cuda")
-    g.manual_seed(11)
-    q = torch.randn((L, S, sh.n_heads, sh.head_dim), device="cuda", generator=g)
-    k = torch.randn((L, S, sh.n_kv_heads, sh.head_dim), device="cuda", generator=g)
-    v = torch.randn((L, S, sh.n_kv_heads, sh.head_dim), device="cuda", generator=g)
-    out = torch.zeros_like(q)
-    for i in range(args.warmup):
-        ctx.prefill_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], stream)
-    torch.cuda.synchronize()
-    reps = max(args.steps // 2, 4)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(reps):
-        ctx.prefill_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], stream)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    ctx.check()
-    ms = e0.elapsed_time(e1) / reps
-    tflops = prefill_flops(sh) / (ms / 1e3) / 1e12
-    res = {"workload": "llama31_8b_prefill_2k", "ms_per_layer": round(ms, 4), "tflops": round(tflops, 2),
-           "flops_per_layer": prefill_flops(sh), "kernel": "prefill_tc_kernel (tcgen05 3xTF32) + prefill_prep_kernel"}
-    if not getattr(args, "no_raw", False):
-        # from the raw projections: RoPE + cache write in the pre-attention kernel
-        ctx.set_rope()
-        for i in range(args.warmup):
-            ctx.prefill_raw_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], stream)
-        torch.cuda.synchronize()
-        e0.record(stream)
-        for i in range(reps):
-            ctx.prefill_raw_dev(i % L, 0, S, q[i % L], k[i % L], v[i % L], out[i % L], stream)
-        e1.record(stream)
-        torch.cuda.synchronize()
-        ctx.check()
-        res["raw_ms_per_layer"] = round(e0.elapsed_time(e1) / reps, 4)
-        res["raw_api"] = "l3p_attn_prefill_raw_dev (RoPE + cache write, then prep + attention)"
-    ctx.close()
-    return res
 
 
 def run_q8(args, torch, layers: int = 16):
@@ -960,6 +1474,8 @@ def main():
     ap.add_argument("--no-q8", action="store_true", help="skip the Q8_0-cache decode measurement")
     ap.add_argument("--no-raw", action="store_true", help="skip the raw-projection (RoPE on device) measurements")
     ap.add_argument("--no-wo", action="store_true", help="skip the wo projection measurement")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs[0], [2], [3] sub-records")
+    ap.add_argument("--no-parity", action="store_true", help="skip the parity leg")
     ap.add_argument("--wo-only", action="store_true", help="wo projection measurement alone (ncu case)")
     ap.add_argument("--long", action="store_true", help="BASELINE configs[2] (128K context) over --gpus ranks")
     ap.add_argument("--seq-parts", type=int, default=1, help="--long: sequence parts per head group")
@@ -996,8 +1512,7 @@ def main():
         import torch
 
         torch.cuda.set_device(0)
-        line = run_prefill(args, torch)
-        line["tf32_dense_tflops_measured"] = round(measure_tf32_peak(torch), 1)
+        line = config5(Job(torch, None, 1, 0, 0), max(args.steps // 2, 4), raw=not args.no_raw)
         print(json.dumps({"mode": "prefill-only", **line}), flush=True)
         return 0
     return run_ours(args)

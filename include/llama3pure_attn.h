@@ -196,10 +196,11 @@ int l3p_attn_set_overlap(l3p_attn_ctx* ctx, int enable);
 long long l3p_attn_launch_count(const l3p_attn_ctx* ctx);
 
 /* The architecture the library's kernels were compiled for, as the CUDA
- * runtime reports it for the decode kernel on `device`: *binary = SASS
- * version (100 for sm_100a), *ptx = PTX version (0 when the image carries no
- * PTX).  Fails with L3P_E_CUDA when the device cannot run the image.  A
- * runtime check of the build; no counterpart in the reference. */
+ * runtime reports it for the decode kernel on `device`: *binary = the SASS
+ * version (100 for sm_100a), *ptx = the virtual architecture that SASS was
+ * compiled from (100 for compute_100a).  Fails with L3P_E_CUDA when the device
+ * cannot run the image.  A runtime check of the build; no counterpart in the
+ * reference. */
 int l3p_attn_device_arch(int device, int* binary, int* ptx);
 
 /* The split-K decomposition a decode launch at `pos` over `n_slices` layers
@@ -323,11 +324,16 @@ int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* 
  * so their projections are partial sums.  Members of a group of n_members
  * export (64-byte CUDA IPC handle of a small exchange region for `dim`-row
  * projections) and import each other's regions once; then
- * l3p_attn_wo_allreduce_dev writes every member's partial straight into every
- * member's memory (peer stores) and adds the members' partials in member order
- * -- the all-reduce of xb2 without a collective library, and the same bits on
- * every member.  Two launches per call; every member calls it for the same
- * layers in the same order.  No counterpart in the reference. */
+ * l3p_attn_wo_allreduce_dev computes this member's partial and, in the same
+ * launch, sums the group's partials over NVLink peer memory: every row block
+ * is summed by one owner member (in member order, so every member gets the
+ * same bits) and sent back to all -- a reduce-scatter and an all-gather of
+ * xb2 without a collective library, about 2 * dim * 4 bytes sent per member.
+ * One launch per call; every member calls it for the same layers in the same
+ * order, on identical GPUs.  A member that never arrives makes the others'
+ * bounded waits give up (L3P_E_TIMEOUT through l3p_attn_check); the group is
+ * then out of step and must be set up anew (new contexts).  No counterpart in
+ * the reference. */
 int l3p_attn_tp_group_export(l3p_attn_ctx* ctx, int n_members, int member, int dim, void* handle);
 int l3p_attn_tp_group_import(l3p_attn_ctx* ctx, const void* handles);
 /* xout[dim] = sum over the group of Wo[:, member's columns] . x[member's rows]. */

@@ -433,11 +433,12 @@ int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float
 
 // Tensor-core prefill: split the cached K/V rows [0, start_pos+n_tok) into
 // tf32 hi/lo chunk images, then run the tcgen05 flash-attention kernel.
-int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
-                      cudaStream_t s) {
+template <int HD>
+int launch_prefill_tc_hd(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
+                         cudaStream_t s) {
   const int n_keys = start_pos + n_tok;
   const int n_ktiles = (n_keys + kPfBN - 1) / kPfBN;
-  const size_t need = (size_t)ctx->kvh_count * n_ktiles * kPfTileFloats;
+  const size_t need = (size_t)ctx->kvh_count * n_ktiles * PfGeom<HD>::kTileFloats;
   if (need > ctx->pf_img_floats) {
     if (ctx->pf_img) {
       L3P_CUDA(ctx, cudaStreamSynchronize(s));
@@ -452,8 +453,8 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
     ctx->pf_img_floats = need;
   }
   const long long off = (long long)layer * ctx->layer_elems;
-  const int cg = ctx->prefill_cg;
-  (cg == 2 ? prefill_prep_kernel<2> : prefill_prep_kernel<1>)<<<dim3(n_ktiles, ctx->kvh_count), 256, 0, s>>>(
+  const int cg = HD == 128 ? ctx->prefill_cg : 1;
+  (cg == 2 ? prefill_prep_kernel<(HD == 128 ? 2 : 1), HD> : prefill_prep_kernel<1, HD>)<<<dim3(n_ktiles, ctx->kvh_count), 256, 0, s>>>(
       ctx->q8 ? nullptr : ctx->kc + off, ctx->q8 ? nullptr : ctx->vc + off, ctx->head_elems, n_keys, n_ktiles,
       ctx->pf_img, ctx->q8 ? ctx->k8 + off : nullptr, ctx->q8 ? ctx->v8 + off : nullptr,
       ctx->q8 ? ctx->ksc + off / 32 : nullptr, ctx->q8 ? ctx->vsc + off / 32 : nullptr);
@@ -478,11 +479,12 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
   a.swa_pattern = ctx->cfg.swa_pattern;
   a.q8 = ctx->q8 ? 1 : 0;
   a.err = ctx->err_dev;
-  if (cg == 2) {
+  if constexpr (HD == 128) {
+    if (cg == 2) {
     cudaLaunchConfig_t lc{};
     lc.gridDim = dim3(a.n_qtiles * a.n_qh, 1, 1);
     lc.blockDim = dim3(256, 1, 1);
-    lc.dynamicSmemBytes = PfCfg<2>::kSmemBytes;
+    lc.dynamicSmemBytes = PfCfg<2, 128>::kSmemBytes;
     lc.stream = s;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -491,13 +493,21 @@ int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, co
     attr[0].val.clusterDim.z = 1;
     lc.attrs = attr;
     lc.numAttrs = 1;
-    L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, prefill_tc_kernel<2>, a));
-  } else {
-    prefill_tc_kernel<1><<<a.n_qtiles * a.n_qh, 256, PfCfg<1>::kSmemBytes, s>>>(a);
+    L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, prefill_tc_kernel<2, 128>, a));
+    ++ctx->launches;
+    return L3P_OK;
+    }
   }
+  prefill_tc_kernel<1, HD><<<a.n_qtiles * a.n_qh, 256, PfCfg<1, HD>::kSmemBytes, s>>>(a);
   ++ctx->launches;
   L3P_CUDA(ctx, cudaGetLastError());
   return L3P_OK;
+}
+
+int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
+                      cudaStream_t s) {
+  if (ctx->hd == 64) return launch_prefill_tc_hd<64>(ctx, layer, start_pos, n_tok, q, out, s);
+  return launch_prefill_tc_hd<128>(ctx, layer, start_pos, n_tok, q, out, s);
 }
 
 int check_pos_full(l3p_attn_ctx* ctx, int pos) {
@@ -605,8 +615,9 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   if (!ki.fn) return bail(L3P_E_UNSUPPORTED, "no decode kernel for this geometry");
   if (cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem) != cudaSuccess)
     return bail(L3P_E_CUDA, "cudaFuncSetAttribute failed");
-  // head_dim 128 prefill runs on the tensor cores unless L3P_PREFILL_PATH=ffma
-  ctx->prefill_tc = c.head_dim == kPfHD;
+  // head_dim 64 and 128 prefill runs on the tensor cores unless
+  // L3P_PREFILL_PATH=ffma (head_dim 256: the decode kernel in token mode)
+  ctx->prefill_tc = c.head_dim == 64 || c.head_dim == 128;
   if (const char* path = getenv("L3P_PREFILL_PATH"))
     if (strcmp(path, "ffma") == 0) ctx->prefill_tc = false;
   // single CTAs by default (measured faster: the pair form pays a second
@@ -617,10 +628,12 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   if (const char* cg = getenv("L3P_PREFILL_CG"))
     if (strcmp(cg, "2") == 0 && ctx->G % 2 == 0) ctx->prefill_cg = 2;
   if (ctx->prefill_tc &&
-      (cudaFuncSetAttribute(prefill_tc_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfCfg<1>::kSmemBytes) !=
-           cudaSuccess ||
-       cudaFuncSetAttribute(prefill_tc_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, PfCfg<2>::kSmemBytes) !=
-           cudaSuccess))
+      (cudaFuncSetAttribute(prefill_tc_kernel<1, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            PfCfg<1, 128>::kSmemBytes) != cudaSuccess ||
+       cudaFuncSetAttribute(prefill_tc_kernel<2, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            PfCfg<2, 128>::kSmemBytes) != cudaSuccess ||
+       cudaFuncSetAttribute(prefill_tc_kernel<1, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                            PfCfg<1, 64>::kSmemBytes) != cudaSuccess))
     return bail(L3P_E_CUDA, "cudaFuncSetAttribute (prefill) failed");
   // clusters of up to 16 CTAs (16 is a non-portable size); record how many of
   // each size fit on this GPU at once (0 = that size is not available)

@@ -1,6 +1,7 @@
 // l3p_groups.cu -- the NVLink groups of the C ABI: sequence groups (partial
-// attention merged through peer memory) and tensor-parallel groups (the wo
-// projection summed through peer memory), seq_xchg.cuh.
+// attention merged through peer memory, seq_xchg.cuh) and tensor-parallel
+// groups (the wo projection summed through peer memory in the tail of its
+// GEMV, wo.cuh).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -112,7 +113,7 @@ L3P_API int l3p_attn_tp_group_export(l3p_attn_ctx* ctx, int n_members, int membe
   if (ctx->tp_region && (ctx->tp_members != n_members || ctx->tp_dim != dim))
     return fail(ctx, L3P_E_INVAL, "the tensor-parallel group is already set up with another shape");
   if (!ctx->tp_region) {
-    const size_t bytes = kXchgFlagBytes + 2ull * n_members * dim * sizeof(float);
+    const size_t bytes = tp_region_bytes(n_members, dim);
     if (cudaMalloc(&ctx->tp_region, bytes) != cudaSuccess) {
       cudaGetLastError();
       ctx->tp_region = nullptr;
@@ -155,29 +156,7 @@ L3P_API int l3p_attn_wo_allreduce_dev(l3p_attn_ctx* ctx, int layer, const float*
   if (int rc = check_aligned(ctx, {x, xout})) return rc;
   DeviceScope dev(ctx->cfg.device);
   cudaStream_t s = pick_stream(ctx, stream);
-  if (int rc = launch_wo(ctx, layer, x, nullptr, s, true)) return rc;
-  TpArgs a{};
-  for (int m = 0; m < ctx->tp_members; ++m) a.peer_flags[m] = static_cast<unsigned*>(ctx->tp_peer[m]);
-  a.my_flags = reinterpret_cast<unsigned*>(ctx->tp_region);
-  a.my_slots = reinterpret_cast<const float*>(ctx->tp_region + kXchgFlagBytes);
-  a.n_members = ctx->tp_members;
-  a.member = ctx->tp_member;
-  a.dim = ctx->tp_dim;
-  a.out = xout;
-  a.err = ctx->err_dev;
-  cudaLaunchConfig_t lc{};
-  lc.gridDim = dim3(1, 1, 1);
-  lc.blockDim = dim3(kTpThreads, 1, 1);
-  lc.stream = s;
-  cudaLaunchAttribute attr[1];
-  if (ctx->overlap) {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-  }
-  L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, tp_sum_kernel, a));
-  ++ctx->launches;
-  return L3P_OK;
+  // one launch: the GEMV and, in its tail, the sum over the group
+  return launch_wo(ctx, layer, x, xout, s, true);
 }
 

@@ -19,13 +19,12 @@ int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream
   const l3p_attn_ctx::WoLayer& L = ctx->wo[layer];
   WoArgs a{};
   if (tp) {
-    // partial rows into every member's exchange slots (seq_xchg.cuh)
+    // y = the group's sum, exchanged through the members' regions (wo.cuh)
     a.tp_members = ctx->tp_members;
     a.tp_member = ctx->tp_member;
-    for (int m = 0; m < ctx->tp_members; ++m)
-      a.tp_slots[m] = reinterpret_cast<float*>(static_cast<uint8_t*>(ctx->tp_peer[m]) + kXchgFlagBytes);
-    a.tp_step = reinterpret_cast<const unsigned*>(ctx->tp_region) + 16;
+    for (int m = 0; m < ctx->tp_members; ++m) a.tp_regions[m] = static_cast<uint8_t*>(ctx->tp_peer[m]);
   }
+  a.err = ctx->err_dev;
   a.w = L.w;
   a.wsc = L.wsc;
   a.row_bytes = L.row_bytes;
@@ -45,6 +44,8 @@ int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream
   const int target = ctx->num_sms * std::max(ctx->wo_ctas_per_sm[k], 1);
   a.rows_per_cta = std::max(1, (a.rows + target - 1) / target);
   const int grid = (a.rows + a.rows_per_cta - 1) / a.rows_per_cta;
+  if (tp && grid > kTpMaxBlocks)
+    return fail(ctx, L3P_E_UNSUPPORTED, "tensor-parallel wo grid of %d CTAs exceeds %d", grid, kTpMaxBlocks);
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(grid, 1, 1);
   lc.blockDim = dim3(nw * 32, 1, 1);

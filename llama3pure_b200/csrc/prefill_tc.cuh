@@ -1,5 +1,5 @@
 // prefill_tc.cuh -- causal prompt attention on the tcgen05 tensor cores in
-// 3xTF32 (sm_100a), head_dim 128.
+// 3xTF32 (sm_100a), head_dim 64 or 128.
 //
 // Semantics are those of the reference's token-by-token prefill
 // (llama3pure-c-engine.c:3499-3613): query token at position p attends to the
@@ -49,15 +49,20 @@
 // Barriers the issuers wait on (kv_peer, s_free, p_full, q_ready) live in the
 // even CTA and count arrivals from both CTAs; barriers the issuers complete
 // (kv_empty, s_full, p_free, pv_done) get one commit per CTA of the pair.
-// Tensor memory (512 columns per CTA): Q hi [0,128) O [128,256) S [256,384)
-// P slot 0 [384,448) P slot 1 [448,512) (each slot: 32 hi then 32 lo columns).
-// Shared memory: Q lo image (64 KB) then the stage ring.
+// Tensor memory (512 columns per CTA): Q hi [0,HD) O [HD,2HD) S [2HD,2HD+128)
+// P slot 0 and slot 1, 64 columns each, after S (each slot: 32 hi then 32 lo
+// columns).  Head_dim 256 does not fit: Q hi and O alone would take all 512
+// columns.
+// Shared memory: Q lo image (128 rows x HD x 4 bytes) then the stage ring.
+// A key tile is HD/32 K chunks then 4 V chunks:
 //   K chunk c (dims 32c..32c+31), this CTA's 128/CG keys: K-major, 128-byte
-//            swizzle, hi then lo.
-//   V chunk v (keys 32v..32v+31), this CTA's 128/CG dims: MN-major, 128-byte
+//            swizzle, hi then lo (32 KB for both CTAs of a pair).
+//   V chunk v (keys 32v..32v+31), this CTA's HD/CG dims: MN-major, 128-byte
 //            swizzle with 32-byte units (the only MN-major layout the tensor
 //            cores accept for 32-bit elements), 32-dim atoms of eight 4-key
-//            groups, hi then lo.
+//            groups, hi then lo (32 * HD * 8 bytes for both CTAs).
+// A stage holds the largest chunk; a V chunk of head_dim 64 fills half of one.
+// CTA pairs (CG = 2) are built for head_dim 128 only.
 #pragma once
 #include "decode_q8.cuh"
 #include "ptx.cuh"
@@ -67,27 +72,41 @@ namespace l3p {
 
 constexpr int kPfBM = 128;  // query rows per CTA
 constexpr int kPfBN = 128;  // keys per tile
-constexpr int kPfHD = 128;  // head_dim of this kernel
-constexpr int kPfChunkBytes = 32768;  // one K or V chunk image, hi + lo, both CTAs' halves
-constexpr int kPfTileFloats = 8 * kPfChunkBytes / 4;  // one key tile: 8 chunks
-constexpr int kPfQloBytes = kPfBM * kPfHD * 4;
+constexpr int kPfKChunkBytes = 32768;  // one K chunk image (128 keys x 32 dims), hi + lo, both CTAs' halves
 constexpr float kPfRescale = 8.f;  // lazy rescale threshold (log2 units)
 constexpr int kProducers = 2;      // producer threads (warps 0, 2)
 
-template <int CG>
+// Key-tile geometry of one head size.
+template <int HD>
+struct PfGeom {
+  static_assert(HD == 64 || HD == 128, "tensor-core prefill: head_dim 64 or 128");
+  static constexpr int kKChunks = HD / 32;          // K chunks per key tile (32 dims each)
+  static constexpr int kVChunks = kPfBN / 32;       // V chunks per key tile (32 keys each)
+  static constexpr int kChunks = kKChunks + kVChunks;
+  static constexpr int kVChunkBytes = 32 * HD * 8;  // 32 keys x HD dims, hi + lo
+  static constexpr int kTileBytes = kKChunks * kPfKChunkBytes + kVChunks * kVChunkBytes;
+  static constexpr int kTileFloats = kTileBytes / 4;
+  static constexpr int kQloBytes = kPfBM * HD * 4;
+};
+
+template <int CG, int HD>
 struct PfCfg {
-  static constexpr int kStageBytes = kPfChunkBytes / CG;  // this CTA's share of a chunk image
+  static_assert(CG == 1 || HD == 128, "CTA pairs are built for head_dim 128");
+  static constexpr int kStageBytes = kPfKChunkBytes / CG;  // this CTA's share of the largest chunk image
   static constexpr int kStageFloats = kStageBytes / 4;
-  static constexpr int kStages = 5 * CG;
-  static constexpr int kRows = 128 / CG;  // B rows per CTA: keys of a K chunk, dims of a V chunk
-  static constexpr int kSmemBytes = kPfQloBytes + kStages * kStageBytes + 1024;  // + alignment slack
+  static constexpr int kKBytes = kPfKChunkBytes / CG;           // this CTA's K chunk
+  static constexpr int kVBytes = PfGeom<HD>::kVChunkBytes / CG;  // this CTA's V chunk
+  static constexpr int kHalfTile = PfGeom<HD>::kTileBytes / CG;  // this CTA's chunks of a key tile
+  static constexpr int kStages = HD == 64 ? 6 : 5 * CG;
+  static constexpr int kRows = 128 / CG;  // B rows per CTA: keys of a K chunk
+  static constexpr int kSmemBytes = PfGeom<HD>::kQloBytes + kStages * kStageBytes + 1024;  // + alignment slack
   static_assert(kSmemBytes <= 232448, "prefill shared memory exceeds the per-CTA limit");
 };
 
 struct PrefillArgs {
-  const float* q;    // [n_tok][n_heads][128], query token t at position q_pos0 + t
+  const float* q;    // [n_tok][n_heads][head_dim], query token t at position q_pos0 + t
   float* out;        // same layout
-  const float* img;  // [kvh_count][n_ktiles][kPfTileFloats] K/V chunk images (prefill_prep_kernel)
+  const float* img;  // [kvh_count][n_ktiles][PfGeom<HD>::kTileFloats] K/V chunk images (prefill_prep_kernel)
   int n_heads, G, kv_head_begin, n_qh;  // owned q heads = n_qh, absolute first = kv_head_begin*G
   int q_pos0, n_tok, n_qtiles, n_ktiles;
   float scale;
@@ -118,10 +137,14 @@ __device__ __forceinline__ uint64_t sdesc_mn_sw128_32b(uint32_t addr) {
 // offset >> 4 without carrying into the next field.
 __device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t byte_off) { return d + (byte_off >> 4); }
 
-template <int CG>
+template <int CG, int HD>
 __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a) {
-  using C = PfCfg<CG>;
+  using C = PfCfg<CG, HD>;
+  using Gm = PfGeom<HD>;
   constexpr int S = C::kStages;
+  constexpr int kPieces = HD / 4;         // 16-byte pieces of a q / out row
+  constexpr int kRowsPerLoad = 128 / HD;  // rows one warp-wide 512-byte access covers
+  constexpr int kQLoads = HD / 4;         // such accesses for a warp's 32 rows
   extern __shared__ unsigned char pf_smem_raw[];
   __shared__ uint32_t s_tmem;
   __shared__ __align__(8) uint64_t bar_kv_full[S], bar_kv_empty[S], bar_kv_peer[S];
@@ -129,7 +152,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
   __shared__ __align__(8) uint64_t bar_pv_done, bar_q_ready, bar_mma_idle[2];
   unsigned char* sbase = (unsigned char*)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
   unsigned char* qlo = sbase;
-  unsigned char* ring = sbase + kPfQloBytes;
+  unsigned char* ring = sbase + Gm::kQloBytes;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0;
@@ -148,17 +171,18 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
   const int nt = j1 - j0 + 1;
 
   // The softmax warps fetch their Q rows before the setup barrier so the
-  // latency overlaps the allocation: each warp its 32 rows, one whole 512-byte
-  // row per load (lane = 16-byte piece), all in flight at once.  Rows past
-  // the batch read the last row and are zeroed later, so no load result is
-  // needed before the barrier.
-  float4 qv[32];
+  // latency overlaps the allocation: each warp its 32 rows, 512 contiguous
+  // bytes per load (1 row of head_dim 128 or 2 rows of 64; lane = 16-byte
+  // piece), all in flight at once.  Rows past the batch read the last row and
+  // are zeroed later, so no load result is needed before the barrier.
+  float4 qv[kQLoads];
   if (warp >= 4) {
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      const int qpos = min(qbase + (warp - 4) * 32 + r, q_end - 1);
-      qv[r] = __ldg(reinterpret_cast<const float4*>(a.q + ((long long)(qpos - a.q_pos0) * a.n_heads + h) * kPfHD) +
-                    lane);
+    for (int r = 0; r < kQLoads; ++r) {
+      const int rr = r * kRowsPerLoad + lane / kPieces;
+      const int qpos = min(qbase + (warp - 4) * 32 + rr, q_end - 1);
+      qv[r] = __ldg(reinterpret_cast<const float4*>(a.q + ((long long)(qpos - a.q_pos0) * a.n_heads + h) * HD) +
+                    lane % kPieces);
     }
   }
   if (warp == 0) {
@@ -190,7 +214,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
     __syncthreads();
   tc::fence_after_sync();
   const uint32_t tm = s_tmem;
-  const uint32_t T_QHI = tm + 0, T_O = tm + 128, T_S = tm + 256, T_P = tm + 384;
+  const uint32_t T_QHI = tm + 0, T_O = tm + HD, T_S = tm + 2 * HD, T_P = tm + 2 * HD + kPfBN;
 
   // bounded waits: cluster-scope acquire when the pair shares the barriers
   auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
@@ -219,7 +243,8 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
     // the ring full.
     if (lane == 0) {
       const int me = warp >> 1;  // chunks c with c % kProducers == me
-      const float* img = a.img + ((long long)kvh_local * a.n_ktiles + j0) * kPfTileFloats + rank * 8 * C::kStageFloats;
+      const unsigned char* img = reinterpret_cast<const unsigned char*>(a.img) +
+                                 ((long long)kvh_local * a.n_ktiles + j0) * Gm::kTileBytes + rank * C::kHalfTile;
       int c = 0;  // chunks enumerated
       bool ok = true;
       // consumption order: K of tile 0; then per step n, K of tile n and V of tile n-1
@@ -227,19 +252,22 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
         for (int part = 0; ok && part < 2; ++part) {
           const int t = n - part;
           if (t < 0 || t >= nt) continue;
-          for (int ch = 0; ch < 4; ++ch, ++c) {
+          const int n_ch = part == 0 ? Gm::kKChunks : Gm::kVChunks;
+          for (int ch = 0; ch < n_ch; ++ch, ++c) {
             if (c % kProducers != me) continue;
             const int s = c % S, u = c / S;
             if (u >= 1 && !wait(&bar_kv_empty[s], (uint32_t)((u - 1) & 1))) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&bar_kv_full[s], (uint32_t)C::kStageBytes);
+            const uint32_t bytes = part == 0 ? C::kKBytes : C::kVBytes;
+            const long long off = part == 0 ? (long long)ch * C::kKBytes
+                                            : (long long)Gm::kKChunks * C::kKBytes + (long long)ch * C::kVBytes;
+            mbar_arrive_expect_tx(&bar_kv_full[s], bytes);
             asm volatile(
                 "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                     smem_addr(ring + s * C::kStageBytes)),
-                "l"(img + (long long)t * kPfTileFloats + (part * 4 + ch) * C::kStageFloats),
-                "r"((uint32_t)C::kStageBytes), "r"(smem_addr(&bar_kv_full[s]))
+                "l"(img + (long long)t * Gm::kTileBytes + off), "r"(bytes), "r"(smem_addr(&bar_kv_full[s]))
                 : "memory");
           }
         }
@@ -251,7 +279,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
   } else if (warp == 1 && rank == 1) {
     // ---------------- relay (odd CTA): chunk landed here -> issuer ----------------
     if (lane == 0) {
-      for (int c = 0; c < 8 * nt; ++c) {
+      for (int c = 0; c < Gm::kChunks * nt; ++c) {
         if (!wait(&bar_kv_full[c % S], (uint32_t)((c / S) & 1))) break;
         mbar_arrive_cluster(mapa_shared(smem_addr(&bar_kv_peer[c % S]), 0));
       }
@@ -263,9 +291,11 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
     // tensor core takes 64 cycles per N=128 MMA: a single issuer leaves it
     // idle, two issuers in different warps keep it busy.
     if (lane == 0) {
-      // chunk c = 4 * block + i of the ring sequence K0 K1 V0 K2 V1 ... V(nt-1)
-      auto k_block = [&](int t) { return t == 0 ? 0 : 2 * t - 1; };
-      auto v_block = [&](int t) { return t + 1 < nt ? 2 * t + 2 : 2 * t + 1; };
+      // first chunk of each block in the ring sequence K0 K1 V0 K2 V1 ... V(nt-1)
+      // (a K block holds HD/32 chunks, a V block 4)
+      constexpr int nK = Gm::kKChunks, nKV = Gm::kChunks;
+      auto k_chunk0 = [&](int t) { return t == 0 ? 0 : nK + (t - 1) * nKV; };
+      auto v_chunk0 = [&](int t) { return t + 1 < nt ? 2 * nK + t * nKV : nK + t * nKV; };
       auto chunk_ready = [&](int c, uint32_t& off) -> bool {
         const int s = c % S, u = c / S;
         off = (uint32_t)(s * C::kStageBytes);
@@ -287,8 +317,8 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
             tc::fence_after_sync();
           }
 #pragma unroll 1
-          for (int ch = 0; ok && ch < 4; ++ch) {
-            const int c = 4 * k_block(t) + ch;
+          for (int ch = 0; ok && ch < nK; ++ch) {
+            const int c = k_chunk0(t) + ch;
             uint32_t off;
             if (!(ok = chunk_ready(c, off))) break;
             const uint64_t kh = desc_add(k_d, off), kl = desc_add(k_d, off + C::kStageBytes / 2);
@@ -308,18 +338,18 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
         tc::commit_g<CG>(smem_addr(&bar_mma_idle[0]));
         wait(&bar_mma_idle[0], 0);
       } else {
-        constexpr uint32_t id_o = tc::idesc_tf32(kPfBM * CG, kPfHD, true);
+        constexpr uint32_t id_o = tc::idesc_tf32(kPfBM * CG, HD, true);
         const uint64_t v_d = sdesc_mn_sw128_32b(smem_addr(ring));
         bool ok = true;
         for (int t = 0; ok && t < nt; ++t) {
 #pragma unroll 1
-          for (int qq = 0; ok && qq < 4; ++qq) {
-            const int c = 4 * v_block(t) + qq, slot = qq & 1;
+          for (int qq = 0; ok && qq < Gm::kVChunks; ++qq) {
+            const int c = v_chunk0(t) + qq, slot = qq & 1;
             uint32_t off;
             if (!(ok = chunk_ready(c, off))) break;
             if (!(ok = wait(&bar_p_full[slot], (uint32_t)((qq >> 1) & 1)))) break;
             tc::fence_after_sync();
-            const uint64_t vh = desc_add(v_d, off), vl = desc_add(v_d, off + C::kStageBytes / 2);
+            const uint64_t vh = desc_add(v_d, off), vl = desc_add(v_d, off + C::kVBytes / 2);
             const uint32_t p_hi = T_P + slot * 64, p_lo = p_hi + 32;
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
@@ -345,21 +375,21 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
     const int kmin = valid ? pf_start_t(a, qpos) : 0;
     const uint32_t lb = (uint32_t)((warp - 4) * 32) << 16;
     // Rows to threads through the Q lo region: 16-byte piece i of row r at
-    // piece i ^ (r % 8) of the row's 512 bytes (conflict-free both ways).
+    // piece i ^ (r % 8) of the row's HD * 4 bytes (conflict-free both ways).
 #pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      const int rr = (warp - 4) * 32 + r;
-      *reinterpret_cast<float4*>(qlo + rr * (kPfHD * 4) + ((lane ^ (rr & 7)) << 4)) =
+    for (int r = 0; r < kQLoads; ++r) {
+      const int rr = (warp - 4) * 32 + r * kRowsPerLoad + lane / kPieces;
+      *reinterpret_cast<float4*>(qlo + rr * (HD * 4) + (((lane % kPieces) ^ (rr & 7)) << 4)) =
           qbase + rr < q_end ? qv[r] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     __syncwarp();
 #pragma unroll
-    for (int i = 0; i < 32; ++i)
-      qv[i] = *reinterpret_cast<const float4*>(qlo + row * (kPfHD * 4) + ((i ^ (row & 7)) << 4));
+    for (int i = 0; i < kPieces; ++i)
+      qv[i] = *reinterpret_cast<const float4*>(qlo + row * (HD * 4) + ((i ^ (row & 7)) << 4));
     // every softmax warp has its row before the Q lo image overwrites the region
     asm volatile("bar.sync 1, 128;" ::: "memory");
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < HD / 32; ++c) {
       float hi[32], lo[32];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
@@ -458,7 +488,7 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
         if (!ok) break;
         tc::fence_after_sync();
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < HD / 32; ++c) {
           float ov[32];
           tc::ld32(T_O + lb + c * 32, ov);
           tc::wait_ld();
@@ -508,9 +538,9 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
       // S is done) so that global stores are whole 512-byte rows.  16-byte
       // piece i of row r sits at piece i ^ (r % 8): conflict-free for the
       // row-per-thread writes and the row-per-warp reads.
-      unsigned char* srow = qlo + row * (kPfHD * 4);
+      unsigned char* srow = qlo + row * (HD * 4);
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < HD / 32; ++c) {
         float ov[32];
         tc::ld32(T_O + lb + c * 32, ov);
         tc::wait_ld();
@@ -521,12 +551,13 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
       }
       __syncwarp();
 #pragma unroll 4
-      for (int r = 0; r < 32; ++r) {
-        const int rr = (warp - 4) * 32 + r;
+      for (int r = 0; r < kQLoads; ++r) {
+        const int rr = (warp - 4) * 32 + r * kRowsPerLoad + lane / kPieces;
+        const int pc = lane % kPieces;
         const int pos = qbase + rr;
         if (pos < q_end)
-          *reinterpret_cast<float4*>(a.out + ((long long)(pos - a.q_pos0) * a.n_heads + h) * kPfHD + 4 * lane) =
-              *reinterpret_cast<const float4*>(qlo + rr * (kPfHD * 4) + ((lane ^ (rr & 7)) << 4));
+          *reinterpret_cast<float4*>(a.out + ((long long)(pos - a.q_pos0) * a.n_heads + h) * HD + 4 * pc) =
+              *reinterpret_cast<const float4*>(qlo + rr * (HD * 4) + ((pc ^ (rr & 7)) << 4));
       }
     }
   }
@@ -541,28 +572,30 @@ __global__ void __launch_bounds__(256, 1) prefill_tc_kernel(const PrefillArgs a)
   }
 }
 
-// K/V chunk images for prefill_tc_kernel<CG>: per (owned KV head, 128-key
-// tile), per CTA half r of the pair: K chunks 0..3 then V chunks 0..3, each
-// hi then lo, from the head-major cache (fp32 kc/vc, or the Q8_0 arrays
+// K/V chunk images for prefill_tc_kernel<CG, HD>: per (owned KV head, 128-key
+// tile), per CTA half r of the pair: the HD/32 K chunks then the 4 V chunks,
+// each hi then lo, from the head-major cache (fp32 kc/vc, or the Q8_0 arrays
 // k8/ksc, v8/vsc when k8 is set).  K chunk c of half r holds keys
 // [r*128/CG, (r+1)*128/CG) of dims 32c..32c+31; V chunk v of half r holds
-// keys 32v..32v+31 of dims [r*128/CG, (r+1)*128/CG).  Keys at or beyond
-// n_keys read as 0.  grid (n_ktiles, kvh_count), 256 threads.
-template <int CG>
+// keys 32v..32v+31 of dims [r*HD/CG, (r+1)*HD/CG).  Keys at or beyond n_keys
+// read as 0.  grid (n_ktiles, kvh_count), 256 threads.
+template <int CG, int HD>
 __global__ void prefill_prep_kernel(const float* __restrict__ kc, const float* __restrict__ vc, long long head_stride,
                                     int n_keys, int n_ktiles, float* __restrict__ img, const int8_t* __restrict__ k8,
                                     const int8_t* __restrict__ v8, const uint16_t* __restrict__ ksc,
                                     const uint16_t* __restrict__ vsc) {
-  using C = PfCfg<CG>;
+  using C = PfCfg<CG, HD>;
+  using Gm = PfGeom<HD>;
   const int j = blockIdx.x, hl = blockIdx.y;
-  unsigned char* base = reinterpret_cast<unsigned char*>(img + ((long long)hl * n_ktiles + j) * kPfTileFloats);
-  constexpr int kHalf = C::kStageBytes / 2;  // bytes of one hi (or lo) image
-  for (int idx = threadIdx.x; idx < kPfBN * kPfHD / 4; idx += blockDim.x) {
-    const int key = idx / (kPfHD / 4), c16 = idx % (kPfHD / 4);  // 16-byte piece of the row
+  unsigned char* base = reinterpret_cast<unsigned char*>(img) + ((long long)hl * n_ktiles + j) * Gm::kTileBytes;
+  constexpr int kVRows = HD / CG;               // dims of a V chunk per CTA half
+  constexpr int kVBase = Gm::kKChunks * C::kKBytes;  // V chunks after the K chunks of a half
+  for (int idx = threadIdx.x; idx < kPfBN * HD / 4; idx += blockDim.x) {
+    const int key = idx / (HD / 4), c16 = idx % (HD / 4);  // 16-byte piece of the row
     const int pos = j * kPfBN + key;
     float4 kx = make_float4(0.f, 0.f, 0.f, 0.f), vx = kx;
     if (pos < n_keys) {
-      const long long e = hl * head_stride + (long long)pos * kPfHD + 4 * c16;
+      const long long e = hl * head_stride + (long long)pos * HD + 4 * c16;
       if (k8) {
         // Q8_0 cache: the values the reference's dot products use, d * int8 (exact)
         const char4 kq = *reinterpret_cast<const char4*>(k8 + e);
@@ -582,17 +615,17 @@ __global__ void prefill_prep_kernel(const float* __restrict__ kc, const float* _
     const int part = c16 & 7;  // 16-byte piece within its 128-byte (32-dim) block
     // K chunk c16/8, half key/kRows: K-major, 128-byte swizzle (piece ^ key % 8)
     const int kr = key / C::kRows, kl = key % C::kRows;
-    const int kb = (kr * 8 + (c16 >> 3)) * C::kStageBytes + kl * 128 + ((part ^ (kl & 7)) << 4);
+    const int kb = kr * C::kHalfTile + (c16 >> 3) * C::kKBytes + kl * 128 + ((part ^ (kl & 7)) << 4);
     *reinterpret_cast<float4*>(base + kb) = khi;
-    *reinterpret_cast<float4*>(base + kb + kHalf) = klo;
-    // V chunk key/32, half dim/kRows: MN-major, 32-byte units ^ (key % 4),
+    *reinterpret_cast<float4*>(base + kb + C::kKBytes / 2) = klo;
+    // V chunk key/32, half dim/kVRows: MN-major, 32-byte units ^ (key % 4),
     // 32-dim atoms of eight 4-key groups
-    const int dim = 4 * c16, vr = dim / C::kRows, atom = (dim % C::kRows) >> 5;
+    const int dim = 4 * c16, vr = dim / kVRows, atom = (dim % kVRows) >> 5;
     const int kv = key & 31, byte = part * 16;
-    const int vb = (vr * 8 + 4 + (key >> 5)) * C::kStageBytes + atom * 4096 + (kv >> 2) * 512 + (kv & 3) * 128 +
-                   ((((byte >> 5) ^ (kv & 3)) << 5) | (byte & 31));
+    const int vb = vr * C::kHalfTile + kVBase + (key >> 5) * C::kVBytes + atom * 4096 + (kv >> 2) * 512 +
+                   (kv & 3) * 128 + ((((byte >> 5) ^ (kv & 3)) << 5) | (byte & 31));
     *reinterpret_cast<float4*>(base + vb) = vhi;
-    *reinterpret_cast<float4*>(base + vb + kHalf) = vlo;
+    *reinterpret_cast<float4*>(base + vb + C::kVBytes / 2) = vlo;
   }
 }
 

@@ -45,15 +45,6 @@ struct XchgArgs {
   int* err;
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // grid: ONE CTA of kXchgThreads threads (warp w merges q heads w, w + warps, ...).
 constexpr int kXchgThreads = 512;
 static __global__ void __launch_bounds__(kXchgThreads) seq_merge_kernel(const XchgArgs a) {
@@ -122,78 +113,6 @@ static __global__ void __launch_bounds__(kXchgThreads) seq_merge_kernel(const Xc
     }
     const float inv = L > 0.f ? 1.f / L : 0.f;
     reinterpret_cast<float4*>(a.out)[o4] = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
-  }
-}
-
-}  // namespace l3p
-
-namespace l3p {
-
-// ---- Tensor-parallel sum of the wo projection over NVLink ------------------
-// The members of a tensor-parallel group hold the wo columns of their own q
-// heads, so each member's projection is a partial sum of xb2.  Each member's
-// exchange region holds flags[kXchgMaxParts] and a step counter (as above),
-// then two slots (by step parity) of [n_members][dim] floats.  The projection
-// kernel stores every row of its partial into slot (step+1)&1, row band
-// [member] of EVERY member's region (peer stores over NVLink); then
-// tp_sum_kernel (one CTA) advances the step, publishes it into each peer's
-// flags, waits (bounded) for theirs and adds the members' bands in member
-// order -- the same order, hence the same bits, on every member.  A member
-// that runs ahead writes the other slot; it cannot get two steps ahead,
-// because the step after needs this member's flag, which is published only
-// when this member's reading of the earlier slot is behind it.
-constexpr int kTpThreads = 512;
-
-struct TpArgs {
-  unsigned* peer_flags[kXchgMaxParts];  // flags (and step counter at +16) of every member
-  unsigned* my_flags;
-  const float* my_slots;                // this member's two slots [2][n_members][dim]
-  int n_members, member, dim;
-  float* out;                           // [dim]
-  int* err;
-};
-
-static __global__ void __launch_bounds__(kTpThreads) tp_sum_kernel(const TpArgs a) {
-  pdl_launch_dependents();
-  pdl_wait();  // the projection's peer stores are complete
-  __shared__ int s_ok;
-  __shared__ unsigned s_step;
-  if (threadIdx.x == 0) {
-    unsigned* step = a.my_flags + 16;
-    const unsigned e = *step + 1;
-    *step = e;
-    __threadfence_system();
-    for (int s = 0; s < a.n_members; ++s)
-      if (s != a.member) st_release_sys(a.peer_flags[s] + a.member, e);
-    int ok = 1;
-    for (int s = 0; s < a.n_members && ok; ++s) {
-      if (s == a.member) continue;
-      const unsigned long long t0 = globaltimer_ns();
-      while ((int)(ld_acquire_sys(a.my_flags + s) - e) < 0) {
-        if (globaltimer_ns() - t0 > kGroupWaitNs) {
-          *reinterpret_cast<volatile int*>(a.err) = kErrTimeout;
-          ok = 0;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    s_ok = ok;
-    s_step = e;
-  }
-  __syncthreads();
-  if (!s_ok) return;
-  const float* slot = a.my_slots + (size_t)(s_step & 1u) * a.n_members * a.dim;
-  for (int r4 = threadIdx.x; r4 < a.dim / 4; r4 += kTpThreads) {
-    float4 acc = __ldcv(reinterpret_cast<const float4*>(slot) + r4);
-    for (int s = 1; s < a.n_members; ++s) {
-      const float4 v = __ldcv(reinterpret_cast<const float4*>(slot + (size_t)s * a.dim) + r4);
-      acc.x += v.x;
-      acc.y += v.y;
-      acc.z += v.z;
-      acc.w += v.w;
-    }
-    reinterpret_cast<float4*>(a.out)[r4] = acc;
   }
 }
 

@@ -57,12 +57,12 @@ struct WoArgs {
   int wc;               // column groups per CTA (power of two <= warps)
   const float* x;       // owned columns of the attention output (x[0] = column q_head0*hd)
   float* y;             // [rows]
-  // tensor-parallel group (seq_xchg.cuh): instead of y, store the partial into
-  // row band `member` of slot (step+1)&1 of every member's exchange slots,
-  // step = *tp_step (read after griddepcontrol.wait)
+  // tensor-parallel group (tp_members > 0): y receives the SUM of every
+  // member's partial, reduce-scattered and all-gathered through the members'
+  // exchange regions (layout in limits.cuh; protocol at wo_tp_exchange)
   int tp_members, tp_member;
-  float* tp_slots[kXchgMaxParts];  // every member's [2][tp_members][rows] slots (own included)
-  const unsigned* tp_step;
+  uint8_t* tp_regions[kXchgMaxParts];  // every member's exchange region (own included)
+  int* err;                            // device error word (kErrTimeout)
 };
 
 // Byte i (0..3) of w as the float 2^23 + byte: exact for every byte.
@@ -238,6 +238,103 @@ struct WoQ6K {
   __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
 };
 
+// Tensor-parallel sum of the partial projections over NVLink, in the tail of
+// the GEMV: a reduce-scatter then an all-gather, spread over the CTAs.  The
+// grid is the same on every member (same rows, kernel and GPU), so CTA j
+// covers the same row block j everywhere; block j is owned by member
+// j % n_members.  Call e (1, 2, ... counted by the device step word, read
+// after griddepcontrol.wait, when the previous call's grid has completed):
+//   1. CTA j stores its partial rows into slot [e&1][member] of the owner's
+//      recv array (a peer store unless it owns the block), then one thread
+//      orders them (fence.acq_rel.sys) and adds 1 to the owner's arrivals[j];
+//   2. the owner's CTA j waits (bounded) until arrivals[j] reaches
+//      e * n_members, sums the members' rows in member order -- the same
+//      order, hence the same bits, on every member -- stores the sum into
+//      result[e&1] of every member and adds 1 to each member's done[j];
+//   3. every CTA j waits (bounded) until its done[j] reaches e and copies the
+//      block's summed rows to y;
+//   4. the last CTA to leave (exit ticket) writes e into the step word.
+// Per call a member sends its dim partial floats once and the owners send dim
+// summed floats to each member: about 2 * dim * 4 bytes over NVLink per
+// member instead of n_members * dim * 4.  Two slots suffice: a member can be
+// at most one call ahead of another, since finishing a call needs every
+// owner's sum of that call.  A wait that gives up sets kErrTimeout in the
+// error word; the group is then out of step and must be set up anew.
+__device__ __forceinline__ bool tp_wait_at_least(const unsigned* p, unsigned want, int* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  while ((int)(ld_acquire_sys(p) - want) < 0) {
+    if (globaltimer_ns() - t0 > kGroupWaitNs) {
+      *reinterpret_cast<volatile int*>(err) = kErrTimeout;
+      return false;
+    }
+    __nanosleep(32);
+  }
+  return true;
+}
+
+__device__ __forceinline__ void wo_tp_exchange(const WoArgs& p, const float* red, int r_begin, int r_end) {
+  __shared__ unsigned s_e;
+  __shared__ int s_ok;
+  const int n = r_end - r_begin;
+  const int N = p.tp_members, me = p.tp_member, j = blockIdx.x;
+  const int owner = j % N;
+  uint8_t* const mine = p.tp_regions[me];
+  unsigned* const hdr = reinterpret_cast<unsigned*>(mine);
+  if (threadIdx.x == 0) {
+    s_e = *reinterpret_cast<volatile unsigned*>(hdr + kTpStepWord) + 1u;
+    s_ok = 1;
+  }
+  __syncthreads();
+  const unsigned e = s_e;
+  const size_t par = e & 1u;
+  // 1. this block's partial rows to the owner
+  float* recv = reinterpret_cast<float*>(p.tp_regions[owner] + kTpRecvOff) + (par * N + me) * p.rows;
+  for (int r = threadIdx.x; r < n; r += blockDim.x) {
+    float s = 0.f;
+    for (int c = 0; c < p.wc; ++c) s += red[c * p.rows_per_cta + r];
+    recv[r_begin + r] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+    red_add_sys(reinterpret_cast<unsigned*>(p.tp_regions[owner] + kTpArrOff) + j, 1u);
+  }
+  // 2. the owner sums the block and sends it to every member
+  if (owner == me) {
+    if (threadIdx.x == 0)
+      s_ok = tp_wait_at_least(reinterpret_cast<const unsigned*>(mine + kTpArrOff) + j, e * (unsigned)N, p.err);
+    __syncthreads();
+    if (s_ok) {
+      const float* rv = reinterpret_cast<const float*>(mine + kTpRecvOff) + par * N * p.rows;
+      const size_t res = tp_result_off(N, p.rows);
+      for (int r = threadIdx.x; r < n; r += blockDim.x) {
+        float s = __ldcv(rv + r_begin + r);
+        for (int m = 1; m < N; ++m) s += __ldcv(rv + (size_t)m * p.rows + r_begin + r);
+        for (int m = 0; m < N; ++m) reinterpret_cast<float*>(p.tp_regions[m] + res)[par * p.rows + r_begin + r] = s;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        fence_acq_rel_sys();
+        for (int m = 0; m < N; ++m) red_add_sys(reinterpret_cast<unsigned*>(p.tp_regions[m] + kTpDoneOff) + j, 1u);
+      }
+    }
+  }
+  // 3. every member: this block's sum into y
+  if (threadIdx.x == 0 && s_ok)
+    s_ok = tp_wait_at_least(reinterpret_cast<const unsigned*>(mine + kTpDoneOff) + j, e, p.err);
+  __syncthreads();
+  if (s_ok) {
+    const float* sum = reinterpret_cast<const float*>(mine + tp_result_off(N, p.rows)) + par * p.rows;
+    for (int r = threadIdx.x; r < n; r += blockDim.x) p.y[r_begin + r] = __ldcv(sum + r_begin + r);
+  }
+  // 4. the last CTA to leave advances the step (the next call reads it after
+  // this grid has completed)
+  if (threadIdx.x == 0 && atomicAdd(hdr + kTpTicketWord, 1u) == gridDim.x - 1) {
+    hdr[kTpTicketWord] = 0u;
+    *reinterpret_cast<volatile unsigned*>(hdr + kTpStepWord) = e;
+  }
+}
+
 // grid: ceil(rows / rows_per_cta) CTAs of NW warps; dynamic shared memory:
 // NW * rows_per_cta floats.
 template <class F, int NW>
@@ -298,14 +395,7 @@ __global__ void __launch_bounds__(NW * 32) wo_gemv_kernel(const WoArgs p) {
     }
     return;
   }
-  // tensor-parallel: the row band of this member in every member's next slot
-  const unsigned next = (*p.tp_step + 1u) & 1u;
-  const size_t band = ((size_t)next * p.tp_members + p.tp_member) * p.rows + r_begin;
-  for (int r = threadIdx.x; r < r_end - r_begin; r += blockDim.x) {
-    float s = 0.f;
-    for (int c = 0; c < p.wc; ++c) s += red[c * p.rows_per_cta + r];
-    for (int m = 0; m < p.tp_members; ++m) p.tp_slots[m][band + r] = s;
-  }
+  wo_tp_exchange(p, red, r_begin, r_end);
 }
 
 }  // namespace l3p

@@ -49,15 +49,42 @@ class OracleCfg(C.Structure):
     ]
 
 
-def lib_path(impl: str, fast: bool = False) -> str:
+def lib_path(impl: str, fast=False) -> str:
+    """fast: False (exact IEEE build), True (-Ofast -march=x86-64-v3) or "v4"
+    (-Ofast -march=x86-64-v4, reference harness only)."""
     if impl == "port":
         return os.path.join(HERE, "liboracle_fast.so" if fast else "liboracle.so")
     if impl == "ref":
-        return os.path.join(HERE, "_ref", "libl3p_ref_fast.so" if fast else "libl3p_ref.so")
+        name = {False: "libl3p_ref.so", True: "libl3p_ref_fast.so", "v4": "libl3p_ref_fast_v4.so"}[fast]
+        return os.path.join(HERE, "_ref", name)
     raise ValueError(impl)
 
 
-def ref_available(fast: bool = False) -> bool:
+def cpu_has_v4() -> bool:
+    """The host CPU runs x86-64-v4 code (AVX-512 F, BW, CD, DQ, VL)."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("flags"):
+                    flags = set(line.split(":", 1)[1].split())
+                    return {"avx512f", "avx512bw", "avx512cd", "avx512dq", "avx512vl"} <= flags
+    except OSError:
+        pass
+    return False
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def ref_available(fast=False) -> bool:
     return os.path.exists(lib_path("ref", fast))
 
 
@@ -66,7 +93,7 @@ def build_port() -> None:
     subprocess.run(["make", "-s", "-C", HERE, "oracle"], check=True)
 
 
-def _load(impl: str, fast: bool):
+def _load(impl: str, fast):
     key = (impl, fast)
     if key in _LIBS:
         return _LIBS[key]
@@ -116,7 +143,7 @@ def _fptr(a):
 class Oracle:
     """One attention context of the oracle: its own KV cache for n_layers."""
 
-    def __init__(self, shape, mode: int = MODE_F32, impl: str = "port", fast: bool = False,
+    def __init__(self, shape, mode: int = MODE_F32, impl: str = "port", fast=False,
                  n_layers: int | None = None, seq_len: int | None = None):
         self.shape = shape
         self.mode = mode
@@ -185,7 +212,7 @@ def primitives(impl: str = "port"):
     return _load(impl, False)[1]
 
 
-def threads(impl: str = "ref", fast: bool = True) -> int:
+def threads(impl: str = "ref", fast=True) -> int:
     fns = _load(impl, fast)[1]
     return int(fns["threads"]()) if "threads" in fns else 1
 

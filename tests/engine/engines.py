@@ -1,6 +1,7 @@
-"""ctypes driver of the two engine builds of tests/engine/Makefile (TEST
-INFRASTRUCTURE ONLY): the reference C engine as it is, and the same engine
-wired to libllama3pure_attn.so.  Each build holds one model at a time."""
+"""ctypes driver of the engine builds of tests/engine/Makefile (TEST
+INFRASTRUCTURE ONLY): the reference C engine as it is (exact IEEE build and
+its own -Ofast release build), and the same engine wired to
+libllama3pure_attn.so.  Each build holds one model at a time."""
 from __future__ import annotations
 
 import ctypes as C
@@ -11,6 +12,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 REF_SO = os.path.join(ROOT, "oracle", "_ref", "libl3p_engine_ref.so")
 WIRED_SO = os.path.join(ROOT, "oracle", "_ref", "libl3p_engine_wired.so")
+OFAST_SO = os.path.join(ROOT, "oracle", "_ref", "libl3p_engine_ofast.so")
 
 
 class EngineCfg(C.Structure):
@@ -28,13 +30,13 @@ MODELS = {
 }
 
 
-def available(wired: bool) -> bool:
-    return os.path.exists(WIRED_SO if wired else REF_SO)
+def available(wired: bool, ofast: bool = False) -> bool:
+    return os.path.exists(WIRED_SO if wired else OFAST_SO if ofast else REF_SO)
 
 
 class Engine:
-    def __init__(self, wired: bool):
-        self.lib = C.CDLL(WIRED_SO if wired else REF_SO)
+    def __init__(self, wired: bool, ofast: bool = False):
+        self.lib = C.CDLL(WIRED_SO if wired else OFAST_SO if ofast else REF_SO)
         self.lib.l3pe_init.argtypes = [C.POINTER(EngineCfg)]
         self.lib.l3pe_init.restype = C.c_int
         self.lib.l3pe_run.argtypes = [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_void_p]

@@ -45,12 +45,12 @@ def test_library_is_compiled_for_sm100a_only():
 
 @pytest.mark.gpu
 def test_runtime_reports_sm100_kernels(lib):
-    """The CUDA runtime's own view of the loaded image: SASS for sm_100 and
-    no PTX to JIT from."""
+    """The CUDA runtime's own view of the loaded image: SASS for sm_100,
+    compiled from the compute_100 virtual architecture."""
     binary, ptx = C.c_int(0), C.c_int(-1)
     assert lib.l3p_attn_device_arch(0, C.byref(binary), C.byref(ptx)) == 0
     assert binary.value == 100
-    assert ptx.value == 0
+    assert ptx.value == 100
 
 
 def _cfg(**kw):

@@ -116,3 +116,35 @@ def test_prefill_image_growth_keeps_rope_tables_and_wo_weights():
     o.close()
     _check(att.reshape(-1), want.reshape(-1), "raw step after image growth")
     _check(xb2, O.matvec(8, w, 256, cols, np.ascontiguousarray(att.reshape(-1))), "wo after image growth")
+
+
+@pytest.mark.parametrize("name,shape", [
+    # Llama-3.2-1B shapes (head_dim 64, tensor cores) and Gemma shapes (head_dim
+    # 256, the decode kernel in token mode) at a 2048-token prompt
+    ("l1b_2k_hd64", CONFIGS["llama32_1b_decode"].with_(n_layers=1, seq_len=2048, pos=2047, seed=16)),
+    ("gemma_2k_hd256", CONFIGS["gemma_2b_decode"].with_(n_layers=1, seq_len=2048, pos=2047, seed=17)),
+])
+def test_prefill_2k_other_head_sizes_match_oracle(name, shape):
+    k, v, q = prefill_inputs(shape, 0)
+    with AttnContext.for_shape(shape, n_layers=1) as ctx:
+        got = ctx.prefill(0, 0, q, k, v)
+    _check(got, _oracle(shape, q, k, v), name)
+
+
+@pytest.mark.parametrize("kv_format", [0, 1])
+def test_prefill_hd64_continuation_and_q8_cache(kv_format):
+    """head_dim 64 on the tensor cores: a prompt continued in a second call
+    (keys of the first call's tiles), ragged lengths, both cache formats."""
+    sh = AttnShape("pf_hd64_cont", 1, 16, 4, 64, 700, pos=699, seed=18)
+    k, v, q = prefill_inputs(sh, 0)
+    with AttnContext.for_shape(sh, n_layers=1, kv_format=kv_format) as ctx:
+        first = ctx.prefill(0, 0, q[:333], k[:333], v[:333])
+        second = ctx.prefill(0, 333, q[333:], k[333:], v[333:])
+    got = np.concatenate([first, second])
+    if kv_format == 0:
+        _check(got, _oracle(sh, q, k, v), "hd64 split prefill")
+    else:
+        o = O.Oracle(sh, O.MODE_Q8, "port", n_layers=1)
+        want, _ = o.prefill(0, 0, q, k, v)
+        o.close()
+        _check(got, want, "hd64 split prefill, Q8_0 cache")
