@@ -433,7 +433,10 @@ def config3(job: Job, reps: int, seq_parts_list=(1, 2)):
                 hs = [None] * job.world
                 job.dist.all_gather_object(hs, h)
                 ctx.seq_group_import(hs[g0:g0 + sp])
-            ctx.set_overlap(True)
+            # programmatic dependent launch only with the merge kernel between
+            # the decodes: back to back, 1 GiB launches measured ~9 us per
+            # layer slower with it (158.5 vs 167.7 us on one B200)
+            ctx.set_overlap(sp > 1)
             if sp > 1:
                 gr = job.graph(lambda s: [ctx.decode_seq_dev(l, sh.pos, q[l], out[l], s) for l in range(L)])
             else:
@@ -1285,6 +1288,202 @@ def run_kernel_only(args):
     return 0
 
 
+def run_decode_trace(args):
+    """Per-stage timeline of the decode launches of a step graph (the headline
+    form: 32 layers of l3p_attn_step_dev with programmatic dependent launch,
+    and the same launches without it), from a build of the library with
+    -DL3P_DECODE_TRACE: every CTA stamps %globaltimer at its start, when
+    griddepcontrol.wait returns, when q is ready, when its last tile is done,
+    when its partial is published and at its exit.  --kv-heads H owns H of
+    the 8 KV heads (the per-rank work at N = 8/H GPUs); --q8 uses a Q8_0 cache.
+    Prints medians over the layers of one replay, in microseconds."""
+    import tempfile as _tf
+
+    import torch
+
+    from llama3pure_b200.attn import AttnContext, load_library
+    from llama3pure_b200.build import LIB_PATH
+    from llama3pure_b200.build import build as build_lib
+
+    torch.cuda.set_device(0)
+    lib_path = os.path.join(os.path.dirname(LIB_PATH), "libllama3pure_attn_trace.so")
+    build_lib(out=lib_path, extra=["-DL3P_DECODE_TRACE"])
+    lib = load_library(lib_path)
+    sh = CONFIGS[WORKLOAD]
+    L, hk = sh.n_layers, args.kv_heads
+    job = Job(torch, None, 1, 0, 0)
+    out_json = {"workload": WORKLOAD, "kv_heads": hk, "kv_format": "q8_0" if args.q8 else "f32", "n_layers": L}
+    for overlap in (True, False):
+        ctx = AttnContext.for_shape(sh, device=0, kv_head_begin=0, kv_head_count=hk, kv_format=1 if args.q8 else 0,
+                                    lib=lib)
+        if args.q8:
+            for layer in range(L):  # random blocks (any bytes time the same)
+                rng = np.random.default_rng(layer)
+                nb = sh.head_dim // 32
+                b = rng.integers(0, 256, size=(sh.n_kv_heads, sh.seq_len, nb * 34), dtype=np.uint8)
+                b.reshape(sh.n_kv_heads, sh.seq_len, nb, 34)[..., 1] = 0x20  # fp16 scales ~0.008
+                ctx.load_kv_q8(layer, 0, b, b)
+            g = torch.Generator(device="cuda")
+            g.manual_seed(3)
+        else:
+            g = job.fill_cache(ctx, L, hk, sh.seq_len, sh.head_dim, 3)
+        q = torch.randn((L, sh.n_heads * sh.head_dim), device="cuda", generator=g)
+        kn = torch.randn((L, sh.n_kv_heads * sh.head_dim), device="cuda", generator=g)
+        vn = torch.randn_like(kn)
+        o = torch.zeros_like(q)
+        ctx.set_overlap(overlap)
+        gr = job.graph(lambda s: [ctx.step_dev(l, sh.pos, q[l], kn[l], vn[l], o[l], s) for l in range(L)])
+        ms = job.time_graph(gr, args.steps)
+        gr.replay()  # the traced replay (slots hold the last launch of each layer)
+        torch.cuda.synchronize()
+        ctx.check()
+        fd, path = _tf.mkstemp(suffix=".bin")
+        os.close(fd)
+        os.environ["L3P_TRACE_FILE"] = path
+        plan = ctx.decode_plan(sh.pos)
+        del gr
+        ctx.close()
+        os.environ.pop("L3P_TRACE_FILE", None)
+        raw = np.fromfile(path, dtype=np.int64)
+        os.unlink(path)
+        n, ctas = int(raw[0]), int(raw[1])
+        recs = []
+        off = 2
+        for _ in range(n):
+            meta = raw[off:off + 6]
+            st = raw[off + 6:off + 6 + ctas * 8].reshape(ctas, 8)[: int(meta[1] * meta[2] * meta[3])].astype(np.float64)
+            recs.append((meta, st))
+            off += 6 + ctas * 8
+        # the launches of the last replay: the L with the highest launch sequence numbers
+        recs = sorted(recs, key=lambda r: r[0][0])[-L:]
+        rows = []
+        for i in range(1, len(recs)):
+            prev_end = recs[i - 1][1][:, 5].max()
+            st = recs[i][1]
+            rows.append({
+                "first_cta_start_after_prev_end": st[:, 0].min() - prev_end,
+                "wait_release_after_prev_end": st[:, 1].min() - prev_end,
+                "ctas_started_before_prev_end": float((st[:, 0] < prev_end).mean()),
+                "q_ready_after_release": np.median(st[:, 2] - st[:, 1]),
+                "last_tile_after_release": st[:, 3].max() - st[:, 1].min(),
+                "median_tile_done_after_release": np.median(st[:, 3] - st[:, 1]),
+                "ticket_after_last_tile": st[:, 4].max() - st[:, 3].max(),
+                "merge_tail_after_last_tile": st[:, 5].max() - st[:, 3].max(),
+                "period": st[:, 5].max() - prev_end,
+            })
+        out_json["overlap" if overlap else "no_overlap"] = {
+            "us_per_layer_timed": round(ms * 1e3 / L, 3), "split_k": plan,
+            **{k: round(float(np.median([r[k] for r in rows])) / (1.0 if k.startswith("ctas") else 1e3), 3)
+               for k in rows[0]}}
+    print(json.dumps({"mode": "decode-trace", **out_json}), flush=True)
+    return 0
+
+
+def run_tp_trace(args):
+    """Under torchrun (N >= 2): stage timeline of the tensor-parallel wo sum
+    (l3p_attn_wo_allreduce_dev, Q8_0 4096 x 4096, each rank the columns of its
+    KV-head shard) from the -DL3P_DECODE_TRACE build, alone (32 launches in a
+    graph) and inside the head-sharded block (raw step + wo + sum per layer).
+    Every CTA stamps %globaltimer at its start, after griddepcontrol.wait,
+    after its GEMV rows, after sending them to the block's owner, (owner) after
+    sending the block's sums to every member, when the block's sums have
+    arrived, and at its exit.  Medians over the launches of one replay, per rank, in us (each
+    GPU's own timer: only differences within one GPU are used)."""
+    import datetime
+    import tempfile as _tf
+
+    import torch
+    import torch.distributed as dist
+
+    from llama3pure_b200.attn import AttnContext, load_library
+    from llama3pure_b200.build import LIB_PATH
+    from llama3pure_b200.build import build as build_lib
+    from llama3pure_b200.shard import plan_shards
+    from llama3pure_b200.synth import wo_weights
+
+    world, rank, local = int(os.environ["WORLD_SIZE"]), int(os.environ["RANK"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    lib_path = os.path.join(os.path.dirname(LIB_PATH), "libllama3pure_attn_trace.so")
+    if rank == 0:
+        build_lib(out=lib_path, extra=["-DL3P_DECODE_TRACE"])
+    dist.barrier()
+    lib = load_library(lib_path)
+    job = Job(torch, dist, world, rank, local)
+    sh = CONFIGS[WORKLOAD]
+    L, dim = sh.n_layers, sh.n_heads * sh.head_dim
+    me = plan_shards(sh.n_kv_heads, sh.seq_len, world, 1)[rank]
+    res = {}
+    for name in ("wo_allreduce_alone", "block"):
+        ctx = AttnContext.for_shape(sh, device=local, kv_head_begin=me.kv_head_begin, kv_head_count=me.kv_head_count,
+                                    lib=lib)
+        g = job.fill_cache(ctx, L, me.kv_head_count, sh.seq_len, sh.head_dim, 11 + rank)
+        q = torch.randn((L, dim), device="cuda", generator=g)
+        kn = torch.randn((L, sh.n_kv_heads * sh.head_dim), device="cuda", generator=g)
+        vn = torch.randn_like(kn)
+        out = torch.zeros_like(q)
+        xb2 = torch.zeros((L, dim), device="cuda")
+        w = wo_weights(8, dim, dim, seed=3)
+        for l in range(L):
+            ctx.set_wo(l, 8, w)
+        ctx.set_rope()
+        h = ctx.tp_group_export(world, rank, dim)
+        hs = [None] * world
+        dist.all_gather_object(hs, h)
+        ctx.tp_group_import(hs)
+        ctx.set_overlap(True)
+        if name == "block":
+            gr = job.graph(lambda s: [(ctx.step_raw_dev(l, sh.pos, q[l], kn[l], vn[l], out[l], s),
+                                       ctx.wo_allreduce_dev(l, out[l], xb2[l], s)) for l in range(L)])
+        else:
+            gr = job.graph(lambda s: [ctx.wo_allreduce_dev(l, out[l], xb2[l], s) for l in range(L)])
+        ms = job.time_graph(gr, args.steps)
+        gr.replay()
+        torch.cuda.synchronize()
+        ctx.check()
+        fd, path = _tf.mkstemp(suffix=".bin")
+        os.close(fd)
+        os.environ["L3P_TRACE_FILE"] = path
+        del gr
+        ctx.close()
+        os.environ.pop("L3P_TRACE_FILE", None)
+        raw = np.fromfile(path, dtype=np.int64)
+        os.unlink(path)
+        n, ctas = int(raw[0]), int(raw[1])
+        recs, off = [], 2
+        for _ in range(n):
+            meta = raw[off:off + 6]
+            st = raw[off + 6:off + 6 + ctas * 8].reshape(ctas, 8)[: int(meta[1] * meta[2] * meta[3])].astype(np.float64)
+            if meta[5] == -1:  # wo launches
+                recs.append((meta, st))
+            off += 6 + ctas * 8
+        recs = sorted(recs, key=lambda r: r[0][0])[-L:]
+        rows = []
+        for i in range(1, len(recs)):
+            st, prev = recs[i][1], recs[i - 1][1]
+            owner = (np.arange(st.shape[0]) % world) == rank
+            rows.append({
+                "release_after_prev_exit": st[:, 1].min() - prev[:, 6].max(),
+                "gemv_done_after_release": st[:, 2].max() - st[:, 1].min(),
+                "sent_after_gemv": np.median(st[:, 3] - st[:, 2]),
+                "owner_sums_sent_after_sent": np.median(st[owner, 4] - st[owner, 3]),
+                "sum_arrived_after_sent": np.median(st[:, 5] - st[:, 3]),
+                "exit_after_sum_arrived": np.median(st[:, 6] - st[:, 5]),
+                "last_exit_after_release": st[:, 6].max() - st[:, 1].min(),
+                "period": st[:, 6].max() - prev[:, 6].max(),
+            })
+        summary = {k: round(float(np.median([r[k] for r in rows])) / 1e3, 3) for k in rows[0]}
+        summary["us_per_layer_timed"] = round(ms * 1e3 / L, 3)
+        per_rank = [None] * world
+        dist.all_gather_object(per_rank, summary)
+        res[name] = per_rank
+    if rank == 0:
+        print(json.dumps({"mode": "tp-trace", "n_gpus": world, **res}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def run_q8(args, torch, layers: int = 16):
     """Decode over the reference's own cache format (kv_format L3P_KV_Q8_0,
     272 bytes per position and KV head instead of 1024) on the workload's
@@ -1484,6 +1683,12 @@ def main():
     ap.add_argument("--q8-only", action="store_true", help="Q8_0-cache decode measurement alone")
     ap.add_argument("--kernel-only", action="store_true", help="decode kernel alone on --layers layers (ncu case)")
     ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--trace-decode", action="store_true",
+                    help="per-stage timeline of the step graph's decode launches (a -DL3P_DECODE_TRACE build)")
+    ap.add_argument("--kv-heads", type=int, default=8, help="--trace-decode: KV heads owned (8/N at N GPUs)")
+    ap.add_argument("--q8", action="store_true", help="--trace-decode: Q8_0 cache")
+    ap.add_argument("--trace-tp", action="store_true",
+                    help="(torchrun, N >= 2) stage timeline of the tensor-parallel wo sum (a -DL3P_DECODE_TRACE build)")
     ap.add_argument("--prefill-only", action="store_true", help="prefill measurement alone (ncu case)")
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per decode launch, if captured (reported as roofline.traffic)")
@@ -1494,6 +1699,10 @@ def main():
         return run_reference_arm(args)
     if args.kernel_only:
         return run_kernel_only(args)
+    if args.trace_decode:
+        return run_decode_trace(args)
+    if args.trace_tp:
+        return run_tp_trace(args)
     if args.long:
         return run_long(args)
     if args.q8_only:

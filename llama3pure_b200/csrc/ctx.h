@@ -62,6 +62,15 @@ struct l3p_attn_ctx {
   int force_nsplit = 0, force_cluster = 0;
   // overlap mode: decode launches carry programmatic stream serialisation
   bool overlap = false;
+  // split-K plans of recent launches, by (tiles, units, rows per tile, CTAs per SM)
+  struct PlanEntry {
+    long long n_tiles = -1, units = -1;
+    int rows = 0, ctas_per_sm = 0, nsplit = 1, cluster = 1;
+  } plan_cache[4];
+  unsigned plan_cache_next = 0;
+  // one-wave decode launches merge through the last-arriving part (ticket)
+  // instead of designated mergers (L3P_DECODE_MERGE=ticket)
+  bool ticket_merge = false;
   // split scratch is used in kScratchSlots rotating slices so that launches
   // overlapping on the GPU never share partials or tickets
   unsigned long long launch_seq = 0;
@@ -106,6 +115,13 @@ struct l3p_attn_ctx {
   bool tp_ready = false;
   uint8_t* tp_region = nullptr;
   void* tp_peer[l3p::kXchgMaxParts] = {};
+  // decode trace (builds with L3P_DECODE_TRACE only): mapped pinned stamps of
+  // the last kTraceSlots decode launches and their grids, written to the file
+  // named by $L3P_TRACE_FILE when the context is destroyed
+  unsigned long long* trace_host = nullptr;
+  unsigned long long* trace_dev = nullptr;
+  long long trace_meta[64][6] = {};  // launch seq, grid x, y, z, layer0, pos0
+  unsigned long long trace_count = 0;
   std::string last_error;
 };
 
@@ -169,6 +185,7 @@ int finish_host_call(l3p_attn_ctx* ctx);
 void owned_rows(const l3p_attn_ctx* ctx, int* row_lo, int* row_hi);
 // Decode core shared by the single-layer, multi-layer, prefill and partial
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
+unsigned long long* trace_slot(l3p_attn_ctx* ctx, int gx, int gy, int gz, int layer, int pos);
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz, const float* q,
                   float* out, float* part_o, float* part_ml, cudaStream_t s, const float* k_new = nullptr,
                   const float* v_new = nullptr, bool allow_overlap = false);

@@ -67,6 +67,22 @@ __device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned* p) {
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_gpu(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void red_add_gpu(unsigned* p, unsigned v) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// L2 prefetch of the 128-byte lines of [p, p + bytes): thread t of the CTA
+// takes line t.  L2 is the point of coherence of global memory, so a line
+// fetched before its producer (the kernel before this one) writes it still
+// reads the written values afterwards.
+__device__ __forceinline__ void prefetch_l2(const void* p, int bytes) {
+  const int line = (int)threadIdx.x;
+  if (line * 128 < bytes)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(p) + line * 128));
+}
 // Programmatic dependent launch: let the next kernel of the stream start
 // launching, and wait for the previous kernel's results (no-ops when the
 // launch carries no programmatic dependency).
@@ -117,7 +133,27 @@ struct DecodeArgs {
   // cache rows of positions >= wait_pos may still be being stored by an
   // earlier launch in flight: copied only after griddepcontrol.wait (INT_MAX: none)
   int wait_pos;
+  unsigned long long* trace;  // per-CTA stage stamps (builds with L3P_DECODE_TRACE), or null
+  // designated mergers (one-wave launches without clusters; null: the ticket
+  // scheme): flags[unit * nsplit + part] = number of mergers still to read
+  // part's partial; parts [0, merge_k) merge, each 1/merge_k of the output
+  unsigned* flags;
 };
+
+// Decode trace, compiled in only with -DL3P_DECODE_TRACE (a separate build for
+// timing studies; the shipped library has none): thread 0 of every CTA stores
+// %globaltimer (ns) at the stages of a launch into trace[cta][k]:
+//   0 CTA start                      1 griddepcontrol.wait returned
+//   2 q ready                        3 position loop done (last copy landed)
+//   4 partial published, ticket taken 5 CTA exit
+#ifdef L3P_DECODE_TRACE
+__device__ __forceinline__ void trace_stamp(unsigned long long* t, int k) {
+  if (t && threadIdx.x == 0)
+    t[(((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 8 + k] = globaltimer_ns();
+}
+#else
+__device__ __forceinline__ void trace_stamp(unsigned long long*, int) {}
+#endif
 
 #ifndef L3P_DECODE_WARPS
 #define L3P_DECODE_WARPS 8  // warps per CTA
@@ -343,6 +379,7 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
   float* const ml_base = a.partial ? a.part_ml + (long long)z * a.ml_zstride + 2 * h0 : nullptr;
 
   if (a.nsplit == 1) {  // this CTA covers the whole range
+    trace_stamp(a.trace, 4);
     for (int idx = threadIdx.x; idx < GT * HD; idx += T) {
       const float L = s_cl[idx / HD];
       out_base[idx] = (a.partial && !(L > 0.f)) ? 0.f : cta_o[idx] / L;
@@ -351,6 +388,7 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
       ml_base[2 * threadIdx.x] = s_cm[threadIdx.x];
       ml_base[2 * threadIdx.x + 1] = s_cl[threadIdx.x];
     }
+    trace_stamp(a.trace, 5);
     return;
   }
 
@@ -358,6 +396,7 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
   int part = split;
   int rank = 0, cs = 1;
   int mergers = 1;  // CTAs of the global stage that each merge a slice, without a cluster
+  bool flag_merge = false;  // designated mergers (a.flags): flags, not the ticket, to reset
   if (a.cluster > 1) {
     // ---- cluster stage: the CTAs of a cluster merge through distributed shared memory ----
     cg::cluster_group cluster = cg::this_cluster();
@@ -410,6 +449,8 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
     }
     if (last_stage) {
       cluster.sync();  // no CTA leaves while another still reads its shared memory
+      trace_stamp(a.trace, 4);
+      trace_stamp(a.trace, 5);
       return;
     }
     __threadfence();
@@ -419,6 +460,49 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
       for (int r = 0; r < cs; ++r) *cluster.map_shared_rank(&s_last, r) = last;
     }
     cluster.sync();
+  } else if (a.flags) {
+    // ---- no cluster, designated mergers: every part publishes its partial
+    // and then its flag (release, no atomic round trip); parts [0, merge_k)
+    // -- resident, as every CTA of a one-wave launch is -- wait until every
+    // flag is set (one flag per thread, all polled at once) and merge their
+    // slice of the output in the global stage below.  Each merger then takes
+    // 1 off every flag; the flags return to 0. ----
+    const long long gslot = ((long long)unit * n_parts + part) * GT * HD;
+    for (int idx = threadIdx.x; idx < GT * HD; idx += T) a.ws_o[gslot + idx] = cta_o[idx];
+    if (threadIdx.x < GT) {
+      a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2] = s_cm[threadIdx.x];
+      a.ws_ml[(((long long)unit * n_parts + part) * GT + threadIdx.x) * 2 + 1] = s_cl[threadIdx.x];
+    }
+    __syncthreads();
+    unsigned* const fl = a.flags + (long long)unit * n_parts;
+    if (threadIdx.x == 0) {
+      fence_acq_rel_gpu();  // the partial (all threads' stores, ordered by the barrier) before the flag
+      st_relaxed_gpu(fl + part, (unsigned)a.merge_k);
+    }
+    trace_stamp(a.trace, 4);
+    if (part >= a.merge_k) {
+      trace_stamp(a.trace, 5);
+      return;
+    }
+    bool arrived = true;
+    const unsigned long long t0 = globaltimer_ns();
+    for (int sp = threadIdx.x; sp < n_parts && arrived; sp += T)
+      while (ld_acquire_gpu(fl + sp) == 0u) {
+        if (globaltimer_ns() - t0 > kGroupWaitNs) {
+          *reinterpret_cast<volatile int*>(a.err) = kErrTimeout;
+          arrived = false;
+          break;
+        }
+        __nanosleep(20);
+      }
+    if (!__syncthreads_and(arrived)) {  // the barrier also orders every thread's reads after the acquires
+      trace_stamp(a.trace, 5);
+      return;
+    }
+    rank = part;
+    cs = mergers = a.merge_k;
+    s_last = 1;  // (read only below, by this CTA)
+    flag_merge = true;
   } else {
     // ---- no cluster: every CTA is a part of the global stage ----
     const long long gslot = ((long long)unit * n_parts + part) * GT * HD;
@@ -456,8 +540,14 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
     rank = s_last - 1;
     cs = mergers = ms.mk;
   }
-  if (!s_last) return;
-  __threadfence();
+  if (!flag_merge) {
+    trace_stamp(a.trace, 4);
+    if (!s_last) {
+      trace_stamp(a.trace, 5);
+      return;
+    }
+    __threadfence();
+  }
 
   // ---- global stage: the last part to finish merges all n_parts partials ----
   // (with a cluster, each rank of the last cluster merges its slice; without,
@@ -471,7 +561,7 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
   const long long slot0 = (long long)unit * n_parts;
   const int slice4 = GT * HD / 4 / cs;
   int pg = 1;
-  if (mergers > 1)  // pg * slice4 <= T: one float4 and part group per thread
+  if (mergers > 1 || flag_merge)  // pg * slice4 <= T: one float4 and part group per thread
     while (2 * pg * slice4 <= T && pg * kMergeBatch < n_parts) pg *= 2;
   const float2* ml2 = reinterpret_cast<const float2*>(a.ws_ml) + slot0 * GT;  // [n_parts][GT]
   const float4* o4 = reinterpret_cast<const float4*>(a.ws_o + slot0 * GT * HD);
@@ -529,6 +619,12 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
       }
     }
   }
+  if (flag_merge) {
+    __syncthreads();  // every thread's reads of the partials are done
+    for (int sp = threadIdx.x; sp < n_parts; sp += T) red_add_gpu(a.flags + (long long)unit * n_parts + sp, 0xffffffffu);
+    trace_stamp(a.trace, 5);
+    return;
+  }
   // ticket ready for the next launch: with several mergers the last one to
   // finish resets it (each adds one more after its merge)
   if (threadIdx.x == 0) {
@@ -538,6 +634,7 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
       a.counters[unit] = 0u;
     }
   }
+  trace_stamp(a.trace, 5);
 }
 
 template <int HD, int GT>
@@ -561,6 +658,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
   const int layer = a.layer0 + z * a.layer_step;
   const int pos = a.pos0 + z * a.pos_step;
   const int kvh = a.kv_head_begin + kvh_local;
+  trace_stamp(a.trace, 0);
 
   const int lo = max(swa_start(a, layer, pos), a.seq_begin);
   const int hi = min(pos + 1, a.seq_begin + a.cap);
@@ -616,6 +714,8 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
   // a warp's tiles come in increasing row order, so from its first tile that
   // reaches wait_row on, it waits first.
   pdl_launch_dependents();
+  // q's lines into L2 now, so that its load after the wait hits L2
+  prefetch_l2(a.q + (long long)z * a.q_zstride + (long long)h0 * HD, GT * HD * 4);
   const int wait_row = min(wait_new ? new_row : INT_MAX, a.wait_pos - lo);
   bool waited = false;
 #pragma unroll
@@ -631,6 +731,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
     cp_async_commit();
   }
   pdl_wait();
+  trace_stamp(a.trace, 1);
 
   // the fused append: one CTA per KV head writes the new row into the cache
   if (fused && split == 0 && hg == 0) {
@@ -669,6 +770,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
 #pragma unroll
     for (int e = 0; e < kQ; ++e) qr[g][e] *= a.scale;
   }
+  trace_stamp(a.trace, 2);
 
   float my_m = -INFINITY, my_l = 0.f;
   float acc[GT][C::kEPL];
@@ -834,6 +936,7 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
     __syncwarp();  // every lane is done with this stage before it is refilled
   }
   cp_async_wait<0>();
+  trace_stamp(a.trace, 3);
   __syncthreads();
   // the lane holding head g's running (max, sum): g (narrow) or g << kSH (wide)
   if constexpr (C::kNarrow) {

@@ -223,6 +223,7 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
   const int layer = a.layer0 + z * a.layer_step;
   const int pos = a.pos0 + z * a.pos_step;
   const int kvh = a.kv_head_begin + kvh_local;
+  trace_stamp(a.trace, 0);
 
   const int lo = max(swa_start(a, layer, pos), a.seq_begin);
   const int hi = min(pos + 1, a.seq_begin + a.cap);
@@ -282,6 +283,7 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
   __shared__ __align__(16) uint32_t s_q8[kQV / 4];  // int8 q, packed
   __shared__ float s_dq[kQV / 32];                  // block scales
   pdl_launch_dependents();
+  prefetch_l2(a.q + (long long)z * a.q_zstride + (long long)h0 * HD, kQV * 4);  // q's lines into L2 before the wait
   if (warp == 0) {
     pdl_wait();
     const float* qg = a.q + (long long)z * a.q_zstride + (long long)h0 * HD;
@@ -323,6 +325,8 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
     cp_async_commit();
   }
   pdl_wait();
+  trace_stamp(a.trace, 1);
+  trace_stamp(a.trace, 2);  // q was quantised by warp 0 before its copies
   constexpr int kNW = (HD / 32 + 3) / 4;  // packed int8 words of a lane's share of a row
   uint32_t nkw[kNW], nvw[kNW];
   uint16_t nkd = 0, nvd = 0;
@@ -505,6 +509,7 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
     __syncwarp();  // every lane is done with this stage and s_p before they are refilled
   }
   cp_async_wait<0>();
+  trace_stamp(a.trace, 3);
   __syncthreads();
   if (lane == 0) {
 #pragma unroll

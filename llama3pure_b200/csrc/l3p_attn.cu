@@ -30,6 +30,10 @@ using namespace l3p_api;
 namespace l3p_api {
 
 constexpr long long kWsOFloats = 8ll << 20;  // 32 MiB of split partials
+#ifdef L3P_DECODE_TRACE
+constexpr int kTraceSlots = 64;    // decode launches whose stamps are kept
+constexpr int kTraceCtas = 4096;   // CTAs per traced launch at most
+#endif
 constexpr long long kCounters = 1 << 16;
 constexpr int kScratchSlots = 4;
 // Global-stage mergers of a one-wave launch (DecodeArgs::merge_k) when a unit
@@ -150,7 +154,11 @@ Plan plan_splits(const PlanLimits* ctx, long long P, long long units, int rows_p
   const long long slots = (long long)ctx->num_sms * ctas_per_sm;
   const double total_us = (double)units * P * row_bytes / 5300e3;
   double best_cost = 1e300;
-  for (int ci = 0; ci < 5; ++ci) {
+  // plain launches only: every cluster plan measured slower than the best
+  // plain plan (8B 8K shards of 1-8 KV heads, 1B, Gemma MQA; one B200, step
+  // graphs with programmatic dependent launch), by 1-10 us.  L3P_DECODE_PLAN
+  // still pins cluster plans (the tests exercise every merge path).
+  for (int ci = 0; ci < 1; ++ci) {
     const int cs = 1 << ci;
     if (cs > 1 && (ctx->max_clusters[ci] <= 0 || cs > n_tiles || ctx->GT * ctx->hd / 4 < cs)) continue;
     for (int nc = 1; nc * cs <= kMaxSplits && nc * cs <= n_tiles; ++nc) {
@@ -165,8 +173,15 @@ Plan plan_splits(const PlanLimits* ctx, long long P, long long units, int rows_p
         waves = (units * ns + slots - 1) / slots;
       const double share = (double)((n_tiles + ns - 1) / ns) * rows_per_tile * row_bytes;
       double cost = std::max(total_us, waves * share / 42e3) + waves * 1.0;
-      if (cs > 1) cost += 5.0;  // cluster launch and merge: measured ~5 us slower than plain plans at 64-128 CTAs
-      if (global) cost += 2.2 + gparts * part_bytes / 60e3;
+      if (global) {
+        // merged by `mergers` CTAs that each read a slice of every partial:
+        // designated mergers in a one-wave launch (as launch_decode sets them)
+        const bool one_wave = waves == 1 && cs == 1;
+        const int by_size = std::max(1, (ctx->GT * ctx->hd / 4 + kDecodeThreads - 1) / kDecodeThreads);
+        const int by_parts = gparts >= 48 ? 4 : gparts >= 24 ? 2 : 1;
+        const int mergers = one_wave ? std::min(gparts, std::max(by_size, by_parts)) : 1;
+        cost += 2.2 + gparts * part_bytes / 60e3 / mergers;
+      }
       if (cost < best_cost - 1e-9) {
         best_cost = cost;
         best.nsplit = ns;
@@ -175,6 +190,29 @@ Plan plan_splits(const PlanLimits* ctx, long long P, long long units, int rows_p
     }
   }
   return best;
+}
+
+PlanLimits limits_of(const l3p_attn_ctx* ctx);
+
+// plan_splits costs ~5 us of host time, and the host entry points run it on
+// every call.  Its estimate depends on the attended length only through the
+// number of tiles, so plans are kept per (tiles, units, kernel) in a small
+// cache: a decode step re-plans once every `rows` positions.
+Plan cached_plan(l3p_attn_ctx* ctx, long long P, long long units, const KernelInfo& ki) {
+  const long long n_tiles = (P + ki.rows - 1) / ki.rows;
+  for (auto& e : ctx->plan_cache)
+    if (e.n_tiles == n_tiles && e.units == units && e.rows == ki.rows && e.ctas_per_sm == ki.ctas_per_sm)
+      return Plan{e.nsplit, e.cluster};
+  const PlanLimits lim = limits_of(ctx);
+  const Plan p = plan_splits(&lim, n_tiles * ki.rows, units, ki.rows, ki.ctas_per_sm);
+  auto& e = ctx->plan_cache[ctx->plan_cache_next++ % 4];
+  e.n_tiles = n_tiles;
+  e.units = units;
+  e.rows = ki.rows;
+  e.ctas_per_sm = ki.ctas_per_sm;
+  e.nsplit = p.nsplit;
+  e.cluster = p.cluster;
+  return p;
 }
 
 PlanLimits limits_of(const l3p_attn_ctx* ctx) {
@@ -246,6 +284,22 @@ int read_err(l3p_attn_ctx* ctx) {
   return L3P_OK;
 }
 
+// Stamp buffer of the next traced launch (builds with L3P_DECODE_TRACE; null
+// otherwise, or when the grid has more CTAs than a slot holds).  Slot
+// metadata: trace ordinal, grid x, y, z, layer, position (-1: a wo launch).
+unsigned long long* trace_slot(l3p_attn_ctx* ctx, int gx, int gy, int gz, int layer, int pos) {
+#ifdef L3P_DECODE_TRACE
+  if (ctx->trace_dev && (long long)gx * gy * gz <= kTraceCtas) {
+    const int ts = (int)(ctx->trace_count % kTraceSlots);
+    long long* m = ctx->trace_meta[ts];
+    m[0] = (long long)ctx->trace_count++, m[1] = gx, m[2] = gy, m[3] = gz, m[4] = layer, m[5] = pos;
+    return ctx->trace_dev + (size_t)ts * kTraceCtas * 8;
+  }
+#endif
+  (void)ctx, (void)gx, (void)gy, (void)gz, (void)layer, (void)pos;
+  return nullptr;
+}
+
 // Decode core shared by the single-layer, multi-layer, prefill and partial
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
@@ -259,8 +313,7 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   const long long hi = std::min<long long>(pos_max + 1, (long long)ctx->cfg.seq_begin + ctx->seq_count);
   const long long P = std::max<long long>(hi - lo, 0);
   const long long units = (long long)nz * ctx->kvh_count * ctx->n_hg;
-  const PlanLimits lim = limits_of(ctx);
-  const Plan plan = plan_splits(&lim, P, units, ki.rows, ki.ctas_per_sm);
+  const Plan plan = cached_plan(ctx, P, units, ki);
   // Rows a fused append of an earlier launch may still be storing.  Under
   // programmatic dependent launch every launch of a chain but the newest is
   // resident at once (each has triggered, and none of its CTAs exits before
@@ -324,9 +377,21 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
   a.wait_pos = wait_pos;
   a.merge_k = 1;
   const long long grid_ctas = (long long)plan.nsplit * units;
-  if (plan.cluster == 1 && plan.nsplit >= kMergersFrom && nz <= 65535 &&
-      grid_ctas <= (long long)ctx->num_sms * ki.ctas_per_sm)
+  const bool one_wave = grid_ctas <= (long long)ctx->num_sms * ki.ctas_per_sm;
+  a.trace = trace_slot(ctx, plan.nsplit, ctx->kvh_count * ctx->n_hg, nz, layer0, pos0);
+  if (plan.cluster == 1 && plan.nsplit > 1 && nz <= 65535 && one_wave && !ctx->ticket_merge &&
+      units * plan.nsplit <= ctx->n_counters / kScratchSlots) {
+    // designated mergers (decode_finish): the flags live in the slot's tickets
+    // array; at least enough mergers that each thread merges one float4 of a
+    // slice, and more for many parts (each merger's threads then split the
+    // parts into groups: one L2 round trip per 16 parts and group)
+    a.flags = a.counters;
+    const int by_size = std::max(1, (ctx->GT * ctx->hd / 4 + ki.threads - 1) / ki.threads);
+    const int by_parts = plan.nsplit >= 48 ? 4 : plan.nsplit >= 24 ? 2 : 1;
+    a.merge_k = std::min(plan.nsplit, std::max(by_size, by_parts));
+  } else if (plan.cluster == 1 && plan.nsplit >= kMergersFrom && nz <= 65535 && one_wave) {
     a.merge_k = kMergers;
+  }
 
   for (int z0 = 0; z0 < nz; z0 += 65535) {
     const int zc = std::min(nz - z0, 65535);
@@ -553,6 +618,10 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
   ctx->recent_stores.resize(c.n_layers);
   ctx->kvh_count = kvh_count;
   ctx->seq_count = seq_count;
+  // L3P_DECODE_MERGE=ticket keeps the last-arrival (ticket) merge for one-wave
+  // launches too (tests compare both)
+  if (const char* m = getenv("L3P_DECODE_MERGE"))
+    if (strcmp(m, "ticket") == 0) ctx->ticket_merge = true;
   if (const char* plan = getenv("L3P_DECODE_PLAN")) {
     if (sscanf(plan, "%d:%d", &ctx->force_nsplit, &ctx->force_cluster) < 1) ctx->force_nsplit = 0;
   }
@@ -608,6 +677,15 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
     return bail(L3P_E_CUDA, "error word allocation failed");
   }
   *ctx->err_host = 0;
+#ifdef L3P_DECODE_TRACE
+  {
+    const size_t tb = (size_t)kTraceSlots * kTraceCtas * 8 * sizeof(unsigned long long);
+    if (cudaHostAlloc(&ctx->trace_host, tb, cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(&ctx->trace_dev, ctx->trace_host, 0) != cudaSuccess)
+      return bail(L3P_E_NOMEM, "trace buffer allocation failed");
+    memset(ctx->trace_host, 0, tb);
+  }
+#endif
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess)
     return bail(L3P_E_CUDA, "stream creation failed");
   ctx->own_stream = true;
@@ -694,6 +772,26 @@ L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
   cudaFree(ctx->tp_region);
   if (ctx->hst) cudaFreeHost(ctx->hst);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
+#ifdef L3P_DECODE_TRACE
+  if (ctx->trace_host) {
+    cudaDeviceSynchronize();
+    if (const char* path = getenv("L3P_TRACE_FILE")) {
+      // [n slots][6 meta][kTraceCtas * 8 stamps] as little-endian int64 / uint64
+      if (FILE* f = fopen(path, "wb")) {
+        const long long n = (long long)std::min<unsigned long long>(ctx->trace_count, kTraceSlots);
+        const long long ctas = kTraceCtas;
+        fwrite(&n, 8, 1, f);
+        fwrite(&ctas, 8, 1, f);
+        for (long long i = 0; i < n; ++i) {
+          fwrite(ctx->trace_meta[i], 8, 6, f);
+          fwrite(ctx->trace_host + (size_t)i * kTraceCtas * 8, 8, (size_t)kTraceCtas * 8, f);
+        }
+        fclose(f);
+      }
+    }
+    cudaFreeHost(ctx->trace_host);
+  }
+#endif
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -750,8 +848,7 @@ L3P_API int l3p_attn_decode_plan(l3p_attn_ctx* ctx, int pos, int n_slices, int* 
   if (!ki.fn) return fail(ctx, L3P_E_UNSUPPORTED, "no decode kernel for head_dim %d", ctx->hd);
   const long long hi = std::min<long long>((long long)pos + 1, (long long)ctx->cfg.seq_begin + ctx->seq_count);
   const long long P = std::max<long long>(hi - ctx->cfg.seq_begin, 0);
-  const PlanLimits lim = limits_of(ctx);
-  const Plan plan = plan_splits(&lim, P, (long long)n_slices * ctx->kvh_count * ctx->n_hg, ki.rows, ki.ctas_per_sm);
+  const Plan plan = cached_plan(ctx, P, (long long)n_slices * ctx->kvh_count * ctx->n_hg, ki);
   if (nsplit) *nsplit = plan.nsplit;
   if (cluster) *cluster = plan.cluster;
   return L3P_OK;
@@ -929,7 +1026,10 @@ L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q,
   memcpy(ctx->hst + qd, k, kvd * 4);
   memcpy(ctx->hst + qd + kvd, v, kvd * 4);
   // one host->device copy of all inputs; the kernel writes the output into
-  // mapped pinned memory, so no device->host copy follows
+  // mapped pinned memory, so no device->host copy follows.  (Carrying the 24 KB
+  // of rows in the kernel's launch parameters instead measured 3-4 us per call
+  // slower on B200: a launch with a large parameter block costs more than the
+  // copy it replaces.)
   L3P_CUDA(ctx, cudaMemcpyAsync(ctx->st_buf, ctx->hst, in * 4, cudaMemcpyHostToDevice, ctx->stream));
   if (int rc = launch_decode(ctx, layer, 0, pos, 0, 1, ctx->st_buf, ctx->hst_dev + in, nullptr, nullptr, ctx->stream,
                              ctx->st_buf + qd, ctx->st_buf + qd + kvd))

@@ -22,11 +22,18 @@ L3P_API int l3p_attn_seq_group_export(l3p_attn_ctx* ctx, int n_parts, int part, 
   if (!ctx || !handle) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (n_parts < 2 || n_parts > kXchgMaxParts || part < 0 || part >= n_parts)
     return fail(ctx, L3P_E_INVAL, "sequence group of %d parts (2..%d), part %d", n_parts, kXchgMaxParts, part);
+  if (ctx->kvh_count * ctx->G > kXchgMaxRows)
+    return fail(ctx, L3P_E_UNSUPPORTED, "sequence group members own %d q heads (at most %d)", ctx->kvh_count * ctx->G,
+                kXchgMaxRows);
   DeviceScope dev(ctx->cfg.device);
+  if (ctx->xg_region && ctx->xg_parts != n_parts)
+    return fail(ctx, L3P_E_INVAL, "the sequence group is already set up with %d parts", ctx->xg_parts);
   if (!ctx->xg_region) {
-    // per layer: [n_heads][hd] partial outputs then [n_heads][2] (m, l), padded to 16 bytes
+    // per layer: [n_heads][hd] partial outputs then [n_heads][2] (m, l), padded to 16 bytes;
+    // then the inbox of [2][n_parts] slots of 64-bit packets
     ctx->xg_slot_floats = ((long long)ctx->cfg.n_heads * (ctx->hd + 2) + 3) / 4 * 4;
-    const size_t bytes = kXchgFlagBytes + (size_t)ctx->cfg.n_layers * ctx->xg_slot_floats * sizeof(float);
+    const size_t bytes = kXchgFlagBytes + (size_t)ctx->cfg.n_layers * ctx->xg_slot_floats * sizeof(float) +
+                         2ull * n_parts * ctx->xg_slot_floats * 8;
     if (cudaMalloc(&ctx->xg_region, bytes) != cudaSuccess) {
       cudaGetLastError();
       ctx->xg_region = nullptr;
@@ -74,12 +81,12 @@ L3P_API int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const
                              s, nullptr, nullptr, true))
     return rc;
   XchgArgs a{};
-  for (int p = 0; p < ctx->xg_parts; ++p) {
-    uint8_t* base = static_cast<uint8_t*>(ctx->xg_peer[p]);
-    a.parts[p] = reinterpret_cast<const float*>(base + kXchgFlagBytes) + slot;
-    a.peer_flags[p] = reinterpret_cast<unsigned*>(base);
-  }
-  a.my_flags = reinterpret_cast<unsigned*>(ctx->xg_region);
+  const size_t inbox_off = kXchgFlagBytes + (size_t)ctx->cfg.n_layers * ctx->xg_slot_floats * sizeof(float);
+  for (int p = 0; p < ctx->xg_parts; ++p)
+    a.inbox[p] = reinterpret_cast<unsigned long long*>(static_cast<uint8_t*>(ctx->xg_peer[p]) + inbox_off);
+  a.mine = mine;
+  a.my_step = reinterpret_cast<unsigned*>(ctx->xg_region) + 16;
+  a.slot_floats = ctx->xg_slot_floats;
   a.n_parts = ctx->xg_parts;
   a.part = ctx->xg_part;
   a.hd = ctx->hd;

@@ -46,6 +46,7 @@ int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream
   const int grid = (a.rows + a.rows_per_cta - 1) / a.rows_per_cta;
   if (tp && grid > kTpMaxBlocks)
     return fail(ctx, L3P_E_UNSUPPORTED, "tensor-parallel wo grid of %d CTAs exceeds %d", grid, kTpMaxBlocks);
+  a.trace = trace_slot(ctx, grid, 1, 1, layer, -1);
   cudaLaunchConfig_t lc{};
   lc.gridDim = dim3(grid, 1, 1);
   lc.blockDim = dim3(nw * 32, 1, 1);

@@ -129,9 +129,45 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
-__device__ __forceinline__ void red_add_sys(unsigned* p, unsigned v) {
-  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+
+// Low-latency packets between GPUs: a float and the call number e that wrote
+// it, in one 64-bit word stored and loaded with relaxed system-scope accesses,
+// which cannot tear -- a receiver that reads e in a packet has its value
+// without any fence or flag.
+__device__ __forceinline__ void ll_store(unsigned long long* p, float v, unsigned e) {
+  const unsigned long long w = ((unsigned long long)e << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_load(const unsigned long long* p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
+}
+// Values of packets p[0], p[stride], ... p[(n-1)*stride] once all carry call e
+// (all loads of a poll in flight together); false after kGroupWaitNs.
+template <int MAXN>
+__device__ __forceinline__ bool ll_wait(const unsigned long long* p, long long stride, int n, unsigned e,
+                                        float (&v)[MAXN], int* err) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (true) {
+    unsigned long long w[MAXN];
+#pragma unroll
+    for (int m = 0; m < MAXN; ++m)
+      if (m < n) w[m] = ll_load(p + m * stride);
+    bool all = true;
+#pragma unroll
+    for (int m = 0; m < MAXN; ++m)
+      if (m < n) {
+        all = all && (unsigned)(w[m] >> 32) == e;
+        v[m] = __uint_as_float((unsigned)w[m]);
+      }
+    if (all) return true;
+    if (globaltimer_ns() - t0 > kGroupWaitNs) {
+      *reinterpret_cast<volatile int*>(err) = kErrTimeout;
+      return false;
+    }
+    __nanosleep(20);
+  }
 }
 
 constexpr float kLog2e = 1.4426950408889634f;

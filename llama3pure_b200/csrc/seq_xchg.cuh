@@ -7,113 +7,108 @@
 //
 // Layout of a context's exchange region (one cudaMalloc, exported by CUDA IPC
 // and mapped by every peer of the group):
-//   flags   [kXchgMaxParts] uint32 at byte 0: flags[s] = the last step for
-//           which member s has published its partials (written by member s)
-//   step    uint32 at byte 64: this member's own step counter (only its own
-//           merge kernel reads and writes it)
-//   parts   from byte 256, [n_layers][n_heads*hd + 2*n_heads] float: per layer
-//           the normalised partial output of every q head ([n_heads][hd]),
-//           then its (m, l) pairs ([n_heads][2]), written by this context's
-//           own decode (partial mode)
-// Each decode_seq step: the partial decode of this GPU's positions writes
-// the layer's slot (a normal split-K launch), then seq_merge_kernel (one CTA)
-//   1. (after griddepcontrol.wait: the partials are complete) advances the
-//      step counter and stores the step into flags[me] of every peer -- a
-//      release store at system scope;
-//   2. waits (at most kGroupWaitNs) until every peer's step has arrived in its
-//      own flags, else sets kErrTimeout in the error word and returns;
-//   3. for each owned q head reads the n_parts triples -- its own locally, the
-//      peers' over NVLink -- and writes the log-sum-exp merge to `out`.
+//   header  [0, 256): u32 step counter at byte 64 (this member's calls so far;
+//           only its own merge kernel reads and writes it)
+//   parts   from byte 256, [n_layers][slot_floats] float: per layer the
+//           normalised partial output of every q head ([n_heads][hd]), then
+//           its (m, l) pairs ([n_heads][2]), written by this context's own
+//           decode (partial mode) and read only by its own merge kernel
+//   inbox   after the parts, [2][n_parts][slot_floats] u64 packets: member
+//           s's partial of the current call, sent by member s
+// Each decode_seq step: the partial decode of this GPU's positions writes the
+// layer's part slot (a normal split-K launch), then seq_merge_kernel (one CTA)
+//   1. (after griddepcontrol.wait: the partial is complete) sends the owned
+//      rows of its partial to slot [e&1][me] of every member's inbox, itself
+//      included, e = its step counter + 1;
+//   2. waits (at most kGroupWaitNs, else kErrTimeout) for every member's
+//      packets in its own inbox and writes the log-sum-exp merge, members in
+//      order (the same bits on every member), to `out`;
+//   3. stores e into its step counter.
+// Every value travels as one 64-bit packet (float | e << 32), stored and
+// loaded with relaxed system-scope 64-bit accesses, which cannot tear: a
+// packet that carries e carries its value, so no fence or flag orders
+// anything (a system-scope fence after peer stores measured ~4.6 us on B200).
 // The step counter lives on the device, so a captured CUDA graph replays
-// correctly.  Members run the same sequence of steps; merge kernels of one
-// member never overlap (each decode waits for the merge before it), and a
-// member that is ahead can only be writing a later layer's slot, never one a
-// slower member still reads.
+// correctly.  Members run the same sequence of steps; two inbox slots
+// suffice, since a member cannot finish call e + 1 (and so send call e + 2)
+// before every member has sent call e + 1, which each does only after its own
+// merge of call e.
 #pragma once
 #include "decode.cuh"
 #include "limits.cuh"
 
 namespace l3p {
 
+constexpr int kXchgMaxRows = 128;  // owned q heads of a sequence-group member at most
+
 struct XchgArgs {
-  const float* parts[kXchgMaxParts];    // this layer's slot in every member's region (own included)
-  unsigned* peer_flags[kXchgMaxParts];  // flags array of every member (own included)
-  unsigned* my_flags;                   // this member's flags; its step counter at my_flags + 16
-  int n_parts, part;                    // group size and this member's index
-  int hd, n_heads, row_begin, n_rows;   // owned q heads [row_begin, row_begin + n_rows)
-  float* out;                           // [n_heads][hd]
+  const float* mine;                        // this layer's partial in this member's part slot
+  unsigned long long* inbox[kXchgMaxParts];  // every member's inbox (own included)
+  unsigned* my_step;                        // this member's step counter
+  long long slot_floats;                    // packets of one member's slot
+  int n_parts, part;                        // group size and this member's index
+  int hd, n_heads, row_begin, n_rows;       // owned q heads [row_begin, row_begin + n_rows)
+  float* out;                               // [n_heads][hd]
   int* err;
 };
 
-// grid: ONE CTA of kXchgThreads threads (warp w merges q heads w, w + warps, ...).
+
+// grid: ONE CTA of kXchgThreads threads.
 constexpr int kXchgThreads = 512;
 static __global__ void __launch_bounds__(kXchgThreads) seq_merge_kernel(const XchgArgs a) {
   pdl_launch_dependents();
-  pdl_wait();  // this GPU's partials are written
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) {
-    unsigned* step = a.my_flags + 16;
-    const unsigned e = *step + 1;
-    *step = e;
-    __threadfence_system();  // the partials (written by the kernel before) precede the flags
-    for (int s = 0; s < a.n_parts; ++s)
-      if (s != a.part) st_release_sys(a.peer_flags[s] + a.part, e);
-    int ok = 1;
-    for (int s = 0; s < a.n_parts && ok; ++s) {
-      if (s == a.part) continue;
-      const unsigned long long t0 = globaltimer_ns();
-      // steps only grow: a member already further on has published this step too
-      while ((int)(ld_acquire_sys(a.my_flags + s) - e) < 0) {
-        if (globaltimer_ns() - t0 > kGroupWaitNs) {
-          *reinterpret_cast<volatile int*>(a.err) = kErrTimeout;
-          ok = 0;
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-    s_ok = ok;
-  }
+  pdl_wait();  // this GPU's partial is written
+  __shared__ unsigned s_e;
+  __shared__ float s_m[kXchgMaxParts][kXchgMaxRows], s_l[kXchgMaxParts][kXchgMaxRows];
+  if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned*>(a.my_step) + 1u;
   __syncthreads();
-  if (!s_ok) return;
-
-  // every thread issues all its loads -- (m, l) of its head and its float4
-  // of the output from every member -- before using any, so the merge costs
-  // one NVLink round trip, not one per member or per element
-  const int hd4 = a.hd / 4;
-  for (int idx = threadIdx.x; idx < a.n_rows * hd4; idx += kXchgThreads) {
-    const int h = a.row_begin + idx / hd4;
-    const long long o4 = (long long)h * hd4 + idx % hd4;                   // float4 of the output
-    const long long ml = (long long)a.n_heads * a.hd / 2 + h;              // float2 (m, l) of head h
-    float2 mlp[kXchgMaxParts];
-    float4 op[kXchgMaxParts];
-#pragma unroll
-    for (int p = 0; p < kXchgMaxParts; ++p) {
-      if (p < a.n_parts) {
-        mlp[p] = __ldcv(reinterpret_cast<const float2*>(a.parts[p]) + ml);
-        op[p] = __ldcv(reinterpret_cast<const float4*>(a.parts[p]) + o4);
-      }
-    }
+  const unsigned e = s_e;
+  const long long par = e & 1u;
+  const int N = a.n_parts;
+  const long long ml0 = (long long)a.n_heads * a.hd;  // (m, l) pairs after the outputs
+  const int n_o = a.n_rows * a.hd;
+  // 1. the owned rows of this member's partial to every member's inbox
+  for (int idx = threadIdx.x; idx < n_o + 2 * a.n_rows; idx += kXchgThreads) {
+    const long long src = idx < n_o ? (long long)a.row_begin * a.hd + idx : ml0 + 2ll * a.row_begin + (idx - n_o);
+    const float v = a.mine[src];
+    for (int m = 0; m < N; ++m) ll_store(a.inbox[m] + (par * N + a.part) * a.slot_floats + src, v, e);
+  }
+  // 2. every member's (m, l) of the owned heads
+  const unsigned long long* in = a.inbox[a.part] + par * N * a.slot_floats;
+  bool ok = true;
+  for (int idx = threadIdx.x; idx < N * a.n_rows && ok; idx += kXchgThreads) {
+    const int m = idx / a.n_rows, h = idx % a.n_rows;
+    float v[2];
+    ok = ll_wait<2>(in + m * a.slot_floats + ml0 + 2ll * (a.row_begin + h), 1, 2, e, v, a.err);
+    s_m[m][h] = v[0];
+    s_l[m][h] = v[1];
+  }
+  if (!__syncthreads_and(ok)) return;
+  // 3. the merge of every owned output element, members in order
+  for (int idx = threadIdx.x; idx < n_o && ok; idx += kXchgThreads) {
+    const int h = idx / a.hd;
+    const long long off = (long long)a.row_begin * a.hd + idx;
+    float o[kXchgMaxParts];
+    ok = ll_wait<kXchgMaxParts>(in + off, a.slot_floats, N, e, o, a.err);
+    if (!ok) break;
     float M = -INFINITY;
 #pragma unroll
-    for (int p = 0; p < kXchgMaxParts; ++p)
-      if (p < a.n_parts) M = fmaxf(M, mlp[p].x);
-    float L = 0.f;
-    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int m = 0; m < kXchgMaxParts; ++m)
+      if (m < N) M = fmaxf(M, s_m[m][h]);
+    float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int p = 0; p < kXchgMaxParts; ++p) {
-      if (p < a.n_parts && mlp[p].x != -INFINITY) {  // empty ranges carry m = -inf and weigh nothing
-        const float w = mlp[p].y * fast_exp2(mlp[p].x - M);
+    for (int m = 0; m < kXchgMaxParts; ++m) {
+      if (m < N && s_m[m][h] != -INFINITY) {  // empty ranges carry m = -inf and weigh nothing
+        const float w = s_l[m][h] * fast_exp2(s_m[m][h] - M);
         L += w;
-        O.x = fmaf(op[p].x, w, O.x);
-        O.y = fmaf(op[p].y, w, O.y);
-        O.z = fmaf(op[p].z, w, O.z);
-        O.w = fmaf(op[p].w, w, O.w);
+        O = fmaf(o[m], w, O);
       }
     }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-    reinterpret_cast<float4*>(a.out)[o4] = make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+    a.out[off] = L > 0.f ? O / L : 0.f;
   }
+  // 4. this call is done on this member
+  __syncthreads();
+  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.my_step) = e;
 }
 
 }  // namespace l3p

@@ -63,6 +63,10 @@ struct WoArgs {
   int tp_members, tp_member;
   uint8_t* tp_regions[kXchgMaxParts];  // every member's exchange region (own included)
   int* err;                            // device error word (kErrTimeout)
+  // stage stamps of the tensor-parallel tail (builds with L3P_DECODE_TRACE):
+  // 0 start, 1 after griddepcontrol.wait, 2 GEMV done, 3 partial sent, 4 owner:
+  // the block's sums sent to every member, 5 this block's sums arrived, 6 exit
+  unsigned long long* trace;
 };
 
 // Byte i (0..3) of w as the float 2^23 + byte: exact for every byte.
@@ -244,95 +248,79 @@ struct WoQ6K {
 // covers the same row block j everywhere; block j is owned by member
 // j % n_members.  Call e (1, 2, ... counted by the device step word, read
 // after griddepcontrol.wait, when the previous call's grid has completed):
-//   1. CTA j stores its partial rows into slot [e&1][member] of the owner's
-//      recv array (a peer store unless it owns the block), then one thread
-//      orders them (fence.acq_rel.sys) and adds 1 to the owner's arrivals[j];
-//   2. the owner's CTA j waits (bounded) until arrivals[j] reaches
-//      e * n_members, sums the members' rows in member order -- the same
-//      order, hence the same bits, on every member -- stores the sum into
-//      result[e&1] of every member and adds 1 to each member's done[j];
-//   3. every CTA j waits (bounded) until its done[j] reaches e and copies the
-//      block's summed rows to y;
+//   1. CTA j sends its partial rows to slot [e&1][member] of the owner's recv
+//      array (peer stores unless it owns the block);
+//   2. the owner's CTA j waits (bounded) for every member's rows of the
+//      block, sums them in member order -- the same order, hence the same
+//      bits, on every member -- and sends the sums to result[e&1] of every
+//      member;
+//   3. every CTA j waits (bounded) for its block's sums and copies them to y;
 //   4. the last CTA to leave (exit ticket) writes e into the step word.
-// Per call a member sends its dim partial floats once and the owners send dim
-// summed floats to each member: about 2 * dim * 4 bytes over NVLink per
-// member instead of n_members * dim * 4.  Two slots suffice: a member can be
-// at most one call ahead of another, since finishing a call needs every
-// owner's sum of that call.  A wait that gives up sets kErrTimeout in the
-// error word; the group is then out of step and must be set up anew.
-__device__ __forceinline__ bool tp_wait_at_least(const unsigned* p, unsigned want, int* err) {
-  const unsigned long long t0 = globaltimer_ns();
-  while ((int)(ld_acquire_sys(p) - want) < 0) {
-    if (globaltimer_ns() - t0 > kGroupWaitNs) {
-      *reinterpret_cast<volatile int*>(err) = kErrTimeout;
-      return false;
-    }
-    __nanosleep(32);
-  }
-  return true;
-}
+// Every value travels as one 64-bit packet (float | e << 32), stored and
+// loaded with relaxed system-scope 64-bit accesses, which cannot tear: a
+// receiver that sees e in a packet has its value, so no fence, counter or flag
+// orders anything (a system-scope fence after the peer stores measured ~4.6 us
+// on B200, twice on the critical path).  Per call a member sends its dim
+// partial rows once and the owners send dim sums to each member: 2 * dim * 8
+// bytes per member.  Two slots suffice: a member can be at most one call
+// ahead of another, since finishing a call needs every owner's sums of it.  A
+// wait that gives up sets kErrTimeout; the group is then out of step and must
+// be set up anew.
 
 __device__ __forceinline__ void wo_tp_exchange(const WoArgs& p, const float* red, int r_begin, int r_end) {
   __shared__ unsigned s_e;
-  __shared__ int s_ok;
   const int n = r_end - r_begin;
   const int N = p.tp_members, me = p.tp_member, j = blockIdx.x;
   const int owner = j % N;
   uint8_t* const mine = p.tp_regions[me];
   unsigned* const hdr = reinterpret_cast<unsigned*>(mine);
-  if (threadIdx.x == 0) {
-    s_e = *reinterpret_cast<volatile unsigned*>(hdr + kTpStepWord) + 1u;
-    s_ok = 1;
-  }
+  if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned*>(hdr + kTpStepWord) + 1u;
   __syncthreads();
   const unsigned e = s_e;
-  const size_t par = e & 1u;
+  const long long par = e & 1u;
+  const size_t res_off = tp_result_off(N, p.rows);
+  bool ok = true;
   // 1. this block's partial rows to the owner
-  float* recv = reinterpret_cast<float*>(p.tp_regions[owner] + kTpRecvOff) + (par * N + me) * p.rows;
+  unsigned long long* recv = reinterpret_cast<unsigned long long*>(p.tp_regions[owner] + kTpRecvOff) +
+                             (par * N + me) * p.rows + r_begin;
   for (int r = threadIdx.x; r < n; r += blockDim.x) {
     float s = 0.f;
     for (int c = 0; c < p.wc; ++c) s += red[c * p.rows_per_cta + r];
-    recv[r_begin + r] = s;
+    ll_store(recv + r, s, e);
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    fence_acq_rel_sys();
-    red_add_sys(reinterpret_cast<unsigned*>(p.tp_regions[owner] + kTpArrOff) + j, 1u);
-  }
+  trace_stamp(p.trace, 3);
   // 2. the owner sums the block and sends it to every member
   if (owner == me) {
-    if (threadIdx.x == 0)
-      s_ok = tp_wait_at_least(reinterpret_cast<const unsigned*>(mine + kTpArrOff) + j, e * (unsigned)N, p.err);
-    __syncthreads();
-    if (s_ok) {
-      const float* rv = reinterpret_cast<const float*>(mine + kTpRecvOff) + par * N * p.rows;
-      const size_t res = tp_result_off(N, p.rows);
-      for (int r = threadIdx.x; r < n; r += blockDim.x) {
-        float s = __ldcv(rv + r_begin + r);
-        for (int m = 1; m < N; ++m) s += __ldcv(rv + (size_t)m * p.rows + r_begin + r);
-        for (int m = 0; m < N; ++m) reinterpret_cast<float*>(p.tp_regions[m] + res)[par * p.rows + r_begin + r] = s;
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        fence_acq_rel_sys();
-        for (int m = 0; m < N; ++m) red_add_sys(reinterpret_cast<unsigned*>(p.tp_regions[m] + kTpDoneOff) + j, 1u);
-      }
+    const unsigned long long* rv = reinterpret_cast<const unsigned long long*>(mine + kTpRecvOff) + par * N * p.rows;
+    for (int r = threadIdx.x; r < n && ok; r += blockDim.x) {
+      float v[kXchgMaxParts];
+      ok = ll_wait<kXchgMaxParts>(rv + r_begin + r, p.rows, N, e, v, p.err);
+      if (!ok) break;
+      float s = v[0];
+#pragma unroll
+      for (int m = 1; m < kXchgMaxParts; ++m)  // member order (unrolled: v stays in registers)
+        if (m < N) s += v[m];
+      for (int m = 0; m < N; ++m)
+        ll_store(reinterpret_cast<unsigned long long*>(p.tp_regions[m] + res_off) + par * p.rows + r_begin + r, s, e);
     }
+    trace_stamp(p.trace, 4);
   }
-  // 3. every member: this block's sum into y
-  if (threadIdx.x == 0 && s_ok)
-    s_ok = tp_wait_at_least(reinterpret_cast<const unsigned*>(mine + kTpDoneOff) + j, e, p.err);
-  __syncthreads();
-  if (s_ok) {
-    const float* sum = reinterpret_cast<const float*>(mine + tp_result_off(N, p.rows)) + par * p.rows;
-    for (int r = threadIdx.x; r < n; r += blockDim.x) p.y[r_begin + r] = __ldcv(sum + r_begin + r);
+  // 3. every member: this block's sums into y
+  const unsigned long long* sum = reinterpret_cast<const unsigned long long*>(mine + res_off) + par * p.rows;
+  for (int r = threadIdx.x; r < n && ok; r += blockDim.x) {
+    float v[1];
+    ok = ll_wait<1>(sum + r_begin + r, 0, 1, e, v, p.err);
+    if (ok) p.y[r_begin + r] = v[0];
   }
+  trace_stamp(p.trace, 5);
   // 4. the last CTA to leave advances the step (the next call reads it after
   // this grid has completed)
+  __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(hdr + kTpTicketWord, 1u) == gridDim.x - 1) {
     hdr[kTpTicketWord] = 0u;
     *reinterpret_cast<volatile unsigned*>(hdr + kTpStepWord) = e;
   }
+  trace_stamp(p.trace, 6);
 }
 
 // grid: ceil(rows / rows_per_cta) CTAs of NW warps; dynamic shared memory:
@@ -348,6 +336,7 @@ __global__ void __launch_bounds__(NW * 32) wo_gemv_kernel(const WoArgs p) {
   const int c0 = wcol * F::kSlice;                 // this warp's slice
   const bool active = c0 + F::col(lane, 0) < p.C;  // lanes past the owned columns idle
   const int n_my = r_end - r_begin > wrow ? (r_end - r_begin - wrow + wr - 1) / wr : 0;
+  trace_stamp(p.trace, 0);
 
   // weights first: they do not depend on the kernel before this one
   pdl_launch_dependents();
@@ -356,6 +345,7 @@ __global__ void __launch_bounds__(NW * 32) wo_gemv_kernel(const WoArgs p) {
   for (int u = 0; u < U; ++u)
     if (active && u < n_my) F::load(p, r_begin + wrow + wr * u, c0, raw[u]);
   pdl_wait();
+  trace_stamp(p.trace, 1);
   float x[F::kLaneCols];
   float xs[2];
   // the lane's columns come in runs of 16 consecutive values (x = 0 past C)
@@ -387,6 +377,7 @@ __global__ void __launch_bounds__(NW * 32) wo_gemv_kernel(const WoArgs p) {
     }
   }
   __syncthreads();
+  trace_stamp(p.trace, 2);
   if (p.tp_members == 0) {
     for (int r = threadIdx.x; r < r_end - r_begin; r += blockDim.x) {
       float s = 0.f;

@@ -162,10 +162,14 @@ def test_errors_are_reported_not_fatal():
 @pytest.mark.parametrize("plan", ["1:1", "5:1", "16:1", "16:16", "32:16", "24:8", "8:2", "64:4", "48:1", "79:1",
                                   "128:1"])
 @pytest.mark.parametrize("name", ["llama31_8b_decode_8k", "gemma_2b_decode"])
-def test_every_merge_path(monkeypatch, plan, name):
-    """Pin the split-K decomposition (single CTA, global last-arriver merge,
-    cluster merge, cluster + global merge) and check each against the oracle."""
+@pytest.mark.parametrize("merge", ["designated", "ticket"])
+def test_every_merge_path(monkeypatch, plan, name, merge):
+    """Pin the split-K decomposition (single CTA, global merge by designated
+    mergers or by the last arriver, cluster merge, cluster + global merge) and
+    check each against the oracle."""
     monkeypatch.setenv("L3P_DECODE_PLAN", plan)
+    if merge == "ticket":
+        monkeypatch.setenv("L3P_DECODE_MERGE", "ticket")
     sh = CONFIGS[name].with_(pos=2047, seq_len=2048)
     k, v, q = decode_inputs(sh, 0)
     with AttnContext.for_shape(sh, n_layers=1) as ctx:
@@ -176,11 +180,15 @@ def test_every_merge_path(monkeypatch, plan, name):
 
 
 @pytest.mark.parametrize("plan", ["79:1", "128:1"])
-def test_several_mergers_across_launches(monkeypatch, plan):
-    """One KV head split 79 or 128 ways fits one wave, so the last four parts
-    to finish each merge a quarter of the output; the unit's ticket must be
-    back at zero for every following launch (several positions in a row)."""
+@pytest.mark.parametrize("merge", ["designated", "ticket"])
+def test_several_mergers_across_launches(monkeypatch, plan, merge):
+    """One KV head split 79 or 128 ways fits one wave: designated mergers
+    (two at head_dim 256 with 8 q heads) or the last four parts to finish
+    each merge a slice of the output; the unit's flags or ticket must be back
+    at zero for every following launch (several positions in a row)."""
     monkeypatch.setenv("L3P_DECODE_PLAN", plan)
+    if merge == "ticket":
+        monkeypatch.setenv("L3P_DECODE_MERGE", "ticket")
     sh = CONFIGS["gemma_2b_decode"].with_(pos=2047, seq_len=2048)
     k, v, q = decode_inputs(sh, 0)
     with AttnContext.for_shape(sh, n_layers=1) as ctx:
@@ -244,3 +252,4 @@ def test_overlap_mode_consecutive_layers(use_graph):
     got = out.cpu().numpy()
     for layer in range(n_layers):
         _check(got[layer], wants[layer], f"overlap layer {layer}")
+
