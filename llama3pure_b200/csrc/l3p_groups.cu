@@ -25,7 +25,7 @@ L3P_API int l3p_attn_seq_group_export(l3p_attn_ctx* ctx, int n_parts, int part, 
   if (ctx->kvh_count * ctx->G > kXchgMaxRows)
     return fail(ctx, L3P_E_UNSUPPORTED, "sequence group members own %d q heads (at most %d)", ctx->kvh_count * ctx->G,
                 kXchgMaxRows);
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   if (ctx->xg_region && ctx->xg_parts != n_parts)
     return fail(ctx, L3P_E_INVAL, "the sequence group is already set up with %d parts", ctx->xg_parts);
   if (!ctx->xg_region) {
@@ -51,7 +51,7 @@ L3P_API int l3p_attn_seq_group_export(l3p_attn_ctx* ctx, int n_parts, int part, 
 L3P_API int l3p_attn_seq_group_import(l3p_attn_ctx* ctx, const void* handles) {
   if (!ctx || !handles) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (!ctx->xg_region) return fail(ctx, L3P_E_INVAL, "l3p_attn_seq_group_export has not been called");
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
   for (int p = 0; p < ctx->xg_parts; ++p) {
     if (p == ctx->xg_part) {
@@ -72,7 +72,7 @@ L3P_API int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const
   if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
   if (!ctx->xg_ready) return fail(ctx, L3P_E_INVAL, "sequence group not connected (export, then import)");
   if (int rc = check_aligned(ctx, {q, out})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   cudaStream_t s = pick_stream(ctx, stream);
   const long long slot = (long long)layer * ctx->xg_slot_floats;
   float* mine = reinterpret_cast<float*>(ctx->xg_region + kXchgFlagBytes) + slot;
@@ -96,7 +96,7 @@ L3P_API int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const
   a.out = out;
   a.err = ctx->err_dev;
   cudaLaunchConfig_t lc{};
-  lc.gridDim = dim3(1, 1, 1);
+  lc.gridDim = dim3((a.n_rows * a.hd + kXchgThreads - 1) / kXchgThreads, 1, 1);
   lc.blockDim = dim3(kXchgThreads, 1, 1);
   lc.stream = s;
   cudaLaunchAttribute attr[1];
@@ -116,7 +116,7 @@ L3P_API int l3p_attn_tp_group_export(l3p_attn_ctx* ctx, int n_members, int membe
   if (n_members < 2 || n_members > kXchgMaxParts || member < 0 || member >= n_members || dim <= 0 || dim % 4)
     return fail(ctx, L3P_E_INVAL, "tensor-parallel group of %d members (2..%d), member %d, dim %d (multiple of 4)",
                 n_members, kXchgMaxParts, member, dim);
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   if (ctx->tp_region && (ctx->tp_members != n_members || ctx->tp_dim != dim))
     return fail(ctx, L3P_E_INVAL, "the tensor-parallel group is already set up with another shape");
   if (!ctx->tp_region) {
@@ -139,7 +139,7 @@ L3P_API int l3p_attn_tp_group_export(l3p_attn_ctx* ctx, int n_members, int membe
 L3P_API int l3p_attn_tp_group_import(l3p_attn_ctx* ctx, const void* handles) {
   if (!ctx || !handles) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (!ctx->tp_region) return fail(ctx, L3P_E_INVAL, "l3p_attn_tp_group_export has not been called");
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
   for (int p = 0; p < ctx->tp_members; ++p) {
     if (p == ctx->tp_member) {
@@ -161,7 +161,7 @@ L3P_API int l3p_attn_wo_allreduce_dev(l3p_attn_ctx* ctx, int layer, const float*
     return fail(ctx, L3P_E_INVAL, "wo of layer %d has %d rows, the group was set up for %d", layer,
                 ctx->wo[layer].rows, ctx->tp_dim);
   if (int rc = check_aligned(ctx, {x, xout})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   cudaStream_t s = pick_stream(ctx, stream);
   // one launch: the GEMV and, in its tail, the sum over the group
   return launch_wo(ctx, layer, x, xout, s, true);

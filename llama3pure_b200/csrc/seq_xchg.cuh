@@ -8,7 +8,8 @@
 // Layout of a context's exchange region (one cudaMalloc, exported by CUDA IPC
 // and mapped by every peer of the group):
 //   header  [0, 256): u32 step counter at byte 64 (this member's calls so far;
-//           only its own merge kernel reads and writes it)
+//           only its own merge kernel reads and writes it), u32 exit ticket of
+//           the merge kernel's CTAs at byte 68
 //   parts   from byte 256, [n_layers][slot_floats] float: per layer the
 //           normalised partial output of every q head ([n_heads][hd]), then
 //           its (m, l) pairs ([n_heads][2]), written by this context's own
@@ -16,14 +17,15 @@
 //   inbox   after the parts, [2][n_parts][slot_floats] u64 packets: member
 //           s's partial of the current call, sent by member s
 // Each decode_seq step: the partial decode of this GPU's positions writes the
-// layer's part slot (a normal split-K launch), then seq_merge_kernel (one CTA)
+// layer's part slot (a normal split-K launch), then seq_merge_kernel (one
+// thread per owned output element)
 //   1. (after griddepcontrol.wait: the partial is complete) sends the owned
 //      rows of its partial to slot [e&1][me] of every member's inbox, itself
 //      included, e = its step counter + 1;
 //   2. waits (at most kGroupWaitNs, else kErrTimeout) for every member's
 //      packets in its own inbox and writes the log-sum-exp merge, members in
 //      order (the same bits on every member), to `out`;
-//   3. stores e into its step counter.
+//   3. the last CTA to finish stores e into its step counter.
 // Every value travels as one 64-bit packet (float | e << 32), stored and
 // loaded with relaxed system-scope 64-bit accesses, which cannot tear: a
 // packet that carries e carries its value, so no fence or flag orders
@@ -53,13 +55,17 @@ struct XchgArgs {
 };
 
 
-// grid: ONE CTA of kXchgThreads threads.
+// grid: ceil(n_rows * hd / kXchgThreads) CTAs of kXchgThreads threads; CTA c
+// sends and merges output elements [c * kXchgThreads, (c + 1) * kXchgThreads)
+// of the owned rows, one per thread (a thread's packet polls then overlap no
+// other of its own), and CTA 0 also sends the (m, l) pairs.
 constexpr int kXchgThreads = 512;
 static __global__ void __launch_bounds__(kXchgThreads) seq_merge_kernel(const XchgArgs a) {
   pdl_launch_dependents();
   pdl_wait();  // this GPU's partial is written
   __shared__ unsigned s_e;
-  __shared__ float s_m[kXchgMaxParts][kXchgMaxRows], s_l[kXchgMaxParts][kXchgMaxRows];
+  constexpr int kHeads = kXchgThreads / 64 + 1;  // owned heads a CTA's elements touch (head_dim >= 64)
+  __shared__ float s_m[kXchgMaxParts][kHeads], s_l[kXchgMaxParts][kHeads];
   if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned*>(a.my_step) + 1u;
   __syncthreads();
   const unsigned e = s_e;
@@ -67,48 +73,61 @@ static __global__ void __launch_bounds__(kXchgThreads) seq_merge_kernel(const Xc
   const int N = a.n_parts;
   const long long ml0 = (long long)a.n_heads * a.hd;  // (m, l) pairs after the outputs
   const int n_o = a.n_rows * a.hd;
-  // 1. the owned rows of this member's partial to every member's inbox
-  for (int idx = threadIdx.x; idx < n_o + 2 * a.n_rows; idx += kXchgThreads) {
-    const long long src = idx < n_o ? (long long)a.row_begin * a.hd + idx : ml0 + 2ll * a.row_begin + (idx - n_o);
+  const int idx = blockIdx.x * kXchgThreads + threadIdx.x;  // this thread's output element
+  const int h_first = blockIdx.x * kXchgThreads / a.hd;     // first owned head of this CTA
+  // 1. this member's partial to every member's inbox (itself included)
+  if (idx < n_o) {
+    const long long src = (long long)a.row_begin * a.hd + idx;
     const float v = a.mine[src];
     for (int m = 0; m < N; ++m) ll_store(a.inbox[m] + (par * N + a.part) * a.slot_floats + src, v, e);
   }
-  // 2. every member's (m, l) of the owned heads
+  if (blockIdx.x == 0)
+    for (int t = threadIdx.x; t < 2 * a.n_rows; t += kXchgThreads) {
+      const long long src = ml0 + 2ll * a.row_begin + t;
+      const float v = a.mine[src];
+      for (int m = 0; m < N; ++m) ll_store(a.inbox[m] + (par * N + a.part) * a.slot_floats + src, v, e);
+    }
+  // 2. every member's (m, l) of the heads this CTA merges
   const unsigned long long* in = a.inbox[a.part] + par * N * a.slot_floats;
+  const int h_count = min(kHeads, a.n_rows - h_first);
   bool ok = true;
-  for (int idx = threadIdx.x; idx < N * a.n_rows && ok; idx += kXchgThreads) {
-    const int m = idx / a.n_rows, h = idx % a.n_rows;
+  if (threadIdx.x < N * h_count) {
+    const int m = threadIdx.x / h_count, hh = threadIdx.x % h_count;
     float v[2];
-    ok = ll_wait<2>(in + m * a.slot_floats + ml0 + 2ll * (a.row_begin + h), 1, 2, e, v, a.err);
-    s_m[m][h] = v[0];
-    s_l[m][h] = v[1];
+    ok = ll_wait<2>(in + m * a.slot_floats + ml0 + 2ll * (a.row_begin + h_first + hh), 1, 2, e, v, a.err);
+    s_m[m][hh] = v[0];
+    s_l[m][hh] = v[1];
   }
-  if (!__syncthreads_and(ok)) return;
-  // 3. the merge of every owned output element, members in order
-  for (int idx = threadIdx.x; idx < n_o && ok; idx += kXchgThreads) {
-    const int h = idx / a.hd;
+  ok = __syncthreads_and(ok);
+  // 3. this thread's output element, members in order (the same bits on every member)
+  if (ok && idx < n_o) {
+    const int hh = idx / a.hd - h_first;
     const long long off = (long long)a.row_begin * a.hd + idx;
     float o[kXchgMaxParts];
-    ok = ll_wait<kXchgMaxParts>(in + off, a.slot_floats, N, e, o, a.err);
-    if (!ok) break;
-    float M = -INFINITY;
+    if (ll_wait<kXchgMaxParts>(in + off, a.slot_floats, N, e, o, a.err)) {
+      float M = -INFINITY;
 #pragma unroll
-    for (int m = 0; m < kXchgMaxParts; ++m)
-      if (m < N) M = fmaxf(M, s_m[m][h]);
-    float L = 0.f, O = 0.f;
+      for (int m = 0; m < kXchgMaxParts; ++m)
+        if (m < N) M = fmaxf(M, s_m[m][hh]);
+      float L = 0.f, O = 0.f;
 #pragma unroll
-    for (int m = 0; m < kXchgMaxParts; ++m) {
-      if (m < N && s_m[m][h] != -INFINITY) {  // empty ranges carry m = -inf and weigh nothing
-        const float w = s_l[m][h] * fast_exp2(s_m[m][h] - M);
-        L += w;
-        O = fmaf(o[m], w, O);
+      for (int m = 0; m < kXchgMaxParts; ++m) {
+        if (m < N && s_m[m][hh] != -INFINITY) {  // empty ranges carry m = -inf and weigh nothing
+          const float w = s_l[m][hh] * fast_exp2(s_m[m][hh] - M);
+          L += w;
+          O = fmaf(o[m], w, O);
+        }
       }
+      a.out[off] = L > 0.f ? O / L : 0.f;
     }
-    a.out[off] = L > 0.f ? O / L : 0.f;
   }
-  // 4. this call is done on this member
+  // 4. the last CTA to leave ends this call on this member (the next call
+  // reads the step after this grid has completed)
   __syncthreads();
-  if (threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.my_step) = e;
+  if (threadIdx.x == 0 && atomicAdd(a.my_step + 1, 1u) == gridDim.x - 1) {
+    a.my_step[1] = 0u;
+    *reinterpret_cast<volatile unsigned*>(a.my_step) = e;
+  }
 }
 
 }  // namespace l3p
