@@ -191,6 +191,24 @@ int l3p_attn_kv_device_ptr(l3p_attn_ctx* ctx, int layer, float** k, float** v);
  * the reference. */
 int l3p_attn_set_overlap(l3p_attn_ctx* ctx, int enable);
 
+/* Host-call server (fp32 caches, the whole sequence on the context): with
+ * enable != 0, l3p_attn_step and l3p_attn_decode no longer launch a kernel,
+ * copy and synchronise per call.  A decode grid stays resident on the
+ * context's stream; a call writes its rows into a mailbox in mapped pinned
+ * memory, and the grid fetches them, appends, decodes and writes the output
+ * back as packets the call polls.  Same arithmetic and results as the
+ * launched path with the same split-K.  The resident grid holds every SM, so:
+ *   - every other entry point of the context first ends it and waits for it
+ *     to leave (the next host call starts it again);
+ *   - it leaves by itself after `idle_us` microseconds without a call
+ *     (0: 20000), and the next call starts it again;
+ *   - work of other contexts or libraries on the same GPU waits until it
+ *     leaves: enable it only where this context has the GPU to itself.
+ * enable == 0 ends it.  L3P_E_UNSUPPORTED for a Q8_0 cache or a sequence
+ * shard.  No counterpart in the reference, whose attention runs in the
+ * calling thread. */
+int l3p_attn_set_host_server(l3p_attn_ctx* ctx, int enable, long long idle_us);
+
 /* Number of kernels this library has launched since the context was created
  * (the benchmark reports it per step).  No counterpart in the reference. */
 long long l3p_attn_launch_count(const l3p_attn_ctx* ctx);

@@ -54,6 +54,7 @@ EXPORTS = (
     "l3p_attn_launch_count",
     "l3p_attn_device_arch",
     "l3p_attn_set_overlap",
+    "l3p_attn_set_host_server",
     "l3p_attn_decode_plan",
     "l3p_attn_set_rope",
     "l3p_attn_rope_dev",
@@ -157,6 +158,7 @@ def load_library(path: str = LIB_PATH):
         "l3p_attn_launch_count": (C.c_longlong, [vp]),
         "l3p_attn_device_arch": (i, [i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "l3p_attn_set_overlap": (i, [vp, i]),
+        "l3p_attn_set_host_server": (i, [vp, i, C.c_longlong]),
         "l3p_attn_decode_plan": (i, [vp, i, i, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
         "l3p_attn_set_rope": (i, [vp, C.POINTER(RopeConfig)]),
         "l3p_attn_rope_dev": (i, [vp, i, i, i, fp, fp, fp, fp, vp]),
@@ -298,6 +300,11 @@ class AttnContext:
     def set_overlap(self, enable: bool) -> None:
         """Programmatic dependent launch for decode (see l3p_attn_set_overlap)."""
         self._ok(self.lib.l3p_attn_set_overlap(self.h, int(bool(enable))), "set_overlap")
+
+    def set_host_server(self, enable: bool, idle_us: int = 0) -> None:
+        """Serve step()/decode() through a resident grid (see
+        l3p_attn_set_host_server)."""
+        self._ok(self.lib.l3p_attn_set_host_server(self.h, int(bool(enable)), int(idle_us)), "set_host_server")
 
     def launch_count(self) -> int:
         return int(self.lib.l3p_attn_launch_count(self.h))

@@ -17,6 +17,10 @@
 
 #define L3P_API extern "C" __attribute__((visibility("default")))
 
+namespace l3p {
+struct DecodeArgs;
+}
+
 struct l3p_attn_ctx {
   l3p_attn_config cfg{};
   int hd = 0, G = 0, GT = 1, n_hg = 1;
@@ -122,10 +126,31 @@ struct l3p_attn_ctx {
   unsigned long long* trace_dev = nullptr;
   long long trace_meta[64][6] = {};  // launch seq, grid x, y, z, layer0, pos0
   unsigned long long trace_count = 0;
+  // host-call server (l3p_attn_set_host_server, l3p_server.cu): a resident
+  // decode grid on `stream` that takes the single-token host calls through a
+  // mailbox in mapped pinned memory (server.cuh)
+  bool srv_on = false;       // the host calls go through the server
+  bool srv_running = false;  // an instance may be resident on `stream`
+  unsigned srv_next = 1;     // number of the next call (never 0)
+  unsigned srv_instance = 0;
+  unsigned long long srv_idle_ns = 0;
+  int srv_nsplit = 0;        // split-K of the running instance
+  unsigned long long* srv_stage = nullptr;  // pinned: the packets of the next call's inbox copy
+  cudaStream_t srv_copy = nullptr;           // the inbox copies
+  uint8_t* srv_outbox = nullptr;             // mapped pinned: output floats, then the mergers' flags
+  uint8_t* srv_outbox_dev = nullptr;
+  uint8_t* srv_dev = nullptr;  // device: inbox, q copies, go words, descriptors, flags
+  long long srv_restarts = 0;       // instances launched
+  long long srv_last_ns = 0;        // steady-clock time the last served call ended
   std::string last_error;
 };
 
 namespace l3p_api {
+
+#ifdef L3P_DECODE_TRACE
+constexpr int kTraceSlots = 64;    // decode launches whose stamps are kept
+constexpr int kTraceCtas = 4096;   // CTAs per traced launch at most
+#endif
 
 // Records the message of a failing entry point and returns its code.
 inline int fail(l3p_attn_ctx* ctx, int code, const char* fmt, ...) {
@@ -161,6 +186,22 @@ struct DeviceScope {
   }
 };
 
+// l3p_server.cu: ends the context's host-call server instance, if one is
+// resident, and waits for it to leave the GPU.
+int stop_server(l3p_attn_ctx* ctx);
+// l3p_server.cu: one l3p_attn_step (k, v non-null) or l3p_attn_decode call
+// through the server, which it starts when none is resident.
+int server_call(l3p_attn_ctx* ctx, int layer, int pos, const float* q, const float* k, const float* v, float* out);
+
+// DeviceScope for the entry points that launch work or touch the context's
+// memory: a resident host-call server would hold every SM, so it is stopped
+// first (the next host call starts it again).
+struct CtxScope : DeviceScope {
+  explicit CtxScope(l3p_attn_ctx* ctx) : DeviceScope(ctx->cfg.device) {
+    if (ctx->srv_running) stop_server(ctx);
+  }
+};
+
 inline cudaStream_t pick_stream(l3p_attn_ctx* ctx, void* s) { return s ? static_cast<cudaStream_t>(s) : ctx->stream; }
 
 // With overlap mode, a launch may start while the kernel before it on the
@@ -193,6 +234,18 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
 int launch_append(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok, const float* k, const float* v, cudaStream_t s);
 int launch_prefill_tc(l3p_attn_ctx* ctx, int layer, int start_pos, int n_tok, const float* q, float* out,
                       cudaStream_t s);
+
+// Decode geometry of the host-call server for a call at `pos`: the plan's
+// split-K (clamped so that the grid is resident at once), the designated
+// mergers, and the kernel (null when the context's cache has no server).
+struct ServerGeom {
+  int nsplit = 1, merge_k = 1, units = 0, threads = 0, smem = 0;
+  const void* fn = nullptr;
+};
+int server_geom(l3p_attn_ctx* ctx, int pos, ServerGeom* g);
+// The context's fields of a decode launch: cache, strides, geometry, scale,
+// error word (everything but the call's layer, position, q, outputs and plan).
+void decode_common_args(const l3p_attn_ctx* ctx, l3p::DecodeArgs* a);
 
 // l3p_preattn.cu
 int check_rope(l3p_attn_ctx* ctx);

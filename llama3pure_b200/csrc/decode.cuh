@@ -138,6 +138,10 @@ struct DecodeArgs {
   // scheme): flags[unit * nsplit + part] = number of mergers still to read
   // part's partial; parts [0, merge_k) merge, each 1/merge_k of the output
   unsigned* flags;
+  // host-call server (server.cuh): a nonzero flag_tag makes every part store
+  // the tag (the call number) as its flag instead of a count, and mergers wait
+  // for the tag, so nothing returns the flags to 0
+  unsigned flag_tag;
 };
 
 // Decode trace, compiled in only with -DL3P_DECODE_TRACE (a separate build for
@@ -477,7 +481,7 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
     unsigned* const fl = a.flags + (long long)unit * n_parts;
     if (threadIdx.x == 0) {
       fence_acq_rel_gpu();  // the partial (all threads' stores, ordered by the barrier) before the flag
-      st_relaxed_gpu(fl + part, (unsigned)a.merge_k);
+      st_relaxed_gpu(fl + part, a.flag_tag ? a.flag_tag : (unsigned)a.merge_k);
     }
     trace_stamp(a.trace, 4);
     if (part >= a.merge_k) {
@@ -487,7 +491,7 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
     bool arrived = true;
     const unsigned long long t0 = globaltimer_ns();
     for (int sp = threadIdx.x; sp < n_parts && arrived; sp += T)
-      while (ld_acquire_gpu(fl + sp) == 0u) {
+      while (a.flag_tag ? ld_acquire_gpu(fl + sp) != a.flag_tag : ld_acquire_gpu(fl + sp) == 0u) {
         if (globaltimer_ns() - t0 > kGroupWaitNs) {
           *reinterpret_cast<volatile int*>(a.err) = kErrTimeout;
           arrived = false;
@@ -620,6 +624,10 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
     }
   }
   if (flag_merge) {
+    if (a.flag_tag) {  // tagged flags are never reset
+      trace_stamp(a.trace, 5);
+      return;
+    }
     __syncthreads();  // every thread's reads of the partials are done
     for (int sp = threadIdx.x; sp < n_parts; sp += T) red_add_gpu(a.flags + (long long)unit * n_parts + sp, 0xffffffffu);
     trace_stamp(a.trace, 5);
@@ -637,11 +645,11 @@ __device__ __forceinline__ void decode_finish(const DecodeArgs& a, DecodeMergeSm
   trace_stamp(a.trace, 5);
 }
 
+// One CTA's share of a decode launch: the body of decode_f32_kernel, also run
+// once per call by the host-call server (server.cuh) over the same grid.
 template <int HD, int GT>
-__global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>::kCtasPerSm)
-    decode_f32_kernel(const DecodeArgs a) {
+__device__ __forceinline__ void decode_f32_cta(const DecodeArgs& a, unsigned char* smem_raw) {
   using C = DecodeCfg<HD, GT>;
-  extern __shared__ __align__(128) unsigned char smem_raw[];
   float* ring = reinterpret_cast<float*>(smem_raw);
   __shared__ DecodeMergeSmem<GT, C::kWarps> ms;
   float (&s_m)[C::kWarps][GT] = ms.m;
@@ -949,6 +957,13 @@ __global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>
     s_l[warp][lane >> C::kSH] = my_l;
   }
   decode_finish<HD, GT, C::kWarps, C::kThreads>(a, ms, ring, acc, warp, lane, split, unit, z, h0);
+}
+
+template <int HD, int GT>
+__global__ void __launch_bounds__(DecodeCfg<HD, GT>::kThreads, DecodeCfg<HD, GT>::kCtasPerSm)
+    decode_f32_kernel(const DecodeArgs a) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  decode_f32_cta<HD, GT>(a, smem_raw);
 }
 
 // Token K/V rows -> head-major cache rows.  k, v: [n_tok][src_stride] with

@@ -22,6 +22,7 @@
 #include "decode.cuh"
 #include "decode_q8.cuh"
 #include "prefill_tc.cuh"
+#include "server.cuh"
 
 using namespace l3p;
 using namespace l3p_api;
@@ -30,12 +31,7 @@ using namespace l3p_api;
 namespace l3p_api {
 
 constexpr long long kWsOFloats = 8ll << 20;  // 32 MiB of split partials
-#ifdef L3P_DECODE_TRACE
-constexpr int kTraceSlots = 64;    // decode launches whose stamps are kept
-constexpr int kTraceCtas = 4096;   // CTAs per traced launch at most
-#endif
 constexpr long long kCounters = 1 << 16;
-constexpr int kScratchSlots = 4;
 // Global-stage mergers of a one-wave launch (DecodeArgs::merge_k) when a unit
 // has at least kMergersFrom parts: measured on the 8B 8K shards, 79 parts
 // (one KV head per GPU) merge 0.8 us faster per layer with 4 mergers, while at
@@ -59,8 +55,11 @@ int decode_smem() {
   return DecodeCfg<HD, GT>::kSmemBytes;
 }
 
+using ServerFn = void (*)(const DecodeArgs, const ServerArgs);
+
 struct KernelInfo {
   DecodeFn fn = nullptr;
+  ServerFn srv = nullptr;  // the host-call server over this kernel's body (fp32 caches)
   int threads = kDecodeThreads;
   int smem = 0;
   int rows = 8;
@@ -88,6 +87,7 @@ KernelInfo kernel_for(int hd, int gt, bool q8 = false) {
 #define L3P_CASE(H, T)                                        \
   if (hd == H && gt == T) {                                   \
     k.fn = decode_fn<H, T>();                                 \
+    k.srv = decode_server_kernel<H, T>;                       \
     k.smem = decode_smem<H, T>();                             \
     k.rows = DecodeCfg<H, T>::kR;                             \
     k.ctas_per_sm = DecodeCfg<H, T>::kCtasPerSm;              \
@@ -300,6 +300,68 @@ unsigned long long* trace_slot(l3p_attn_ctx* ctx, int gx, int gy, int gz, int la
   return nullptr;
 }
 
+void decode_common_args(const l3p_attn_ctx* ctx, DecodeArgs* a) {
+  a->kc = ctx->kc;
+  a->vc = ctx->vc;
+  a->kc_w = ctx->kc;
+  a->k8 = ctx->k8;
+  a->v8 = ctx->v8;
+  a->ksc = ctx->ksc;
+  a->vsc = ctx->vsc;
+  a->new_zstride = (long long)ctx->cfg.n_kv_heads * ctx->hd;
+  a->layer_stride = ctx->layer_elems;
+  a->head_stride = ctx->head_elems;
+  a->q_zstride = (long long)ctx->cfg.n_heads * ctx->hd;
+  a->ml_zstride = 2ll * ctx->cfg.n_heads;
+  a->err = ctx->err_dev;
+  a->scale = ctx->scale;
+  a->seq_begin = ctx->cfg.seq_begin;
+  a->cap = ctx->seq_count;
+  a->kv_head_begin = ctx->cfg.kv_head_begin;
+  a->G = ctx->G;
+  a->n_hg = ctx->n_hg;
+  a->is_gemma3 = ctx->cfg.is_gemma3;
+  a->swa_window = ctx->cfg.swa_window;
+  a->swa_pattern = ctx->cfg.swa_pattern;
+  a->layer_step = 0;
+  a->pos_step = 0;
+  a->wait_pos = INT_MAX;
+  a->merge_k = 1;
+  a->cluster = 1;
+}
+
+// Designated mergers of a one-wave launch without clusters: at least enough
+// that each thread merges one float4 of a slice, and more for many parts
+// (each merger's threads then split the parts into groups: one L2 round trip
+// per 16 parts and group).
+int designated_mergers(const l3p_attn_ctx* ctx, int nsplit, int threads) {
+  const int by_size = std::max(1, (ctx->GT * ctx->hd / 4 + threads - 1) / threads);
+  const int by_parts = nsplit >= 48 ? 4 : nsplit >= 24 ? 2 : 1;
+  return std::min(nsplit, std::max(by_size, by_parts));
+}
+
+int server_geom(l3p_attn_ctx* ctx, int pos, ServerGeom* g) {
+  const KernelInfo ki = kernel_for(ctx->hd, ctx->GT, ctx->q8);
+  if (!ki.srv) return fail(ctx, L3P_E_UNSUPPORTED, "the host-call server serves fp32 caches only");
+  const long long lo = ctx->cfg.seq_begin;
+  const long long hi = std::min<long long>((long long)pos + 1, lo + ctx->seq_count);
+  const long long P = std::max<long long>(hi - lo, 0);
+  const long long units = (long long)ctx->kvh_count * ctx->n_hg;
+  const long long slots = (long long)ctx->num_sms * ki.ctas_per_sm;
+  if (units > slots) return fail(ctx, L3P_E_UNSUPPORTED, "%lld decode units do not fit on the GPU at once", units);
+  // the plan of a decode launch, without clusters, and no more parts than
+  // leave the whole grid resident (the server's CTAs wait for one another)
+  const Plan p = cached_plan(ctx, P, units, ki);
+  int ns = std::max(1, std::min<int>(p.nsplit, (int)(slots / units)));
+  g->nsplit = ns;
+  g->merge_k = ns > 1 ? designated_mergers(ctx, ns, ki.threads) : 1;
+  g->units = (int)units;
+  g->threads = ki.threads;
+  g->smem = ki.smem;
+  g->fn = reinterpret_cast<const void*>(ki.srv);
+  return L3P_OK;
+}
+
 // Decode core shared by the single-layer, multi-layer, prefill and partial
 // entry points.  z-slices are layers (layer_step=1) or tokens (pos_step=1).
 int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int pos_step, int nz,
@@ -334,48 +396,26 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
     for (int z = 0; z < nz; ++z) ctx->recent_stores[layer0 + z * layer_step].emplace_back(seq, pos0 + z * pos_step);
 
   DecodeArgs a{};
-  a.kc = ctx->kc;
-  a.vc = ctx->vc;
-  a.kc_w = ctx->kc;
-  a.k8 = ctx->k8;
-  a.v8 = ctx->v8;
-  a.ksc = ctx->ksc;
-  a.vsc = ctx->vsc;
+  decode_common_args(ctx, &a);
   a.k_new = k_new;
   a.v_new = v_new;
-  a.new_zstride = (long long)ctx->cfg.n_kv_heads * ctx->hd;
-  a.layer_stride = ctx->layer_elems;
-  a.head_stride = ctx->head_elems;
   a.q = q;
-  a.q_zstride = (long long)ctx->cfg.n_heads * ctx->hd;
   a.out = out;
   a.part_o = part_o;
   a.part_ml = part_ml;
-  a.ml_zstride = 2ll * ctx->cfg.n_heads;
   a.ws_o = ctx->ws_o + slot * (ctx->ws_o_floats / kScratchSlots);
   a.ws_ml = ctx->ws_ml + slot * (ctx->ws_ml_floats / kScratchSlots);
   a.counters = ctx->counters + slot * (ctx->n_counters / kScratchSlots);
-  a.err = ctx->err_dev;
-  a.scale = ctx->scale;
   a.layer0 = layer0;
   a.layer_step = layer_step;
   a.pos0 = pos0;
   a.pos_step = pos_step;
-  a.seq_begin = ctx->cfg.seq_begin;
-  a.cap = ctx->seq_count;
-  a.kv_head_begin = ctx->cfg.kv_head_begin;
-  a.G = ctx->G;
-  a.n_hg = ctx->n_hg;
   a.nsplit = plan.nsplit;
   a.cluster = plan.cluster;
-  a.is_gemma3 = ctx->cfg.is_gemma3;
-  a.swa_window = ctx->cfg.swa_window;
-  a.swa_pattern = ctx->cfg.swa_pattern;
   a.partial = part_o != nullptr;
   // several mergers for the global stage when every CTA of the launch is
   // resident at once (a merger waits for its unit's last part)
   a.wait_pos = wait_pos;
-  a.merge_k = 1;
   const long long grid_ctas = (long long)plan.nsplit * units;
   const bool one_wave = grid_ctas <= (long long)ctx->num_sms * ki.ctas_per_sm;
   a.trace = trace_slot(ctx, plan.nsplit, ctx->kvh_count * ctx->n_hg, nz, layer0, pos0);
@@ -386,9 +426,7 @@ int launch_decode(l3p_attn_ctx* ctx, int layer0, int layer_step, int pos0, int p
     // slice, and more for many parts (each merger's threads then split the
     // parts into groups: one L2 round trip per 16 parts and group)
     a.flags = a.counters;
-    const int by_size = std::max(1, (ctx->GT * ctx->hd / 4 + ki.threads - 1) / ki.threads);
-    const int by_parts = plan.nsplit >= 48 ? 4 : plan.nsplit >= 24 ? 2 : 1;
-    a.merge_k = std::min(plan.nsplit, std::max(by_size, by_parts));
+    a.merge_k = designated_mergers(ctx, plan.nsplit, ki.threads);
   } else if (plan.cluster == 1 && plan.nsplit >= kMergersFrom && nz <= 65535 && one_wave) {
     a.merge_k = kMergers;
   }
@@ -742,7 +780,7 @@ L3P_API int l3p_attn_create(const l3p_attn_config* cfg, l3p_attn_ctx** out) {
 
 L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
   if (!ctx) return;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   cudaFree(ctx->kc);
   cudaFree(ctx->vc);
@@ -771,6 +809,10 @@ L3P_API void l3p_attn_destroy(l3p_attn_ctx* ctx) {
     if (p != ctx->tp_member && ctx->tp_peer[p]) cudaIpcCloseMemHandle(ctx->tp_peer[p]);
   cudaFree(ctx->tp_region);
   if (ctx->hst) cudaFreeHost(ctx->hst);
+  if (ctx->srv_outbox) cudaFreeHost(ctx->srv_outbox);
+  if (ctx->srv_stage) cudaFreeHost(ctx->srv_stage);
+  if (ctx->srv_copy) cudaStreamDestroy(ctx->srv_copy);
+  cudaFree(ctx->srv_dev);
   if (ctx->err_host) cudaFreeHost(ctx->err_host);
 #ifdef L3P_DECODE_TRACE
   if (ctx->trace_host) {
@@ -802,7 +844,7 @@ L3P_API const char* l3p_attn_last_error(const l3p_attn_ctx* ctx) {
 
 L3P_API int l3p_attn_check(l3p_attn_ctx* ctx) {
   if (!ctx) return L3P_E_INVAL;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
   L3P_CUDA(ctx, cudaDeviceSynchronize());
   return read_err(ctx);
@@ -810,7 +852,7 @@ L3P_API int l3p_attn_check(l3p_attn_ctx* ctx) {
 
 L3P_API int l3p_attn_set_stream(l3p_attn_ctx* ctx, void* stream) {
   if (!ctx) return L3P_E_INVAL;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
   ctx->own_stream = false;
   ctx->stream = static_cast<cudaStream_t>(stream);
@@ -863,7 +905,7 @@ L3P_API int l3p_attn_kv_append_dev(l3p_attn_ctx* ctx, int layer, int pos, const 
   if (int rc = check_layer(ctx, layer)) return rc;
   if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
   if (int rc = check_aligned(ctx, {k, v})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   return launch_append(ctx, layer, pos, 1, k, v, pick_stream(ctx, stream));
 }
 
@@ -872,7 +914,7 @@ L3P_API int l3p_attn_decode_dev(l3p_attn_ctx* ctx, int layer, int pos, const flo
   if (int rc = check_layer(ctx, layer)) return rc;
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, out})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), nullptr,
                        nullptr, true);
 }
@@ -883,7 +925,7 @@ L3P_API int l3p_attn_step_dev(l3p_attn_ctx* ctx, int layer, int pos, const float
   if (int rc = check_layer(ctx, layer)) return rc;
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   // one launch: the decode stores the new row (quantised first for a Q8_0
   // cache, c:3299-3312) and attends to it from its producer's copy
   return launch_decode(ctx, layer, 0, pos, 0, 1, q, out, nullptr, nullptr, pick_stream(ctx, stream), k, v, true);
@@ -896,7 +938,7 @@ L3P_API int l3p_attn_decode_layers_dev(l3p_attn_ctx* ctx, int layer0, int n_laye
   if (int rc = check_layer(ctx, layer0 + n_layers - 1)) return rc;
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, out})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   return launch_decode(ctx, layer0, 1, pos, 0, n_layers, q, out, nullptr, nullptr, pick_stream(ctx, stream),
                        nullptr, nullptr, true);
 }
@@ -907,7 +949,7 @@ L3P_API int l3p_attn_decode_partial_dev(l3p_attn_ctx* ctx, int layer, int pos, c
   if (int rc = check_layer(ctx, layer)) return rc;
   if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
   if (int rc = check_aligned(ctx, {q, part_o})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   return launch_decode(ctx, layer, 0, pos, 0, 1, q, nullptr, part_o, part_ml, pick_stream(ctx, stream), nullptr,
                        nullptr, true);
 }
@@ -918,7 +960,7 @@ L3P_API int l3p_attn_lse_merge_dev(l3p_attn_ctx* ctx, int n_parts, int rows_per_
       row_begin + n_rows > rows_per_part)
     return ctx ? fail(ctx, L3P_E_INVAL, "bad merge arguments") : L3P_E_INVAL;
   if (n_rows == 0) return L3P_OK;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   lse_merge_kernel<<<n_rows, 128, 0, pick_stream(ctx, stream)>>>(n_parts, rows_per_part, row_begin, ctx->hd,
                                                                  parts_o, parts_ml, out);
   ++ctx->launches;
@@ -935,7 +977,7 @@ L3P_API int l3p_attn_prefill_dev(l3p_attn_ctx* ctx, int layer, int start_pos, in
     return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", start_pos, start_pos + n_tok, ctx->cfg.seq_len);
   if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
   if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   cudaStream_t s = pick_stream(ctx, stream);
   if (int rc = launch_append(ctx, layer, start_pos, n_tok, k, v, s)) return rc;
   if (ctx->prefill_tc) return launch_prefill_tc(ctx, layer, start_pos, n_tok, q, out, s);
@@ -973,7 +1015,7 @@ L3P_API int l3p_attn_kv_append(l3p_attn_ctx* ctx, int layer, int pos, const floa
   if (!ctx || !k || !v) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
   if (pos < 0 || pos >= ctx->cfg.seq_len) return fail(ctx, L3P_E_RANGE, "pos %d outside [0, %d)", pos, ctx->cfg.seq_len);
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
   if (int rc = ensure_staging(ctx, 2 * kvd)) return rc;
   if (int rc = ensure_host_staging(ctx, 2 * kvd)) return rc;
@@ -988,7 +1030,8 @@ L3P_API int l3p_attn_decode(l3p_attn_ctx* ctx, int layer, int pos, const float* 
   if (!ctx || !q || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
   if (int rc = check_pos_full(ctx, pos)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  if (ctx->srv_on) return server_call(ctx, layer, pos, q, nullptr, nullptr, out);
+  CtxScope dev(ctx);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd;
   if (int rc = ensure_staging(ctx, qd)) return rc;
   if (int rc = ensure_host_staging(ctx, 2 * qd)) return rc;
@@ -1014,7 +1057,8 @@ L3P_API int l3p_attn_step(l3p_attn_ctx* ctx, int layer, int pos, const float* q,
   if (!ctx || !q || !k || !v || !out) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
   if (int rc = check_pos_full(ctx, pos)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  if (ctx->srv_on) return server_call(ctx, layer, pos, q, k, v, out);
+  CtxScope dev(ctx);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
   const size_t in = qd + 2 * kvd;  // staged inputs: q | k | v
   if (int rc = ensure_staging(ctx, in)) return rc;
@@ -1047,7 +1091,7 @@ L3P_API int l3p_attn_prefill(l3p_attn_ctx* ctx, int layer, int start_pos, int n_
   if (start_pos < 0 || start_pos + n_tok > ctx->cfg.seq_len)
     return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", start_pos, start_pos + n_tok, ctx->cfg.seq_len);
   if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
   const size_t nq = qd * n_tok, nkv = kvd * n_tok;
   if (int rc = ensure_staging(ctx, 2 * nq + 2 * nkv)) return rc;
@@ -1079,7 +1123,7 @@ L3P_API int l3p_attn_load_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, 
     return fail(ctx, L3P_E_RANGE, "positions [%d, %d) outside [0, %d)", pos0, pos0 + n_pos, ctx->cfg.seq_len);
   const int lo = std::max(pos0, ctx->cfg.seq_begin), hi = std::min(pos0 + n_pos, ctx->cfg.seq_begin + ctx->seq_count);
   if (hi <= lo) return L3P_OK;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t row = (size_t)ctx->hd;
   if (ctx->q8) {
     // stage each head's rows and quantise them on the device, as kv_append does
@@ -1117,7 +1161,7 @@ L3P_API int l3p_attn_read_kv(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, 
     return fail(ctx, L3P_E_RANGE, "positions [%d, %d) outside [0, %d)", pos0, pos0 + n_pos, ctx->cfg.seq_len);
   const int lo = std::max(pos0, ctx->cfg.seq_begin), hi = std::min(pos0 + n_pos, ctx->cfg.seq_begin + ctx->seq_count);
   if (hi <= lo) return L3P_OK;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t row = (size_t)ctx->hd;
   if (ctx->q8) {
     // dequantised values d * int8 (exact in fp32)
@@ -1162,7 +1206,7 @@ int q8_block_io(l3p_attn_ctx* ctx, int layer, int pos0, int n_pos, uint8_t* kb, 
     return fail(ctx, L3P_E_RANGE, "positions [%d, %d) outside [0, %d)", pos0, pos0 + n_pos, ctx->cfg.seq_len);
   const int lo = std::max(pos0, ctx->cfg.seq_begin), hi = std::min(pos0 + n_pos, ctx->cfg.seq_begin + ctx->seq_count);
   if (hi <= lo) return L3P_OK;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t rowb = (size_t)ctx->hd / 32 * 34;
   const long long nblk = (long long)(hi - lo) * (ctx->hd / 32);
   const size_t bytes = (size_t)nblk * 34;

@@ -165,7 +165,7 @@ L3P_API int l3p_attn_set_rope(l3p_attn_ctx* ctx, const l3p_attn_rope_config* rop
   std::vector<float2> tab, tab_swa;
   build(theta, tab);
   if (gemma) build(theta_swa, tab_swa);
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
   if (ctx->rope_tab_swa != ctx->rope_tab) cudaFree(ctx->rope_tab_swa);
   cudaFree(ctx->rope_tab);
@@ -209,7 +209,7 @@ L3P_API int l3p_attn_rope_dev(l3p_attn_ctx* ctx, int layer, int pos0, int n_tok,
   if (int rc = check_aligned(ctx, {q, k, q_out, k_out})) return rc;
   if (int rc = check_rope(ctx)) return rc;
   if (n_tok == 0) return L3P_OK;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   return launch_rope(ctx, layer, pos0, n_tok, q, k, nullptr, q_out, k_out, false, pick_stream(ctx, stream));
 }
 
@@ -220,7 +220,7 @@ L3P_API int l3p_attn_step_raw_dev(l3p_attn_ctx* ctx, int layer, int pos, const f
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
   if (int rc = check_rope(ctx)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   return step_raw_core(ctx, layer, pos, q, k, v, out, pick_stream(ctx, stream), true);
 }
 
@@ -234,7 +234,7 @@ L3P_API int l3p_attn_prefill_raw_dev(l3p_attn_ctx* ctx, int layer, int start_pos
   if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
   if (int rc = check_aligned(ctx, {q, k, v, out})) return rc;
   if (int rc = check_rope(ctx)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   return prefill_raw_core(ctx, layer, start_pos, n_tok, q, k, v, out, pick_stream(ctx, stream));
 }
 
@@ -247,7 +247,7 @@ L3P_API int l3p_attn_step_raw(l3p_attn_ctx* ctx, int layer, int pos, const float
   if (int rc = check_layer(ctx, layer)) return rc;
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_rope(ctx)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
   const size_t in = qd + 2 * kvd;  // staged inputs: q | k | v
   if (int rc = ensure_staging(ctx, in)) return rc;
@@ -276,7 +276,7 @@ L3P_API int l3p_attn_prefill_raw(l3p_attn_ctx* ctx, int layer, int start_pos, in
     return fail(ctx, L3P_E_RANGE, "tokens [%d, %d) outside [0, %d)", start_pos, start_pos + n_tok, ctx->cfg.seq_len);
   if (int rc = check_pos_full(ctx, start_pos + n_tok - 1)) return rc;
   if (int rc = check_rope(ctx)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
   const size_t nq = qd * n_tok, nkv = kvd * n_tok;
   if (int rc = ensure_staging(ctx, 2 * nq + 2 * nkv)) return rc;

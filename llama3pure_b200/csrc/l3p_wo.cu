@@ -128,7 +128,7 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
       for (size_t b = 0; b < nb; ++b)
         memcpy(&w[(size_t)r * row_bytes + b * WoQ6K::kBlockBytes], src + (size_t)r * src_row + (b0 + b) * 210, 210);
   }
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
   if (ctx->wo.empty()) {
     ctx->wo.resize(ctx->cfg.n_layers);
@@ -171,7 +171,7 @@ L3P_API int l3p_attn_wo_dev(l3p_attn_ctx* ctx, int layer, const float* x, float*
   if (!ctx || !x || !xout) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (int rc = check_wo(ctx, layer)) return rc;
   if (int rc = check_aligned(ctx, {x, xout})) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   return launch_wo(ctx, layer, x, xout, pick_stream(ctx, stream));
 }
 
@@ -181,7 +181,7 @@ L3P_API int l3p_attn_wo_dev(l3p_attn_ctx* ctx, int layer, const float* x, float*
 L3P_API int l3p_attn_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* xout) {
   if (!ctx || !x || !xout) return ctx ? fail(ctx, L3P_E_INVAL, "null pointer") : L3P_E_INVAL;
   if (int rc = check_wo(ctx, layer)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, dim = ctx->wo[layer].rows;
   if (int rc = ensure_host_staging(ctx, qd + dim)) return rc;
   int r0, r1;
@@ -203,7 +203,7 @@ L3P_API int l3p_attn_step_raw_wo(l3p_attn_ctx* ctx, int layer, int pos, const fl
   if (int rc = check_pos_full(ctx, pos)) return rc;
   if (int rc = check_rope(ctx)) return rc;
   if (int rc = check_wo(ctx, layer)) return rc;
-  DeviceScope dev(ctx->cfg.device);
+  CtxScope dev(ctx);
   const size_t qd = (size_t)ctx->cfg.n_heads * ctx->hd, kvd = (size_t)ctx->cfg.n_kv_heads * ctx->hd;
   const size_t dim = ctx->wo[layer].rows;
   const size_t in = qd + 2 * kvd;  // staged inputs: q | k | v

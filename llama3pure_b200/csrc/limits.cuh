@@ -1,9 +1,14 @@
-// limits.cuh -- sizes shared by the NVLink group kernels (seq_xchg.cuh, wo.cuh)
-// and the host context (ctx.h).
+// limits.cuh -- sizes shared by the kernels (the NVLink groups of
+// seq_xchg.cuh and wo.cuh, the host-call server) and the host context (ctx.h).
 #pragma once
 #include <cstddef>
 
 namespace l3p {
+
+// The split-K scratch of a context (partials, (m, l) pairs, tickets) is used
+// in this many rotating slices, so that decode launches overlapping on the
+// GPU never share one; the host-call server uses slices 0 and 1 by call parity.
+constexpr int kScratchSlots = 4;
 
 constexpr int kXchgMaxParts = 16;    // members of a sequence or tensor-parallel group
 constexpr int kXchgFlagBytes = 256;  // flags and step counter ahead of an exchange region's slots
