@@ -1478,9 +1478,8 @@ def run_tp_trace(args):
     KV-head shard) from the -DL3P_DECODE_TRACE build, alone (32 launches in a
     graph) and inside the head-sharded block (raw step + wo + sum per layer).
     Every CTA stamps %globaltimer at its start, after griddepcontrol.wait,
-    after its GEMV rows, after sending them to the block's owner, (owner) after
-    sending the block's sums to every member, when the block's sums have
-    arrived, and at its exit.  Medians over the launches of one replay, per rank, in us (each
+    after its GEMV rows, after sending them to every member, when every
+    member's rows of its block have arrived and are summed, and at its exit.  Medians over the launches of one replay, per rank, in us (each
     GPU's own timer: only differences within one GPU are used)."""
     import datetime
     import tempfile as _tf
@@ -1554,16 +1553,14 @@ def run_tp_trace(args):
         rows = []
         for i in range(1, len(recs)):
             st, prev = recs[i][1], recs[i - 1][1]
-            owner = (np.arange(st.shape[0]) % world) == rank
             rows.append({
-                "release_after_prev_exit": st[:, 1].min() - prev[:, 6].max(),
+                "release_after_prev_exit": st[:, 1].min() - prev[:, 5].max(),
                 "gemv_done_after_release": st[:, 2].max() - st[:, 1].min(),
                 "sent_after_gemv": np.median(st[:, 3] - st[:, 2]),
-                "owner_sums_sent_after_sent": np.median(st[owner, 4] - st[owner, 3]),
-                "sum_arrived_after_sent": np.median(st[:, 5] - st[:, 3]),
-                "exit_after_sum_arrived": np.median(st[:, 6] - st[:, 5]),
-                "last_exit_after_release": st[:, 6].max() - st[:, 1].min(),
-                "period": st[:, 6].max() - prev[:, 6].max(),
+                "summed_after_sent": np.median(st[:, 4] - st[:, 3]),
+                "exit_after_summed": np.median(st[:, 5] - st[:, 4]),
+                "last_exit_after_release": st[:, 5].max() - st[:, 1].min(),
+                "period": st[:, 5].max() - prev[:, 5].max(),
             })
         summary = {k: round(float(np.median([r[k] for r in rows])) / 1e3, 3) for k in rows[0]}
         summary["us_per_layer_timed"] = round(ms * 1e3 / L, 3)

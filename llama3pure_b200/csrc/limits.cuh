@@ -15,20 +15,15 @@ constexpr int kXchgFlagBytes = 256;  // flags and step counter ahead of an excha
 
 // Exchange region of a tensor-parallel group (wo.cuh), byte offsets:
 //   [0, 256)        header: u32 step (calls completed) at 64, u32 exit ticket at 68
-//   kTpRecvOff      u64 recv[2][n_members][dim]: partial rows sent to this
-//                   member for the row blocks it owns
-//   tp_result_off   u64 result[2][dim]: summed rows sent by the owners
+//   kTpRecvOff      u64 recv[2][n_members][dim]: every member's partial rows
 // Every u64 is a packet: the float in the low 32 bits, the call number e in
 // the high 32 (never 0: calls count from 1).  The slots alternate by call parity.
 constexpr int kTpMaxBlocks = 4096;      // CTAs of a tensor-parallel projection at most
 constexpr unsigned kTpStepWord = 16;    // u32 index of the step counter in the header
 constexpr unsigned kTpTicketWord = 17;  // u32 index of the exit ticket
 constexpr size_t kTpRecvOff = kXchgFlagBytes;
-__host__ __device__ constexpr size_t tp_result_off(int members, int dim) {
-  return kTpRecvOff + 2ull * members * dim * 8;
-}
 __host__ __device__ constexpr size_t tp_region_bytes(int members, int dim) {
-  return tp_result_off(members, dim) + 2ull * dim * 8;
+  return kTpRecvOff + 2ull * members * dim * 8;
 }
 
 }  // namespace l3p

@@ -64,8 +64,8 @@ struct WoArgs {
   uint8_t* tp_regions[kXchgMaxParts];  // every member's exchange region (own included)
   int* err;                            // device error word (kErrTimeout)
   // stage stamps of the tensor-parallel tail (builds with L3P_DECODE_TRACE):
-  // 0 start, 1 after griddepcontrol.wait, 2 GEMV done, 3 partial sent, 4 owner:
-  // the block's sums sent to every member, 5 this block's sums arrived, 6 exit
+  // 0 start, 1 after griddepcontrol.wait, 2 GEMV done, 3 partial sent to every
+  // member, 4 every member's rows arrived and summed, 5 exit
   unsigned long long* trace;
 };
 
@@ -243,84 +243,72 @@ struct WoQ6K {
 };
 
 // Tensor-parallel sum of the partial projections over NVLink, in the tail of
-// the GEMV: a reduce-scatter then an all-gather, spread over the CTAs.  The
-// grid is the same on every member (same rows, kernel and GPU), so CTA j
-// covers the same row block j everywhere; block j is owned by member
-// j % n_members.  Call e (1, 2, ... counted by the device step word, read
-// after griddepcontrol.wait, when the previous call's grid has completed):
-//   1. CTA j sends its partial rows to slot [e&1][member] of the owner's recv
-//      array (peer stores unless it owns the block);
-//   2. the owner's CTA j waits (bounded) for every member's rows of the
-//      block, sums them in member order -- the same order, hence the same
-//      bits, on every member -- and sends the sums to result[e&1] of every
-//      member;
-//   3. every CTA j waits (bounded) for its block's sums and copies them to y;
-//   4. the last CTA to leave (exit ticket) writes e into the step word.
+// the GEMV: an all-to-all of the partial rows, one NVLink crossing, spread
+// over the CTAs.  The grid is the same on every member (same rows, kernel and
+// GPU), so CTA j covers the same row block j everywhere.  Call e (1, 2, ...
+// counted by the device step word, read after griddepcontrol.wait, when the
+// previous call's grid has completed):
+//   1. CTA j sends its partial rows to slot [e&1][member] of every member's
+//      recv array (peer stores, its own included);
+//   2. CTA j waits (bounded) for every member's rows of its block, sums them
+//      in member order -- the same order, hence the same bits, on every
+//      member -- and writes the sums to y;
+//   3. the last CTA to leave (exit ticket) writes e into the step word.
 // Every value travels as one 64-bit packet (float | e << 32), stored and
 // loaded with relaxed system-scope 64-bit accesses, which cannot tear: a
 // receiver that sees e in a packet has its value, so no fence, counter or flag
 // orders anything (a system-scope fence after the peer stores measured ~4.6 us
-// on B200, twice on the critical path).  Per call a member sends its dim
-// partial rows once and the owners send dim sums to each member: 2 * dim * 8
-// bytes per member.  Two slots suffice: a member can be at most one call
-// ahead of another, since finishing a call needs every owner's sums of it.  A
-// wait that gives up sets kErrTimeout; the group is then out of step and must
-// be set up anew.
+// on B200).  Per call a member sends its dim partial rows to each of the
+// n_members - 1 others, dim * 8 bytes each.  A reduce-scatter (partials to
+// the block's owner) followed by an all-gather (sums from the owner) sends
+// less but crosses NVLink twice: 8.8 against 7.6 us per call at two members.
+// Two slots suffice: finishing call e needs every member's rows of call e,
+// so no member sends call e + 2 (slot e&1) before every member has read
+// call e.  A wait that gives up sets kErrTimeout; the group is then out of
+// step and must be set up anew.
 
 __device__ __forceinline__ void wo_tp_exchange(const WoArgs& p, const float* red, int r_begin, int r_end) {
   __shared__ unsigned s_e;
   const int n = r_end - r_begin;
-  const int N = p.tp_members, me = p.tp_member, j = blockIdx.x;
-  const int owner = j % N;
+  const int N = p.tp_members, me = p.tp_member;
   uint8_t* const mine = p.tp_regions[me];
   unsigned* const hdr = reinterpret_cast<unsigned*>(mine);
   if (threadIdx.x == 0) s_e = *reinterpret_cast<volatile unsigned*>(hdr + kTpStepWord) + 1u;
   __syncthreads();
   const unsigned e = s_e;
   const long long par = e & 1u;
-  const size_t res_off = tp_result_off(N, p.rows);
-  bool ok = true;
-  // 1. this block's partial rows to the owner
-  unsigned long long* recv = reinterpret_cast<unsigned long long*>(p.tp_regions[owner] + kTpRecvOff) +
-                             (par * N + me) * p.rows + r_begin;
+  // 1. this block's partial rows to every member
   for (int r = threadIdx.x; r < n; r += blockDim.x) {
     float s = 0.f;
     for (int c = 0; c < p.wc; ++c) s += red[c * p.rows_per_cta + r];
-    ll_store(recv + r, s, e);
+    for (int m = 0; m < N; ++m)
+      ll_store(reinterpret_cast<unsigned long long*>(p.tp_regions[m] + kTpRecvOff) + (par * N + me) * p.rows +
+                   r_begin + r,
+               s, e);
   }
   trace_stamp(p.trace, 3);
-  // 2. the owner sums the block and sends it to every member
-  if (owner == me) {
-    const unsigned long long* rv = reinterpret_cast<const unsigned long long*>(mine + kTpRecvOff) + par * N * p.rows;
-    for (int r = threadIdx.x; r < n && ok; r += blockDim.x) {
-      float v[kXchgMaxParts];
-      ok = ll_wait<kXchgMaxParts>(rv + r_begin + r, p.rows, N, e, v, p.err);
-      if (!ok) break;
-      float s = v[0];
-#pragma unroll
-      for (int m = 1; m < kXchgMaxParts; ++m)  // member order (unrolled: v stays in registers)
-        if (m < N) s += v[m];
-      for (int m = 0; m < N; ++m)
-        ll_store(reinterpret_cast<unsigned long long*>(p.tp_regions[m] + res_off) + par * p.rows + r_begin + r, s, e);
-    }
-    trace_stamp(p.trace, 4);
-  }
-  // 3. every member: this block's sums into y
-  const unsigned long long* sum = reinterpret_cast<const unsigned long long*>(mine + res_off) + par * p.rows;
+  // 2. every member's rows of this block, summed in member order
+  const unsigned long long* rv = reinterpret_cast<const unsigned long long*>(mine + kTpRecvOff) + par * N * p.rows;
+  bool ok = true;
   for (int r = threadIdx.x; r < n && ok; r += blockDim.x) {
-    float v[1];
-    ok = ll_wait<1>(sum + r_begin + r, 0, 1, e, v, p.err);
-    if (ok) p.y[r_begin + r] = v[0];
+    float v[kXchgMaxParts];
+    ok = ll_wait<kXchgMaxParts>(rv + r_begin + r, p.rows, N, e, v, p.err);
+    if (!ok) break;
+    float s = v[0];
+#pragma unroll
+    for (int m = 1; m < kXchgMaxParts; ++m)  // member order (unrolled: v stays in registers)
+      if (m < N) s += v[m];
+    p.y[r_begin + r] = s;
   }
-  trace_stamp(p.trace, 5);
-  // 4. the last CTA to leave advances the step (the next call reads it after
+  trace_stamp(p.trace, 4);
+  // 3. the last CTA to leave advances the step (the next call reads it after
   // this grid has completed)
   __syncthreads();
   if (threadIdx.x == 0 && atomicAdd(hdr + kTpTicketWord, 1u) == gridDim.x - 1) {
     hdr[kTpTicketWord] = 0u;
     *reinterpret_cast<volatile unsigned*>(hdr + kTpStepWord) = e;
   }
-  trace_stamp(p.trace, 6);
+  trace_stamp(p.trace, 5);
 }
 
 // grid: ceil(rows / rows_per_cta) CTAs of NW warps; dynamic shared memory:
