@@ -343,10 +343,11 @@ int l3p_attn_decode_seq_dev(l3p_attn_ctx* ctx, int layer, int pos, const float* 
  * export (64-byte CUDA IPC handle of a small exchange region for `dim`-row
  * projections) and import each other's regions once; then
  * l3p_attn_wo_allreduce_dev computes this member's partial and, in the same
- * launch, sums the group's partials over NVLink peer memory: every row block
- * is summed by one owner member (in member order, so every member gets the
- * same bits) and sent back to all -- a reduce-scatter and an all-gather of
- * xb2 without a collective library, about 2 * dim * 4 bytes sent per member.
+ * launch, sums the group's partials over NVLink peer memory: every member
+ * sends its partial rows to every member and sums all members' rows in member
+ * order (so every member gets the same bits) -- an all-reduce of xb2 in one
+ * crossing, without a collective library, (n_members - 1) * dim * 8 bytes sent
+ * per member.
  * One launch per call; every member calls it for the same layers in the same
  * order, on identical GPUs.  A member that never arrives makes the others'
  * bounded waits give up (L3P_E_TIMEOUT through l3p_attn_check); the group is
