@@ -762,11 +762,11 @@ def parity_leg(job: Job):
         res["gemma_mqa_decode"] = {"workload": gs.name + " layer 0 (one GPU)", **_cmp(got, want)}
     del k, v
 
-    # the wo projection: 4096 x 4096 (Llama-3.1-8B), three GGUF types; at N > 1
+    # the wo projection: 4096 x 4096 (Llama-3.1-8B), six GGUF types; at N > 1
     # the tensor-parallel sum over NVLink on every rank, two steps
     dim = cols = sh.n_heads * sh.head_dim
     x = wo_input(cols, seed=7)
-    for name, wt in (("q8_0", 8), ("q4_k", 12), ("q6_k", 14)):
+    for name, wt in (("q8_0", 8), ("q2_k", 10), ("q3_k", 11), ("q4_k", 12), ("q5_k", 13), ("q6_k", 14)):
         w = wo_weights(wt, dim, cols, seed=6)
         with AttnContext.for_shape(sh, n_layers=1, seq_len=16, device=job.local, kv_head_begin=me.kv_head_begin,
                                    kv_head_count=me.kv_head_count) as ctx:
@@ -1674,8 +1674,9 @@ def run_wo(args, torch, layers: int = 16):
     stream = torch.cuda.Stream()
     peak, peak_kind = measured_peaks()
     res = {"shape": f"{dim} x {cols}", "layers_cycled": layers, "peak_kind": peak_kind}
-    for name, wt, nbytes in (("q8_0", 8, cols // 32 * 34), ("q4_k", 12, cols // 256 * 144),
-                             ("q6_k", 14, cols // 256 * 210)):
+    for name, wt, nbytes in (("q8_0", 8, cols // 32 * 34), ("q2_k", 10, cols // 256 * 84),
+                             ("q3_k", 11, cols // 256 * 110), ("q4_k", 12, cols // 256 * 144),
+                             ("q5_k", 13, cols // 256 * 176), ("q6_k", 14, cols // 256 * 210)):
         ctx = AttnContext.for_shape(sh, n_layers=layers, seq_len=16)
         ctx.set_stream(stream)
         w = wo_weights(wt, dim, cols, seed=5)

@@ -291,7 +291,10 @@ int l3p_attn_prefill_raw_dev(l3p_attn_ctx* ctx, int layer, int start_pos, int n_
  * the types with a row dequantiser); the library multiplies the same values
  * in a different summation order (within 1e-4 of the reference). */
 #define L3P_W_Q8_0 8  /* GGML_TYPE_Q8_0 (c:102): 34-byte blocks of 32 values */
+#define L3P_W_Q2_K 10 /* GGML_TYPE_Q2_K (c:104): 84-byte blocks of 256 values */
+#define L3P_W_Q3_K 11 /* GGML_TYPE_Q3_K (c:105): 110-byte blocks of 256 values */
 #define L3P_W_Q4_K 12 /* GGML_TYPE_Q4_K (c:106): 144-byte blocks of 256 values */
+#define L3P_W_Q5_K 13 /* GGML_TYPE_Q5_K (c:107): 176-byte blocks of 256 values */
 #define L3P_W_Q6_K 14 /* GGML_TYPE_Q6_K (c:108): 210-byte blocks of 256 values */
 
 /* Hand layer `layer`'s attn_output.weight to the context: `dim` rows of

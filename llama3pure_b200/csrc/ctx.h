@@ -104,7 +104,7 @@ struct l3p_attn_ctx {
   };
   std::vector<WoLayer> wo;
   float* wo_x = nullptr;
-  int wo_ctas_per_sm[6] = {0, 0, 0, 0, 0, 0};  // (Q8_0, Q4_K, Q6_K) x (4, 8 warps)
+  int wo_ctas_per_sm[12] = {};  // (Q8_0, Q4_K, Q6_K, Q5_K, Q2_K, Q3_K) x (4, 8 warps)
   // sequence group over NVLink (l3p_attn_seq_group_*): this context's exchange
   // region (flags, then per-layer partial slots; seq_xchg.cuh), the members'
   // regions mapped into this process, and the step counter

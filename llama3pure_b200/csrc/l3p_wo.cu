@@ -12,6 +12,29 @@
 
 using namespace l3p;
 
+namespace {
+
+// The GEMV kernels, (format, 4 or 8 warps): index 2 * wo_format_index + (8 warps)
+using WoKernel = void (*)(const WoArgs);
+constexpr int kWoKernelCount = 12;
+const WoKernel kWoKernels[kWoKernelCount] = {
+    wo_gemv_kernel<WoQ8, 4>,  wo_gemv_kernel<WoQ8, 8>,  wo_gemv_kernel<WoQ4K, 4>, wo_gemv_kernel<WoQ4K, 8>,
+    wo_gemv_kernel<WoQ6K, 4>, wo_gemv_kernel<WoQ6K, 8>, wo_gemv_kernel<WoQ5K, 4>, wo_gemv_kernel<WoQ5K, 8>,
+    wo_gemv_kernel<WoQ2K, 4>, wo_gemv_kernel<WoQ2K, 8>, wo_gemv_kernel<WoQ3K, 4>, wo_gemv_kernel<WoQ3K, 8>};
+
+int wo_format_index(int type) {
+  switch (type) {
+    case L3P_W_Q8_0: return 0;
+    case L3P_W_Q4_K: return 1;
+    case L3P_W_Q6_K: return 2;
+    case L3P_W_Q5_K: return 3;
+    case L3P_W_Q2_K: return 4;
+    default: return 5;  // L3P_W_Q3_K
+  }
+}
+
+}  // namespace
+
 namespace l3p_api {
 
 // The wo GEMV of `layer` (wo.cuh): y[dim] = W[:, owned columns] . x[owned columns].
@@ -33,7 +56,7 @@ int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream
   a.C = ctx->kvh_count * ctx->G * ctx->hd;
   a.x = x + (long long)ctx->cfg.kv_head_begin * ctx->G * ctx->hd;
   a.y = y;
-  const int fi = L.type == L3P_W_Q8_0 ? 0 : L.type == L3P_W_Q4_K ? 1 : 2;
+  const int fi = wo_format_index(L.type);
   const int slice = L.type == L3P_W_Q6_K ? WoQ6K::kSlice : WoQ8::kSlice;
   const int slices = (a.C + slice - 1) / slice;
   a.wc = 1;
@@ -60,14 +83,7 @@ int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream
     lc.attrs = attr;
     lc.numAttrs = 1;
   }
-  switch (k) {
-    case 0: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ8, 4>, a)); break;
-    case 1: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ8, 8>, a)); break;
-    case 2: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ4K, 4>, a)); break;
-    case 3: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ4K, 8>, a)); break;
-    case 4: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ6K, 4>, a)); break;
-    default: L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, wo_gemv_kernel<WoQ6K, 8>, a)); break;
-  }
+  L3P_CUDA(ctx, cudaLaunchKernelEx(&lc, kWoKernels[k], a));
   ++ctx->launches;
   return L3P_OK;
 }
@@ -86,12 +102,18 @@ using namespace l3p_api;
 L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* rows, int dim) {
   if (!ctx || !rows || dim <= 0) return ctx ? fail(ctx, L3P_E_INVAL, "bad argument") : L3P_E_INVAL;
   if (int rc = check_layer(ctx, layer)) return rc;
-  int vals, bytes;  // values and bytes per GGUF block
+  int vals, bytes, dev_bytes;  // values and bytes per GGUF block, bytes per device block
   switch (type) {
-    case L3P_W_Q8_0: vals = 32, bytes = 34; break;
-    case L3P_W_Q4_K: vals = 256, bytes = 144; break;
-    case L3P_W_Q6_K: vals = 256, bytes = 210; break;
-    default: return fail(ctx, L3P_E_UNSUPPORTED, "wo weight type %d (Q8_0 = 8, Q4_K = 12, Q6_K = 14 are supported)", type);
+    case L3P_W_Q8_0: vals = 32, bytes = 34, dev_bytes = 32; break;
+    case L3P_W_Q2_K: vals = 256, bytes = 84, dev_bytes = WoQ2K::kBlockBytes; break;
+    case L3P_W_Q3_K: vals = 256, bytes = 110, dev_bytes = WoQ3K::kBlockBytes; break;
+    case L3P_W_Q4_K: vals = 256, bytes = 144, dev_bytes = 144; break;
+    case L3P_W_Q5_K: vals = 256, bytes = 176, dev_bytes = WoQ5K::kBlockBytes; break;
+    case L3P_W_Q6_K: vals = 256, bytes = 210, dev_bytes = WoQ6K::kBlockBytes; break;
+    default:
+      return fail(ctx, L3P_E_UNSUPPORTED,
+                  "wo weight type %d (Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14 are supported)",
+                  type);
   }
   const int hd = ctx->hd, cols = ctx->cfg.n_heads * hd;
   const int c_lo = ctx->cfg.kv_head_begin * ctx->G * hd, C = ctx->kvh_count * ctx->G * hd;
@@ -117,16 +139,13 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
         sc[(size_t)r * sc_stride + 2 * b + 1] = blk[1];
         memcpy(&w[(size_t)r * C + b * 32], blk + 2, 32);
       }
-  } else if (type == L3P_W_Q4_K) {
-    row_bytes = (long long)nb * 144;
-    w.resize((size_t)dim * row_bytes);
-    for (int r = 0; r < dim; ++r) memcpy(&w[(size_t)r * row_bytes], src + (size_t)r * src_row + b0 * 144, nb * 144);
   } else {
-    row_bytes = (long long)nb * WoQ6K::kBlockBytes;
+    // K-quants: each GGUF block at the start of a 16-byte aligned device block
+    row_bytes = (long long)nb * dev_bytes;
     w.assign((size_t)dim * row_bytes, 0);
     for (int r = 0; r < dim; ++r)
       for (size_t b = 0; b < nb; ++b)
-        memcpy(&w[(size_t)r * row_bytes + b * WoQ6K::kBlockBytes], src + (size_t)r * src_row + (b0 + b) * 210, 210);
+        memcpy(&w[(size_t)r * row_bytes + b * dev_bytes], src + (size_t)r * src_row + (b0 + b) * bytes, bytes);
   }
   CtxScope dev(ctx);
   L3P_CUDA(ctx, cudaStreamSynchronize(ctx->stream));
@@ -138,11 +157,8 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
       return fail(ctx, L3P_E_NOMEM, "wo input buffer allocation failed");
     }
     // resident CTAs per SM of each kernel (grid sizing)
-    const void* fns[6] = {(const void*)wo_gemv_kernel<WoQ8, 4>,  (const void*)wo_gemv_kernel<WoQ8, 8>,
-                          (const void*)wo_gemv_kernel<WoQ4K, 4>, (const void*)wo_gemv_kernel<WoQ4K, 8>,
-                          (const void*)wo_gemv_kernel<WoQ6K, 4>, (const void*)wo_gemv_kernel<WoQ6K, 8>};
-    for (int i = 0; i < 6; ++i)
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctx->wo_ctas_per_sm[i], fns[i], (i % 2 ? 8 : 4) * 32,
+    for (int i = 0; i < kWoKernelCount; ++i)
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctx->wo_ctas_per_sm[i], kWoKernels[i], (i % 2 ? 8 : 4) * 32,
                                                         (size_t)(i % 2 ? 8 : 4) * 64 * sizeof(float)) != cudaSuccess) {
         cudaGetLastError();
         ctx->wo_ctas_per_sm[i] = 1;

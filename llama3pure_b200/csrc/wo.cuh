@@ -187,6 +187,151 @@ struct WoQ4K {
   }
 };
 
+// Q5_K: Q4_K's lanes and sub-block pairs plus the fifth bit of every value
+// from qh (c:834-871): sub-block 2p takes bit 2p of qh[l], 2p+1 bit 2p+1.
+// Device block: the GGUF block as is (176 bytes: d, dmin, 12 scale bytes,
+// qh[32], qs[128]).
+struct WoQ5K {
+  static constexpr int kSlice = 1024;  // 4 blocks of 256
+  static constexpr int kLaneCols = 32;
+  static constexpr int kUnroll = 6;
+  static constexpr int kBlockBytes = 176;
+  struct Raw {
+    uint4 h;   // d, dmin, 12 scale bytes
+    uint4 q;   // 16 bytes of qs: low nibbles (sub-block 2p), high (2p+1)
+    uint4 qh;  // qh[16*(c%2) ..+16): the fifth bits of those values
+  };
+  __device__ static int col(int lane, int i) { return WoQ4K::col(lane, i); }
+  __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
+    const int lane = threadIdx.x & 31;
+    const uint8_t* blk = p.w + (long long)row * p.row_bytes + (long long)(c0 / 256 + (lane >> 3)) * kBlockBytes;
+    r.h = __ldg(reinterpret_cast<const uint4*>(blk));
+    r.qh = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * (lane & 1)));
+    r.q = __ldg(reinterpret_cast<const uint4*>(blk + 48 + 16 * (lane & 7)));
+  }
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&xs)[2]) {
+    const int lane = threadIdx.x & 31, p = (lane & 7) >> 1;
+    const float d = fp16_to_f32((uint16_t)(r.h.x & 0xffffu)), dmin = fp16_to_f32((uint16_t)(r.h.x >> 16));
+    int sc0, m0, sc1, m1;
+    WoQ4K::scale_min(r.h.y, r.h.z, r.h.w, 2 * p, sc0, m0);
+    WoQ4K::scale_min(r.h.y, r.h.z, r.h.w, 2 * p + 1, sc1, m1);
+    const uint32_t q[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
+    const uint32_t hb[4] = {r.qh.x, r.qh.y, r.qh.z, r.qh.w};
+    float2 lo = make_float2(0.f, 0.f), hi = lo;
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      const uint32_t l5 = (q[i / 4] & 0x0f0f0f0fu) | (((hb[i / 4] >> (2 * p)) & 0x01010101u) << 4);
+      const uint32_t h5 = ((q[i / 4] >> 4) & 0x0f0f0f0fu) | (((hb[i / 4] >> (2 * p + 1)) & 0x01010101u) << 4);
+      lo = __ffma2_rn(byte_pair(l5, i % 4, kTwo23), make_float2(x[i], x[i + 1]), lo);
+      hi = __ffma2_rn(byte_pair(h5, i % 4, kTwo23), make_float2(x[16 + i], x[17 + i]), hi);
+    }
+    return d * ((float)sc0 * (lo.x + lo.y) + (float)sc1 * (hi.x + hi.y)) -
+           dmin * ((float)m0 * xs[0] + (float)m1 * xs[1]);
+  }
+  __device__ static void xsums(const float (&x)[kLaneCols], float (&xs)[2]) { WoQ4K::xsums(x, xs); }
+};
+
+// Q2_K and Q3_K: per half h of a 256-value block, bit pair j of 32 quant
+// bytes gives 32 values (two sub-blocks of 16).  lane = 8*block + 4h + j
+// takes those 32 values, columns 128h + 32j + i (c:748-832).
+__device__ __forceinline__ int wo_k2_col(int lane, int i) {
+  return 256 * (lane >> 3) + 128 * ((lane >> 2) & 1) + 32 * (lane & 3) + i;
+}
+
+// Q2_K: value = (d * (s & 15)) * q - dmin * (s >> 4), q 2-bit, s the
+// sub-block's scale byte (scales[8h + 2j], [8h + 2j + 1]).  Device block
+// (96 bytes): the GGUF block's 84 (scales[16], qs[64], d, dmin), padded.
+struct WoQ2K {
+  static constexpr int kSlice = 1024;  // 4 blocks of 256
+  static constexpr int kLaneCols = 32;
+  static constexpr int kUnroll = 8;
+  static constexpr int kBlockBytes = 96;
+  struct Raw {
+    uint4 q0, q1;  // qs[32h ..+32)
+    uint32_t dd;   // d, dmin
+    uint16_t sc;   // the two sub-blocks' scale bytes
+  };
+  __device__ static int col(int lane, int i) { return wo_k2_col(lane, i); }
+  __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
+    const int lane = threadIdx.x & 31, h = (lane >> 2) & 1, j = lane & 3;
+    const uint8_t* blk = p.w + (long long)row * p.row_bytes + (long long)(c0 / 256 + (lane >> 3)) * kBlockBytes;
+    r.q0 = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 32 * h));
+    r.q1 = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * h));
+    r.sc = __ldg(reinterpret_cast<const uint16_t*>(blk + 8 * h + 2 * j));
+    r.dd = __ldg(reinterpret_cast<const uint32_t*>(blk + 80));
+  }
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&xs)[2]) {
+    const int shift = 2 * (threadIdx.x & 3);
+    const float d = fp16_to_f32((uint16_t)(r.dd & 0xffffu)), dmin = fp16_to_f32((uint16_t)(r.dd >> 16));
+    const int s0 = r.sc & 0xff, s1 = r.sc >> 8;
+    const uint32_t a[4] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w};
+    const uint32_t b[4] = {r.q1.x, r.q1.y, r.q1.z, r.q1.w};
+    float2 lo = make_float2(0.f, 0.f), hi = lo;
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      lo = __ffma2_rn(byte_pair((a[i / 4] >> shift) & 0x03030303u, i % 4, kTwo23), make_float2(x[i], x[i + 1]), lo);
+      hi = __ffma2_rn(byte_pair((b[i / 4] >> shift) & 0x03030303u, i % 4, kTwo23), make_float2(x[16 + i], x[17 + i]),
+                      hi);
+    }
+    return d * ((float)(s0 & 15) * (lo.x + lo.y) + (float)(s1 & 15) * (hi.x + hi.y)) -
+           dmin * ((float)(s0 >> 4) * xs[0] + (float)(s1 >> 4) * xs[1]);
+  }
+  __device__ static void xsums(const float (&x)[kLaneCols], float (&xs)[2]) { WoQ4K::xsums(x, xs); }
+};
+
+// Q3_K: value = (d * (s - 32)) * (q - 4 * !hbit), q 2-bit, hbit bit 4h + j of
+// hmask[i], s the sub-block's 6-bit scale: the low nibble of byte k (k < 8)
+// or the high nibble of byte k - 8, above it bit pair k/4 of byte 8 + k%4.
+// Device block (112 bytes): the GGUF block's 110 (hmask[32], qs[64],
+// scales[12], d), padded.
+struct WoQ3K {
+  static constexpr int kSlice = 1024;  // 4 blocks of 256
+  static constexpr int kLaneCols = 32;
+  static constexpr int kUnroll = 4;
+  static constexpr int kBlockBytes = 112;
+  struct Raw {
+    uint4 q0, q1;  // qs[32h ..+32)
+    uint4 m0, m1;  // hmask[0 ..32)
+    uint4 s;       // scales[12], d
+  };
+  __device__ static int col(int lane, int i) { return wo_k2_col(lane, i); }
+  __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
+    const int lane = threadIdx.x & 31, h = (lane >> 2) & 1;
+    const uint8_t* blk = p.w + (long long)row * p.row_bytes + (long long)(c0 / 256 + (lane >> 3)) * kBlockBytes;
+    r.m0 = __ldg(reinterpret_cast<const uint4*>(blk));
+    r.m1 = __ldg(reinterpret_cast<const uint4*>(blk + 16));
+    r.q0 = __ldg(reinterpret_cast<const uint4*>(blk + 32 + 32 * h));
+    r.q1 = __ldg(reinterpret_cast<const uint4*>(blk + 48 + 32 * h));
+    r.s = __ldg(reinterpret_cast<const uint4*>(blk + 96));
+  }
+  __device__ static int scale(const uint4& s, int k) {
+    const int low = k < 8 ? WoQ4K::sbyte(s.x, s.y, s.z, k) & 15 : WoQ4K::sbyte(s.x, s.y, s.z, k - 8) >> 4;
+    const int high = (WoQ4K::sbyte(s.x, s.y, s.z, 8 + (k & 3)) >> (2 * (k >> 2))) & 3;
+    return (low | (high << 4)) - 32;
+  }
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&)[2]) {
+    const int lane = threadIdx.x & 31, h = (lane >> 2) & 1, j = lane & 3;
+    const int shift = 2 * j, bit = 4 * h + j;
+    const float d = fp16_to_f32((uint16_t)(r.s.w & 0xffffu));
+    const int sc0 = scale(r.s, 8 * h + 2 * j), sc1 = scale(r.s, 8 * h + 2 * j + 1);
+    const uint32_t a[4] = {r.q0.x, r.q0.y, r.q0.z, r.q0.w};
+    const uint32_t b[4] = {r.q1.x, r.q1.y, r.q1.z, r.q1.w};
+    const uint32_t ma[4] = {r.m0.x, r.m0.y, r.m0.z, r.m0.w};
+    const uint32_t mb[4] = {r.m1.x, r.m1.y, r.m1.z, r.m1.w};
+    float2 lo = make_float2(0.f, 0.f), hi = lo;
+#pragma unroll
+    for (int i = 0; i < 16; i += 2) {
+      // q + 4*hbit in 0..7; the value is that minus 4
+      const uint32_t ua = ((a[i / 4] >> shift) & 0x03030303u) | (((ma[i / 4] >> bit) & 0x01010101u) << 2);
+      const uint32_t ub = ((b[i / 4] >> shift) & 0x03030303u) | (((mb[i / 4] >> bit) & 0x01010101u) << 2);
+      lo = __ffma2_rn(byte_pair(ua, i % 4, kTwo23 + 4.f), make_float2(x[i], x[i + 1]), lo);
+      hi = __ffma2_rn(byte_pair(ub, i % 4, kTwo23 + 4.f), make_float2(x[16 + i], x[17 + i]), hi);
+    }
+    return d * ((float)sc0 * (lo.x + lo.y) + (float)sc1 * (hi.x + hi.y));
+  }
+  __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
+};
+
 struct WoQ6K {
   static constexpr int kSlice = 2048;  // 8 blocks of 256
   static constexpr int kLaneCols = 64;

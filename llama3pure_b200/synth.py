@@ -122,13 +122,15 @@ def raw_qkv_inputs(shape: AttnShape, layer: int, n_tok: int):
     return q, k, v, q_norm, k_norm
 
 
-W_BLOCK = {8: (32, 34), 12: (256, 144), 14: (256, 210)}  # GGUF type -> (values, bytes) per block
+# GGUF type -> (values, bytes) per block: Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K
+W_BLOCK = {8: (32, 34), 10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210)}
 
 
 def wo_weights(wtype: int, rows: int, cols: int, seed: int, scale: float = 0.02) -> np.ndarray:
     """Random GGUF weight rows (uint8 [rows][cols/values*bytes]) of a Q8_0,
-    Q4_K or Q6_K tensor whose values are ~N(0, scale): every quant byte drawn
-    uniformly, every fp16 scale set so that the block spans about +-3 scale.
+    Q2_K, Q3_K, Q4_K, Q5_K or Q6_K tensor whose values are ~N(0, scale): every
+    quant byte drawn uniformly, every fp16 scale set so that the block spans
+    about +-3 scale.
     Generator: rng_for(seed + 2000, wtype)."""
     n, nb = W_BLOCK[wtype]
     g = rng_for(seed + 2000, wtype)
@@ -144,6 +146,17 @@ def wo_weights(wtype: int, rows: int, cols: int, seed: int, scale: float = 0.02)
         # value = d*sc*q - dmin*m, q in 0..15, sc and m 6-bit
         blocks[..., 0:2] = f16(g.uniform(0.5, 1.5, shp) * scale / 63.0 * 0.75)
         blocks[..., 2:4] = f16(g.uniform(0.5, 1.5, shp) * scale / 63.0 * 0.75 * 7.5)
+    elif wtype == 13:
+        # Q5_K: value = d*sc*q - dmin*m, q in 0..31, sc and m 6-bit
+        blocks[..., 0:2] = f16(g.uniform(0.5, 1.5, shp) * scale / 63.0 * 0.375)
+        blocks[..., 2:4] = f16(g.uniform(0.5, 1.5, shp) * scale / 63.0 * 0.375 * 15.5)
+    elif wtype == 10:
+        # Q2_K: value = d*sc*q - dmin*m, q in 0..3, sc and m 4-bit
+        blocks[..., 80:82] = f16(g.uniform(0.5, 1.5, shp) * scale / 15.0 * 2.0)
+        blocks[..., 82:84] = f16(g.uniform(0.5, 1.5, shp) * scale / 15.0 * 3.0)
+    elif wtype == 11:
+        # Q3_K: value = d*(sc-32)*q, q in -4..3, sc 6-bit
+        blocks[..., 108:110] = f16(g.uniform(0.5, 1.5, shp) * scale * 3.0 / (32.0 * 4.0))
     else:
         # value = d*sc*(q-32), q 6-bit, sc int8
         blocks[..., 208:210] = f16(g.uniform(0.5, 1.5, shp) * scale * 3.0 / (32.0 * 127.0))

@@ -456,7 +456,10 @@ int l3po_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer,
 long long l3po_w_row_bytes(int type, int cols) {
     switch (type) {
         case L3P_W_Q8_0: return (long long)(cols / 32) * 34;
+        case L3P_W_Q2_K: return (long long)(cols / QK_SUPER) * 84;
+        case L3P_W_Q3_K: return (long long)(cols / QK_SUPER) * 110;
         case L3P_W_Q4_K: return (long long)(cols / QK_SUPER) * 144;
+        case L3P_W_Q5_K: return (long long)(cols / QK_SUPER) * 176;
         case L3P_W_Q6_K: return (long long)(cols / QK_SUPER) * 210;
         default: return 0;
     }
@@ -506,6 +509,86 @@ static void deq_q4_k(const uint8_t* src, float* dst, int cols) {
     }
 }
 
+/* Q5_K: Q4_K's layout with a fifth bit per value: sub-block 2p (low nibbles
+ * of qs[32p..32p+32)) takes bit 2p of qh[l], sub-block 2p+1 (high nibbles)
+ * bit 2p+1, each worth 16 (c:834-871). */
+static void deq_q5_k(const uint8_t* src, float* dst, int cols) {
+    for (int b = 0; b < cols / QK_SUPER; ++b) {
+        const uint8_t* blk = src + (size_t)b * 176;
+        float d = l3po_fp16_to_fp32(rd16(blk)), dmin = l3po_fp16_to_fp32(rd16(blk + 2));
+        const uint8_t* sc = blk + 4;
+        const uint8_t* qh = blk + 16;
+        const uint8_t* qs = blk + 48;
+        float* y = dst + (size_t)b * QK_SUPER;
+        for (int p = 0; p < 4; ++p) {
+            int s0, m0, s1, m1;
+            k4_scale_min(sc, 2 * p, &s0, &m0);
+            k4_scale_min(sc, 2 * p + 1, &s1, &m1);
+            float dl = d * s0, ml = dmin * m0, dh = d * s1, mh = dmin * m1;
+            for (int l = 0; l < 32; ++l) {
+                int lo = (qs[32 * p + l] & 15) + (((qh[l] >> (2 * p)) & 1) ? 16 : 0);
+                int hi = (qs[32 * p + l] >> 4) + (((qh[l] >> (2 * p + 1)) & 1) ? 16 : 0);
+                y[64 * p + l] = dl * lo - ml;
+                y[64 * p + 32 + l] = dh * hi - mh;
+            }
+        }
+    }
+}
+
+/* Q2_K: two halves of 128 values, each from 32 quant bytes; within a half,
+ * bit pair j (shift 2j) of bytes 0..15 and 16..31 gives two sub-blocks of
+ * 16, scale byte s = scales[8h + 2j (+1)]: value = (d * (s & 15)) * q -
+ * dmin * (s >> 4) (c:748-784). */
+static void deq_q2_k(const uint8_t* src, float* dst, int cols) {
+    for (int b = 0; b < cols / QK_SUPER; ++b) {
+        const uint8_t* blk = src + (size_t)b * 84;
+        const uint8_t* sc = blk;
+        const uint8_t* qs = blk + 16;
+        float d = l3po_fp16_to_fp32(rd16(blk + 80)), dmin = l3po_fp16_to_fp32(rd16(blk + 82));
+        float* y = dst + (size_t)b * QK_SUPER;
+        for (int h = 0; h < 2; ++h)
+            for (int j = 0; j < 4; ++j)
+                for (int g = 0; g < 2; ++g) {
+                    int s = sc[8 * h + 2 * j + g];
+                    float dl = d * (s & 15), ml = dmin * (s >> 4);
+                    for (int l = 0; l < 16; ++l)
+                        y[128 * h + 32 * j + 16 * g + l] = dl * ((qs[32 * h + 16 * g + l] >> (2 * j)) & 3) - ml;
+                }
+    }
+}
+
+/* Q3_K: Q2_K's quant layout with a third bit from hmask (set: +0, clear:
+ * -4, bit 4h + j of hmask[l]) and 16 signed 6-bit scales (stored - 32):
+ * the low nibbles of bytes 0..7 and, above them, bit pairs of bytes 8..11
+ * (c:786-832). */
+static int q3_scale(const uint8_t* sc, int k) {
+    int low = k < 8 ? (sc[k] & 15) : (sc[k - 8] >> 4);
+    int high = (sc[8 + (k & 3)] >> (2 * (k >> 2))) & 3;
+    return (low | (high << 4)) - 32;
+}
+
+static void deq_q3_k(const uint8_t* src, float* dst, int cols) {
+    for (int b = 0; b < cols / QK_SUPER; ++b) {
+        const uint8_t* blk = src + (size_t)b * 110;
+        const uint8_t* hm = blk;
+        const uint8_t* qs = blk + 32;
+        const uint8_t* sc = blk + 96;
+        float d = l3po_fp16_to_fp32(rd16(blk + 108));
+        float* y = dst + (size_t)b * QK_SUPER;
+        for (int h = 0; h < 2; ++h)
+            for (int j = 0; j < 4; ++j)
+                for (int g = 0; g < 2; ++g) {
+                    float dl = d * q3_scale(sc, 8 * h + 2 * j + g);
+                    int bit = 4 * h + j;
+                    for (int l = 0; l < 16; ++l) {
+                        int i = 16 * g + l;
+                        int q = ((qs[32 * h + i] >> (2 * j)) & 3) - (((hm[i] >> bit) & 1) ? 0 : 4);
+                        y[128 * h + 32 * j + i] = dl * q;
+                    }
+                }
+    }
+}
+
 /* Q6_K: two halves of 128 values; value = d * scale * (6-bit q - 32), the 6
  * bits from a nibble of ql and two bits of qh (c:873-902). */
 static void deq_q6_k(const uint8_t* src, float* dst, int cols) {
@@ -544,7 +627,10 @@ int l3po_matvec(int type, const void* w, int rows, int cols, const float* x, flo
     for (int r = 0; r < rows; ++r) {
         const uint8_t* row = (const uint8_t*)w + (size_t)r * rb;
         if (type == L3P_W_Q8_0) deq_q8_0(row, buf, cols);
+        else if (type == L3P_W_Q2_K) deq_q2_k(row, buf, cols);
+        else if (type == L3P_W_Q3_K) deq_q3_k(row, buf, cols);
         else if (type == L3P_W_Q4_K) deq_q4_k(row, buf, cols);
+        else if (type == L3P_W_Q5_K) deq_q5_k(row, buf, cols);
         else deq_q6_k(row, buf, cols);
         float s = 0.0f;
         for (int j = 0; j < cols; ++j) s += buf[j] * x[j];

@@ -65,7 +65,10 @@ typedef struct {
 
 /* Weight types of the wo projection (GGUF tensor types, ggml numbering). */
 #define L3P_W_Q8_0 8  /* 34-byte blocks of 32: fp16 d, 32 int8 */
+#define L3P_W_Q2_K 10 /* 84-byte blocks of 256: 16 scale|min bytes, 64 bytes of 2-bit quants, fp16 d, dmin */
+#define L3P_W_Q3_K 11 /* 110-byte blocks of 256: 32 high-bit bytes, 64 bytes of 2-bit quants, 12 scale bytes, fp16 d */
 #define L3P_W_Q4_K 12 /* 144-byte blocks of 256: fp16 d, dmin, 12 scale bytes, 128 nibble bytes */
+#define L3P_W_Q5_K 13 /* 176-byte blocks of 256: fp16 d, dmin, 12 scale bytes, 32 high-bit bytes, 128 nibble bytes */
 #define L3P_W_Q6_K 14 /* 210-byte blocks of 256: 128 low-nibble, 64 high-bit, 16 int8 scales, fp16 d */
 
 /* ---- restatement (oracle/l3p_oracle.c) ---- */

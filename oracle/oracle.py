@@ -239,8 +239,9 @@ def rope(shape, layer: int, pos0: int, q: np.ndarray, k: np.ndarray, rope_theta:
     return q, k
 
 
-W_Q8_0, W_Q4_K, W_Q6_K = 8, 12, 14
-W_BLOCK = {W_Q8_0: (32, 34), W_Q4_K: (256, 144), W_Q6_K: (256, 210)}  # values, bytes per block
+W_Q8_0, W_Q2_K, W_Q3_K, W_Q4_K, W_Q5_K, W_Q6_K = 8, 10, 11, 12, 13, 14
+W_BLOCK = {W_Q8_0: (32, 34), W_Q2_K: (256, 84), W_Q3_K: (256, 110), W_Q4_K: (256, 144), W_Q5_K: (256, 176),
+           W_Q6_K: (256, 210)}  # values, bytes per block
 
 
 def w_row_bytes(wtype: int, cols: int) -> int:

@@ -116,12 +116,17 @@ def wo_cases():
         ("q4_k_9x2048", O.W_Q4_K, 9, 2048, 4),
         ("q6_k_40x4096", O.W_Q6_K, 40, 4096, 5),
         ("q6_k_7x2048", O.W_Q6_K, 7, 2048, 6),
+        ("q2_k_33x4096", O.W_Q2_K, 33, 4096, 7),
+        ("q3_k_35x4096", O.W_Q3_K, 35, 4096, 8),
+        ("q5_k_31x4096", O.W_Q5_K, 31, 4096, 9),
+        ("q5_k_5x2048", O.W_Q5_K, 5, 2048, 10),
     ]
 
 
 def write_wo_golden():
     """tests/golden/wo_golden.npz: the wo projection through the reference's
-    own matmul_quantized (dequantise rows, fp32 dots) for Q8_0, Q4_K, Q6_K."""
+    own matmul_quantized (dequantise rows, fp32 dots) for Q8_0, Q2_K, Q3_K,
+    Q4_K, Q5_K, Q6_K: the types with a row dequantiser (c:2063-2073)."""
     data = {}
     names = []
     for name, wt, rows, cols, seed in wo_cases():

@@ -70,7 +70,7 @@ def _worker(rank, world, port, wtype, out_dir):
 
 
 @pytest.mark.skipif(_n_gpus() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("wtype", [O.W_Q8_0, O.W_Q4_K, O.W_Q6_K])
+@pytest.mark.parametrize("wtype", [O.W_Q8_0, O.W_Q2_K, O.W_Q3_K, O.W_Q4_K, O.W_Q5_K, O.W_Q6_K])
 def test_wo_allreduce_over_nvlink(wtype):
     import torch.multiprocessing as mp
 

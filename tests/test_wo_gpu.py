@@ -18,7 +18,8 @@ from llama3pure_b200.synth import CONFIGS, GEMMA_SWA, raw_qkv_inputs, tolerance_
 pytestmark = pytest.mark.gpu
 
 WO_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "wo_golden.npz")
-TYPES = {"q8_0": O.W_Q8_0, "q4_k": O.W_Q4_K, "q6_k": O.W_Q6_K}
+TYPES = {"q8_0": O.W_Q8_0, "q2_k": O.W_Q2_K, "q3_k": O.W_Q3_K, "q4_k": O.W_Q4_K, "q5_k": O.W_Q5_K,
+         "q6_k": O.W_Q6_K}
 SHAPES = {
     "l8b": CONFIGS["llama31_8b_decode_8k"].with_(seq_len=64, n_layers=2),       # 4096 x 4096
     "l1b": CONFIGS["llama32_1b_decode"].with_(seq_len=64, n_layers=2),          # 2048 x 2048
