@@ -762,11 +762,12 @@ def parity_leg(job: Job):
         res["gemma_mqa_decode"] = {"workload": gs.name + " layer 0 (one GPU)", **_cmp(got, want)}
     del k, v
 
-    # the wo projection: 4096 x 4096 (Llama-3.1-8B), six GGUF types; at N > 1
+    # the wo projection: 4096 x 4096 (Llama-3.1-8B), every GGUF weight type; at N > 1
     # the tensor-parallel sum over NVLink on every rank, two steps
     dim = cols = sh.n_heads * sh.head_dim
     x = wo_input(cols, seed=7)
-    for name, wt in (("q8_0", 8), ("q2_k", 10), ("q3_k", 11), ("q4_k", 12), ("q5_k", 13), ("q6_k", 14)):
+    for name, wt in (("q8_0", 8), ("q2_k", 10), ("q3_k", 11), ("q4_k", 12), ("q5_k", 13), ("q6_k", 14), ("q4_0", 2),
+                     ("q4_1", 3), ("q5_0", 6), ("q5_1", 7), ("iq4_nl", 20), ("f32", 0), ("f16", 1), ("bf16", 29)):
         w = wo_weights(wt, dim, cols, seed=6)
         with AttnContext.for_shape(sh, n_layers=1, seq_len=16, device=job.local, kv_head_begin=me.kv_head_begin,
                                    kv_head_count=me.kv_head_count) as ctx:
@@ -1676,7 +1677,10 @@ def run_wo(args, torch, layers: int = 16):
     res = {"shape": f"{dim} x {cols}", "layers_cycled": layers, "peak_kind": peak_kind}
     for name, wt, nbytes in (("q8_0", 8, cols // 32 * 34), ("q2_k", 10, cols // 256 * 84),
                              ("q3_k", 11, cols // 256 * 110), ("q4_k", 12, cols // 256 * 144),
-                             ("q5_k", 13, cols // 256 * 176), ("q6_k", 14, cols // 256 * 210)):
+                             ("q5_k", 13, cols // 256 * 176), ("q6_k", 14, cols // 256 * 210),
+                             ("q4_0", 2, cols // 32 * 18), ("q4_1", 3, cols // 32 * 20), ("q5_0", 6, cols // 32 * 22),
+                             ("q5_1", 7, cols // 32 * 24), ("iq4_nl", 20, cols // 32 * 18), ("f32", 0, cols * 4),
+                             ("f16", 1, cols * 2), ("bf16", 29, cols * 2)):
         ctx = AttnContext.for_shape(sh, n_layers=layers, seq_len=16)
         ctx.set_stream(stream)
         w = wo_weights(wt, dim, cols, seed=5)

@@ -290,6 +290,14 @@ int l3p_attn_prefill_raw_dev(l3p_attn_ctx* ctx, int layer, int start_pos, int n_
  * fp32 dot products (matmul_quantized -> matmul_deq_4row, c:2091-2176, for
  * the types with a row dequantiser); the library multiplies the same values
  * in a different summation order (within 1e-4 of the reference). */
+#define L3P_W_F32 0     /* GGML_TYPE_F32 (c:96): float rows */
+#define L3P_W_F16 1     /* GGML_TYPE_F16 (c:97): fp16 rows */
+#define L3P_W_Q4_0 2    /* GGML_TYPE_Q4_0 (c:98): 18-byte blocks of 32 values */
+#define L3P_W_Q4_1 3    /* GGML_TYPE_Q4_1 (c:99): 20-byte blocks of 32 values */
+#define L3P_W_Q5_0 6    /* GGML_TYPE_Q5_0 (c:100): 22-byte blocks of 32 values */
+#define L3P_W_Q5_1 7    /* GGML_TYPE_Q5_1 (c:101): 24-byte blocks of 32 values */
+#define L3P_W_IQ4_NL 20 /* GGML_TYPE_IQ4_NL (c:110): 18-byte blocks of 32 values */
+#define L3P_W_BF16 29   /* GGML_TYPE_BF16 (c:111): bfloat16 rows */
 #define L3P_W_Q8_0 8  /* GGML_TYPE_Q8_0 (c:102): 34-byte blocks of 32 values */
 #define L3P_W_Q2_K 10 /* GGML_TYPE_Q2_K (c:104): 84-byte blocks of 256 values */
 #define L3P_W_Q3_K 11 /* GGML_TYPE_Q3_K (c:105): 110-byte blocks of 256 values */

@@ -95,7 +95,8 @@ struct l3p_attn_ctx {
   // weight rows in the device layout of wo.cuh, and the attention output
   // buffer of the combined host call
   struct WoLayer {
-    int type = 0;  // 0 = not set
+    bool set = false;  // l3p_attn_set_wo has been called for the layer
+    int type = 0;      // GGUF type number (0 is F32)
     int rows = 0;
     long long row_bytes = 0;
     int sc_stride = 0;  // bytes per row of Q8_0 scales
@@ -104,7 +105,7 @@ struct l3p_attn_ctx {
   };
   std::vector<WoLayer> wo;
   float* wo_x = nullptr;
-  int wo_ctas_per_sm[12] = {};  // (Q8_0, Q4_K, Q6_K, Q5_K, Q2_K, Q3_K) x (4, 8 warps)
+  int wo_ctas_per_sm[l3p::kWoKernelCount] = {};  // per wo GEMV kernel (l3p_wo.cu's table)
   // sequence group over NVLink (l3p_attn_seq_group_*): this context's exchange
   // region (flags, then per-layer partial slots; seq_xchg.cuh), the members'
   // regions mapped into this process, and the step counter

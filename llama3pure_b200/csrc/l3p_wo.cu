@@ -16,11 +16,21 @@ namespace {
 
 // The GEMV kernels, (format, 4 or 8 warps): index 2 * wo_format_index + (8 warps)
 using WoKernel = void (*)(const WoArgs);
-constexpr int kWoKernelCount = 12;
 const WoKernel kWoKernels[kWoKernelCount] = {
-    wo_gemv_kernel<WoQ8, 4>,  wo_gemv_kernel<WoQ8, 8>,  wo_gemv_kernel<WoQ4K, 4>, wo_gemv_kernel<WoQ4K, 8>,
-    wo_gemv_kernel<WoQ6K, 4>, wo_gemv_kernel<WoQ6K, 8>, wo_gemv_kernel<WoQ5K, 4>, wo_gemv_kernel<WoQ5K, 8>,
-    wo_gemv_kernel<WoQ2K, 4>, wo_gemv_kernel<WoQ2K, 8>, wo_gemv_kernel<WoQ3K, 4>, wo_gemv_kernel<WoQ3K, 8>};
+    wo_gemv_kernel<WoQ8, 4>,                wo_gemv_kernel<WoQ8, 8>,
+    wo_gemv_kernel<WoQ4K, 4>,               wo_gemv_kernel<WoQ4K, 8>,
+    wo_gemv_kernel<WoQ6K, 4>,               wo_gemv_kernel<WoQ6K, 8>,
+    wo_gemv_kernel<WoQ5K, 4>,               wo_gemv_kernel<WoQ5K, 8>,
+    wo_gemv_kernel<WoQ2K, 4>,               wo_gemv_kernel<WoQ2K, 8>,
+    wo_gemv_kernel<WoQ3K, 4>,               wo_gemv_kernel<WoQ3K, 8>,
+    wo_gemv_kernel<WoQ8x<kQxQ4_0>, 4>,      wo_gemv_kernel<WoQ8x<kQxQ4_0>, 8>,
+    wo_gemv_kernel<WoQ8x<kQxQ4_1>, 4>,      wo_gemv_kernel<WoQ8x<kQxQ4_1>, 8>,
+    wo_gemv_kernel<WoQ8x<kQxQ5_0>, 4>,      wo_gemv_kernel<WoQ8x<kQxQ5_0>, 8>,
+    wo_gemv_kernel<WoQ8x<kQxQ5_1>, 4>,      wo_gemv_kernel<WoQ8x<kQxQ5_1>, 8>,
+    wo_gemv_kernel<WoQ8x<kQxIQ4NL>, 4>,     wo_gemv_kernel<WoQ8x<kQxIQ4NL>, 8>,
+    wo_gemv_kernel<WoFloat<kFlF32>, 4>,     wo_gemv_kernel<WoFloat<kFlF32>, 8>,
+    wo_gemv_kernel<WoFloat<kFlF16>, 4>,     wo_gemv_kernel<WoFloat<kFlF16>, 8>,
+    wo_gemv_kernel<WoFloat<kFlBF16>, 4>,    wo_gemv_kernel<WoFloat<kFlBF16>, 8>};
 
 int wo_format_index(int type) {
   switch (type) {
@@ -29,7 +39,15 @@ int wo_format_index(int type) {
     case L3P_W_Q6_K: return 2;
     case L3P_W_Q5_K: return 3;
     case L3P_W_Q2_K: return 4;
-    default: return 5;  // L3P_W_Q3_K
+    case L3P_W_Q3_K: return 5;
+    case L3P_W_Q4_0: return 6;
+    case L3P_W_Q4_1: return 7;
+    case L3P_W_Q5_0: return 8;
+    case L3P_W_Q5_1: return 9;
+    case L3P_W_IQ4_NL: return 10;
+    case L3P_W_F32: return 11;
+    case L3P_W_F16: return 12;
+    default: return 13;  // L3P_W_BF16
   }
 }
 
@@ -90,7 +108,7 @@ int launch_wo(l3p_attn_ctx* ctx, int layer, const float* x, float* y, cudaStream
 
 int check_wo(l3p_attn_ctx* ctx, int layer) {
   if (int rc = check_layer(ctx, layer)) return rc;
-  if (ctx->wo.empty() || ctx->wo[layer].type == 0)
+  if (ctx->wo.empty() || !ctx->wo[layer].set)
     return fail(ctx, L3P_E_INVAL, "l3p_attn_set_wo has not been called for layer %d", layer);
   return L3P_OK;
 }
@@ -110,15 +128,25 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
     case L3P_W_Q4_K: vals = 256, bytes = 144, dev_bytes = 144; break;
     case L3P_W_Q5_K: vals = 256, bytes = 176, dev_bytes = WoQ5K::kBlockBytes; break;
     case L3P_W_Q6_K: vals = 256, bytes = 210, dev_bytes = WoQ6K::kBlockBytes; break;
+    case L3P_W_Q4_0:
+    case L3P_W_IQ4_NL: vals = 32, bytes = 18, dev_bytes = 16; break;
+    case L3P_W_Q4_1: vals = 32, bytes = 20, dev_bytes = 16; break;
+    case L3P_W_Q5_0: vals = 32, bytes = 22, dev_bytes = 16; break;
+    case L3P_W_Q5_1: vals = 32, bytes = 24, dev_bytes = 16; break;
+    case L3P_W_F32: vals = 1, bytes = 4, dev_bytes = 4; break;
+    case L3P_W_F16:
+    case L3P_W_BF16: vals = 1, bytes = 2, dev_bytes = 2; break;
     default:
       return fail(ctx, L3P_E_UNSUPPORTED,
-                  "wo weight type %d (Q8_0 = 8, Q2_K = 10, Q3_K = 11, Q4_K = 12, Q5_K = 13, Q6_K = 14 are supported)",
+                  "wo weight type %d (the GGUF types F32 = 0, F16 = 1, Q4_0 = 2, Q4_1 = 3, Q5_0 = 6, Q5_1 = 7, "
+                  "Q8_0 = 8, Q2_K .. Q6_K = 10 .. 14, IQ4_NL = 20, BF16 = 29 are supported)",
                   type);
   }
   const int hd = ctx->hd, cols = ctx->cfg.n_heads * hd;
   const int c_lo = ctx->cfg.kv_head_begin * ctx->G * hd, C = ctx->kvh_count * ctx->G * hd;
   const int max_c = 8 * (type == L3P_W_Q6_K ? WoQ6K::kSlice : WoQ8::kSlice);
-  if (cols % vals || c_lo % vals || C % vals || C > max_c)
+  // float rows: whole 32-column lane runs (a lane loads 32 values)
+  if (cols % vals || c_lo % vals || C % vals || C > max_c || (vals == 1 && (C % 32 || c_lo % 32)))
     return fail(ctx, L3P_E_UNSUPPORTED, "owned wo columns [%d, %d) do not fall on %d-value blocks or exceed %d", c_lo,
                 c_lo + C, vals, max_c);
   const uint8_t* src = static_cast<const uint8_t*>(rows);
@@ -138,6 +166,30 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
         sc[(size_t)r * sc_stride + 2 * b] = blk[0];  // fp16 scale, little-endian
         sc[(size_t)r * sc_stride + 2 * b + 1] = blk[1];
         memcpy(&w[(size_t)r * C + b * 32], blk + 2, 32);
+      }
+  } else if (vals == 1) {
+    // float rows: the owned columns as they are
+    row_bytes = (long long)C * bytes;
+    w.resize((size_t)dim * row_bytes);
+    for (int r = 0; r < dim; ++r)
+      memcpy(&w[(size_t)r * row_bytes], src + (size_t)r * src_row + (size_t)c_lo * bytes, (size_t)C * bytes);
+  } else if (vals == 32) {
+    // Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL: the 16 quant bytes of every block, and
+    // per block 8 bytes [d, m, qh] (m and qh 0 where the type has none)
+    row_bytes = (long long)nb * 16;
+    sc_stride = (int)(nb * 8);
+    w.resize((size_t)dim * row_bytes);
+    sc.assign((size_t)dim * sc_stride, 0);
+    const int m_off = (type == L3P_W_Q4_1 || type == L3P_W_Q5_1) ? 2 : -1;
+    const int qh_off = type == L3P_W_Q5_0 ? 2 : type == L3P_W_Q5_1 ? 4 : -1;
+    for (int r = 0; r < dim; ++r)
+      for (size_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = src + (size_t)r * src_row + (b0 + b) * bytes;
+        uint8_t* meta = &sc[(size_t)r * sc_stride + b * 8];
+        memcpy(meta, blk, 2);
+        if (m_off >= 0) memcpy(meta + 2, blk + m_off, 2);
+        if (qh_off >= 0) memcpy(meta + 4, blk + qh_off, 4);
+        memcpy(&w[(size_t)r * row_bytes + b * 16], blk + bytes - 16, 16);
       }
   } else {
     // K-quants: each GGUF block at the start of a 16-byte aligned device block
@@ -176,6 +228,7 @@ L3P_API int l3p_attn_set_wo(l3p_attn_ctx* ctx, int layer, int type, const void* 
   }
   L3P_CUDA(ctx, cudaMemcpy(L.w, w.data(), w.size(), cudaMemcpyHostToDevice));
   if (!sc.empty()) L3P_CUDA(ctx, cudaMemcpy(L.wsc, sc.data(), sc.size(), cudaMemcpyHostToDevice));
+  L.set = true;
   L.type = type;
   L.rows = dim;
   L.row_bytes = row_bytes;

@@ -10,6 +10,9 @@ namespace l3p {
 // GPU never share one; the host-call server uses slices 0 and 1 by call parity.
 constexpr int kScratchSlots = 4;
 
+// wo GEMV kernels: 14 weight formats x (4, 8 warps)
+constexpr int kWoKernelCount = 28;
+
 constexpr int kXchgMaxParts = 16;    // members of a sequence or tensor-parallel group
 constexpr int kXchgFlagBytes = 256;  // flags and step counter ahead of an exchange region's slots
 

@@ -2,13 +2,16 @@
 // `wo` projection xout = Wo . xb with GGUF-quantised weights (c:3362,
 // js:5191), tensor-parallel by head.
 //
-// The reference dequantises four weight rows at a time to fp32 and forms
-// fp32 dot products with xb (matmul_quantized -> matmul_deq_4row,
-// c:2091-2176) for the types that have a row dequantiser; those are the types
-// here:
-//   Q8_0  (34-byte blocks of 32)   value = d * q8                 (c:691-702)
-//   Q4_K  (144-byte blocks of 256) value = d*sc_j * q4 - dmin*m_j (c:704-746)
-//   Q6_K  (210-byte blocks of 256) value = d * sc_k * (q6 - 32)   (c:873-902)
+// The reference's matmul_quantized (c:2091-2132) takes one of three paths
+// per weight type, and so does this file:
+//   - row dequantiser, fp32 dots (matmul_deq_4row, c:2136-2176):
+//       Q8_0  (34-byte blocks of 32)   value = d * q8                 (c:691-702)
+//       Q2_K, Q3_K, Q5_K: the formats at WoQ2K, WoQ3K, WoQ5K (c:748-871)
+//       Q4_K  (144-byte blocks of 256) value = d*sc_j * q4 - dmin*m_j (c:704-746)
+//       Q6_K  (210-byte blocks of 256) value = d * sc_k * (q6 - 32)   (c:873-902)
+//   - x quantised to Q8_0, exact integer block dots: Q4_0, Q4_1, Q5_0, Q5_1,
+//     IQ4_NL (WoQ8x);
+//   - fp32 dots with the converted weights: F32, F16, BF16 (WoFloat).
 // The products are the same; the summation order is not (per lane, then
 // across lanes and warps; scale factors applied per sub-block), which moves
 // results by a few ulps of the row sum, inside the 1e-4 contract.
@@ -80,11 +83,18 @@ __device__ __forceinline__ float2 byte_pair(uint32_t w, int i, float bias) {
   return __fadd2_rn(make_float2(byte_f(w, i), byte_f(w, i + 1)), make_float2(-bias, -bias));
 }
 
-// Per-format lane work: the lane's columns, its loads of one row's slice and
-// the dot product.
+// Sums of x over the two 16-value runs of a lane (the formats with mins).
+struct WoSums {
+  float s[2];
+};
+
+// Per-format lane work: the lane's columns, its state of x (prepared once per
+// launch), its loads of one row's slice and the dot product.
+
 struct WoQ8 {
   static constexpr int kSlice = 1024;  // columns per warp slice
   static constexpr int kLaneCols = 32;
+  using X = WoSums;  // per-lane state of x, prepared once per launch
   static constexpr int kUnroll = 8;
   struct Raw {
     uint4 a, b;
@@ -107,7 +117,7 @@ struct WoQ8 {
       r.d1 = 0;
     }
   }
-  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&)[2]) {
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const WoSums&) {
     // int8 q: (q ^ 0x80) is q + 128 as an unsigned byte
     const uint32_t wa[4] = {r.a.x ^ 0x80808080u, r.a.y ^ 0x80808080u, r.a.z ^ 0x80808080u, r.a.w ^ 0x80808080u};
     const uint32_t wb[4] = {r.b.x ^ 0x80808080u, r.b.y ^ 0x80808080u, r.b.z ^ 0x80808080u, r.b.w ^ 0x80808080u};
@@ -122,12 +132,13 @@ struct WoQ8 {
     return fp16_to_f32(r.d0) * ((s[0].x + s[1].x) + (s[0].y + s[1].y)) +
            fp16_to_f32(r.d1) * ((t[0].x + t[1].x) + (t[0].y + t[1].y));
   }
-  __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
+  __device__ static void prep(const float (&)[kLaneCols], WoSums& xs) { xs.s[0] = xs.s[1] = 0.f; }
 };
 
 struct WoQ4K {
   static constexpr int kSlice = 1024;  // 4 blocks of 256
   static constexpr int kLaneCols = 32;
+  using X = WoSums;  // per-lane state of x, prepared once per launch
   static constexpr int kUnroll = 8;
   struct Raw {
     uint4 h;  // d, dmin, 12 scale bytes
@@ -160,7 +171,7 @@ struct WoQ4K {
       m = (sbyte(s0, s1, s2, j + 4) >> 4) | ((sbyte(s0, s1, s2, j) >> 6) << 4);
     }
   }
-  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&xs)[2]) {
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const WoSums& xs) {
     const int lane = threadIdx.x & 31, p = (lane & 7) >> 1;
     const float d = fp16_to_f32((uint16_t)(r.h.x & 0xffffu)), dmin = fp16_to_f32((uint16_t)(r.h.x >> 16));
     int sc0, m0, sc1, m1;
@@ -175,14 +186,14 @@ struct WoQ4K {
       hi = __ffma2_rn(byte_pair(h4, i % 4, kTwo23), make_float2(x[16 + i], x[17 + i]), hi);
     }
     return d * ((float)sc0 * (lo.x + lo.y) + (float)sc1 * (hi.x + hi.y)) -
-           dmin * ((float)m0 * xs[0] + (float)m1 * xs[1]);
+           dmin * ((float)m0 * xs.s[0] + (float)m1 * xs.s[1]);
   }
-  __device__ static void xsums(const float (&x)[kLaneCols], float (&xs)[2]) {
-    xs[0] = xs[1] = 0.f;
+  __device__ static void prep(const float (&x)[kLaneCols], WoSums& xs) {
+    xs.s[0] = xs.s[1] = 0.f;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      xs[0] += x[i];
-      xs[1] += x[16 + i];
+      xs.s[0] += x[i];
+      xs.s[1] += x[16 + i];
     }
   }
 };
@@ -194,6 +205,7 @@ struct WoQ4K {
 struct WoQ5K {
   static constexpr int kSlice = 1024;  // 4 blocks of 256
   static constexpr int kLaneCols = 32;
+  using X = WoSums;  // per-lane state of x, prepared once per launch
   static constexpr int kUnroll = 6;
   static constexpr int kBlockBytes = 176;
   struct Raw {
@@ -209,7 +221,7 @@ struct WoQ5K {
     r.qh = __ldg(reinterpret_cast<const uint4*>(blk + 16 + 16 * (lane & 1)));
     r.q = __ldg(reinterpret_cast<const uint4*>(blk + 48 + 16 * (lane & 7)));
   }
-  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&xs)[2]) {
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const WoSums& xs) {
     const int lane = threadIdx.x & 31, p = (lane & 7) >> 1;
     const float d = fp16_to_f32((uint16_t)(r.h.x & 0xffffu)), dmin = fp16_to_f32((uint16_t)(r.h.x >> 16));
     int sc0, m0, sc1, m1;
@@ -226,9 +238,9 @@ struct WoQ5K {
       hi = __ffma2_rn(byte_pair(h5, i % 4, kTwo23), make_float2(x[16 + i], x[17 + i]), hi);
     }
     return d * ((float)sc0 * (lo.x + lo.y) + (float)sc1 * (hi.x + hi.y)) -
-           dmin * ((float)m0 * xs[0] + (float)m1 * xs[1]);
+           dmin * ((float)m0 * xs.s[0] + (float)m1 * xs.s[1]);
   }
-  __device__ static void xsums(const float (&x)[kLaneCols], float (&xs)[2]) { WoQ4K::xsums(x, xs); }
+  __device__ static void prep(const float (&x)[kLaneCols], WoSums& xs) { WoQ4K::prep(x, xs); }
 };
 
 // Q2_K and Q3_K: per half h of a 256-value block, bit pair j of 32 quant
@@ -244,6 +256,7 @@ __device__ __forceinline__ int wo_k2_col(int lane, int i) {
 struct WoQ2K {
   static constexpr int kSlice = 1024;  // 4 blocks of 256
   static constexpr int kLaneCols = 32;
+  using X = WoSums;  // per-lane state of x, prepared once per launch
   static constexpr int kUnroll = 8;
   static constexpr int kBlockBytes = 96;
   struct Raw {
@@ -260,7 +273,7 @@ struct WoQ2K {
     r.sc = __ldg(reinterpret_cast<const uint16_t*>(blk + 8 * h + 2 * j));
     r.dd = __ldg(reinterpret_cast<const uint32_t*>(blk + 80));
   }
-  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&xs)[2]) {
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const WoSums& xs) {
     const int shift = 2 * (threadIdx.x & 3);
     const float d = fp16_to_f32((uint16_t)(r.dd & 0xffffu)), dmin = fp16_to_f32((uint16_t)(r.dd >> 16));
     const int s0 = r.sc & 0xff, s1 = r.sc >> 8;
@@ -274,9 +287,9 @@ struct WoQ2K {
                       hi);
     }
     return d * ((float)(s0 & 15) * (lo.x + lo.y) + (float)(s1 & 15) * (hi.x + hi.y)) -
-           dmin * ((float)(s0 >> 4) * xs[0] + (float)(s1 >> 4) * xs[1]);
+           dmin * ((float)(s0 >> 4) * xs.s[0] + (float)(s1 >> 4) * xs.s[1]);
   }
-  __device__ static void xsums(const float (&x)[kLaneCols], float (&xs)[2]) { WoQ4K::xsums(x, xs); }
+  __device__ static void prep(const float (&x)[kLaneCols], WoSums& xs) { WoQ4K::prep(x, xs); }
 };
 
 // Q3_K: value = (d * (s - 32)) * (q - 4 * !hbit), q 2-bit, hbit bit 4h + j of
@@ -287,6 +300,7 @@ struct WoQ2K {
 struct WoQ3K {
   static constexpr int kSlice = 1024;  // 4 blocks of 256
   static constexpr int kLaneCols = 32;
+  using X = WoSums;  // per-lane state of x, prepared once per launch
   static constexpr int kUnroll = 4;
   static constexpr int kBlockBytes = 112;
   struct Raw {
@@ -309,7 +323,7 @@ struct WoQ3K {
     const int high = (WoQ4K::sbyte(s.x, s.y, s.z, 8 + (k & 3)) >> (2 * (k >> 2))) & 3;
     return (low | (high << 4)) - 32;
   }
-  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&)[2]) {
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const WoSums&) {
     const int lane = threadIdx.x & 31, h = (lane >> 2) & 1, j = lane & 3;
     const int shift = 2 * j, bit = 4 * h + j;
     const float d = fp16_to_f32((uint16_t)(r.s.w & 0xffffu));
@@ -329,12 +343,13 @@ struct WoQ3K {
     }
     return d * ((float)sc0 * (lo.x + lo.y) + (float)sc1 * (hi.x + hi.y));
   }
-  __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
+  __device__ static void prep(const float (&)[kLaneCols], WoSums& xs) { xs.s[0] = xs.s[1] = 0.f; }
 };
 
 struct WoQ6K {
   static constexpr int kSlice = 2048;  // 8 blocks of 256
   static constexpr int kLaneCols = 64;
+  using X = WoSums;  // per-lane state of x, prepared once per launch
   static constexpr int kUnroll = 4;
   static constexpr int kBlockBytes = 224;
   struct Raw {
@@ -357,7 +372,7 @@ struct WoQ6K {
     r.sc = __ldg(reinterpret_cast<const uint2*>(blk + 192 + 8 * h));
     r.d = __ldg(reinterpret_cast<const uint16_t*>(blk + 208));
   }
-  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const float (&)[2]) {
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const WoSums&) {
     const int j = threadIdx.x & 1;
     const uint32_t a[4] = {r.l0.x, r.l0.y, r.l0.z, r.l0.w};
     const uint32_t b[4] = {r.l1.x, r.l1.y, r.l1.z, r.l1.w};
@@ -384,7 +399,155 @@ struct WoQ6K {
     return fp16_to_f32(r.d) * (sc(j) * (s0.x + s0.y) + sc(j + 2) * (s1.x + s1.y) + sc(j + 4) * (s2.x + s2.y) +
                                sc(j + 6) * (s3.x + s3.y));
   }
-  __device__ static void xsums(const float (&)[kLaneCols], float (&xs)[2]) { xs[0] = xs[1] = 0.f; }
+  __device__ static void prep(const float (&)[kLaneCols], WoSums& xs) { xs.s[0] = xs.s[1] = 0.f; }
+};
+
+// The types the reference multiplies with x quantised to Q8_0
+// (matmul_quantized's q8 path, c:2102-2116): x is quantised per 32-value
+// block exactly as quantize_row_q8_0 does (c:1508-1529, the cache quantiser's
+// steps, so the same int8 values and fp16 scale), and every weight block
+// gives an exact int32 sum of products, scaled as the reference does:
+//   Q4_0   dw*dx*isum, q = nibble - 8                (c:1625-1643)
+//   Q4_1   dw*dx*isum + mw*dx*xsum, q = nibble       (c:1646-1665)
+//   Q5_0   dw*dx*isum, q = (nibble | qh bit << 4) - 16 (c:1668-1690)
+//   Q5_1   dw*dx*isum + mw*dx*xsum, q = nibble | qh bit << 4 (c:1693-1717)
+//   IQ4_NL dw*dx*isum, q = the format's table at the nibble (c:1994-2013)
+// Lane l takes one block, columns [32l, 32l+32) of its slice.  Device layout:
+// the quant bytes [dim][C/32][16], then per block 8 bytes [d, m, qh] in `wsc`
+// ([dim][sc_stride]).
+enum : int { kQxQ4_0, kQxQ4_1, kQxQ5_0, kQxQ5_1, kQxIQ4NL };
+
+struct WoQ8xState {
+  uint32_t q[8];  // the lane's 32 int8 values of x, packed
+  float dx;       // their fp16 scale, as a float
+  int xsum;       // their sum
+};
+
+// four 4-bit values t (bits 0..3) -> bit 0 of bytes 0..3
+__device__ __forceinline__ uint32_t spread4(uint32_t t) { return (t * 0x00204081u) & 0x01010101u; }
+
+// IQ4_NL's 16 values (the format's table, c:204-206)
+constexpr int8_t kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+__host__ __device__ constexpr uint32_t iq4nl_word(int i) {
+  return (uint32_t)(uint8_t)kIq4nl[i] | (uint32_t)(uint8_t)kIq4nl[i + 1] << 8 |
+         (uint32_t)(uint8_t)kIq4nl[i + 2] << 16 | (uint32_t)(uint8_t)kIq4nl[i + 3] << 24;
+}
+
+// IQ4_NL: the table value of each byte of w (each 0..15), as signed bytes
+__device__ __forceinline__ uint32_t iq4nl_lookup(uint32_t w) {
+  // two permute tables of 8 entries
+  constexpr uint32_t t0 = iq4nl_word(0), t1 = iq4nl_word(4), t2 = iq4nl_word(8), t3 = iq4nl_word(12);
+  const uint32_t sel = (w & 7u) | ((w >> 4) & 0x70u) | ((w >> 8) & 0x700u) | ((w >> 12) & 0x7000u);
+  const uint32_t lo = __byte_perm(t0, t1, sel), hi = __byte_perm(t2, t3, sel);
+  const uint32_t m = ((w >> 3) & 0x01010101u) * 0xffu;  // bytes with bit 3 set take the high table
+  return (lo & ~m) | (hi & m);
+}
+
+template <int T>
+struct WoQ8x {
+  static constexpr int kSlice = 1024;
+  static constexpr int kLaneCols = 32;
+  using X = WoQ8xState;
+  static constexpr int kUnroll = 8;
+  struct Raw {
+    uint4 q;     // 16 quant bytes: byte j holds values j (low nibble) and j + 16 (high)
+    uint2 meta;  // fp16 d | fp16 m << 16, qh
+  };
+  __device__ static int col(int lane, int i) { return 32 * lane + i; }
+  __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
+    const int lane = threadIdx.x & 31;
+    const long long b = c0 / 32 + lane;
+    r.q = __ldg(reinterpret_cast<const uint4*>(p.w + (long long)row * p.row_bytes + b * 16));
+    r.meta = __ldg(reinterpret_cast<const uint2*>(p.wsc + (long long)row * p.sc_stride + b * 8));
+  }
+  __device__ static void prep(const float (&x)[kLaneCols], X& xs) {
+    xs.dx = fp16_to_f32(q8_quantize_lanes<32>(x, xs.q));
+    int sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sum = __dp4a((int)xs.q[k], 0x01010101, sum);
+    xs.xsum = sum;
+  }
+  __device__ static float dot(const Raw& r, const float (&)[kLaneCols], const X& xs) {
+    const uint32_t q[4] = {r.q.x, r.q.y, r.q.z, r.q.w};
+    const uint32_t qh = r.meta.y;
+    int isum = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint32_t lo = q[k] & 0x0f0f0f0fu, hi = (q[k] >> 4) & 0x0f0f0f0fu;  // values 4k.. and 16+4k..
+      if constexpr (T == kQxQ5_0 || T == kQxQ5_1) {
+        lo |= spread4((qh >> (4 * k)) & 15u) << 4;
+        hi |= spread4((qh >> (16 + 4 * k)) & 15u) << 4;
+      }
+      if constexpr (T == kQxIQ4NL) {
+        lo = iq4nl_lookup(lo);
+        hi = iq4nl_lookup(hi);
+      }
+      isum = __dp4a((int)lo, (int)xs.q[k], isum);
+      isum = __dp4a((int)hi, (int)xs.q[4 + k], isum);
+    }
+    if constexpr (T == kQxQ4_0) isum -= 8 * xs.xsum;
+    if constexpr (T == kQxQ5_0) isum -= 16 * xs.xsum;
+    const float dw = fp16_to_f32((uint16_t)(r.meta.x & 0xffffu));
+    if constexpr (T == kQxQ4_1 || T == kQxQ5_1) {
+      const float mw = fp16_to_f32((uint16_t)(r.meta.x >> 16));
+      return dw * xs.dx * (float)isum + mw * xs.dx * (float)xs.xsum;
+    } else {
+      return dw * xs.dx * (float)isum;
+    }
+  }
+};
+
+// F32 / F16 / BF16 rows: fp32 products with x (vec_dot_f32 / vec_dot_f16 /
+// vec_dot_bf16, c:1467-1494).  Lane l takes columns [32l, 32l+32) of its
+// slice; device layout: the owned columns of each row as they are.
+enum : int { kFlF32, kFlF16, kFlBF16 };
+
+template <int T>
+struct WoFloat {
+  static constexpr int kSlice = 1024;
+  static constexpr int kLaneCols = 32;
+  using X = WoSums;
+  static constexpr int kWords = T == kFlF32 ? 8 : 4;  // 16-byte loads per lane and row
+  static constexpr int kUnroll = T == kFlF32 ? 2 : 4;
+  struct Raw {
+    uint4 v[kWords];
+  };
+  __device__ static int col(int lane, int i) { return 32 * lane + i; }
+  __device__ static void load(const WoArgs& p, int row, int c0, Raw& r) {
+    const int lane = threadIdx.x & 31;
+    const uint4* s = reinterpret_cast<const uint4*>(p.w + (long long)row * p.row_bytes +
+                                                   (long long)(c0 + 32 * lane) * (T == kFlF32 ? 4 : 2));
+#pragma unroll
+    for (int k = 0; k < kWords; ++k) r.v[k] = __ldg(s + k);
+  }
+  __device__ static void prep(const float (&)[kLaneCols], X& xs) { xs.s[0] = xs.s[1] = 0.f; }
+  __device__ static float dot(const Raw& r, const float (&x)[kLaneCols], const X&) {
+    float2 a = make_float2(0.f, 0.f), b = a;
+#pragma unroll
+    for (int k = 0; k < kWords; ++k) {
+      const uint32_t w[4] = {r.v[k].x, r.v[k].y, r.v[k].z, r.v[k].w};
+      if constexpr (T == kFlF32) {
+        a = __ffma2_rn(make_float2(__uint_as_float(w[0]), __uint_as_float(w[1])), make_float2(x[4 * k], x[4 * k + 1]), a);
+        b = __ffma2_rn(make_float2(__uint_as_float(w[2]), __uint_as_float(w[3])),
+                       make_float2(x[4 * k + 2], x[4 * k + 3]), b);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 f;
+          if constexpr (T == kFlF16) {
+            f = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+          } else {
+            f = make_float2(__uint_as_float(w[e] << 16), __uint_as_float(w[e] & 0xffff0000u));
+          }
+          if (e % 2 == 0)
+            a = __ffma2_rn(f, make_float2(x[8 * k + 2 * e], x[8 * k + 2 * e + 1]), a);
+          else
+            b = __ffma2_rn(f, make_float2(x[8 * k + 2 * e], x[8 * k + 2 * e + 1]), b);
+        }
+      }
+    }
+    return (a.x + a.y) + (b.x + b.y);
+  }
 };
 
 // Tensor-parallel sum of the partial projections over NVLink, in the tail of
@@ -480,7 +643,7 @@ __global__ void __launch_bounds__(NW * 32) wo_gemv_kernel(const WoArgs p) {
   pdl_wait();
   trace_stamp(p.trace, 1);
   float x[F::kLaneCols];
-  float xs[2];
+  typename F::X xs;
   // the lane's columns come in runs of 16 consecutive values (x = 0 past C)
 #pragma unroll
   for (int i = 0; i < F::kLaneCols; i += 4) {
@@ -491,7 +654,7 @@ __global__ void __launch_bounds__(NW * 32) wo_gemv_kernel(const WoArgs p) {
     x[i + 2] = t.z;
     x[i + 3] = t.w;
   }
-  F::xsums(x, xs);
+  F::prep(x, xs);
 
   for (int t0 = 0; t0 < n_my; t0 += U) {
     float acc[U];

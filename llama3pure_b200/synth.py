@@ -122,8 +122,10 @@ def raw_qkv_inputs(shape: AttnShape, layer: int, n_tok: int):
     return q, k, v, q_norm, k_norm
 
 
-# GGUF type -> (values, bytes) per block: Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K
-W_BLOCK = {8: (32, 34), 10: (256, 84), 11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210)}
+# GGUF type -> (values, bytes) per block: F32, F16, Q4_0, Q4_1, Q5_0, Q5_1,
+# Q8_0, Q2_K, Q3_K, Q4_K, Q5_K, Q6_K, IQ4_NL, BF16
+W_BLOCK = {0: (1, 4), 1: (1, 2), 2: (32, 18), 3: (32, 20), 6: (32, 22), 7: (32, 24), 8: (32, 34), 10: (256, 84),
+           11: (256, 110), 12: (256, 144), 13: (256, 176), 14: (256, 210), 20: (32, 18), 29: (1, 2)}
 
 
 def wo_weights(wtype: int, rows: int, cols: int, seed: int, scale: float = 0.02) -> np.ndarray:
@@ -140,6 +142,21 @@ def wo_weights(wtype: int, rows: int, cols: int, seed: int, scale: float = 0.02)
         return np.ascontiguousarray(np.asarray(a, np.float16)).view(np.uint8).reshape(a.shape + (2,))
 
     shp = (rows, cols // n)
+    if wtype in (0, 1, 29):
+        # float rows: the values themselves, ~N(0, scale)
+        v = g.standard_normal((rows, cols)).astype(np.float32) * np.float32(scale)
+        if wtype == 0:
+            return np.ascontiguousarray(v.view(np.uint8).reshape(rows, -1))
+        if wtype == 1:
+            return np.ascontiguousarray(v.astype(np.float16).view(np.uint8).reshape(rows, -1))
+        return np.ascontiguousarray((v.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8).reshape(rows, -1))
+    if wtype in (2, 3, 6, 7, 20):
+        # 32-value blocks: d (and m) first; q 4-bit (5 with qh), IQ4_NL table values up to 127
+        qmax = {2: 8.0, 3: 15.0, 6: 16.0, 7: 31.0, 20: 127.0}[wtype]
+        blocks[..., 0:2] = f16(g.uniform(0.5, 1.5, shp) * scale * 3.0 / qmax)
+        if wtype in (3, 7):
+            blocks[..., 2:4] = f16(-g.uniform(0.5, 1.5, shp) * scale * 3.0 / 2.0)
+        return np.ascontiguousarray(blocks.reshape(rows, -1))
     if wtype == 8:
         blocks[..., 0:2] = f16(g.uniform(2.0, 4.0, shp) * scale / 127.0)
     elif wtype == 12:

@@ -455,6 +455,14 @@ int l3po_rope(const l3p_oracle_cfg* cfg, const l3p_oracle_rope* rope, int layer,
 
 long long l3po_w_row_bytes(int type, int cols) {
     switch (type) {
+        case L3P_W_F32: return (long long)cols * 4;
+        case L3P_W_F16:
+        case L3P_W_BF16: return (long long)cols * 2;
+        case L3P_W_Q4_0:
+        case L3P_W_IQ4_NL: return (long long)(cols / 32) * 18;
+        case L3P_W_Q4_1: return (long long)(cols / 32) * 20;
+        case L3P_W_Q5_0: return (long long)(cols / 32) * 22;
+        case L3P_W_Q5_1: return (long long)(cols / 32) * 24;
         case L3P_W_Q8_0: return (long long)(cols / 32) * 34;
         case L3P_W_Q2_K: return (long long)(cols / QK_SUPER) * 84;
         case L3P_W_Q3_K: return (long long)(cols / QK_SUPER) * 110;
@@ -619,9 +627,99 @@ static void deq_q6_k(const uint8_t* src, float* dst, int cols) {
     }
 }
 
+/* The types without a row dequantiser take the reference's other two paths
+ * of matmul_quantized (c:2102-2132): */
+
+/* IQ4_NL's 16 non-linear values (the format's table, c:204-206). */
+static const int8_t kIq4nl[16] = {-127, -104, -83, -65, -49, -35, -22, -10, 1, 13, 25, 38, 53, 69, 89, 113};
+
+/* Q4_0 / Q4_1 / Q5_0 / Q5_1 / IQ4_NL: x quantised to Q8_0 once
+ * (quantize_row_q8_0, c:1508-1529: the cache quantiser's steps), then per
+ * row and 32-value block an exact int32 sum of products, accumulated in fp32
+ * in block order as dw*dx*isum (+ mw*dx*xsum with a min), as
+ * vec_dot_{q4_0,q4_1,q5_0,q5_1,iq4_nl}_q8_0 (c:1625-1717, c:1994-2013). */
+static float q8x_row_dot(int type, const uint8_t* row, const uint8_t* xq, int cols) {
+    float sum = 0.0f;
+    for (int b = 0; b < cols / 32; ++b) {
+        const uint8_t* xb = xq + (size_t)b * QBLOCK;
+        const int8_t* xs = (const int8_t*)(xb + 2);
+        float dx = block_scale(xb);
+        const uint8_t* blk;
+        float dw, mw = 0.0f;
+        uint32_t qh = 0;
+        const uint8_t* qs;
+        switch (type) {
+            case L3P_W_Q4_0:
+            case L3P_W_IQ4_NL: blk = row + (size_t)b * 18; qs = blk + 2; break;
+            case L3P_W_Q4_1: blk = row + (size_t)b * 20; qs = blk + 4; mw = l3po_fp16_to_fp32(rd16(blk + 2)); break;
+            case L3P_W_Q5_0:
+                blk = row + (size_t)b * 22;
+                qh = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) | ((uint32_t)blk[5] << 24);
+                qs = blk + 6;
+                break;
+            default: /* Q5_1 */
+                blk = row + (size_t)b * 24;
+                mw = l3po_fp16_to_fp32(rd16(blk + 2));
+                qh = (uint32_t)blk[4] | ((uint32_t)blk[5] << 8) | ((uint32_t)blk[6] << 16) | ((uint32_t)blk[7] << 24);
+                qs = blk + 8;
+                break;
+        }
+        dw = l3po_fp16_to_fp32(rd16(blk));
+        int isum = 0, xsum = 0;
+        for (int j = 0; j < 16; ++j) {
+            int lo = qs[j] & 15, hi = qs[j] >> 4;
+            switch (type) {
+                case L3P_W_Q4_0: lo -= 8; hi -= 8; break;
+                case L3P_W_IQ4_NL: lo = kIq4nl[lo]; hi = kIq4nl[hi]; break;
+                case L3P_W_Q5_0: lo = (lo | (((qh >> j) & 1) << 4)) - 16; hi = (hi | (((qh >> (j + 16)) & 1) << 4)) - 16; break;
+                case L3P_W_Q5_1: lo |= ((qh >> j) & 1) << 4; hi |= ((qh >> (j + 16)) & 1) << 4; break;
+                default: break; /* Q4_1 */
+            }
+            isum += xs[j] * lo + xs[j + 16] * hi;
+            xsum += xs[j] + xs[j + 16];
+        }
+        if (type == L3P_W_Q4_1 || type == L3P_W_Q5_1)
+            sum += dw * dx * (float)isum + mw * dx * (float)xsum;
+        else
+            sum += dw * dx * (float)isum;
+    }
+    return sum;
+}
+
+/* F32 / F16 / BF16: fp32 products of x and the converted weight, summed in
+ * index order (vec_dot_f16 / vec_dot_bf16 / vec_dot_f32, c:1467-1494). */
+static float float_row_dot(int type, const uint8_t* row, const float* x, int cols) {
+    float sum = 0.0f;
+    for (int i = 0; i < cols; ++i) {
+        float w;
+        if (type == L3P_W_F32) {
+            memcpy(&w, row + (size_t)i * 4, 4);
+        } else if (type == L3P_W_F16) {
+            w = l3po_fp16_to_fp32(rd16(row + (size_t)i * 2));
+        } else {
+            uint32_t u = (uint32_t)rd16(row + (size_t)i * 2) << 16;
+            memcpy(&w, &u, 4);
+        }
+        sum += x[i] * w;
+    }
+    return sum;
+}
+
 int l3po_matvec(int type, const void* w, int rows, int cols, const float* x, float* out) {
     long long rb = l3po_w_row_bytes(type, cols);
     if (rb <= 0 || !w || !x || !out || rows < 0) return -1;
+    if (type == L3P_W_F32 || type == L3P_W_F16 || type == L3P_W_BF16) {
+        for (int r = 0; r < rows; ++r) out[r] = float_row_dot(type, (const uint8_t*)w + (size_t)r * rb, x, cols);
+        return 0;
+    }
+    if (type == L3P_W_Q4_0 || type == L3P_W_Q4_1 || type == L3P_W_Q5_0 || type == L3P_W_Q5_1 || type == L3P_W_IQ4_NL) {
+        uint8_t* xq = (uint8_t*)malloc((size_t)(cols / 32) * QBLOCK);
+        if (!xq) return -4;
+        l3po_q8_quantize(x, xq, cols);
+        for (int r = 0; r < rows; ++r) out[r] = q8x_row_dot(type, (const uint8_t*)w + (size_t)r * rb, xq, cols);
+        free(xq);
+        return 0;
+    }
     float* buf = (float*)malloc(sizeof(float) * (size_t)cols);
     if (!buf) return -4;
     for (int r = 0; r < rows; ++r) {

@@ -64,6 +64,14 @@ typedef struct {
 } l3p_oracle_rope;
 
 /* Weight types of the wo projection (GGUF tensor types, ggml numbering). */
+#define L3P_W_F32 0     /* float rows */
+#define L3P_W_F16 1     /* fp16 rows */
+#define L3P_W_Q4_0 2    /* 18-byte blocks of 32: fp16 d, 16 nibble bytes (q - 8) */
+#define L3P_W_Q4_1 3    /* 20-byte blocks of 32: fp16 d, m, 16 nibble bytes */
+#define L3P_W_Q5_0 6    /* 22-byte blocks of 32: fp16 d, 4 high-bit bytes, 16 nibble bytes (q - 16) */
+#define L3P_W_Q5_1 7    /* 24-byte blocks of 32: fp16 d, m, 4 high-bit bytes, 16 nibble bytes */
+#define L3P_W_IQ4_NL 20 /* 18-byte blocks of 32: fp16 d, 16 nibble bytes indexing a 16-value table */
+#define L3P_W_BF16 29   /* bfloat16 rows */
 #define L3P_W_Q8_0 8  /* 34-byte blocks of 32: fp16 d, 32 int8 */
 #define L3P_W_Q2_K 10 /* 84-byte blocks of 256: 16 scale|min bytes, 64 bytes of 2-bit quants, fp16 d, dmin */
 #define L3P_W_Q3_K 11 /* 110-byte blocks of 256: 32 high-bit bytes, 64 bytes of 2-bit quants, 12 scale bytes, fp16 d */

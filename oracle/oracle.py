@@ -239,9 +239,12 @@ def rope(shape, layer: int, pos0: int, q: np.ndarray, k: np.ndarray, rope_theta:
     return q, k
 
 
+W_F32, W_F16, W_Q4_0, W_Q4_1, W_Q5_0, W_Q5_1 = 0, 1, 2, 3, 6, 7
 W_Q8_0, W_Q2_K, W_Q3_K, W_Q4_K, W_Q5_K, W_Q6_K = 8, 10, 11, 12, 13, 14
-W_BLOCK = {W_Q8_0: (32, 34), W_Q2_K: (256, 84), W_Q3_K: (256, 110), W_Q4_K: (256, 144), W_Q5_K: (256, 176),
-           W_Q6_K: (256, 210)}  # values, bytes per block
+W_IQ4_NL, W_BF16 = 20, 29
+W_BLOCK = {W_F32: (1, 4), W_F16: (1, 2), W_BF16: (1, 2), W_Q4_0: (32, 18), W_Q4_1: (32, 20), W_Q5_0: (32, 22),
+           W_Q5_1: (32, 24), W_IQ4_NL: (32, 18), W_Q8_0: (32, 34), W_Q2_K: (256, 84), W_Q3_K: (256, 110),
+           W_Q4_K: (256, 144), W_Q5_K: (256, 176), W_Q6_K: (256, 210)}  # values, bytes per block
 
 
 def w_row_bytes(wtype: int, cols: int) -> int:

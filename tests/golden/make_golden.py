@@ -120,13 +120,24 @@ def wo_cases():
         ("q3_k_35x4096", O.W_Q3_K, 35, 4096, 8),
         ("q5_k_31x4096", O.W_Q5_K, 31, 4096, 9),
         ("q5_k_5x2048", O.W_Q5_K, 5, 2048, 10),
+        ("q4_0_29x4096", O.W_Q4_0, 29, 4096, 11),
+        ("q4_1_27x4096", O.W_Q4_1, 27, 4096, 12),
+        ("q5_0_25x4096", O.W_Q5_0, 25, 4096, 13),
+        ("q5_1_23x4096", O.W_Q5_1, 23, 4096, 14),
+        ("iq4_nl_21x4096", O.W_IQ4_NL, 21, 4096, 15),
+        ("q4_0_6x2048", O.W_Q4_0, 6, 2048, 16),
+        ("f32_19x4096", O.W_F32, 19, 4096, 17),
+        ("f16_17x4096", O.W_F16, 17, 4096, 18),
+        ("bf16_15x4096", O.W_BF16, 15, 4096, 19),
     ]
 
 
 def write_wo_golden():
     """tests/golden/wo_golden.npz: the wo projection through the reference's
-    own matmul_quantized (dequantise rows, fp32 dots) for Q8_0, Q2_K, Q3_K,
-    Q4_K, Q5_K, Q6_K: the types with a row dequantiser (c:2063-2073)."""
+    own matmul_quantized for every GGUF weight type it reads: dequantised rows
+    and fp32 dots for Q8_0 and the K-quants (c:2063-2073), x quantised to Q8_0
+    and integer block dots for Q4_0, Q4_1, Q5_0, Q5_1, IQ4_NL, fp32 dots for
+    F32, F16, BF16 (c:2091-2132)."""
     data = {}
     names = []
     for name, wt, rows, cols, seed in wo_cases():

@@ -240,7 +240,7 @@ def _wo_names():
 
 @pytest.mark.parametrize("name", _wo_names())
 def test_wo_matvec_matches_golden(name):
-    """Dequantise-then-dot of Q8_0 / Q2_K / Q3_K / Q4_K / Q5_K / Q6_K rows, bit for bit against the
+    """The wo projection of every GGUF weight type the reference reads, bit for bit against the
     reference's own matmul_quantized (golden from oracle/_ref)."""
     from llama3pure_b200.synth import wo_input, wo_weights
 
@@ -254,7 +254,8 @@ def test_wo_matvec_matches_golden(name):
 
 
 @pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built (needs the reference source)")
-@pytest.mark.parametrize("wt", [O.W_Q8_0, O.W_Q2_K, O.W_Q3_K, O.W_Q4_K, O.W_Q5_K, O.W_Q6_K])
+@pytest.mark.parametrize("wt", [O.W_Q8_0, O.W_Q2_K, O.W_Q3_K, O.W_Q4_K, O.W_Q5_K, O.W_Q6_K, O.W_Q4_0, O.W_Q4_1,
+                                O.W_Q5_0, O.W_Q5_1, O.W_IQ4_NL, O.W_F32, O.W_F16, O.W_BF16])
 def test_wo_port_bit_identical_to_reference(wt):
     from llama3pure_b200.synth import wo_weights
 

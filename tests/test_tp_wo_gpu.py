@@ -70,7 +70,8 @@ def _worker(rank, world, port, wtype, out_dir):
 
 
 @pytest.mark.skipif(_n_gpus() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("wtype", [O.W_Q8_0, O.W_Q2_K, O.W_Q3_K, O.W_Q4_K, O.W_Q5_K, O.W_Q6_K])
+@pytest.mark.parametrize("wtype", [O.W_Q8_0, O.W_Q2_K, O.W_Q3_K, O.W_Q4_K, O.W_Q5_K, O.W_Q6_K, O.W_Q4_0, O.W_Q4_1,
+                                   O.W_Q5_0, O.W_Q5_1, O.W_IQ4_NL, O.W_F32, O.W_F16, O.W_BF16])
 def test_wo_allreduce_over_nvlink(wtype):
     import torch.multiprocessing as mp
 

@@ -19,7 +19,8 @@ pytestmark = pytest.mark.gpu
 
 WO_GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "wo_golden.npz")
 TYPES = {"q8_0": O.W_Q8_0, "q2_k": O.W_Q2_K, "q3_k": O.W_Q3_K, "q4_k": O.W_Q4_K, "q5_k": O.W_Q5_K,
-         "q6_k": O.W_Q6_K}
+         "q6_k": O.W_Q6_K, "q4_0": O.W_Q4_0, "q4_1": O.W_Q4_1, "q5_0": O.W_Q5_0, "q5_1": O.W_Q5_1,
+         "iq4_nl": O.W_IQ4_NL, "f32": O.W_F32, "f16": O.W_F16, "bf16": O.W_BF16}
 SHAPES = {
     "l8b": CONFIGS["llama31_8b_decode_8k"].with_(seq_len=64, n_layers=2),       # 4096 x 4096
     "l1b": CONFIGS["llama32_1b_decode"].with_(seq_len=64, n_layers=2),          # 2048 x 2048
@@ -221,7 +222,7 @@ def test_wo_errors():
             ctx.wo(0, np.zeros(2048, np.float32))
         assert e.value.code == -1  # set_wo not called
         with pytest.raises(AttnError) as e:
-            ctx.set_wo(0, 2, np.zeros((4, 2048 // 32 * 18), np.uint8))  # Q4_0: no row dequantiser path here
+            ctx.set_wo(0, 9, np.zeros((4, 2048 // 32 * 36), np.uint8))  # Q8_1: no matmul path in the reference
         assert e.value.code == -6
     # hd 64, one KV head of 4 q heads owns columns [256, 512): whole Q4_K blocks
     with AttnContext.for_shape(sh, kv_head_begin=1, kv_head_count=1) as ctx:
