@@ -211,7 +211,10 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
   extern __shared__ __align__(128) unsigned char smem_raw[];
   float* ring = reinterpret_cast<float*>(smem_raw);
   __shared__ DecodeMergeSmem<GT, C::kWarps> ms;
-  __shared__ __align__(16) float s_p[C::kWarps][C::kR * GT];  // softmax weights of the current tile
+  // per row of the current tile, block of the row and q head: softmax weight
+  // times the V block's scale, the factor accumulator += int8 v * factor uses
+  constexpr int kNB = HD / 32;
+  __shared__ __align__(16) float s_w[C::kWarps][C::kR][kNB][GT];
 
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -444,42 +447,31 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
 #pragma unroll
       for (int e = 0; e < C::kEPL; ++e) acc[g][e] *= alpha;
     }
-    float* sp = s_p[warp];
-    if (sg == 0) {
+    // lane sg of a row's 8 (each holds the row's weights of every head)
+    // takes block sg of the row: its scale times each head's weight
+    float (*sw)[kNB][GT] = s_w[warp];
+    if (sg < kNB) {
 #pragma unroll
-      for (int pp = 0; pp < C::kR / 4; ++pp)
+      for (int pp = 0; pp < C::kR / 4; ++pp) {
+        const int r = rq + 4 * pp;
+        const float dvb = fp16_to_f32(vst[r * kNB + sg]);
 #pragma unroll
-        for (int g = 0; g < GT; ++g) sp[(rq + 4 * pp) * GT + g] = sc[pp][g];
+        for (int g = 0; g < GT; ++g) sw[r][sg][g] = dvb * sc[pp][g];
+      }
     }
     __syncwarp();
     // ---- values: 32 lanes per V row, lane_elem layout ----
 #pragma unroll
     for (int r = 0; r < C::kR; ++r) {
-      float pr[GT];
-      if constexpr (GT >= 4) {
-#pragma unroll
-        for (int g = 0; g < GT; g += 4) {
-          const float4 t = lds128(sp + r * GT + g);
-          pr[g] = t.x;
-          pr[g + 1] = t.y;
-          pr[g + 2] = t.z;
-          pr[g + 3] = t.w;
-        }
-      } else {
-#pragma unroll
-        for (int g = 0; g < GT; ++g) pr[g] = sp[r * GT + g];
-      }
       // int8 -> fp32 exactly, two values per instruction: byte b + 128 as the
       // low mantissa byte of 2^23, minus 2^23 + 128
       float2 vx[C::kEPL / 2];
-      float dv[(C::kEPL + 3) / 4];
       const float2 kBias = make_float2(-8388736.0f, -8388736.0f);
       if constexpr (HD == 64) {
         const uint32_t t = *reinterpret_cast<const uint16_t*>(vt + r * HD + 2 * lane) ^ 0x8080u;
         vx[0] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(t, 0x4B000000u, 0x7540)),
                                        __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7541))),
                            kBias);
-        dv[0] = fp16_to_f32(vst[r * (HD / 32) + lane / 16]);
       } else {
 #pragma unroll
         for (int c = 0; c < HD / 128; ++c) {
@@ -490,23 +482,41 @@ __global__ void __launch_bounds__(DecodeQ8Cfg<HD, GT>::kThreads, DecodeQ8Cfg<HD,
           vx[2 * c + 1] = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(t, 0x4B000000u, 0x7542)),
                                                  __uint_as_float(__byte_perm(t, 0x4B000000u, 0x7543))),
                                      kBias);
-          dv[c] = fp16_to_f32(vst[r * (HD / 32) + c * 4 + lane / 8]);
         }
       }
       // acc += v * (block scale * weight), as c:1605; the packed FMA rounds
-      // each half like fmaf
+      // each half like fmaf.  Value e of the lane lies in block
+      // HD == 64 ? lane / 16 : (e / 4) * 4 + lane / 8.
 #pragma unroll
-      for (int g = 0; g < GT; ++g) {
+      for (int c = 0; c < (C::kEPL + 3) / 4; ++c) {
+        const int b = HD == 64 ? lane / 16 : c * 4 + lane / 8;
+        float f[GT];
 #pragma unroll
-        for (int e = 0; e < C::kEPL; e += 2) {
-          const float sw = dv[e / 4] * pr[g];
-          const float2 r2 = __ffma2_rn(vx[e / 2], make_float2(sw, sw), make_float2(acc[g][e], acc[g][e + 1]));
-          acc[g][e] = r2.x;
-          acc[g][e + 1] = r2.y;
+        for (int g = 0; g < GT; g += 4) {
+          if constexpr (GT >= 4) {
+            const float4 t = lds128(&sw[r][b][g]);
+            f[g] = t.x;
+            f[g + 1] = t.y;
+            f[g + 2] = t.z;
+            f[g + 3] = t.w;
+          }
+        }
+        if constexpr (GT < 4) {
+#pragma unroll
+          for (int g = 0; g < GT; ++g) f[g] = sw[r][b][g];
+        }
+#pragma unroll
+        for (int g = 0; g < GT; ++g) {
+#pragma unroll
+          for (int e = 4 * c; e < 4 * c + 4 && e < C::kEPL; e += 2) {
+            const float2 r2 = __ffma2_rn(vx[e / 2], make_float2(f[g], f[g]), make_float2(acc[g][e], acc[g][e + 1]));
+            acc[g][e] = r2.x;
+            acc[g][e + 1] = r2.y;
+          }
         }
       }
     }
-    __syncwarp();  // every lane is done with this stage and s_p before they are refilled
+    __syncwarp();  // every lane is done with this stage and s_w before they are refilled
   }
   cp_async_wait<0>();
   trace_stamp(a.trace, 3);
